@@ -1,0 +1,124 @@
+/* B200 (sm_100a) backend of llama3.x.c's Q8_0 W8A8 kernel API: the C-ABI of libllama3x_cuda.so.
+ *
+ * Each entry point keeps the name, argument order and meaning of the reference function it replaces (cited below as
+ * include/kernels.h:LINE or include/gemm.h:LINE of LucianCrainic/llama3.x.c), with two differences:
+ *   1. Every pointer is a DEVICE pointer (CUDA global memory). Work is queued on the calling thread's stream
+ *      (kernels_set_stream; the legacy default stream until then) and the call returns before the GPU finishes;
+ *      kc_status() waits for the stream and reports errors the kernels found (non-finite activations, timeouts).
+ *   2. "Team" becomes "stream": kernels_set_stream replaces kernels_set_team / kernels_set_thread_team
+ *      (include/kernels.h:24-28).
+ * Errors keep the reference's behaviour by default: invalid arguments and CUDA failures print the message and exit(1),
+ * as fail() does (include/runtime.h:29). kc_set_fail_mode(KC_FAIL_RETURN) instead records the message
+ * (kc_last_error) and returns without queuing work, for callers that cannot lose the process.
+ *
+ * Weight layout is the checkpoint's: values row-major [rows][ld] int8 (ld a multiple of gs), scales [rows][ld / gs]
+ * fp32. Pointers passed to the GEMV/GEMM must be 16-byte aligned and n, ld multiples of 16 (cudaMalloc'd buffers with
+ * the reference's shapes satisfy this). The supported group sizes are gs % 16 == 0, gs <= 1024 for the GEMV and
+ * gs % 32 == 0 for the tensor-core GEMM; W8A32 inputs (K8Input.q == NULL) are refused. */
+#ifndef LLAMA3X_KERNELS_CUDA_H
+#define LLAMA3X_KERNELS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* include/kernels.h:101-109 */
+typedef struct {
+  const int8_t *q;
+  const float *s;
+} K8Weight;
+typedef struct {
+  const int8_t *q;
+  const float *s;
+  const float *f;
+} K8Input;
+
+/* include/kernels.h:84 */
+typedef enum { K_STORE, K_ADD, K_PARTIAL, K_SWIGLU } KernelEpilogue;
+/* include/gemm.h:15-20 */
+typedef enum { GEMM_STORE, GEMM_ADD, GEMM_SWIGLU, GEMM_PARTIAL } GemmKind;
+enum { GEMM_MAX_SEGMENTS = 3 }; /* include/gemm.h:32 */
+
+/* include/gemm.h:118-125. pw / pw3 (the reference's AMX-packed copies) are ignored: the tensor-core path reads the
+ * checkpoint's row-major values directly through TMA. */
+typedef struct {
+  float *c;
+  int ldc;
+  K8Weight w, w3;
+  const int8_t *pw, *pw3;
+  int n;
+  GemmKind kind;
+} GemmQ8Segment;
+
+/* include/gemm.h:126, extended with this backend's two kernels. PORTABLE / AVX512 / AMX are CPU rungs and are not
+ * compiled in here (k_gemm_q8_backend_test returns 0 for them, as the reference does for a rung it lacks). */
+typedef enum {
+  Q8_GEMM_PORTABLE,
+  Q8_GEMM_AVX512,
+  Q8_GEMM_AMX,
+  Q8_GEMM_GPU_DP4A = 16,   /* the row kernel (decode GEMV), one launch per activation row */
+  Q8_GEMM_GPU_TCGEN05 = 17 /* tcgen05 int8 MMA with TMEM accumulators, fed by TMA */
+} Q8GemmBackend;
+
+/* ---- set-up (include/kernels.h:16-31) ---------------------------------------------------------------------------- */
+void kernels_init(void);                /* binds the library to the current CUDA device */
+const char *kernels_name(void);         /* "sm_100a" after kernels_init, NULL before */
+void kernels_set_stream(void *stream);  /* cudaStream_t for this thread's kernels; NULL = legacy default stream */
+
+/* ---- error handling (runtime.h fail() analogue) ----------------------------------------------------------------- */
+enum { KC_FAIL_EXIT = 0, KC_FAIL_RETURN = 1 };
+void kc_set_fail_mode(int mode);
+const char *kc_last_error(void); /* last recorded message, "" if none; cleared by kc_clear_error */
+void kc_clear_error(void);
+/* Waits for this thread's stream, then returns and clears the device error bits (1 = non-finite activation in a
+ * quantizer, 2 = a bounded wait timed out, 4 = bad arguments), or -1 for a CUDA error. In KC_FAIL_EXIT mode a
+ * nonzero result fails like the reference ("nonfinite activation during INT8 quantization"). */
+int kc_status(void);
+
+/* ---- quantizer (include/kernels.h:110, include/gemm.h:130) ------------------------------------------------------- */
+void k_quantize(int8_t *q, float *s, const float *x, int n, int gs);
+void k_quantize_rows(int8_t *q, float *s, const float *x, size_t ldx, int m, int n, int gs);
+
+/* ---- decode GEMV (include/kernels.h:111-122) --------------------------------------------------------------------- */
+void k_matmul_q8(float *out, const K8Input *x, K8Weight w, int n, int d, int gs);
+void k_matmul_q8_add(float *out, const K8Input *x, K8Weight w, int n, int d, int gs);
+void k_matmul_q8_qkv(float *q, float *k, float *v, const K8Input *x, K8Weight wq, K8Weight wk, K8Weight wv, int n,
+                     int dq, int dkv, int gs);
+void k_matmul_q8_swiglu(float *out, const K8Input *x, K8Weight w1, K8Weight w3, int n, int d, int gs);
+void k_matmul_q8_ld(float *out, const K8Input *x, const K8Weight *w, size_t ld, int n, int d, int gs, int kind);
+void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, const K8Weight *w3, size_t ld, int n,
+                           int d, int gs);
+
+/* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
+void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count);
+Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count);
+
+/* ---- supporting kernels (include/kernels.h:57-68) ---------------------------------------------------------------- */
+void k_rmsnorm(float *out, const float *x, const float *weight, int size, float epsilon);
+void k_rmsnorm_rows(float *out, const float *x, const float *weight, int rows, int size, float epsilon);
+void k_rope_apply(float *q, float *k, const float *table, int n_heads, int n_kv_heads, int head_dim);
+void k_rope_apply_rows(float *q, size_t q_stride, float *k, size_t k_stride, const float *table, size_t table_stride,
+                       int rows, int n_heads, int n_kv_heads, int head_dim);
+
+/* Fused RMSNorm + quantize: the reference's k_rmsnorm_rows followed by k_quantize_rows (src/tp.c:403-404,
+ * src/tp.c:539-540) in one kernel. `out` (the fp32 normalized rows, stride size) may be NULL. Bitwise equal to the
+ * pair on the reference's AVX-512 ISA. */
+void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t ldx, const float *weight, int rows,
+                       int size, float epsilon, int gs);
+
+/* ---- test hooks (include/testing.h:67-69) ------------------------------------------------------------------------ */
+/* One named backend; returns 0 when it is not compiled in (the CPU rungs). */
+int k_gemm_q8_backend_test(Q8GemmBackend backend, const int8_t *xq, const float *xs, int m, int k, int gs,
+                           const GemmQ8Segment *segments, int count);
+/* The exact int32 group dots of the tensor-core kernel, dots[(g * m + r) * n + c] (k_gemm_q8_amx_dots_test's layout),
+ * from row-major weights wq[n][k] instead of an AMX-packed copy. Returns 0 when unsupported. */
+int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, const int8_t *wq, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,322 @@
+// The C-ABI of libllama3x_cuda.so (include/kernels_cuda.h): argument checks with the reference's messages, the
+// fail()-style error policy, the per-thread stream, and dispatch to the kernels.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../../include/kernels_cuda.h"
+#include "common.cuh"
+#include "kernels_cuda_internal.h"
+
+__device__ unsigned kc_error_word;
+
+namespace {
+
+thread_local cudaStream_t tl_stream = nullptr;
+thread_local char tl_error[512];
+int fail_mode = KC_FAIL_EXIT;
+bool initialized = false;
+
+}  // namespace
+
+static bool kc_fail(const char *format, ...) {
+  va_list args;
+  va_start(args, format);
+  vsnprintf(tl_error, sizeof(tl_error), format, args);
+  va_end(args);
+  if (fail_mode == KC_FAIL_EXIT) {
+    fprintf(stderr, "error: %s\n", tl_error);
+    exit(EXIT_FAILURE);
+  }
+  return false;
+}
+
+static bool launched(int rc, const char *what) {
+  if (rc == 0)
+    return true;
+  if (rc == -1)
+    return kc_fail("%s: shape not supported by the sm_100a kernels", what);
+  return kc_fail("%s: CUDA launch failed: %s", what, cudaGetErrorString(cudaGetLastError()));
+}
+
+int kc_device_sms() {
+  static int sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64)
+    return 148;
+  if (!sms[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = v > 0 ? v : 148;
+  }
+  return sms[dev];
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+extern "C" {
+
+void kernels_init(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaFree(nullptr) != cudaSuccess) {
+    kc_fail("kernels_init: no usable CUDA device");
+    return;
+  }
+  cudaDeviceProp prop;
+  cudaGetDeviceProperties(&prop, dev);
+  if (prop.major != 10) {
+    kc_fail("kernels_init: device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, prop.major,
+            prop.minor);
+    return;
+  }
+  kc_device_sms();
+  initialized = true;
+}
+
+const char *kernels_name(void) { return initialized ? "sm_100a" : NULL; }
+
+void kernels_set_stream(void *stream) { tl_stream = static_cast<cudaStream_t>(stream); }
+
+void kc_set_fail_mode(int mode) { fail_mode = mode == KC_FAIL_RETURN ? KC_FAIL_RETURN : KC_FAIL_EXIT; }
+
+const char *kc_last_error(void) { return tl_error; }
+
+void kc_clear_error(void) { tl_error[0] = 0; }
+
+int kc_status(void) {
+  cudaError_t e = cudaStreamSynchronize(tl_stream);
+  if (e != cudaSuccess) {
+    kc_fail("CUDA error: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  unsigned bits = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&bits, kc_error_word, sizeof(bits)) != cudaSuccess) {
+    kc_fail("CUDA error reading the device error word");
+    return -1;
+  }
+  if (bits) {
+    cudaMemcpyToSymbol(kc_error_word, &zero, sizeof(zero));
+    if (bits & KC_ERR_NONFINITE)
+      kc_fail("nonfinite activation during INT8 quantization");
+    else if (bits & KC_ERR_TIMEOUT)
+      kc_fail("a device-side wait timed out");
+    else
+      kc_fail("a kernel rejected its arguments");
+  }
+  return (int)bits;
+}
+
+// ---- quantizer ----------------------------------------------------------------------------------------------------
+
+void k_quantize_rows(int8_t *q, float *s, const float *x, size_t ldx, int m, int n, int gs) {
+  if (gs <= 0 || m < 0 || n < 0 || ldx < (size_t)n) {
+    kc_fail("k_quantize_rows: invalid shape m=%d n=%d ldx=%zu gs=%d", m, n, ldx, gs);
+    return;
+  }
+  launched(kc_launch_quantize_rows(q, s, x, (long long)ldx, m, n, gs, tl_stream), "k_quantize_rows");
+}
+
+void k_quantize(int8_t *q, float *s, const float *x, int n, int gs) { k_quantize_rows(q, s, x, (size_t)n, 1, n, gs); }
+
+// ---- decode GEMV --------------------------------------------------------------------------------------------------
+
+static bool gemv_shape_ok(const char *name, const K8Input *x, size_t ld, int n, int gs) {
+  if (!x || !x->q || !x->s)
+    return kc_fail("%s: W8A32 activations (K8Input.q == NULL) are not supported by the sm_100a backend", name);
+  if (gs <= 0 || gs % 16 || gs > 1024)
+    return kc_fail("%s: group size %d is not supported (need a multiple of 16 up to 1024)", name, gs);
+  if (n < 0 || n % gs)
+    return kc_fail("%s: %d inputs are not a whole number of %d-groups", name, n, gs);
+  if (ld < (size_t)n || ld % (size_t)gs)
+    return kc_fail("%s: row stride %zu must be at least %d and a multiple of the group size %d", name, ld, n, gs);
+  if (!aligned16(x->q))
+    return kc_fail("%s: activations must be 16-byte aligned", name);
+  return true;
+}
+
+static bool weight_ok(const char *name, K8Weight w) {
+  if (!w.q || !w.s)
+    return kc_fail("%s: missing weight values or scales", name);
+  if (!aligned16(w.q))
+    return kc_fail("%s: weight values must be 16-byte aligned", name);
+  return true;
+}
+
+static void gemv(const char *name, const KcGemvSeg *segs, int nseg, const K8Input *x, size_t ld, int n, int gs,
+                 int kind) {
+  if (!gemv_shape_ok(name, x, ld, n, gs))
+    return;
+  for (int i = 0; i < nseg; i++) {
+    if (segs[i].d < 0) {
+      kc_fail("%s: negative row count", name);
+      return;
+    }
+    if (!weight_ok(name, K8Weight{segs[i].wq, segs[i].ws}) ||
+        (kind == KC_SWIGLU && !weight_ok(name, K8Weight{segs[i].w3q, segs[i].w3s})))
+      return;
+  }
+  launched(kc_launch_gemv(segs, nseg, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
+}
+
+void k_matmul_q8(float *out, const K8Input *x, K8Weight w, int n, int d, int gs) {
+  KcGemvSeg s = {out, w.q, w.s, nullptr, nullptr, d};
+  gemv("k_matmul_q8", &s, 1, x, (size_t)n, n, gs, KC_STORE);
+}
+
+void k_matmul_q8_add(float *out, const K8Input *x, K8Weight w, int n, int d, int gs) {
+  KcGemvSeg s = {out, w.q, w.s, nullptr, nullptr, d};
+  gemv("k_matmul_q8_add", &s, 1, x, (size_t)n, n, gs, KC_ADD);
+}
+
+void k_matmul_q8_qkv(float *q, float *k, float *v, const K8Input *x, K8Weight wq, K8Weight wk, K8Weight wv, int n,
+                     int dq, int dkv, int gs) {
+  KcGemvSeg s[3] = {{q, wq.q, wq.s, nullptr, nullptr, dq},
+                    {k, wk.q, wk.s, nullptr, nullptr, dkv},
+                    {v, wv.q, wv.s, nullptr, nullptr, dkv}};
+  gemv("k_matmul_q8_qkv", s, 3, x, (size_t)n, n, gs, KC_STORE);
+}
+
+void k_matmul_q8_swiglu(float *out, const K8Input *x, K8Weight w1, K8Weight w3, int n, int d, int gs) {
+  KcGemvSeg s = {out, w1.q, w1.s, w3.q, w3.s, d};
+  gemv("k_matmul_q8_swiglu", &s, 1, x, (size_t)n, n, gs, KC_SWIGLU);
+}
+
+void k_matmul_q8_ld(float *out, const K8Input *x, const K8Weight *w, size_t ld, int n, int d, int gs, int kind) {
+  if (kind != K_STORE && kind != K_ADD && kind != K_PARTIAL) {
+    kc_fail("k_matmul_q8_ld: invalid epilogue kind %d", kind);
+    return;
+  }
+  KcGemvSeg s = {out, w->q, w->s, nullptr, nullptr, d};
+  gemv("k_matmul_q8_ld", &s, 1, x, ld, n, gs, kind);
+}
+
+void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, const K8Weight *w3, size_t ld, int n,
+                           int d, int gs) {
+  KcGemvSeg s = {out, w1->q, w1->s, w3->q, w3->s, d};
+  gemv("k_matmul_q8_swiglu_ld", &s, 1, x, ld, n, gs, KC_SWIGLU);
+}
+
+// ---- batched prefill GEMM -----------------------------------------------------------------------------------------
+
+static int kc_kind_of(GemmKind k) {
+  switch (k) {
+    case GEMM_STORE: return KC_STORE;
+    case GEMM_ADD: return KC_ADD;
+    case GEMM_SWIGLU: return KC_SWIGLU;
+    case GEMM_PARTIAL: return KC_PARTIAL;
+  }
+  return -1;
+}
+
+static bool gemm_args_ok(const char *name, const int8_t *xq, const float *xs, int m, int k, int gs,
+                         const GemmQ8Segment *segments, int count) {
+  if (count < 1 || count > GEMM_MAX_SEGMENTS)
+    return kc_fail("GEMM needs 1..%d segments, got %d", GEMM_MAX_SEGMENTS, count);
+  if (gs <= 0 || k % gs)
+    return kc_fail("Q8 GEMM: K=%d is not a multiple of the group size %d", k, gs);
+  for (int s = 0; s < count; s++) {
+    if (kc_kind_of(segments[s].kind) < 0)
+      return kc_fail("%s: invalid GEMM kind %d", name, (int)segments[s].kind);
+    if (segments[s].kind == GEMM_SWIGLU && !segments[s].w3.q)
+      return kc_fail("GEMM_SWIGLU needs a second weight matrix");
+    if (segments[s].ldc < segments[s].n)
+      return kc_fail("%s: ldc %d is shorter than the %d outputs", name, segments[s].ldc, segments[s].n);
+  }
+  if (m < 0 || k < 0)
+    return kc_fail("%s: negative shape", name);
+  (void)xq, (void)xs;
+  return true;
+}
+
+static void gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
+                           int count) {
+  // One row-kernel launch per activation row; the segments of a row share one launch (they share the activations).
+  int groups = k / gs;
+  for (int r = 0; r < m; r++) {
+    for (int s = 0; s < count; s++) {
+      const GemmQ8Segment &g = segments[s];
+      KcGemvSeg seg = {g.c + (size_t)r * g.ldc, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
+      K8Input in = {xq + (size_t)r * k, xs + (size_t)r * groups, nullptr};
+      gemv("k_gemm_q8", &seg, 1, &in, (size_t)k, k, gs, kc_kind_of(g.kind));
+    }
+  }
+}
+
+Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count) {
+  (void)gs, (void)segments, (void)count;
+  return Q8_GEMM_GPU_DP4A;
+}
+
+static bool gemm_run(Q8GemmBackend backend, const int8_t *xq, const float *xs, int m, int k, int gs,
+                     const GemmQ8Segment *segments, int count) {
+  if (!gemm_args_ok("k_gemm_q8", xq, xs, m, k, gs, segments, count))
+    return true;
+  if (m == 0 || k == 0)
+    return true;
+  if (backend == Q8_GEMM_GPU_DP4A) {
+    gemm_rows_dp4a(xq, xs, m, k, gs, segments, count);
+    return true;
+  }
+  return false;
+}
+
+void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count) {
+  gemm_run(k_gemm_q8_pick(gs, segments, count), xq, xs, m, k, gs, segments, count);
+}
+
+int k_gemm_q8_backend_test(Q8GemmBackend backend, const int8_t *xq, const float *xs, int m, int k, int gs,
+                           const GemmQ8Segment *segments, int count) {
+  if (backend != Q8_GEMM_GPU_DP4A)
+    return 0;
+  return gemm_run(backend, xq, xs, m, k, gs, segments, count) ? 1 : 0;
+}
+
+int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, const int8_t *wq, int n) {
+  (void)dots, (void)xq, (void)m, (void)k, (void)gs, (void)wq, (void)n;
+  return 0;
+}
+
+// ---- supporting kernels -------------------------------------------------------------------------------------------
+
+void k_rmsnorm_rows(float *out, const float *x, const float *weight, int rows, int size, float epsilon) {
+  if (rows < 0 || size <= 0) {
+    kc_fail("k_rmsnorm_rows: invalid shape rows=%d size=%d", rows, size);
+    return;
+  }
+  launched(kc_launch_rmsnorm(out, nullptr, nullptr, x, weight, rows, size, size, epsilon, 0, tl_stream),
+           "k_rmsnorm_rows");
+}
+
+void k_rmsnorm(float *out, const float *x, const float *weight, int size, float epsilon) {
+  k_rmsnorm_rows(out, x, weight, 1, size, epsilon);
+}
+
+void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t ldx, const float *weight, int rows,
+                       int size, float epsilon, int gs) {
+  if (rows < 0 || size <= 0 || gs <= 0 || size % gs || gs > 256 || ldx < (size_t)size) {
+    kc_fail("k_rmsnorm_q8_rows: invalid shape rows=%d size=%d ldx=%zu gs=%d", rows, size, ldx, gs);
+    return;
+  }
+  launched(kc_launch_rmsnorm(out, q, s, x, weight, rows, size, (long long)ldx, epsilon, gs, tl_stream),
+           "k_rmsnorm_q8_rows");
+}
+
+void k_rope_apply_rows(float *q, size_t q_stride, float *k, size_t k_stride, const float *table, size_t table_stride,
+                       int rows, int n_heads, int n_kv_heads, int head_dim) {
+  if (rows < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_kv_heads > n_heads || head_dim <= 0 || head_dim % 2) {
+    kc_fail("k_rope_apply_rows: invalid shape");
+    return;
+  }
+  launched(kc_launch_rope_rows(q, (long long)q_stride, k, (long long)k_stride, table, (long long)table_stride, rows,
+                               n_heads, n_kv_heads, head_dim, tl_stream),
+           "k_rope_apply_rows");
+}
+
+void k_rope_apply(float *q, float *k, const float *table, int n_heads, int n_kv_heads, int head_dim) {
+  k_rope_apply_rows(q, 0, k, 0, table, 0, 1, n_heads, n_kv_heads, head_dim);
+}
+
+}  // extern "C"

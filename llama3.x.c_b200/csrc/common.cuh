@@ -1,0 +1,115 @@
+// Shared device helpers for the sm_100a Q8_0 kernels: the device error word, bounded mbarrier waits, 1-D bulk
+// (TMA) copies, and the exact float epilogues the reference's C source implies.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// Error bits the kernels set in the per-device error word (read back by the C-ABI layer, kc_status()).
+enum : unsigned {
+  KC_ERR_NONFINITE = 1u,   // k_quantize met a non-finite activation (src/gemv.c:599-600 fails the same way)
+  KC_ERR_TIMEOUT = 2u,     // a bounded wait on an mbarrier or flag gave up
+  KC_ERR_BAD_ARGS = 4u,    // a kernel was launched with arguments its host checks should have refused
+};
+
+// One word per device, in the library's own device memory; kernels OR error bits into it.
+extern __device__ unsigned kc_error_word;
+
+__device__ __forceinline__ void kc_raise(unsigned bits) { atomicOr(&kc_error_word, bits); }
+
+__device__ __forceinline__ uint64_t kc_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every spin in this library gives up after this many nanoseconds and raises KC_ERR_TIMEOUT.
+constexpr uint64_t KC_WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete; false (and KC_ERR_TIMEOUT raised) after KC_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity))
+    return true;
+  uint64_t start = kc_globaltimer();
+  for (unsigned i = 1;; i++) {
+    if (mbar_try_wait(bar, parity))
+      return true;
+    if ((i & 255u) == 0 && kc_globaltimer() - start > KC_WAIT_NS) {
+      kc_raise(KC_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// 1-D bulk copy global -> shared through the TMA unit, completing `bytes` of transaction count on `bar`.
+// dst and src 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ int4 lds128(const void *p) {
+  int4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
+__device__ __forceinline__ int dot16(int4 a, int4 b, int acc) {
+  acc = __dp4a(a.x, b.x, acc);
+  acc = __dp4a(a.y, b.y, acc);
+  acc = __dp4a(a.z, b.z, acc);
+  acc = __dp4a(a.w, b.w, acc);
+  return acc;
+}
+
+// silu_gate (src/gemv.c:246-250): value *= 1 / (1 + expf(-value)); value * gate. The exponential is taken in double
+// and rounded once to float, which agrees with glibc's expf (error < 0.502 ulp) except where the exact value lies
+// within a hair of a float rounding midpoint.
+__device__ __forceinline__ float silu_gate_dev(float value, float gate) {
+  float e = (float)exp(-(double)value);
+  value = __fmul_rn(value, __fdiv_rn(1.0f, __fadd_rn(1.0f, e)));
+  return __fmul_rn(value, gate);
+}
+
+// k_quantize's per-value rule (src/gemv.c:617-621): q = (int8)roundf(clamp(x / scale, -127, 127)), 0 when scale == 0.
+__device__ __forceinline__ int quantize_value(float x, float scale) {
+  float v = scale == 0.0f ? 0.0f : __fdiv_rn(x, scale);
+  v = fmaxf(-127.0f, fminf(127.0f, v));
+  return (int)roundf(v);
+}

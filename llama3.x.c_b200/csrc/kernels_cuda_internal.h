@@ -1,0 +1,33 @@
+// Internal interface between the C-ABI layer (abi.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// Epilogue kinds, numerically equal to the reference's KernelEpilogue / GemmKind (include/kernels.h:84,
+// include/gemm.h:15-20): STORE, ADD, PARTIAL, SWIGLU.
+enum { KC_STORE = 0, KC_ADD = 1, KC_PARTIAL = 2, KC_SWIGLU = 3 };
+
+struct KcGemvSeg {
+  float *out;
+  const int8_t *wq;
+  const float *ws;
+  const int8_t *w3q;  // SWIGLU only
+  const float *w3s;
+  int d;
+};
+
+int kc_device_sms();
+
+// Returns 0 on launch, -1 for a shape the kernel does not support, -2 on a launch error.
+int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                   int kind, cudaStream_t stream, int grid_limit);
+
+int kc_launch_quantize_rows(int8_t *q, float *s, const float *x, long long ldx, int m, int n, int gs,
+                            cudaStream_t stream);
+int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const float *w, int rows, int size,
+                      long long ldx, float eps, int gs, cudaStream_t stream);
+int kc_launch_rope_rows(float *q, long long q_stride, float *k, long long k_stride, const float *table,
+                        long long table_stride, int rows, int n_heads, int n_kv_heads, int head_dim,
+                        cudaStream_t stream);

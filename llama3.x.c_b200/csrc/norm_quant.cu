@@ -1,0 +1,193 @@
+// Activation quantizer, RMSNorm (+ fused quantize) and RoPE for sm_100a.
+//
+// - quantize_rows_kernel: k_quantize / k_quantize_rows (src/gemv.c:589-624, src/gemm.c:818-830), one warp per group.
+//   max|x| is exact in any order; the scale is the IEEE quotient max / 127.0f and each value is
+//   roundf(clamp(x / scale)), so the int8 values and scales are bitwise the reference's on every ISA.
+// - rmsnorm_kernel: rmsnorm_avx512's order (src/kernels_simd.c:136-161), reproduced lane for lane: 64 threads keep
+//   the four 16-lane FMA accumulators over 64-value steps (tail into the first), then (a0+a1)+(a2+a3) and GCC's
+//   _mm512_reduce_add_ps tree, then ss / size + eps, 1 / sqrtf, o = w * (ss * x). With `q` set, the output is also
+//   quantized in gs-groups in the same kernel (the k_rmsnorm -> k_quantize pair of src/tp.c:403-404 fused).
+// - rope_rows_kernel: k_rope_apply (src/kernels_simd.c:203-227): a*c - b*s and a*s + b*c without contraction, from a
+//   host-computed table (k_rope_table), so the rotation is bitwise the reference's.
+#include "common.cuh"
+#include "kernels_cuda_internal.h"
+
+namespace {
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__global__ void quantize_rows_kernel(int8_t *q, float *s, const float *x, long long ldx, int m, int n, int gs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = n / gs;
+  const long long gid = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (gid >= (long long)m * groups)
+    return;
+  const int row = (int)(gid / groups), g = (int)(gid - (long long)row * groups);
+  const float *xg = x + row * ldx + (long long)g * gs;
+  float mx = 0.0f;
+  int bad = 0;
+  for (int i = lane; i < gs; i += 32) {
+    float v = xg[i];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0)
+      kc_raise(KC_ERR_NONFINITE);
+    return;
+  }
+  mx = warp_max(mx);
+  const float scale = __fdiv_rn(mx, 127.0f);
+  if (lane == 0)
+    s[(long long)row * groups + g] = scale;
+  int8_t *qg = q + (long long)row * n + (long long)g * gs;
+  for (int i = lane; i < gs; i += 32)
+    qg[i] = (int8_t)quantize_value(xg[i], scale);
+}
+
+constexpr int kNormThreads = 256;
+constexpr int kMaxValuesPerLane = 8;  // fused quantize: gs <= 256
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_t *q, float *s, const float *x,
+                                                                const float *w, int size, long long ldx, float eps,
+                                                                int gs) {
+  __shared__ float lanes[64];
+  __shared__ float inv;
+  const int tid = threadIdx.x, row = blockIdx.x;
+  const float *xr = x + row * ldx;
+  if (tid < 64) {
+    float a = 0.0f;
+    int j = 0;
+    for (; j + 64 <= size; j += 64)
+      a = __fmaf_rn(xr[j + tid], xr[j + tid], a);
+    if (tid < 16)
+      for (; j < size; j += 16)
+        if (j + tid < size)
+          a = __fmaf_rn(xr[j + tid], xr[j + tid], a);
+    lanes[tid] = a;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float v[16], t8[8], t4[4];
+    for (int l = 0; l < 16; l++)
+      v[l] = __fadd_rn(__fadd_rn(lanes[l], lanes[16 + l]), __fadd_rn(lanes[32 + l], lanes[48 + l]));
+    for (int l = 0; l < 8; l++)
+      t8[l] = __fadd_rn(v[8 + l], v[l]);
+    for (int l = 0; l < 4; l++)
+      t4[l] = __fadd_rn(t8[4 + l], t8[l]);
+    float ss = __fadd_rn(__fadd_rn(t4[0], t4[2]), __fadd_rn(t4[1], t4[3]));
+    ss = __fdiv_rn(ss, (float)size);
+    ss = __fadd_rn(ss, eps);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+  }
+  __syncthreads();
+  const float ss = inv;
+  if (!q) {
+    float *orow = out + (long long)row * size;
+    for (int j = tid; j < size; j += kNormThreads)
+      orow[j] = __fmul_rn(w[j], __fmul_rn(ss, xr[j]));
+    return;
+  }
+  const int warp = tid >> 5, lane = tid & 31, groups = size / gs;
+  for (int g = warp; g < groups; g += kNormThreads / 32) {
+    float o[kMaxValuesPerLane];
+    float mx = 0.0f;
+#pragma unroll
+    for (int t = 0; t < kMaxValuesPerLane; t++) {
+      int i = lane + 32 * t;
+      if (i < gs) {
+        int j = g * gs + i;
+        o[t] = __fmul_rn(w[j], __fmul_rn(ss, xr[j]));
+        mx = fmaxf(mx, fabsf(o[t]));
+      }
+    }
+    int bad = 0;
+#pragma unroll
+    for (int t = 0; t < kMaxValuesPerLane; t++)
+      if (lane + 32 * t < gs)
+        bad |= !isfinite(o[t]);
+    if (__any_sync(0xffffffffu, bad)) {
+      if (lane == 0)
+        kc_raise(KC_ERR_NONFINITE);
+      return;
+    }
+    mx = warp_max(mx);
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (lane == 0)
+      s[(long long)row * groups + g] = scale;
+#pragma unroll
+    for (int t = 0; t < kMaxValuesPerLane; t++) {
+      int i = lane + 32 * t;
+      if (i < gs) {
+        long long j = (long long)g * gs + i;
+        q[(long long)row * size + j] = (int8_t)quantize_value(o[t], scale);
+        if (out)
+          out[(long long)row * size + j] = o[t];
+      }
+    }
+  }
+}
+
+__global__ void rope_rows_kernel(float *q, long long q_stride, float *k, long long k_stride, const float *table,
+                                 long long table_stride, int rows, int n_heads, int n_kv_heads, int head_dim) {
+  const int half = head_dim / 2;
+  const int per_row = (n_heads + n_kv_heads) * half;
+  const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (long long)rows * per_row)
+    return;
+  const int row = (int)(id / per_row);
+  int p = (int)(id - (long long)row * per_row);
+  float *v;
+  if (p < n_heads * half) {
+    v = q + row * q_stride;
+  } else {
+    p -= n_heads * half;
+    v = k + row * k_stride;
+  }
+  const int h = p / half, j = 2 * (p - h * half);
+  const float *t = table + row * table_stride;
+  const float c = t[j], sn = t[head_dim + j + 1];
+  float *e = v + (long long)h * head_dim + j;
+  const float a = e[0], b = e[1];
+  e[0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+  e[1] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+}
+
+}  // namespace
+
+int kc_launch_quantize_rows(int8_t *q, float *s, const float *x, long long ldx, int m, int n, int gs,
+                            cudaStream_t stream) {
+  long long groups = (long long)m * (n / gs);
+  if (groups == 0)
+    return 0;
+  const int warps = 8;
+  quantize_rows_kernel<<<(unsigned)((groups + warps - 1) / warps), warps * 32, 0, stream>>>(q, s, x, ldx, m, n, gs);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const float *w, int rows, int size,
+                      long long ldx, float eps, int gs, cudaStream_t stream) {
+  if (rows == 0 || size == 0)
+    return 0;
+  if (q && (gs <= 0 || gs > 32 * kMaxValuesPerLane || size % gs))
+    return -1;
+  rmsnorm_kernel<<<rows, kNormThreads, 0, stream>>>(out, q, s, x, w, size, ldx, eps, gs);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+int kc_launch_rope_rows(float *q, long long q_stride, float *k, long long k_stride, const float *table,
+                        long long table_stride, int rows, int n_heads, int n_kv_heads, int head_dim,
+                        cudaStream_t stream) {
+  long long total = (long long)rows * (n_heads + n_kv_heads) * (head_dim / 2);
+  if (total == 0)
+    return 0;
+  rope_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(q, q_stride, k, k_stride, table,
+                                                                          table_stride, rows, n_heads, n_kv_heads,
+                                                                          head_dim);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

@@ -1,0 +1,61 @@
+/* TEST INFRASTRUCTURE ONLY -- never linked into, loaded by, or called from the product path.
+ *
+ * CPU restatement of the reference's Q8_0 W8A8 hot path (LucianCrainic/llama3.x.c), used by tests/, by
+ * __graft_entry__.smoke() and by bench.py's cpu_baseline leg as the checker. Every function names the reference
+ * file:line it restates. Parity is pinned two ways (tests/test_oracle.py):
+ *   - against the reference itself, compiled from its own sources into oracle/_ref/ by oracle/Makefile, on seeded
+ *     inputs (when oracle/_ref is present);
+ *   - against golden vectors under tests/golden/ produced by that compiled reference (tests/golden/make_golden.py),
+ *     including the reference test suite's own known-answer quantizer ties (tests/kernels.c:111-116).
+ * Functions return 0 on success and a negative code where the reference would call fail(). */
+#ifndef Q8_ORACLE_H
+#define Q8_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ORC_STORE = 0, ORC_ADD = 1, ORC_PARTIAL = 2, ORC_SWIGLU = 3 };
+
+/* k_quantize (src/gemv.c:589-624): per group max|x| (non-finite input fails), scale = max / 127.0f,
+ * q = (int8)roundf(clamp(x / scale, -127, 127)), q = 0 when the scale is 0. Returns -1 on non-finite input. */
+int orc_quantize(int8_t *q, float *s, const float *x, int n, int gs);
+/* k_quantize_rows (src/gemm.c:818-830): k_quantize per row; row r of x has stride ldx, of q stride n, of s n/gs. */
+int orc_quantize_rows(int8_t *q, float *s, const float *x, size_t ldx, int m, int n, int gs);
+
+/* Exact int32 group dots, dots[(g * m + r) * n + c] (the layout of k_gemm_q8_amx_dots_test, src/gemm.c:1043-1066). */
+void orc_group_dots(int32_t *dots, const int8_t *xq, int m, int k, int gs, const int8_t *wq, size_t ldw, int n);
+
+/* The scalar GEMV order (q8_dots, src/gemv.c:417-438): val += ((float)ival) * ws * xs per group, ascending. */
+void orc_gemv_scalar(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, size_t ld,
+                     int n, int d, int gs);
+
+/* The AMX-INT8 order (amx_q8_chunk, src/gemm.c:554-610): acc = fmaf((float)dot * xs, ws, acc) per group, ascending,
+ * from acc = 0. C[m][n] for one segment; `kind` applies the epilogue of q8_gemm_chunks (src/gemm.c:963-989):
+ * STORE / PARTIAL write, ADD accumulates, SWIGLU writes silu_gate(acc(w), acc(w3)). */
+void orc_gemm_amx_order(float *c, int ldc, const int8_t *xq, const float *xs, int m, int k, int gs, const int8_t *wq,
+                        const float *ws, const int8_t *w3q, const float *w3s, size_t ldw, int n, int kind);
+
+/* silu_gate (src/gemv.c:246-250). */
+float orc_silu_gate(float value, float gate);
+
+/* rmsnorm_eps, the scalar order (src/kernels.c:8-21). */
+void orc_rmsnorm_scalar(float *o, const float *x, const float *w, int size, float eps);
+/* rmsnorm_avx512 (src/kernels_simd.c:136-161): four 16-lane FMA accumulators over 64-value steps, a masked tail into
+ * the first, _mm512_reduce_add_ps of (a0 + a1) + (a2 + a3), then the scalar epilogue. */
+void orc_rmsnorm_avx512_order(float *o, const float *x, const float *w, int size, float eps);
+
+/* k_rope_table (src/kernels_simd.c:194-201) with rope_frequency (src/kernels.c:49-60); k_rope_apply scalar
+ * (src/kernels_simd.c:203-227). */
+void orc_rope_table(float *table, int position, int head_dim, float theta, int rope_type, float factor, float low,
+                    float high, int original);
+void orc_rope_apply(float *q, float *k, const float *table, int n_heads, int n_kv_heads, int head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

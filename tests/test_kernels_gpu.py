@@ -1,0 +1,268 @@
+"""GPU parity tests of the sm_100a kernels through the C-ABI, against the oracle (and the reference's golden vectors).
+
+Bar (written per test): bit-exact for int8 values, scales, int32 group dots and the fp32 GEMV/GEMM outputs, which
+follow the reference's AMX-INT8 rescale order; within the reference's own budget (2e-5 * sum|w.x| + 1e-6,
+tests/kernels.c:138-170) against its scalar GEMV; SwiGLU within 2 ulp (expf) of the oracle.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(Path(__file__).parent / "golden" / "q8_golden.npz")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+def bits(a):
+    a = np.ascontiguousarray(a)
+    return a.view(np.int32) if a.dtype == np.float32 else a
+
+
+def ulp_diff(a, b):
+    a, b = bits(np.asarray(a, np.float32)).astype(np.int64), bits(np.asarray(b, np.float32)).astype(np.int64)
+    a = np.where(a < 0, -(a & 0x7FFFFFFF), a)
+    b = np.where(b < 0, -(b & 0x7FFFFFFF), b)
+    return np.abs(a - b)
+
+
+# ---- quantizer ------------------------------------------------------------------------------------------------------
+
+def test_quantize_ties_known_answer(kc):
+    x, gs = GOLDEN["quant_ties_x"], int(GOLDEN["quant_ties_gs"])
+    q, s = kc.quantize(dev(x), gs)
+    kc.status()
+    assert (host(q) == GOLDEN["quant_ties_q"]).all()
+    assert (bits(host(s)) == bits(GOLDEN["quant_ties_s"])).all()
+
+
+@pytest.mark.parametrize("n,gs", [(256, 64), (4096, 64), (512, 128), (192, 32), (1792, 64)])
+def test_quantize_golden(kc, n, gs):
+    q, s = kc.quantize(dev(GOLDEN[f"quant_{n}_{gs}_x"]), gs)
+    kc.status()
+    assert (host(q) == GOLDEN[f"quant_{n}_{gs}_q"]).all()
+    assert (bits(host(s)) == bits(GOLDEN[f"quant_{n}_{gs}_s"])).all()
+
+
+@pytest.mark.parametrize("m,n,gs,ldx", [(1, 64, 64, 64), (7, 4096, 64, 4100), (128, 14336, 64, 14336),
+                                        (3, 96, 16, 96), (2, 2048, 256, 2048)])
+def test_quantize_rows_matches_oracle(kc, oracle, m, n, gs, ldx):
+    rng = np.random.default_rng(m * n)
+    x = (rng.standard_normal((m, ldx)) * rng.uniform(1e-3, 1e3, (m, 1))).astype(np.float32)
+    x[:, :gs] = 0.0  # an all-zero group per row: scale 0, values 0
+    xt = dev(x)
+    q = torch.empty((m, n), dtype=torch.int8, device="cuda")
+    s = torch.empty((m, n // gs), dtype=torch.float32, device="cuda")
+    kc.k_quantize_rows(q, s, xt, ldx, m, n, gs)
+    kc.status()
+    oq, os_ = oracle.quantize(x[:, :n], gs)
+    assert (host(q) == oq).all()
+    assert (bits(host(s)) == bits(os_)).all()
+
+
+def test_quantize_nonfinite_fails_like_the_reference(kc):
+    x = torch.ones(128, device="cuda")
+    x[70] = float("nan")
+    kc.quantize(x, 64)
+    with pytest.raises(kc.KernelError, match="nonfinite activation"):
+        kc.status()
+    assert kc.status() == 0  # the error word was cleared
+
+
+def test_invalid_arguments_fail_like_the_reference(kc):
+    x = torch.ones(128, device="cuda")
+    q = torch.empty(128, dtype=torch.int8, device="cuda")
+    s = torch.empty(2, device="cuda")
+    w = torch.empty((4, 128), dtype=torch.int8, device="cuda")
+    with pytest.raises(kc.KernelError, match="row stride"):
+        kc.k_matmul_q8_ld(torch.empty(4, device="cuda"), q, s, w, s, 100, 128, 4, 64, kc.K_STORE)
+    with pytest.raises(kc.KernelError, match="invalid epilogue kind"):
+        kc.k_matmul_q8_ld(torch.empty(4, device="cuda"), q, s, w, s, 128, 128, 4, 64, kc.K_SWIGLU)
+    with pytest.raises(kc.KernelError, match="segments"):
+        kc.k_gemm_q8(q, s, 1, 128, 64, [])
+
+
+# ---- decode GEMV ----------------------------------------------------------------------------------------------------
+
+def make_case(oracle, d, n, gs, seed, ld=None):
+    rng = np.random.default_rng(seed)
+    ld = ld or n
+    wq, ws = oracle.seeded_q8_matrix(d, ld, gs, seed)
+    xq, xs = oracle.quantize(rng.standard_normal(n).astype(np.float32), gs)
+    return wq, ws, xq, xs
+
+
+GEMV_SHAPES = [(37, 1024, 64), (8192, 2048, 64), (4096, 14336, 64), (1, 64, 64), (33, 192, 32), (300, 512, 16),
+               (65, 1024, 128), (6144, 4096, 64), (77, 1792, 64)]
+
+
+@pytest.mark.parametrize("d,n,gs", GEMV_SHAPES)
+def test_gemv_store_bitwise(kc, oracle, d, n, gs):
+    wq, ws, xq, xs = make_case(oracle, d, n, gs, d + n)
+    y = kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs)
+    kc.status()
+    ref = oracle.gemm(xq, xs, wq, ws, gs)[0]
+    assert (bits(host(y)) == bits(ref)).all()
+
+
+def test_gemv_golden_amx_and_scalar(kc, oracle):
+    key = "amx_1_40_512"
+    if key + "_c" in GOLDEN:
+        y = kc.gemv(dev(GOLDEN[key + "_xq"][0]), dev(GOLDEN[key + "_xs"][0]), dev(GOLDEN[key + "_wq"]),
+                    dev(GOLDEN[key + "_ws"]), 64)
+        kc.status()
+        assert (bits(host(y)) == bits(GOLDEN[key + "_c"][0])).all()
+    for d, n in [(37, 1024), (16, 4096)]:
+        k = f"gemv_{d}_{n}"
+        wq, ws, xq, xs = (GOLDEN[k + s] for s in ("_wq", "_ws", "_xq", "_xs"))
+        y = host(kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), 64))
+        kc.status()
+        dots = oracle.group_dots(xq, wq, 64)[:, 0, :].astype(np.float64)
+        mag = oracle.group_dots(np.abs(xq).astype(np.int8), np.abs(wq).astype(np.int8), 64)[:, 0, :]
+        exact = (dots * ws.T * xs[:, None]).sum(0)
+        budget = 2e-5 * (mag * ws.T * xs[:, None]).sum(0) + 1e-6
+        assert np.all(np.abs(y - GOLDEN[k + "_y"]) <= 2 * budget)
+        assert np.all(np.abs(y - exact) <= budget)
+
+
+@pytest.mark.parametrize("d,n,gs", [(37, 1024, 64), (4096, 4096, 64)])
+def test_gemv_add_and_partial(kc, oracle, d, n, gs):
+    wq, ws, xq, xs = make_case(oracle, d, n, gs, 7)
+    base = np.random.default_rng(1).standard_normal(d).astype(np.float32)
+    out = dev(base)
+    kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs, kind=kc.K_ADD, out=out)
+    part = kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs, kind=kc.K_PARTIAL)
+    kc.status()
+    ref = oracle.gemm(xq, xs, wq, ws, gs, kind=oracle.ADD, c=base[None])[0]
+    assert (bits(host(out)) == bits(ref)).all()
+    assert (bits(host(part)) == bits(oracle.gemm(xq, xs, wq, ws, gs)[0])).all()
+
+
+def test_gemv_column_slice_with_row_stride(kc, oracle):
+    # A column shard (Wo / W2 under tensor parallelism): rows of stride ld, the owned n columns, the owned activations.
+    d, ld, n, gs = 96, 2048, 512, 64
+    wq, ws, xq, xs = make_case(oracle, d, ld, gs, 11)
+    col0 = 1024
+    wslice, sslice = np.ascontiguousarray(wq[:, col0:col0 + n]), np.ascontiguousarray(ws[:, col0 // gs:(col0 + n) // gs])
+    rng = np.random.default_rng(2)
+    xq2, xs2 = oracle.quantize(rng.standard_normal(n).astype(np.float32), gs)
+    wt, st = dev(wq), dev(ws)
+    out = torch.zeros(d, device="cuda")
+    kc.k_matmul_q8_ld(out, dev(xq2), dev(xs2), wt[:, col0:], st[:, col0 // gs:], ld, n, d, gs, kc.K_PARTIAL)
+    kc.status()
+    assert (bits(host(out)) == bits(oracle.gemm(xq2, xs2, wslice, sslice, gs)[0])).all()
+
+
+def test_gemv_qkv_three_segments(kc, oracle):
+    n, dq, dkv, gs = 2048, 2048, 512, 64
+    mats = [make_case(oracle, r, n, gs, 20 + i)[:2] for i, r in enumerate((dq, dkv, dkv))]
+    _, _, xq, xs = make_case(oracle, 1, n, gs, 23)
+    outs = [torch.zeros(r, device="cuda") for r in (dq, dkv, dkv)]
+    kc.k_matmul_q8_qkv(*outs, dev(xq), dev(xs), *[(dev(a), dev(b)) for a, b in mats], n, dq, dkv, gs)
+    kc.status()
+    for o, (wq, ws) in zip(outs, mats):
+        assert (bits(host(o)) == bits(oracle.gemm(xq, xs, wq, ws, gs)[0])).all()
+
+
+@pytest.mark.parametrize("d,n", [(40, 1024), (8192, 2048), (14336, 4096)])
+def test_gemv_swiglu(kc, oracle, d, n):
+    gs = 64
+    w1q, w1s, xq, xs = make_case(oracle, d, n, gs, 31)
+    w3q, w3s = oracle.seeded_q8_matrix(d, n, gs, 32)
+    out = kc.gemv(dev(xq), dev(xs), dev(w1q), dev(w1s), gs, kind=kc.K_SWIGLU, w3=(dev(w3q), dev(w3s)))
+    kc.status()
+    ref = oracle.gemm(xq, xs, w1q, w1s, gs, kind=oracle.SWIGLU, w3q=w3q, w3s=w3s)[0]
+    assert ulp_diff(host(out), ref).max() <= 2
+
+
+def test_gemv_config0_full_size_properties(kc, oracle):
+    # Config 0 (8192 x 2048, N(0, 0.02) weights, N(0, 1) activations): bitwise against the oracle, and linear in the
+    # activation scales (doubling every xs doubles y exactly: the rescale multiplies by a power of two).
+    wq, ws, xq, xs = make_case(oracle, 8192, 2048, 64, 0)
+    y = host(kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), 64))
+    y2 = host(kc.gemv(dev(xq), dev(xs * 2), dev(wq), dev(ws), 64))
+    kc.status()
+    assert (bits(y) == bits(oracle.gemm(xq, xs, wq, ws, 64)[0])).all()
+    assert (bits(y2) == bits(y * 2)).all()
+
+
+# ---- GEMM (k_gemm_q8) -----------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,d,k", [(1, 40, 512), (7, 48, 1024), (33, 32, 256)])
+def test_gemm_golden_amx(kc, m, d, k):
+    key = f"amx_{m}_{d}_{k}"
+    if key + "_c" not in GOLDEN:
+        pytest.skip("golden file was made on a CPU without AMX")
+    c = kc.gemm(dev(GOLDEN[key + "_xq"]), dev(GOLDEN[key + "_xs"]), dev(GOLDEN[key + "_wq"]), dev(GOLDEN[key + "_ws"]),
+                64)
+    kc.status()
+    assert (bits(host(c)) == bits(GOLDEN[key + "_c"])).all()
+
+
+def test_gemm_segments_and_kinds(kc, oracle):
+    m, k, gs = 5, 1024, 64
+    rng = np.random.default_rng(3)
+    xq, xs = oracle.quantize(rng.standard_normal((m, k)).astype(np.float32), gs)
+    wa = oracle.seeded_q8_matrix(64, k, gs, 40)
+    wb = oracle.seeded_q8_matrix(48, k, gs, 41)
+    w3 = oracle.seeded_q8_matrix(48, k, gs, 42)
+    base = rng.standard_normal((m, 64)).astype(np.float32)
+    ca, cb = dev(base), torch.zeros((m, 48), device="cuda")
+    segs = [kc.segment(ca, (dev(wa[0]), dev(wa[1])), kc.GEMM_ADD),
+            kc.segment(cb, (dev(wb[0]), dev(wb[1])), kc.GEMM_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))]
+    kc.k_gemm_q8(dev(xq), dev(xs), m, k, gs, segs)
+    kc.status()
+    assert (bits(host(ca)) == bits(oracle.gemm(xq, xs, *wa, gs, kind=oracle.ADD, c=base))).all()
+    ref = oracle.gemm(xq, xs, *wb, gs, kind=oracle.SWIGLU, w3q=w3[0], w3s=w3[1])
+    assert ulp_diff(host(cb), ref).max() <= 2
+
+
+# ---- RMSNorm, fused quantize, RoPE ----------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n", [17, 64, 2048, 4099])
+def test_rmsnorm_bitwise_avx512_order(kc, n):
+    x, w = GOLDEN[f"rms_{n}_x"], GOLDEN[f"rms_{n}_w"]
+    out = torch.empty(n, device="cuda")
+    kc.k_rmsnorm(out, dev(x), dev(w), n, 1e-5)
+    kc.status()
+    assert (bits(host(out)) == bits(GOLDEN[f"rms_{n}_avx512"])).all()
+    assert np.allclose(host(out), GOLDEN[f"rms_{n}_scalar"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("rows,size,gs", [(1, 4096, 64), (37, 2048, 64), (3, 512, 128)])
+def test_rmsnorm_quantize_fused(kc, oracle, rows, size, gs):
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, size)).astype(np.float32) * 3
+    w = rng.uniform(0.5, 1.5, size).astype(np.float32)
+    q = torch.empty((rows, size), dtype=torch.int8, device="cuda")
+    s = torch.empty((rows, size // gs), device="cuda")
+    o = torch.empty((rows, size), device="cuda")
+    kc.k_rmsnorm_q8_rows(q, s, o, dev(x), size, dev(w), rows, size, 1e-5, gs)
+    kc.status()
+    ro = oracle.rmsnorm(x, w, 1e-5)
+    rq, rs = oracle.quantize(ro, gs)
+    assert (bits(host(o)) == bits(ro)).all()
+    assert (host(q) == rq).all() and (bits(host(s)) == bits(rs)).all()
+
+
+def test_rope_rows_bitwise(kc, oracle):
+    rows, nh, nkv, hd = 5, 8, 2, 64
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((rows, nh * hd)).astype(np.float32)
+    k = rng.standard_normal((rows, nkv * hd)).astype(np.float32)
+    tables = np.stack([oracle.rope_table(100 + i, hd) for i in range(rows)])
+    qt, kt = dev(q), dev(k)
+    kc.k_rope_apply_rows(qt, nh * hd, kt, nkv * hd, dev(tables), 2 * hd, rows, nh, nkv, hd)
+    kc.status()
+    for i in range(rows):
+        rq, rk = oracle.rope_apply(q[i], k[i], tables[i], nh, nkv, hd)
+        assert (bits(host(qt)[i]) == bits(rq)).all() and (bits(host(kt)[i]) == bits(rk)).all()
