@@ -12,9 +12,9 @@
  * (kc_last_error) and returns without queuing work, for callers that cannot lose the process.
  *
  * Weight layout is the checkpoint's: values row-major [rows][ld] int8 (ld a multiple of gs), scales [rows][ld / gs]
- * fp32. Pointers passed to the GEMV/GEMM must be 16-byte aligned and n, ld multiples of 16 (cudaMalloc'd buffers with
- * the reference's shapes satisfy this). The supported group sizes are gs % 16 == 0, gs <= 1024 for the GEMV and
- * gs % 32 == 0 for the tensor-core GEMM; W8A32 inputs (K8Input.q == NULL) are refused. */
+ * fp32. Weight values, weight scales and activations passed to the GEMV/GEMM must be 16-byte aligned, and ld / gs a
+ * multiple of 4 (cudaMalloc'd buffers with the reference's shapes satisfy this). The supported group sizes are the
+ * powers of two 16..256 (the checkpoints use 64); W8A32 inputs (K8Input.q == NULL) are refused. */
 #ifndef LLAMA3X_KERNELS_CUDA_H
 #define LLAMA3X_KERNELS_CUDA_H
 
@@ -67,6 +67,9 @@ typedef enum {
 void kernels_init(void);                /* binds the library to the current CUDA device */
 const char *kernels_name(void);         /* "sm_100a" after kernels_init, NULL before */
 void kernels_set_stream(void *stream);  /* cudaStream_t for this thread's kernels; NULL = legacy default stream */
+/* Programmatic dependent launch for the GEMV/GEMM (on by default): their weight streams start while the previous
+ * kernel in the stream finishes. No reference counterpart (a CPU team has no launch latency to hide). */
+void kernels_set_pdl(int on);
 
 /* ---- error handling (runtime.h fail() analogue) ----------------------------------------------------------------- */
 enum { KC_FAIL_EXIT = 0, KC_FAIL_RETURN = 1 };

@@ -46,6 +46,7 @@ _SIGNATURES = {
     "kernels_init": (None, []),
     "kernels_name": (_c.c_char_p, []),
     "kernels_set_stream": (None, [_c.c_void_p]),
+    "kernels_set_pdl": (None, [_c.c_int]),
     "kc_set_fail_mode": (None, [_c.c_int]),
     "kc_last_error": (_c.c_char_p, []),
     "kc_clear_error": (None, []),
@@ -204,8 +205,10 @@ def k_matmul_q8_swiglu_ld(out, xq, xs, w1, w3, ld, n, d, gs):
 def segment(c, w, kind=GEMM_STORE, w3=None, ldc=None):
     """A GemmQ8Segment for k_gemm_q8: c [m][n] float32 (row stride ldc), w = (wq [n][k], ws [n][k/gs])."""
     n = w[0].shape[0]
-    return GemmQ8Segment(_ptr(c), ldc if ldc is not None else c.stride(0), _weight(*w),
-                         _weight(*w3) if w3 is not None else K8Weight(None, None), None, None, n, kind)
+    seg = GemmQ8Segment(_ptr(c), ldc if ldc is not None else c.stride(0), _weight(*w),
+                        _weight(*w3) if w3 is not None else K8Weight(None, None), None, None, n, kind)
+    seg._tensors = (c, w, w3)  # the struct holds raw pointers: keep the device memory alive with it
+    return seg
 
 
 def _segments(segs):

@@ -56,7 +56,7 @@ def build(force=False, verbose=False):
         subprocess.run(cmd, check=True)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-rdc=true", "-shared", "-Xcompiler", "-fPIC", *objs, "-o", str(tmp), "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-rdc=true", "-shared", "-Xcompiler", "-fPIC", *objs, "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

@@ -18,6 +18,7 @@ thread_local cudaStream_t tl_stream = nullptr;
 thread_local char tl_error[512];
 int fail_mode = KC_FAIL_EXIT;
 bool initialized = false;
+bool pdl_on = true;
 
 }  // namespace
 
@@ -55,7 +56,7 @@ int kc_device_sms() {
   return sms[dev];
 }
 
-static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+bool kc_pdl_enabled() { return pdl_on; }
 
 extern "C" {
 
@@ -79,6 +80,8 @@ void kernels_init(void) {
 const char *kernels_name(void) { return initialized ? "sm_100a" : NULL; }
 
 void kernels_set_stream(void *stream) { tl_stream = static_cast<cudaStream_t>(stream); }
+
+void kernels_set_pdl(int on) { pdl_on = on != 0; }
 
 void kc_set_fail_mode(int mode) { fail_mode = mode == KC_FAIL_RETURN ? KC_FAIL_RETURN : KC_FAIL_EXIT; }
 
@@ -126,22 +129,18 @@ void k_quantize(int8_t *q, float *s, const float *x, int n, int gs) { k_quantize
 static bool gemv_shape_ok(const char *name, const K8Input *x, size_t ld, int n, int gs) {
   if (!x || !x->q || !x->s)
     return kc_fail("%s: W8A32 activations (K8Input.q == NULL) are not supported by the sm_100a backend", name);
-  if (gs <= 0 || gs % 16 || gs > 1024)
-    return kc_fail("%s: group size %d is not supported (need a multiple of 16 up to 1024)", name, gs);
+  if (gs <= 0)
+    return kc_fail("%s: invalid group size %d", name, gs);
   if (n < 0 || n % gs)
     return kc_fail("%s: %d inputs are not a whole number of %d-groups", name, n, gs);
   if (ld < (size_t)n || ld % (size_t)gs)
     return kc_fail("%s: row stride %zu must be at least %d and a multiple of the group size %d", name, ld, n, gs);
-  if (!aligned16(x->q))
-    return kc_fail("%s: activations must be 16-byte aligned", name);
   return true;
 }
 
 static bool weight_ok(const char *name, K8Weight w) {
   if (!w.q || !w.s)
     return kc_fail("%s: missing weight values or scales", name);
-  if (!aligned16(w.q))
-    return kc_fail("%s: weight values must be 16-byte aligned", name);
   return true;
 }
 

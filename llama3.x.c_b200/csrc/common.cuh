@@ -82,6 +82,34 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
       : "memory");
 }
 
+// 2-D tiled TMA load of the box at (x, y) (x in elements of the innermost dimension; x * element size must be a
+// multiple of 16 bytes) into shared memory, completing its bytes on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3-D tiled TMA load of the box at (x, y, z) into shared memory, completing its bytes on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its independent prologue now, and wait for
+// the previous kernel's results. Both are no-ops unless the launch carries the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ int4 lds128(const void *p) {
   int4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"

@@ -9,31 +9,53 @@
 // AVX-512 GEMVs within the reference's own Q8 budget (tests/kernels.c:138-170).
 //
 // Data movement: the weight bytes are HBM-bound. Each CTA owns a contiguous range of output rows (the static split of
-// q8_team_static, src/gemv.c:483-490), walks it in sub-tiles of 32 physical weight rows, and streams each sub-tile
-// through shared memory in 1 KiB K-chunks with 1-D bulk copies (the TMA unit, one copy per row, completing on an
-// mbarrier), several stages deep. Inside a stage, lane r of every warp owns weight row r, and warp w takes groups
-// w, w+8, ... of the chunk, so the int32 dots need no shuffles; warp 0 then runs the ordered fp32 chain for all 32
-// rows (one lane per row) from a small transposed buffer. Rows in shared memory are padded by 16 bytes so the 16-byte
-// loads of 8 consecutive lanes hit distinct banks.
+// q8_team_static, src/gemv.c:483-490), walks it in sub-tiles of 32 physical weight rows that never straddle a
+// segment, and streams each sub-tile through shared memory in 1 KiB K-chunks with TMA tensor copies: one 3-D box
+// [8 K-blocks x 32 rows x 128 B] (128-byte swizzled; two 16-row halves from w1 and w3 for SwiGLU) for the weights and
+// one box of the chunk's weight scales, completing on one mbarrier, several stages deep (TMA issue costs tens of
+// cycles per instruction, so a stage is one or two instructions, not one per row or per 128 B). Inside a stage, lane r of every
+// dot warp owns weight row r and warp w takes groups w, w+8, ... of the chunk, so the int32 dots need no shuffles and,
+// thanks to the swizzle, 8 consecutive lanes read 8 distinct bank quads. A ninth warp runs the ordered fp32 chain for
+// all 32 rows (one lane per row) from a double-buffered transposed buffer, writes the outputs and refills the freed
+// stage. Dot warps and the chain warp hand the buffers over with named barriers; no CTA-wide barrier sits in the loop.
+//
+// Launch overlap: the kernel lets its dependent start at once (griddepcontrol.launch_dependents) and issues its first
+// weight stages before waiting on the kernel it depends on (griddepcontrol.wait), so under programmatic dependent
+// launch the weight stream overlaps the previous kernel's tail. Activations and outputs are touched only after the
+// wait.
+#include <cuda.h>
+#include <string.h>
+
 #include "common.cuh"
 #include "kernels_cuda_internal.h"
+#include "tmap.h"
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kTileRows = 32;  // physical weight rows per sub-tile (one per lane)
-constexpr int kPad = 16;
-constexpr int kMaxGroupsPerChunk = 32;
+constexpr int kDotWarps = 8;
+constexpr int kThreads = (kDotWarps + 1) * 32;  // 8 dot warps + 1 chain/producer warp
+constexpr int kTileRows = 32;                   // physical weight rows per sub-tile (one per lane)
+constexpr int kChunk = 1024;                    // K bytes per stage
+constexpr int kBoxCols = 128;                   // bytes per 128B-swizzled box row
+constexpr int kBoxes = kChunk / kBoxCols;
+constexpr int kWeightStage = kTileRows * kChunk;
+// Named barriers (0 is __syncthreads): T_FULL + b / T_EMPTY + b for the two chain buffers b.
+constexpr int kBarTFull = 1, kBarTEmpty = 3;
 
 struct GemvSegDev {
   float *out;
-  const int8_t *wq;
-  const float *ws;
-  const int8_t *w3q;
-  const float *w3s;
   int d;
   int unit0;
+};
+
+// Tensor maps stay in parameter space (the TMA unit reads them there); the scalars travel in a separate by-value
+// struct that the kernel copies into registers with static indices (dynamic indexing into parameter space turns
+// every access into a slow generic load).
+struct __align__(64) GemvMaps {
+  CUtensorMap wmap[3];  // weights of each segment (w1 for SwiGLU), boxes [128 B x box_rows]
+  CUtensorMap smap[3];  // weight scales, boxes [gpc floats x box_rows]
+  CUtensorMap w3map;    // SwiGLU: w3 and its scales
+  CUtensorMap s3map;
 };
 
 struct GemvArgs {
@@ -41,263 +63,476 @@ struct GemvArgs {
   int nseg;
   const int8_t *xq;
   const float *xs;
-  int n;          // inputs (K)
-  long long ld;   // weight row stride in values (multiple of gs)
+  int n;        // inputs (K)
   int gs;
-  int kind;       // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU
-  int units;      // output rows over all segments
-  int kc;         // bytes per K-chunk
+  int kind;     // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU
+  int units;    // output rows over all segments
   int nchunks;
-  int depth;      // pipeline stages
-  int ws_vec4;    // weight-scale rows are 16-byte aligned: load them as float4
+  int depth;    // pipeline stages
+  int stage_bytes;
+  int kblock;   // weight maps are 3-D k-block maps: one TMA instruction per stage (and per w1/w3 half)
 };
 
-struct RowRef {
-  const int8_t *wq;
-  const float *ws;
-  float *out;
-  int local;
+struct Sub {
+  int seg, row0, cnt, unit;  // segment, its first local row, rows (units) in the sub-tile, global unit of row0
 };
 
-__device__ __forceinline__ RowRef row_of(const GemvArgs &a, int unit, bool second) {
-  int s = 0;
-  if (a.nseg > 1 && unit >= a.seg[1].unit0)
-    s = 1;
-  if (a.nseg > 2 && unit >= a.seg[2].unit0)
-    s = 2;
-  const GemvSegDev &g = a.seg[s];
-  RowRef r;
-  r.local = unit - g.unit0;
-  r.out = g.out;
-  r.wq = (second ? g.w3q : g.wq) + (long long)r.local * a.ld;
-  r.ws = (second ? g.w3s : g.ws) + (long long)r.local * (a.ld / a.gs);
-  return r;
+// The CTA's share of each segment, [lo, hi) in global units, and its sub-tile counts, kept in registers.
+struct Plan {
+  int lo[3], hi[3], nsub[3], unit0[3];
+  int tile_shift;  // log2 of the sub-tile size (32 or 16 units)
+};
+
+__device__ __forceinline__ Plan make_plan(const GemvArgs &a, int u0, int u1, int tile_shift) {
+  Plan p;
+  p.tile_shift = tile_shift;
+#pragma unroll
+  for (int s = 0; s < 3; s++) {
+    p.unit0[s] = a.seg[s].unit0;
+    p.lo[s] = max(u0, a.seg[s].unit0);
+    p.hi[s] = s < a.nseg ? min(u1, a.seg[s].unit0 + a.seg[s].d) : p.lo[s];
+    p.nsub[s] = p.hi[s] > p.lo[s] ? ((p.hi[s] - p.lo[s] + (1 << tile_shift) - 1) >> tile_shift) : 0;
+  }
+  return p;
 }
 
-struct StageInfo {
-  int ub;      // first unit of the sub-tile
-  int cnt;     // units in the sub-tile
-  int chunk;   // K-chunk index
-  int bytes;   // bytes of this chunk per row
-};
-
-__device__ __forceinline__ StageInfo stage_info(const GemvArgs &a, int u0, int u1, int tile_units, int i) {
-  StageInfo s;
-  int sub = i / a.nchunks;
-  s.chunk = i - sub * a.nchunks;
-  s.ub = u0 + sub * tile_units;
-  s.cnt = min(tile_units, u1 - s.ub);
-  s.bytes = min(a.kc, a.n - s.chunk * a.kc);
-  return s;
+// Sub-tile k of the CTA's unit range: tiles of up to 2^tile_shift units that never cross a segment boundary.
+__device__ __forceinline__ Sub subtile(const Plan &p, int k) {
+  Sub r = {0, 0, 0, 0};
+  int s = 0;
+  if (k >= p.nsub[0]) {
+    k -= p.nsub[0];
+    s = 1;
+    if (k >= p.nsub[1]) {
+      k -= p.nsub[1];
+      s = 2;
+    }
+  }
+  const int lo = s == 0 ? p.lo[0] : s == 1 ? p.lo[1] : p.lo[2];
+  const int hi = s == 0 ? p.hi[0] : s == 1 ? p.hi[1] : p.hi[2];
+  const int u0s = s == 0 ? p.unit0[0] : s == 1 ? p.unit0[1] : p.unit0[2];
+  r.seg = s;
+  r.unit = lo + (k << p.tile_shift);
+  r.row0 = r.unit - u0s;
+  r.cnt = min(1 << p.tile_shift, hi - r.unit);
+  return r;
 }
 
 __device__ __forceinline__ bool lane_active(bool swiglu, int lane, int cnt) {
   return swiglu ? (lane & 15) < cnt : lane < cnt;
 }
 
-// Issued by all 32 lanes of one warp: lane r copies physical row r of the stage.
-__device__ __forceinline__ void issue_stage(const GemvArgs &a, const StageInfo &s, bool swiglu, int lane,
-                                            uint8_t *buf, uint64_t *bar) {
-  int rows = swiglu ? 2 * s.cnt : s.cnt;
+__device__ __forceinline__ void bar_sync_named(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive_named(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Stage layout: the weights of one 32-row sub-tile (two 16-row halves, w1 then w3, for SwiGLU) as 8 K-blocks of
+// [half rows][128 B] per half, 128B-swizzled; then the weight scales [32 rows][gpc floats].
+// Issued by the chain warp. With k-block maps lane 0 (and lane 1 for w3) moves a whole half in one instruction;
+// otherwise lanes b < 8 (and 16 + b) move one [rows x 128 B] box each. Lanes 30/31 load the scale box(es). Every box
+// is copied whole (rows past the sub-tile are the next rows of the segment, or the tensor map's zero fill past the
+// matrix), so the transaction count is fixed per stage.
+__device__ __forceinline__ void issue_stage(const GemvMaps &m, int gpc, int kblock, const Sub &t, int chunk, bool swiglu,
+                                            int lane, uint8_t *buf, uint64_t *bar) {
   if (lane == 0)
-    mbar_arrive_expect_tx(bar, (unsigned)(rows * s.bytes));
+    mbar_arrive_expect_tx(bar, (unsigned)(kWeightStage + kTileRows * gpc * 4));
   __syncwarp();
-  if (lane_active(swiglu, lane, s.cnt)) {
-    int unit = s.ub + (swiglu ? (lane & 15) : lane);
-    RowRef r = row_of(a, unit, swiglu && lane >= 16);
-    bulk_g2s(buf + lane * (a.kc + kPad), r.wq + (long long)s.chunk * a.kc, (unsigned)s.bytes, bar);
-  }
-}
-
-__device__ __forceinline__ void load_scales(const GemvArgs &a, const StageInfo &s, bool swiglu, int lane,
-                                            float (&w)[kMaxGroupsPerChunk]) {
-  if (!lane_active(swiglu, lane, s.cnt))
-    return;
-  int unit = s.ub + (swiglu ? (lane & 15) : lane);
-  RowRef r = row_of(a, unit, swiglu && lane >= 16);
-  int gpc = a.kc / a.gs, g0 = s.chunk * gpc, groups = s.bytes / a.gs;
-  const float *p = r.ws + g0;
-  if (a.ws_vec4 && (groups & 3) == 0) {
-#pragma unroll
-    for (int g = 0; g < kMaxGroupsPerChunk; g += 4)
-      if (g < groups) {
-        float4 v = __ldg(reinterpret_cast<const float4 *>(p + g));
-        w[g] = v.x, w[g + 1] = v.y, w[g + 2] = v.z, w[g + 3] = v.w;
-      }
+  const int half = swiglu ? kTileRows / 2 : kTileRows;
+  const int kb_stride = half * kBoxCols;
+  const CUtensorMap *w = swiglu ? &m.wmap[0] : &m.wmap[0] + t.seg;
+  const CUtensorMap *sm = swiglu ? &m.smap[0] : &m.smap[0] + t.seg;
+  if (kblock) {
+    if (lane == 0)
+      tma_load_3d(buf, w, 0, t.row0, chunk * kBoxes, bar);
+    if (swiglu && lane == 1)
+      tma_load_3d(buf + half * kChunk, &m.w3map, 0, t.row0, chunk * kBoxes, bar);
   } else {
-#pragma unroll
-    for (int g = 0; g < kMaxGroupsPerChunk; g++)
-      if (g < groups)
-        w[g] = __ldg(p + g);
+    const int x0 = chunk * kChunk;
+    if (lane < kBoxes)
+      tma_load_2d(buf + lane * kb_stride, w, x0 + lane * kBoxCols, t.row0, bar);
+    else if (swiglu && lane >= 16 && lane < 16 + kBoxes)
+      tma_load_2d(buf + half * kChunk + (lane - 16) * kb_stride, &m.w3map, x0 + (lane - 16) * kBoxCols, t.row0, bar);
   }
+  if (lane == 31)
+    tma_load_2d(buf + kWeightStage, sm, chunk * gpc, t.row0, bar);
+  if (swiglu && lane == 30)
+    tma_load_2d(buf + kWeightStage + half * gpc * 4, &m.s3map, chunk * gpc, t.row0, bar);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const GemvArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
+// Byte offset inside a stage of the 16-byte piece `k16` (0 .. 63 along K) of physical row r (0 .. 31): its half,
+// its K-block k16 / 8, its row within the half, then the 128B swizzle (piece index XOR row within the 8-row atom).
+template <int HALF>
+__device__ __forceinline__ int piece_offset(int r, int k16) {
+  return (r >= HALF ? HALF * kChunk : 0) + (k16 >> 3) * (HALF * kBoxCols) + (r & (HALF - 1)) * kBoxCols +
+         (((k16 & 7) ^ (r & 7)) << 4);
+}
+
+// Exact int32 dot of group g of physical row r with the activations (4 independent dp4a chains for gs 64).
+template <int GS, int HALF>
+__device__ __forceinline__ int group_dot(const uint8_t *buf, const int8_t *xrow, int r, int g, int gs) {
+  if (GS == 64) {
+    int4 w[4], x[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      w[q] = lds128(buf + piece_offset<HALF>(r, g * 4 + q));
+      x[q] = lds128(xrow + g * 64 + q * 16);
+    }
+    int d0 = dot16(w[0], x[0], 0), d1 = dot16(w[1], x[1], 0), d2 = dot16(w[2], x[2], 0), d3 = dot16(w[3], x[3], 0);
+    return (d0 + d1) + (d2 + d3);
+  }
+  int dot = 0;
+  for (int q = 0; q < gs / 16; q++)
+    dot = dot16(lds128(buf + piece_offset<HALF>(r, g * (gs / 16) + q)), lds128(xrow + g * gs + q * 16), dot);
+  return dot;
+}
+
+template <int GS>
+__global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  pdl_launch_dependents();
   const bool swiglu = a.kind == KC_SWIGLU;
-  const int tile_units = swiglu ? kTileRows / 2 : kTileRows;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, c = blockIdx.x;
-  const int u0 = (int)((long long)a.units * c / G), u1 = (int)((long long)a.units * (c + 1) / G);
+  const int u0 = a.units * c / G, u1 = a.units * (c + 1) / G;  // units * grid < 2^31 (checked on the host)
   if (u1 <= u0)
     return;
-  const int nsub = (u1 - u0 + tile_units - 1) / tile_units;
-  const int S = nsub * a.nchunks;
-  const int gpc = a.kc / a.gs;
-  const int row_bytes = a.kc + kPad;
+  const Plan plan = make_plan(a, u0, u1, swiglu ? 4 : 5);
+  const int nchunks = a.nchunks, depth = a.depth, stage_bytes = a.stage_bytes, n = a.n;
+  const int S = (plan.nsub[0] + plan.nsub[1] + plan.nsub[2]) * nchunks;
+  const int gs = GS ? GS : a.gs;
+  const int gpc = kChunk / gs;
+  float *const out0 = a.seg[0].out, *const out1 = a.seg[1].out, *const out2 = a.seg[2].out;
 
-  // Carve shared memory: barriers, abort flag, activation scales, activations, the chain buffer, the stages.
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  int *abort_flag = reinterpret_cast<int *>(smem + 8 * 16);
-  float *XS = reinterpret_cast<float *>(smem + 256);
-  int8_t *XQ = reinterpret_cast<int8_t *>(smem + 256 + ((a.n / a.gs * 4 + 15) & ~15));
-  float *T = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(XQ) + ((a.n + 15) & ~15));
-  uint8_t *stages = reinterpret_cast<uint8_t *>(T) + 2 * kMaxGroupsPerChunk * kTileRows * 4;
+  // Shared memory: the stages (1024-byte aligned for the swizzle), then barriers, flags, chain buffers, activations.
+  uint8_t *stages = smem;
+  uint8_t *tail = smem + depth * stage_bytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(tail);
+  volatile int *abort_flag = reinterpret_cast<int *>(tail + 8 * 8);
+  volatile int *issued = reinterpret_cast<int *>(tail + 8 * 8 + 4);
+  float *T = reinterpret_cast<float *>(tail + 128);
+  float *XS = T + 2 * gpc * kTileRows;
+  int8_t *XQ = reinterpret_cast<int8_t *>(XS + ((n / gs + 3) & ~3));
 
   if (tid == 0) {
-    for (int i = 0; i < a.depth; i++)
+    for (int i = 0; i < depth; i++)
       mbar_init(&bars[i], 1);
     *abort_flag = 0;
+    *issued = min(depth, S);
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == 0)
-    for (int i = 0; i < a.depth && i < S; i++)
-      issue_stage(a, stage_info(a, u0, u1, tile_units, i), swiglu, lane, stages + i * kTileRows * row_bytes,
+  if (warp == kDotWarps) {
+    // Weights do not depend on the previous kernel: start streaming them before waiting for it.
+    for (int i = 0; i < depth && i < S; i++)
+      issue_stage(m, gpc, a.kblock, subtile(plan, i / nchunks), i % nchunks, swiglu, lane, stages + i * stage_bytes,
                   &bars[i]);
-  // Activations (quantized) and their scales, once per CTA.
-  for (int i = tid; i < a.n / 16; i += kThreads)
+  }
+  pdl_wait();
+  for (int i = tid; i < n / 16; i += kThreads)
     reinterpret_cast<int4 *>(XQ)[i] = __ldg(reinterpret_cast<const int4 *>(a.xq) + i);
-  for (int i = tid; i < a.n / a.gs; i += kThreads)
+  for (int i = tid; i < n / gs; i += kThreads)
     XS[i] = __ldg(a.xs + i);
-
-  float wcur[kMaxGroupsPerChunk], wnext[kMaxGroupsPerChunk];
-  float acc = 0.0f;
-  int aborted_at = -1;
-  if (warp == 0)
-    load_scales(a, stage_info(a, u0, u1, tile_units, 0), swiglu, lane, wcur);
   __syncthreads();
 
-  for (int i = 0; i < S; i++) {
-    const int slot = i % a.depth;
-    const StageInfo s = stage_info(a, u0, u1, tile_units, i);
-    if (warp == 0 && i + 1 < S)
-      load_scales(a, stage_info(a, u0, u1, tile_units, i + 1), swiglu, lane, wnext);
-    if (!mbar_wait_bounded(&bars[slot], (unsigned)(i / a.depth) & 1u))
-      *abort_flag = 1;
-    const uint8_t *buf = stages + slot * kTileRows * row_bytes;
-    float *Tb = T + (i & 1) * kMaxGroupsPerChunk * kTileRows;
-    const int groups = s.bytes / a.gs;
-    if (lane_active(swiglu, lane, s.cnt)) {
-      const uint8_t *wrow = buf + lane * row_bytes;
-      const int8_t *xrow = XQ + s.chunk * a.kc;
-      for (int g = warp; g < groups; g += kWarps) {
-        int dot = 0;
-        for (int q = 0; q < a.gs; q += 16)
-          dot = dot16(lds128(wrow + g * a.gs + q), lds128(xrow + g * a.gs + q), dot);
-        Tb[g * kTileRows + lane] = __fmul_rn(__int2float_rn(dot), XS[s.chunk * gpc + g]);
-      }
-    }
-    __syncthreads();
-    if (*abort_flag) {
-      aborted_at = i;
-      break;
-    }
-    if (warp == 0) {
-      if (i + a.depth < S)
-        issue_stage(a, stage_info(a, u0, u1, tile_units, i + a.depth), swiglu, lane,
-                    stages + slot * kTileRows * row_bytes, &bars[slot]);
-      // The ordered chain: one lane per physical row, groups ascending.
-#pragma unroll
-      for (int g = 0; g < kMaxGroupsPerChunk; g++)
-        if (g < groups)
-          acc = __fmaf_rn(Tb[g * kTileRows + lane], wcur[g], acc);
-      if (s.chunk == a.nchunks - 1) {
-        float gate = __shfl_down_sync(0xffffffffu, acc, 16);
-        if (swiglu) {
-          if (lane < s.cnt) {
-            RowRef r = row_of(a, s.ub + lane, false);
-            r.out[r.local] = silu_gate_dev(acc, gate);
+  if (warp < kDotWarps) {
+    // ---- dot warps: exact int32 group dots of 32 rows, scaled by the activation scale, into T[stage & 1] ----
+    int slot = 0, chunk = 0, sub = 0;
+    unsigned phase = 0;
+    for (int i = 0; i < S; i++) {
+      const Sub t = subtile(plan, sub);
+      if (!*abort_flag && !mbar_wait_bounded(&bars[slot], phase))
+        *abort_flag = 1;
+      if (i >= 2)
+        bar_sync_named(kBarTEmpty + (i & 1), kThreads);
+      const uint8_t *buf = stages + slot * stage_bytes;
+      float *Tb = T + (i & 1) * gpc * kTileRows;
+      const int groups = min(gpc, (n - chunk * kChunk) / gs);
+      if (lane_active(swiglu, lane, t.cnt)) {
+        const int8_t *xrow = XQ + chunk * kChunk;
+        const float *xsc = XS + chunk * gpc;
+        if (GS == 64 && groups == 16) {
+          // Both of this warp's groups at once: 8 independent dp4a chains in flight.
+          const int g0 = warp, g1 = warp + kDotWarps;
+          const int d0 = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g0, gs) : group_dot<GS, 32>(buf, xrow, lane, g0, gs);
+          const int d1 = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g1, gs) : group_dot<GS, 32>(buf, xrow, lane, g1, gs);
+          Tb[g0 * kTileRows + lane] = __fmul_rn(__int2float_rn(d0), xsc[g0]);
+          Tb[g1 * kTileRows + lane] = __fmul_rn(__int2float_rn(d1), xsc[g1]);
+        } else {
+          for (int g = warp; g < groups; g += kDotWarps) {
+            const int d = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g, gs) : group_dot<GS, 32>(buf, xrow, lane, g, gs);
+            Tb[g * kTileRows + lane] = __fmul_rn(__int2float_rn(d), xsc[g]);
           }
-        } else if (lane < s.cnt) {
-          RowRef r = row_of(a, s.ub + lane, false);
+        }
+      }
+      bar_arrive_named(kBarTFull + (i & 1), kThreads);
+      if (++slot == depth)
+        slot = 0, phase ^= 1u;
+      if (++chunk == nchunks)
+        chunk = 0, sub++;
+    }
+  } else {
+    // ---- chain warp: the ordered fp32 accumulation (one lane per row), the epilogue, and the TMA producer ----
+    float acc = 0.0f;
+    int slot = 0, chunk = 0, sub = 0;
+    int nchunk = depth % nchunks, nsub = depth / nchunks;  // chunk and sub-tile of stage i + depth
+    for (int i = 0; i < S; i++) {
+      const Sub t = subtile(plan, sub);
+      bar_sync_named(kBarTFull + (i & 1), kThreads);
+      const float *Tb = T + (i & 1) * gpc * kTileRows;
+      const float *wsr = reinterpret_cast<const float *>(stages + slot * stage_bytes + kWeightStage) + lane * gpc;
+      const int groups = min(gpc, (n - chunk * kChunk) / gs);
+      if (GS == 64 && groups == 16 && lane_active(swiglu, lane, t.cnt)) {
+        // Load the chunk's 16 scaled dots and 16 weight scales first, then run the 16 dependent FMAs.
+        float tv[16], wv[16];
+#pragma unroll
+        for (int g = 0; g < 16; g += 4) {
+          float4 w4 = *reinterpret_cast<const float4 *>(wsr + g);
+          wv[g] = w4.x, wv[g + 1] = w4.y, wv[g + 2] = w4.z, wv[g + 3] = w4.w;
+        }
+#pragma unroll
+        for (int g = 0; g < 16; g++)
+          tv[g] = Tb[g * kTileRows + lane];
+#pragma unroll
+        for (int g = 0; g < 16; g++)
+          acc = __fmaf_rn(tv[g], wv[g], acc);
+      } else if (lane_active(swiglu, lane, t.cnt)) {
+        for (int g = 0; g < groups; g += 4) {
+          float4 w4 = *reinterpret_cast<const float4 *>(wsr + g);
+          acc = __fmaf_rn(Tb[g * kTileRows + lane], w4.x, acc);
+          if (g + 1 < groups)
+            acc = __fmaf_rn(Tb[(g + 1) * kTileRows + lane], w4.y, acc);
+          if (g + 2 < groups)
+            acc = __fmaf_rn(Tb[(g + 2) * kTileRows + lane], w4.z, acc);
+          if (g + 3 < groups)
+            acc = __fmaf_rn(Tb[(g + 3) * kTileRows + lane], w4.w, acc);
+        }
+      }
+      if (chunk == nchunks - 1) {
+        float gate = __shfl_down_sync(0xffffffffu, acc, 16);
+        float *out = (t.seg == 0 ? out0 : t.seg == 1 ? out1 : out2) + t.row0;
+        if (swiglu) {
+          if (lane < t.cnt)
+            out[lane] = silu_gate_dev(acc, gate);
+        } else if (lane < t.cnt) {
           if (a.kind == KC_ADD)
-            r.out[r.local] = __fadd_rn(r.out[r.local], acc);
+            out[lane] = __fadd_rn(out[lane], acc);
           else
-            r.out[r.local] = acc;
+            out[lane] = acc;
         }
         acc = 0.0f;
       }
-#pragma unroll
-      for (int g = 0; g < kMaxGroupsPerChunk; g++)
-        wcur[g] = wnext[g];
+      // Stage i is fully consumed (dot warps passed T_FULL after their last read of its weights, and the chain has
+      // read its scales): refill the slot with stage i + depth.
+      if (i + depth < S && !*abort_flag) {
+        issue_stage(m, gpc, a.kblock, subtile(plan, nsub), nchunk, swiglu, lane, stages + slot * stage_bytes,
+                    &bars[slot]);
+        if (lane == 0)
+          *issued = i + depth + 1;
+      }
+      if (++nchunk == nchunks)
+        nchunk = 0, nsub++;
+      if (i + 2 < S)
+        bar_arrive_named(kBarTEmpty + (i & 1), kThreads);
+      if (++slot == depth)
+        slot = 0;
+      if (++chunk == nchunks)
+        chunk = 0, sub++;
     }
   }
-  // After an abort, let the copies this CTA issued (stages aborted_at .. aborted_at + depth - 1) land, with bounded
-  // waits, before its shared memory goes away.
-  if (aborted_at >= 0 && tid == 0)
-    for (int j = aborted_at; j < S && j < aborted_at + a.depth; j++)
-      mbar_wait_bounded(&bars[j % a.depth], (unsigned)(j / a.depth) & 1u);
+  // After an abort, let every copy still in flight land (bounded waits) before the shared memory goes away: for each
+  // slot, the latest stage issued into it.
+  __syncthreads();
+  if (*abort_flag && tid == 0)
+    for (int j = max(0, *issued - depth); j < *issued; j++)
+      mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
+}
+
+// The general rung, for shapes the TMA kernel cannot describe (group sizes below 16 or not a power of two, scale rows
+// that are not 16-byte multiples, unaligned pointers): one warp per output row, the group dot reduced exactly across
+// the warp, lane 0 applying the same ordered rescale. Slow but bitwise identical to the fast kernel.
+__global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, GemvSegDev s1, GemvSegDev s2,
+                                                               const int8_t *wq0, const int8_t *wq1, const int8_t *wq2,
+                                                               const float *ws0, const float *ws1, const float *ws2,
+                                                               const int8_t *w3q, const float *w3s, int nseg,
+                                                               const int8_t *xq, const float *xs, int n, long long ld,
+                                                               int gs, int kind, int units) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (unit >= units)
+    return;
+  int s = (nseg > 1 && unit >= s1.unit0) ? 1 : 0;
+  if (nseg > 2 && unit >= s2.unit0)
+    s = 2;
+  const GemvSegDev seg = s == 0 ? s0 : s == 1 ? s1 : s2;
+  const int row = unit - seg.unit0;
+  const int8_t *wq = (s == 0 ? wq0 : s == 1 ? wq1 : wq2) + row * ld;
+  const float *ws = (s == 0 ? ws0 : s == 1 ? ws1 : ws2) + row * (ld / gs);
+  float acc[2] = {0.0f, 0.0f};
+  for (int pass = 0; pass < (kind == KC_SWIGLU ? 2 : 1); pass++) {
+    const int8_t *w = pass ? w3q + row * ld : wq;
+    const float *sc = pass ? w3s + row * (ld / gs) : ws;
+    for (int g = 0; g < n / gs; g++) {
+      int dot = 0;
+      for (int k = lane; k < gs; k += 32)
+        dot += (int)xq[g * gs + k] * (int)w[g * gs + k];
+#pragma unroll
+      for (int o = 16; o; o >>= 1)
+        dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      acc[pass] = __fmaf_rn(__fmul_rn(__int2float_rn(dot), xs[g]), sc[g], acc[pass]);
+    }
+  }
+  if (lane == 0) {
+    float *out = seg.out + row;
+    if (kind == KC_SWIGLU)
+      *out = silu_gate_dev(acc[0], acc[1]);
+    else if (kind == KC_ADD)
+      *out = __fadd_rn(*out, acc[0]);
+    else
+      *out = acc[0];
+  }
+}
+
+size_t smem_bytes(int n, int gs, int stage_bytes, int depth) {
+  return (size_t)depth * stage_bytes + 128 + (size_t)2 * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
+         (size_t)((n + 15) & ~15);
+}
+
+bool encode_weight(CUtensorMap *wmap, CUtensorMap *smap, const int8_t *wq, const float *ws, int rows, int n,
+                   long long ld, int gs, int box_rows, bool kblock) {
+  const int gpc = kChunk / gs;
+  bool ok = kblock ? kc_tmap_kblocks(wmap, wq, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxes, box_rows)
+                   : kc_tmap_2d(wmap, wq, 1, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxCols, box_rows, true);
+  return ok &&
+         kc_tmap_2d(smap, ws, 4, (uint64_t)(n / gs), (uint64_t)rows, (uint64_t)(ld / gs) * 4, gpc, box_rows, false);
 }
 
 }  // namespace
 
-size_t kc_gemv_smem_bytes(int n, int gs, int kc, int depth) {
-  return 256 + (size_t)((n / gs * 4 + 15) & ~15) + (size_t)((n + 15) & ~15) +
-         (size_t)2 * kMaxGroupsPerChunk * kTileRows * 4 + (size_t)depth * kTileRows * (kc + kPad);
-}
-
-// Host launcher (argument validation is the C-ABI layer's job).
-int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
-                   int kind, cudaStream_t stream, int grid_limit) {
-  GemvArgs a = {};
+static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld,
+                          int gs, int kind, cudaStream_t stream) {
+  GemvSegDev d[3] = {};
+  const int8_t *wq[3] = {};
+  const float *ws[3] = {};
   int units = 0;
-  bool vec4 = ((ld / gs) % 4) == 0;
   for (int s = 0; s < nseg; s++) {
-    a.seg[s].out = segs[s].out;
-    a.seg[s].wq = segs[s].wq;
-    a.seg[s].ws = segs[s].ws;
-    a.seg[s].w3q = segs[s].w3q;
-    a.seg[s].w3s = segs[s].w3s;
-    a.seg[s].d = segs[s].d;
-    a.seg[s].unit0 = units;
+    d[s].out = segs[s].out, d[s].d = segs[s].d, d[s].unit0 = units;
+    wq[s] = segs[s].wq, ws[s] = segs[s].ws;
     units += segs[s].d;
-    vec4 = vec4 && ((uintptr_t)segs[s].ws % 16 == 0) && (!segs[s].w3s || (uintptr_t)segs[s].w3s % 16 == 0);
   }
   if (units == 0 || n == 0)
     return 0;
-  a.nseg = nseg;
-  a.xq = xq;
-  a.xs = xs;
-  a.n = n;
-  a.ld = ld;
-  a.gs = gs;
-  a.kind = kind;
-  a.units = units;
-  a.kc = gs >= 32 ? 1024 : 512;
-  if (a.kc < gs)
-    a.kc = gs;
-  a.nchunks = (n + a.kc - 1) / a.kc;
-  a.ws_vec4 = vec4 ? 1 : 0;
-  const size_t budget = 220 * 1024;
-  size_t fixed = kc_gemv_smem_bytes(n, gs, a.kc, 0);
-  size_t per_stage = (size_t)kTileRows * (a.kc + kPad);
-  if (fixed + 2 * per_stage > budget)
+  gemv_q8_generic_kernel<<<(units + 7) / 8, 256, 0, stream>>>(d[0], d[1], d[2], wq[0], wq[1], wq[2], ws[0], ws[1],
+                                                              ws[2], segs[0].w3q, segs[0].w3s, nseg, xq, xs, n, ld, gs,
+                                                              kind, units);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                      int kind, cudaStream_t stream, int grid_limit);
+
+// Host launcher (argument validation is the C-ABI layer's job): the TMA kernel where the shape allows it, else the
+// general rung.
+int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                   int kind, cudaStream_t stream, int grid_limit) {
+  int rc = launch_tma(segs, nseg, xq, xs, n, ld, gs, kind, stream, grid_limit);
+  if (rc == -1)
+    rc = launch_generic(segs, nseg, xq, xs, n, ld, gs, kind, stream);
+  return rc;
+}
+
+static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                      int kind, cudaStream_t stream, int grid_limit) {
+  thread_local GemvMaps M;
+  GemvArgs A;
+  memset(&M, 0, sizeof(M));
+  memset(&A, 0, sizeof(A));
+  if (gs < 16 || gs > kChunk || (gs & (gs - 1)) || n % gs || ld % gs || ld < n || ((ld / gs) * 4) % 16 ||
+      ((uintptr_t)xq & 15))
     return -1;
-  int depth = (int)((budget - fixed) / per_stage);
-  a.depth = depth > 6 ? 6 : depth;
-  size_t smem = kc_gemv_smem_bytes(n, gs, a.kc, a.depth);
-  int sms = kc_device_sms();
+  const bool swiglu = kind == KC_SWIGLU;
+  const int box_rows = swiglu ? kTileRows / 2 : kTileRows;
+  int units = 0;
+  for (int s = 0; s < nseg; s++) {
+    A.seg[s].out = segs[s].out;
+    A.seg[s].d = segs[s].d;
+    A.seg[s].unit0 = units;
+    units += segs[s].d;
+    if (segs[s].d > 0 && (((uintptr_t)segs[s].ws & 15) || (swiglu && ((uintptr_t)segs[s].w3s & 15))))
+      return -1;
+  }
+  // Prefer the 3-D k-block maps (one TMA instruction per stage); fall back to 2-D boxes if the driver refuses them.
+  bool kblock = n % kBoxCols == 0;
+  for (int attempt = 0; attempt < 2; attempt++) {
+    bool ok = true;
+    for (int s = 0; s < nseg && ok; s++) {
+      if (segs[s].d == 0)
+        continue;
+      ok = encode_weight(&M.wmap[s], &M.smap[s], segs[s].wq, segs[s].ws, segs[s].d, n, ld, gs, box_rows, kblock) &&
+           (!swiglu ||
+            encode_weight(&M.w3map, &M.s3map, segs[s].w3q, segs[s].w3s, segs[s].d, n, ld, gs, box_rows, kblock));
+    }
+    if (ok)
+      break;
+    if (!kblock)
+      return -1;
+    kblock = false;
+  }
+  if (units == 0 || n == 0)
+    return 0;
+  if ((long long)units * 1024 >= (1ll << 31))
+    return -1;
+  A.nseg = nseg;
+  A.kblock = kblock ? 1 : 0;
+  A.xq = xq;
+  A.xs = xs;
+  A.n = n;
+  A.gs = gs;
+  A.kind = kind;
+  A.units = units;
+  A.nchunks = (n + kChunk - 1) / kChunk;
+  A.stage_bytes = (kWeightStage + kTileRows * (kChunk / gs) * 4 + 1023) & ~1023;
+#ifndef KC_GEMV_SMEM_BUDGET
+#define KC_GEMV_SMEM_BUDGET (200 * 1024)
+#endif
+#ifndef KC_GEMV_MAX_DEPTH
+#define KC_GEMV_MAX_DEPTH 4
+#endif
+  const size_t budget = KC_GEMV_SMEM_BUDGET;
+  if (smem_bytes(n, gs, A.stage_bytes, 2) > budget)
+    return -1;
+  int depth = 2;
+  while (depth < KC_GEMV_MAX_DEPTH && smem_bytes(n, gs, A.stage_bytes, depth + 1) <= budget)
+    depth++;
+  A.depth = depth;
+  const size_t smem = smem_bytes(n, gs, A.stage_bytes, depth);
+  const int sms = kc_device_sms();
   int grid = units < sms ? units : sms;
   if (grid_limit > 0 && grid > grid_limit)
     grid = grid_limit;
-  static bool attr_set[64];
+  static bool attr_set[64][2];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemv_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_set[dev] = true;
+  const int variant = gs == 64 ? 0 : 1;
+  if (dev < 64 && !attr_set[dev][variant]) {
+    cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr_set[dev][variant] = true;
   }
-  gemv_q8_kernel<<<grid, kThreads, smem, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = variant == 0 ? cudaLaunchKernelEx(&cfg, gemv_q8_kernel<64>, M, A)
+                               : cudaLaunchKernelEx(&cfg, gemv_q8_kernel<0>, M, A);
+  return e == cudaSuccess ? 0 : -2;
 }

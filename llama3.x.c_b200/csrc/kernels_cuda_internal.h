@@ -19,6 +19,8 @@ struct KcGemvSeg {
 };
 
 int kc_device_sms();
+// Programmatic dependent launch of the kernels that support it (kernels_set_pdl; on by default).
+bool kc_pdl_enabled();
 
 // Returns 0 on launch, -1 for a shape the kernel does not support, -2 on a launch error.
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,

@@ -101,8 +101,11 @@ def make_case(oracle, d, n, gs, seed, ld=None):
     return wq, ws, xq, xs
 
 
-GEMV_SHAPES = [(37, 1024, 64), (8192, 2048, 64), (4096, 14336, 64), (1, 64, 64), (33, 192, 32), (300, 512, 16),
-               (65, 1024, 128), (6144, 4096, 64), (77, 1792, 64)]
+# The reference suite's own shapes (tests/kernels.c:101: n/d/gs 64/5/16, 192/7/32, 256/4/64, 4096/9/64, 512/3/128,
+# 64/2/4) -- the odd ones run on the general rung -- plus the configs' shapes and ragged row counts.
+GEMV_SHAPES = [(5, 64, 16), (7, 192, 32), (4, 256, 64), (9, 4096, 64), (3, 512, 128), (2, 64, 4),
+               (37, 1024, 64), (8192, 2048, 64), (4096, 14336, 64), (1, 64, 64), (300, 512, 16), (65, 1024, 128),
+               (6144, 4096, 64), (77, 1792, 64), (1000, 2048, 256)]
 
 
 @pytest.mark.parametrize("d,n,gs", GEMV_SHAPES)
@@ -162,8 +165,9 @@ def test_gemv_column_slice_with_row_stride(kc, oracle):
     assert (bits(host(out)) == bits(oracle.gemm(xq2, xs2, wslice, sslice, gs)[0])).all()
 
 
-def test_gemv_qkv_three_segments(kc, oracle):
-    n, dq, dkv, gs = 2048, 2048, 512, 64
+@pytest.mark.parametrize("n,dq,dkv", [(2048, 2048, 512), (1024, 100, 37), (4096, 4096, 1024)])
+def test_gemv_qkv_three_segments(kc, oracle, n, dq, dkv):
+    gs = 64
     mats = [make_case(oracle, r, n, gs, 20 + i)[:2] for i, r in enumerate((dq, dkv, dkv))]
     _, _, xq, xs = make_case(oracle, 1, n, gs, 23)
     outs = [torch.zeros(r, device="cuda") for r in (dq, dkv, dkv)]
