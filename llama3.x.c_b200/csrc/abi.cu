@@ -232,7 +232,7 @@ static bool gemm_args_ok(const char *name, const int8_t *xq, const float *xs, in
 
 static void gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
                            int count) {
-  // One row-kernel launch per activation row; the segments of a row share one launch (they share the activations).
+  // One row-kernel launch per activation row and segment.
   int groups = k / gs;
   for (int r = 0; r < m; r++) {
     for (int s = 0; s < count; s++) {
@@ -244,8 +244,53 @@ static void gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int 
   }
 }
 
+static int to_kc_segs(const GemmQ8Segment *segments, int count, KcGemmSeg *out) {
+  for (int s = 0; s < count; s++) {
+    const GemmQ8Segment &g = segments[s];
+    out[s] = KcGemmSeg{g.c, g.ldc, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n, kc_kind_of(g.kind)};
+  }
+  return count;
+}
+
+// Scratch for the transposed activation scales of k_gemm_q8, one buffer per device, grown on demand (the only
+// allocation the GEMM entry points make; the engine passes its own transposed scales instead).
+static float *gemm_scratch(size_t floats) {
+  static float *buf[64];
+  static size_t cap[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64)
+    return nullptr;
+  if (cap[dev] < floats) {
+    if (buf[dev])
+      cudaFree(buf[dev]);
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    if (cudaMalloc(&buf[dev], floats * sizeof(float)) != cudaSuccess)
+      return nullptr;
+    cap[dev] = floats;
+  }
+  return buf[dev];
+}
+
+// Activation rows from which the tensor-core GEMM beats one GEMV launch per row (the reference's k_gemm_q8_pick
+// threshold analogue; measured on B200 with the configuration-4 sweep).
+static const int kTcMinRows = 8;
+
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count) {
   (void)gs, (void)segments, (void)count;
+  return Q8_GEMM_GPU_TCGEN05;
+}
+
+static Q8GemmBackend pick(const int8_t *xq, int m, int k, int gs, const GemmQ8Segment *segments, int count) {
+  KcGemmSeg segs[GEMM_MAX_SEGMENTS];
+  to_kc_segs(segments, count, segs);
+  bool swiglu_ok = true;
+  for (int s = 0; s < count; s++)
+    if (segs[s].kind == KC_SWIGLU && count != 1)
+      swiglu_ok = false;
+  if (m >= kTcMinRows && swiglu_ok && kc_gemm_tc_supported(segs, count, xq, m, k, gs))
+    return Q8_GEMM_GPU_TCGEN05;
   return Q8_GEMM_GPU_DP4A;
 }
 
@@ -259,23 +304,51 @@ static bool gemm_run(Q8GemmBackend backend, const int8_t *xq, const float *xs, i
     gemm_rows_dp4a(xq, xs, m, k, gs, segments, count);
     return true;
   }
+  if (backend == Q8_GEMM_GPU_TCGEN05) {
+    KcGemmSeg segs[GEMM_MAX_SEGMENTS];
+    to_kc_segs(segments, count, segs);
+    for (int s = 0; s < count; s++)
+      if (segs[s].kind == KC_SWIGLU && count != 1) {
+        kc_fail("k_gemm_q8: the tensor-core GEMM takes a SwiGLU pair as its only segment");
+        return true;
+      }
+    if (!kc_gemm_tc_supported(segs, count, xq, m, k, gs)) {
+      kc_fail("k_gemm_q8: shape not supported by the tensor-core GEMM (gs 64, K %% 256 == 0, aligned operands)");
+      return true;
+    }
+    float *xsT = gemm_scratch(kc_gemm_xst_floats(m, k / gs));
+    if (!xsT) {
+      kc_fail("k_gemm_q8: cannot allocate the transposed-scale scratch");
+      return true;
+    }
+    if (launched(kc_launch_transpose_scales(xsT, xs, m, k / gs, tl_stream), "k_gemm_q8"))
+      launched(kc_launch_gemm_tc(segs, count, xq, xsT, m, k, nullptr, tl_stream), "k_gemm_q8");
+    return true;
+  }
   return false;
 }
 
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count) {
-  gemm_run(k_gemm_q8_pick(gs, segments, count), xq, xs, m, k, gs, segments, count);
+  gemm_run(pick(xq, m, k, gs, segments, count), xq, xs, m, k, gs, segments, count);
 }
 
 int k_gemm_q8_backend_test(Q8GemmBackend backend, const int8_t *xq, const float *xs, int m, int k, int gs,
                            const GemmQ8Segment *segments, int count) {
-  if (backend != Q8_GEMM_GPU_DP4A)
+  if (backend != Q8_GEMM_GPU_DP4A && backend != Q8_GEMM_GPU_TCGEN05)
     return 0;
   return gemm_run(backend, xq, xs, m, k, gs, segments, count) ? 1 : 0;
 }
 
 int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, const int8_t *wq, int n) {
-  (void)dots, (void)xq, (void)m, (void)k, (void)gs, (void)wq, (void)n;
-  return 0;
+  KcGemmSeg seg = {nullptr, n, wq, nullptr, nullptr, nullptr, n, KC_STORE};
+  // The dots mode ignores the scales; point the scale operands at valid scratch of the right size.
+  const int groups = gs > 0 ? k / gs : 0;
+  float *scratch = gemm_scratch(kc_gemm_xst_floats(m, groups) + (size_t)n * groups + 4);
+  if (!scratch || gs != 64 || k % 256 || m <= 0 || n <= 0 || ((uintptr_t)xq & 15) || ((uintptr_t)wq & 15))
+    return 0;
+  seg.ws = scratch + kc_gemm_xst_floats(m, groups);
+  seg.ws = reinterpret_cast<const float *>(((uintptr_t)seg.ws + 15) & ~(uintptr_t)15);
+  return kc_launch_gemm_tc(&seg, 1, xq, scratch, m, k, dots, tl_stream) == 0 ? 1 : 0;
 }
 
 // ---- supporting kernels -------------------------------------------------------------------------------------------

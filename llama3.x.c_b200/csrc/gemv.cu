@@ -191,7 +191,9 @@ __device__ __forceinline__ int group_dot(const uint8_t *buf, const int8_t *xrow,
 
 template <int GS>
 __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  // The 128-byte swizzle is a function of the address bits, so the stages start on a 1024-byte boundary.
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   pdl_launch_dependents();
   const bool swiglu = a.kind == KC_SWIGLU;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -398,7 +400,7 @@ __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, Gem
 
 size_t smem_bytes(int n, int gs, int stage_bytes, int depth) {
   return (size_t)depth * stage_bytes + 128 + (size_t)2 * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
-         (size_t)((n + 15) & ~15);
+         (size_t)((n + 15) & ~15) + 1024;
 }
 
 bool encode_weight(CUtensorMap *wmap, CUtensorMap *smap, const int8_t *wq, const float *ws, int rows, int n,

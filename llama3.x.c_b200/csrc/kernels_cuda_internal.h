@@ -26,6 +26,26 @@ bool kc_pdl_enabled();
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
                    int kind, cudaStream_t stream, int grid_limit);
 
+// One GEMM segment (GemmQ8Segment without the AMX-packed copies), kind in KC_* terms.
+struct KcGemmSeg {
+  float *c;
+  int ldc;
+  const int8_t *wq;
+  const float *ws;
+  const int8_t *w3q;  // SWIGLU only
+  const float *w3s;
+  int n;
+  int kind;
+};
+
+// The tcgen05 GEMM (gemm_tc.cu): gs 64, K % 256 == 0, 16-byte aligned operands. It reads the activation scales
+// transposed, xsT [K / 64][round_up(M, 4)] (kc_launch_transpose_scales makes them from the row-major xs).
+bool kc_gemm_tc_supported(const KcGemmSeg *segs, int nseg, const int8_t *xq, int M, int K, int gs);
+size_t kc_gemm_xst_floats(int M, int groups);
+int kc_launch_transpose_scales(float *xsT, const float *xs, int M, int groups, cudaStream_t stream);
+int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const float *xsT, int M, int K,
+                      int32_t *dots, cudaStream_t stream);
+
 int kc_launch_quantize_rows(int8_t *q, float *s, const float *x, long long ldx, int m, int n, int gs,
                             cudaStream_t stream);
 int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const float *w, int rows, int size,

@@ -270,3 +270,93 @@ def test_rope_rows_bitwise(kc, oracle):
     for i in range(rows):
         rq, rk = oracle.rope_apply(q[i], k[i], tables[i], nh, nkv, hd)
         assert (bits(host(qt)[i]) == bits(rq)).all() and (bits(host(kt)[i]) == bits(rk)).all()
+
+
+# ---- tensor-core GEMM (tcgen05) -------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 256), (5, 40, 512), (200, 300, 1024), (1, 7, 256)])
+def test_gemm_tc_group_dots_exact(kc, oracle, m, n, k):
+    # The int32 group dots straight out of TMEM (k_gemm_q8_dots_test), against the exact integer oracle.
+    rng = np.random.default_rng(m + n + k)
+    wq = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    xq = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    dots = torch.zeros((k // 64, m, n), dtype=torch.int32, device="cuda")
+    assert kc.k_gemm_q8_dots_test(dots, dev(xq), m, k, 64, dev(wq), n) == 1
+    kc.status()
+    assert (host(dots) == oracle.group_dots(xq, wq, 64)).all()
+
+
+TC_SHAPES = [(128, 128, 256), (33, 48, 1024), (257, 300, 2048), (7, 4096, 4096), (130, 129, 14336)]
+
+
+@pytest.mark.parametrize("m,n,k", TC_SHAPES)
+def test_gemm_tc_store_bitwise(kc, oracle, m, n, k):
+    rng = np.random.default_rng(m * 7 + n)
+    wq, ws = oracle.seeded_q8_matrix(n, k, 64, n)
+    xq, xs = oracle.quantize(rng.standard_normal((m, k)).astype(np.float32), 64)
+    c = kc.gemm(dev(xq), dev(xs), dev(wq), dev(ws), 64, backend=kc.Q8_GEMM_GPU_TCGEN05)
+    kc.status()
+    assert (bits(host(c)) == bits(oracle.gemm(xq, xs, wq, ws, 64))).all()
+
+
+@pytest.mark.parametrize("m,d,k", [(7, 48, 1024), (33, 32, 256)])
+def test_gemm_tc_golden_amx(kc, m, d, k):
+    # Bitwise the reference's own AMX-INT8 backend (golden vectors made by the compiled reference).
+    key = f"amx_{m}_{d}_{k}"
+    if key + "_c" not in GOLDEN:
+        pytest.skip("golden file was made on a CPU without AMX")
+    c = kc.gemm(dev(GOLDEN[key + "_xq"]), dev(GOLDEN[key + "_xs"]), dev(GOLDEN[key + "_wq"]), dev(GOLDEN[key + "_ws"]),
+                64, backend=kc.Q8_GEMM_GPU_TCGEN05)
+    kc.status()
+    assert (bits(host(c)) == bits(GOLDEN[key + "_c"])).all()
+
+
+def test_gemm_tc_add_swiglu_and_segments(kc, oracle):
+    m, k, gs = 150, 1024, 64
+    rng = np.random.default_rng(11)
+    xq, xs = oracle.quantize(rng.standard_normal((m, k)).astype(np.float32), gs)
+    wa, wb, wc = (oracle.seeded_q8_matrix(r, k, gs, 50 + r) for r in (100, 37, 37))
+    base = rng.standard_normal((m, 100)).astype(np.float32)
+    ca, cb, cc = dev(base), torch.zeros((m, 37), device="cuda"), torch.zeros((m, 37), device="cuda")
+    segs = [kc.segment(ca, (dev(wa[0]), dev(wa[1])), kc.GEMM_ADD), kc.segment(cb, (dev(wb[0]), dev(wb[1]))),
+            kc.segment(cc, (dev(wc[0]), dev(wc[1])), kc.GEMM_PARTIAL)]
+    assert kc.k_gemm_q8_backend_test(kc.Q8_GEMM_GPU_TCGEN05, dev(xq), dev(xs), m, k, gs, segs) == 1
+    kc.status()
+    assert (bits(host(ca)) == bits(oracle.gemm(xq, xs, *wa, gs, kind=oracle.ADD, c=base))).all()
+    assert (bits(host(cb)) == bits(oracle.gemm(xq, xs, *wb, gs))).all()
+    assert (bits(host(cc)) == bits(oracle.gemm(xq, xs, *wc, gs))).all()
+    w1, w3 = oracle.seeded_q8_matrix(200, k, gs, 61), oracle.seeded_q8_matrix(200, k, gs, 62)
+    out = kc.gemm(dev(xq), dev(xs), dev(w1[0]), dev(w1[1]), gs, kind=kc.GEMM_SWIGLU, w3=(dev(w3[0]), dev(w3[1])),
+                  backend=kc.Q8_GEMM_GPU_TCGEN05)
+    kc.status()
+    ref = oracle.gemm(xq, xs, *w1, gs, kind=oracle.SWIGLU, w3q=w3[0], w3s=w3[1])
+    assert ulp_diff(host(out), ref).max() <= 2
+
+
+def test_gemm_tc_config1_full_size(kc, oracle):
+    # Config 1 up-projection at T=128 (14336 x 4096): bitwise the oracle on a sample of 96 weight rows, and bitwise the
+    # decode GEMV (a different kernel, same arithmetic) for 3 token rows -- size-independent checks.
+    T, N, K, gs = 128, 14336, 4096, 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+    wq, ws = kc.quantize(torch.randn((N, K), generator=g, device="cuda") * 0.02, gs)
+    xq, xs = kc.quantize(torch.randn((T, K), generator=g, device="cuda"), gs)
+    c = kc.gemm(xq, xs, wq, ws, gs, backend=kc.Q8_GEMM_GPU_TCGEN05)
+    kc.status()
+    rows = np.random.default_rng(1).choice(N, 96, replace=False)
+    hw = host(wq)[rows]
+    ref = oracle.gemm(host(xq), host(xs), hw, host(ws)[rows], gs)
+    assert (bits(host(c)[:, rows]) == bits(ref)).all()
+    for t in (0, 77, 127):
+        y = kc.gemv(xq[t], xs[t], wq, ws, gs)
+        kc.status()
+        assert (bits(host(y)) == bits(host(c)[t])).all()
+
+
+def test_k_gemm_q8_picks_tensor_cores_for_batches(kc, oracle):
+    m, k, gs = 64, 1024, 64
+    rng = np.random.default_rng(4)
+    wq, ws = oracle.seeded_q8_matrix(96, k, gs, 9)
+    xq, xs = oracle.quantize(rng.standard_normal((m, k)).astype(np.float32), gs)
+    c = kc.gemm(dev(xq), dev(xs), dev(wq), dev(ws), gs)
+    kc.status()
+    assert (bits(host(c)) == bits(oracle.gemm(xq, xs, wq, ws, gs))).all()
