@@ -73,6 +73,34 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity
   }
 }
 
+// The same wait for threads that share an SM sub-partition with busy warps: each try_wait suspends the thread in
+// hardware (up to `hint_ns`, waking when the phase completes) instead of spinning on the issue port.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, unsigned parity, unsigned hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t *bar, unsigned parity) {
+  if (mbar_try_wait_sleep(bar, parity, 1000u))
+    return true;
+  uint64_t start = kc_globaltimer();
+  for (unsigned i = 1;; i++) {
+    if (mbar_try_wait_sleep(bar, parity, 1000u))
+      return true;
+    if ((i & 15u) == 0 && kc_globaltimer() - start > KC_WAIT_NS) {
+      kc_raise(KC_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // 1-D bulk copy global -> shared through the TMA unit, completing `bytes` of transaction count on `bar`.
 // dst and src 16-byte aligned, bytes a multiple of 16. No multicast.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {

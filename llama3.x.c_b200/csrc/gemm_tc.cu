@@ -7,23 +7,26 @@
 // every group dot is an exact int32 (tcgen05.mma kind::i8, two K=32 steps per 64-group), and every output rescales
 // the groups in ascending order as acc = fmaf((float)dot * xs, ws, acc) from acc = 0.
 //
-// Tiling: the MMA's M side is 128 weight rows (64 w1 + 64 w3 rows for SwiGLU), its N side 128 tokens; a persistent
-// CTA per SM walks its tiles (tokens fastest, so the CTAs running together share weight stripes in L2).
-//   warp 0      TMA producer: per stage (two groups, 128 B of K) one [128 x 128 B] weight box, one [128 x 128 B]
-//               activation box (both 128B-swizzled, the canonical K-major UMMA layout) and the stage's transposed
-//               activation scales [2 groups x 128 tokens]; a ring of 4 stages.
-//   warp 1      MMA issuer: allocates 256 TMEM columns (two 128 x 128 int32 buffers), issues two MMAs per group into
-//               the buffer the epilogue has released, commits the buffer to the epilogue and the stage to the ring.
-//   warps 4-11  epilogue (warp % 4 = TMEM lane quadrant = 32 weight rows, (warp - 4) / 4 = 64-token half): per
-//               group it reads its 32 x 64 int32 dots and promotes them with packed f32x2 instructions, then refills
-//               its part of the buffer with the exponent bias and releases it.
-// Group promotion without integer->float conversions: each buffer holds the int32 pattern of 1.5 * 2^23 before the
-// group's MMAs accumulate onto it, so the result read back IS the float 1.5 * 2^23 + dot exactly (|dot| <= 64*127^2
-// < 2^22); one subtraction recovers (float)dot. The promotion is then sub, mul, fma per pair of outputs.
+// Tiling: the MMA's M side is 128 weight rows (for SwiGLU 64 w1 and 64 w3 rows, interleaved in 16-row blocks so
+// that the two halves of an output sit in lanes L and L+16 of one warp), its N side 128 tokens; a persistent CTA per
+// SM walks its tiles (tokens fastest, so the CTAs running together share weight stripes in L2).
+//   warp 0      TMA producer: per stage (two groups, 128 B of K) one [128 x 128 B] weight box (eight 16-row boxes
+//               for SwiGLU) and one [128 x 128 B] activation box, both 128B-swizzled (the canonical K-major UMMA
+//               layout), into a ring of 6 stages the MMA releases; and the stage's transposed activation scales
+//               [2 groups x 128 tokens] into a ring of 8 the epilogue releases.
+//   warp 1      MMA issuer: allocates 512 TMEM columns (four 128 x 128 int32 buffers), issues two MMAs per group into
+//               the next buffer the epilogue has released, commits the buffer to the epilogue and the stage to the ring.
+//   warps 2-9   epilogue (warp % 4 = TMEM lane quadrant = 32 weight rows, (warp - 2) / 4 = 64-token half): per
+//               group it reads its 32 x 64 int32 dots in 16-column chunks (each read in flight while the previous
+//               chunk is promoted with packed f32x2 instructions) and releases the buffer once the last chunk is in
+//               registers. Four buffers let the MMA run up to three groups ahead of the promotion.
+// Group promotion: the group's first MMA overwrites its TMEM buffer (no clearing), the epilogue converts each exact
+// int32 dot to float (exact: |dot| <= 64*127^2 < 2^24) and applies mul, fma as packed pairs.
 //
 // Every mbarrier wait is bounded (a timeout raises KC_ERR_TIMEOUT, sets a CTA abort flag that turns the remaining
 // waits into no-ops, and the CTA still releases its TMEM).
 #include <cuda.h>
+#include <stdio.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -35,23 +38,23 @@ namespace {
 
 constexpr int kTM = 128;                      // weight rows per tile (MMA M)
 constexpr int kTN = 128;                      // tokens per tile (MMA N)
-constexpr int kStages = 4;
+constexpr int kStages = 6;                    // operand ring (released by the MMA)
+constexpr int kXsStages = 8;                  // activation-scale ring (released by the epilogue)
 constexpr int kStageA = kTM * 128;            // weights: 128 rows x 128 B
 constexpr int kStageB = kTN * 128;            // activations: 128 tokens x 128 B
-constexpr int kStageX = 2 * kTN * 4;          // activation scales: 2 groups x 128 tokens
-constexpr int kStageBytes = kStageA + kStageB + 1024;
-constexpr int kXchBytes = kTN * 64 * 4;       // SwiGLU exchange: 128 tokens x 64 w3 rows
-constexpr int kThreads = 12 * 32;
-constexpr int kEpiWarp0 = 4;
-constexpr int kEpiWarps = 8;
-constexpr int kTmemCols = 256;
-constexpr uint32_t kBiasBits = 0x4B400000u;   // 1.5 * 2^23
-constexpr float kBias = 12582912.0f;
-constexpr int kBarXchFull = 1, kBarXchFree = 2;  // named barriers among the epilogue warps
+constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kStageX = 2 * kTN * 4;          // activation scales of one stage: 2 groups x 128 tokens
+constexpr int kEpiWarp0 = 2;                  // warps 0 (TMA) and 1 (MMA) come first
+constexpr int kEpiCols = 64;                  // token columns per epilogue thread
+constexpr int kEpiWarps = 4 * (kTN / kEpiCols);  // 4 lane quadrants x column halves
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kTmemBufs = 4;                  // 128-column int32 accumulators in flight
+constexpr int kTmemCols = kTmemBufs * 128;
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kXsStages * kStageX + 512 + 1024;
 
 struct __align__(64) GemmMaps {
-  CUtensorMap w[3];  // weights per segment (w1 for SwiGLU): boxes [128 B x 128 rows] (64 rows for SwiGLU)
-  CUtensorMap w3;    // SwiGLU second matrix
+  CUtensorMap w[3];  // weights per segment: boxes [128 B x 128 rows]; SwiGLU w1: [128 B x 16 rows]
+  CUtensorMap w3;    // SwiGLU w3: [128 B x 16 rows]
   CUtensorMap x;     // activations [M][K]: boxes [128 B x 128 tokens]
   CUtensorMap xs;    // transposed activation scales [groups][ldt]: boxes [128 tokens x 2 groups]
 };
@@ -93,37 +96,54 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs &a, int t) {
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity, volatile int *abort_flag) {
   if (*abort_flag)
     return false;
-  if (mbar_wait_bounded(bar, parity))
+  if (mbar_wait_sleep_bounded(bar, parity))
     return true;
   *abort_flag = 1;
   return false;
 }
 
-__device__ __forceinline__ void bar_sync_epi(int id) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kEpiWarps * 32) : "memory");
+// Promotes 16 token columns of one group: acc[p] = fma(((float)dot) * xs, ws, acc[p]) for 8 column pairs. The int32
+// dots convert exactly (|dot| <= 64 * 127^2 < 2^24).
+__device__ __forceinline__ void promote16(uint64_t *acc, const uint32_t (&r)[16], const float *xs, uint64_t ws2) {
+  const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+#pragma unroll
+  for (int p4 = 0; p4 < 4; p4++) {
+    const float4 x = xs4[p4];
+    const uint64_t f0 = f2_pack(__int2float_rn((int)r[4 * p4]), __int2float_rn((int)r[4 * p4 + 1]));
+    const uint64_t f1 = f2_pack(__int2float_rn((int)r[4 * p4 + 2]), __int2float_rn((int)r[4 * p4 + 3]));
+    acc[2 * p4] = f2_fma(f2_mul(f0, f2_pack(x.x, x.y)), ws2, acc[2 * p4]);
+    acc[2 * p4 + 1] = f2_fma(f2_mul(f1, f2_pack(x.z, x.w)), ws2, acc[2 * p4 + 1]);
+  }
 }
 
+template <bool DOTS>  // DOTS: the test hook's variant, which stores the raw int32 group dots instead of promoting
 __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_constant__ GemmMaps mp, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // The 128-byte swizzle is a function of the address bits, so the operand stages start on a 1024-byte boundary.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t *stages = smem;
-  float *xch = reinterpret_cast<float *>(smem + kStages * kStageBytes);
-  uint8_t *tail = smem + kStages * kStageBytes + kXchBytes;
+  float *xsring = reinterpret_cast<float *>(smem + kStages * kStageBytes);
+  uint8_t *tail = smem + kStages * kStageBytes + kXsStages * kStageX;
   uint64_t *full = reinterpret_cast<uint64_t *>(tail);
   uint64_t *empty = full + kStages;
-  uint64_t *tfull = empty + kStages;
-  uint64_t *tempty = tfull + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+  uint64_t *xfull = empty + kStages;
+  uint64_t *xempty = xfull + kXsStages;
+  uint64_t *tfull = xempty + kXsStages;
+  uint64_t *tempty = tfull + kTmemBufs;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + kTmemBufs);
   volatile int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1 + kEpiWarps);
+      mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kXsStages; i++) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kTmemBufs; i++) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], kEpiWarps);
     }
@@ -141,30 +161,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
   const int G = gridDim.x;
   const int spt = a.stages_per_tile, groups = a.groups;
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
+  if (warp == 0) {
+    // ---- TMA producer (the whole warp loops and waits, so no lane idles at the CTA barrier; lane 0 issues) ----
     int st = 0;
     for (int t = blockIdx.x; t < a.total_tiles; t += G) {
       const Tile tl = decode_tile(a, t);
       for (int j = 0; j < spt; j++, st++) {
         const int slot = st % kStages, use = st / kStages;
-        if (!wait_or_abort(&empty[slot], (use & 1) ^ 1, abort_flag))
+        const int xslot = st % kXsStages, xuse = st / kXsStages;
+        if (!wait_or_abort(&empty[slot], (use & 1) ^ 1, abort_flag) ||
+            !wait_or_abort(&xempty[xslot], (xuse & 1) ^ 1, abort_flag))
           continue;
         uint8_t *base = stages + slot * kStageBytes;
-        mbar_arrive_expect_tx(&full[slot], kStageA + kStageB + kStageX);
+        if (lane != 0)
+          continue;
+        mbar_arrive_expect_tx(&full[slot], kStageBytes);
+        mbar_arrive_expect_tx(&xfull[xslot], kStageX);
         const int k0 = j * 128;
         if (tl.swiglu) {
-          tma_load_2d(base, &mp.w[0], k0, tl.n0, &full[slot]);
-          tma_load_2d(base + kStageA / 2, &mp.w3, k0, tl.n0, &full[slot]);
+          // Rows 32i .. 32i+15 of the tile are w1 rows n0+16i .., rows 32i+16 .. 32i+31 the matching w3 rows, so
+          // lanes L and L+16 of every epilogue warp hold the two halves of one SwiGLU output.
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            tma_load_2d(base + (32 * i) * 128, &mp.w[0], k0, tl.n0 + 16 * i, &full[slot]);
+            tma_load_2d(base + (32 * i + 16) * 128, &mp.w3, k0, tl.n0 + 16 * i, &full[slot]);
+          }
         } else {
           tma_load_2d(base, &mp.w[0] + tl.s, k0, tl.n0, &full[slot]);
         }
         tma_load_2d(base + kStageA, &mp.x, k0, tl.m0, &full[slot]);
-        tma_load_2d(base + kStageA + kStageB, &mp.xs, tl.m0, 2 * j, &full[slot]);
+        tma_load_2d(xsring + xslot * (kStageX / 4), &mp.xs, tl.m0, 2 * j, &xfull[xslot]);
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
+  } else if (warp == 1) {
+    // ---- MMA issuer (the whole warp loops and waits; lane 0 issues the MMAs and commits) ----
     const uint32_t idesc = umma_idesc_i8(kTM, kTN);
     int st = 0, gidx = 0;
     for (int t = blockIdx.x; t < a.total_tiles; t += G) {
@@ -175,152 +205,143 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
         const uint8_t *base = stages + slot * kStageBytes;
         const uint64_t adesc = umma_desc_sw128(base), bdesc = umma_desc_sw128(base + kStageA);
         for (int gg = 0; gg < 2 && 2 * j + gg < groups; gg++, gidx++) {
-          const int b = gidx & 1, ub = gidx >> 1;
-          const bool ok = wait_or_abort(&tempty[b], ub & 1, abort_flag) && have;
+          const int b = gidx % kTmemBufs, ub = gidx / kTmemBufs;
+          // A fresh barrier's preceding phase counts as complete, so the first use of each buffer does not wait.
+          const bool ok = wait_or_abort(&tempty[b], (ub & 1) ^ 1, abort_flag) && have;
           tc_fence_after();
-          if (ok) {
+          if (ok && lane == 0) {
+            // The group's first K step overwrites the buffer, the second accumulates onto it.
 #pragma unroll
             for (int k = 0; k < 2; k++) {
               const uint64_t off = (uint64_t)((gg * 64 + k * 32) >> 4);
-              umma_i8(tmem + b * kTN, adesc + off, bdesc + off, idesc, true);
+              umma_i8(tmem + b * kTN, adesc + off, bdesc + off, idesc, k > 0);
             }
           }
-          umma_commit(&tfull[b]);
+          if (lane == 0)
+            umma_commit(&tfull[b]);
+          __syncwarp();
         }
-        umma_commit(&empty[slot]);
+        if (lane == 0)
+          umma_commit(&empty[slot]);
+        __syncwarp();
       }
     }
   } else if (warp >= kEpiWarp0) {
     // ---- epilogue: promotion of every group, in order ----
-    const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
+    const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;  // lane quadrant, 64-token column half
     const int row = 32 * q + lane;  // TMEM lane = row of the weight tile
-    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + 64 * h;
-    // Both buffers start out holding the bias.
-    tmem_st32_fill(tq, kBiasBits);
-    tmem_st32_fill(tq + 32, kBiasBits);
-    tmem_st32_fill(tq + kTN, kBiasBits);
-    tmem_st32_fill(tq + kTN + 32, kBiasBits);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&tempty[0]);
-      mbar_arrive(&tempty[1]);
-    }
-    const uint64_t negbias2 = f2_pack(-kBias, -kBias);
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + kEpiCols * h;
     int st = 0, gidx = 0;
     for (int t = blockIdx.x; t < a.total_tiles; t += G) {
       const Tile tl = decode_tile(a, t);
-      const GemmSegDev sg = tl.s == 0 ? a.seg[0] : tl.s == 1 ? a.seg[1] : a.seg[2];
-      const bool w3row = tl.swiglu && row >= kTM / 2;
-      const int n = tl.n0 + (tl.swiglu ? (row & (kTM / 2 - 1)) : row);
-      const bool row_ok = n < sg.n;
-      const float *wsr = (w3row ? sg.ws3 : sg.ws) + (size_t)min(n, sg.n - 1) * groups;
-      float4 w_cur = __ldg(reinterpret_cast<const float4 *>(wsr));
-      float4 w_n1 = groups > 4 ? __ldg(reinterpret_cast<const float4 *>(wsr + 4)) : w_cur;
-      float4 w_n2 = groups > 8 ? __ldg(reinterpret_cast<const float4 *>(wsr + 8)) : w_cur;
-      uint64_t acc[32];
+      // Scalars of this tile's segment (selected field by field: a whole-struct select would go to local memory).
+      const int seg_n = tl.s == 0 ? a.seg[0].n : tl.s == 1 ? a.seg[1].n : a.seg[2].n;
+      const int seg_ldc = tl.s == 0 ? a.seg[0].ldc : tl.s == 1 ? a.seg[1].ldc : a.seg[2].ldc;
+      const int seg_kind = tl.s == 0 ? a.seg[0].kind : tl.s == 1 ? a.seg[1].kind : a.seg[2].kind;
+      float *const seg_c = tl.s == 0 ? a.seg[0].c : tl.s == 1 ? a.seg[1].c : a.seg[2].c;
+      const float *const seg_ws = tl.s == 0 ? a.seg[0].ws : tl.s == 1 ? a.seg[1].ws : a.seg[2].ws;
+      const bool w3row = tl.swiglu && lane >= 16;
+      const int n = tl.n0 + (tl.swiglu ? 16 * q + (lane & 15) : row);
+      const bool row_ok = n < seg_n;
+      const float *wsr = (w3row ? a.seg[0].ws3 : seg_ws) + (size_t)min(n, seg_n - 1) * groups;
+      uint64_t acc[kEpiCols / 2];
 #pragma unroll
-      for (int i = 0; i < 32; i++)
+      for (int i = 0; i < kEpiCols / 2; i++)
         acc[i] = 0;
+      // TMEM reads are software-pipelined against the promotion in 16-column chunks: the next chunk is in flight
+      // while the current one is promoted. rA holds chunk 0 of the current group on entry to each group.
+      uint32_t rA[16], rB[16];
+      bool ok = wait_or_abort(&tfull[gidx % kTmemBufs], (gidx / kTmemBufs) & 1, abort_flag);
+      tc_fence_after();
+      tmem_ld16(tq + (gidx % kTmemBufs) * kTN, rA);
+      tmem_wait_ld();
       for (int j = 0; j < spt; j++, st++) {
-        const int slot = st % kStages, use = st / kStages;
-        wait_or_abort(&full[slot], use & 1, abort_flag);
-        const float *xsT = reinterpret_cast<const float *>(stages + slot * kStageBytes + kStageA + kStageB);
+        const int xslot = st % kXsStages;
+        wait_or_abort(&xfull[xslot], (st / kXsStages) & 1, abort_flag);
+        const float *xsT = xsring + xslot * (kStageX / 4);
         for (int gg = 0; gg < 2 && 2 * j + gg < groups; gg++, gidx++) {
-          const int g = 2 * j + gg;
-          const int b = gidx & 1, ub = gidx >> 1;
-          const bool ok = wait_or_abort(&tfull[b], ub & 1, abort_flag);
-          tc_fence_after();
-          if ((g & 3) == 0 && g > 0) {
-            w_cur = w_n1;
-            w_n1 = w_n2;
-            if (g + 8 < groups)
-              w_n2 = __ldg(reinterpret_cast<const float4 *>(wsr + g + 8));
-          }
-          const float wv = (g & 3) == 0 ? w_cur.x : (g & 3) == 1 ? w_cur.y : (g & 3) == 2 ? w_cur.z : w_cur.w;
+          const int g = 2 * j + gg, b = gidx % kTmemBufs;
+          const bool last = g + 1 == groups;
+          const float wv = __ldg(wsr + g);
           const uint64_t ws2 = f2_pack(wv, wv);
-          const float4 *xs4 = reinterpret_cast<const float4 *>(xsT + gg * kTN + 64 * h);
-          // Two halves of 32 columns: read, promote, then refill the buffer with the bias and release it.
+          const float *xs = xsT + gg * kTN + kEpiCols * h;
+          const uint32_t tb = tq + b * kTN;
+          const bool promote = ok && !DOTS;
+          const bool dump = DOTS && ok && row_ok && tl.s == 0 && !tl.swiglu;
 #pragma unroll
-          for (int half = 0; half < 2; half++) {
-            uint32_t r[32];
-            tmem_ld32(tq + b * kTN + 32 * half, r);
+          for (int c = 0; c < 4; c += 2) {
+            tmem_ld16(tb + 16 * (c + 1), rB);
+            if (promote)
+              promote16(acc + 8 * c, rA, xs + 16 * c, ws2);
+            if (dump)
+#pragma unroll
+              for (int i = 0; i < 16; i++)
+                if (tl.m0 + kEpiCols * h + 16 * c + i < a.M)
+                  a.dots[((size_t)g * a.M + tl.m0 + kEpiCols * h + 16 * c + i) * seg_n + n] =
+                      (int32_t)rA[i];
             tmem_wait_ld();
-            if (!ok)
-              continue;
-            if (a.dots) {
-              if (row_ok && tl.s == 0 && !tl.swiglu)
-                for (int c = 0; c < 32; c++) {
-                  const int m = tl.m0 + 64 * h + 32 * half + c;
-                  if (m < a.M)
-                    a.dots[((size_t)g * a.M + m) * sg.n + n] = (int32_t)(r[c] - kBiasBits);
-                }
-              continue;
+            const bool ok_cur = ok;
+            if (c == 0) {
+              tmem_ld16(tb + 32, rA);
+            } else {
+              // All 64 columns are in registers: release the buffer.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0)
+                mbar_arrive(&tempty[b]);
+              if (!last) {  // chunk 0 of the next group
+                const int bn = (gidx + 1) % kTmemBufs;
+                ok = wait_or_abort(&tfull[bn], ((gidx + 1) / kTmemBufs) & 1, abort_flag);
+                tc_fence_after();
+                tmem_ld16(tq + bn * kTN, rA);
+              }
             }
+            if (ok_cur && !DOTS)
+              promote16(acc + 8 * (c + 1), rB, xs + 16 * (c + 1), ws2);
+            if (dump)
 #pragma unroll
-            for (int c4 = 0; c4 < 8; c4++) {
-              const float4 x = xs4[8 * half + c4];
-              const int c = 4 * c4;
-              uint64_t f0 = f2_add(f2_pack_bits(r[c], r[c + 1]), negbias2);
-              uint64_t f1 = f2_add(f2_pack_bits(r[c + 2], r[c + 3]), negbias2);
-              f0 = f2_mul(f0, f2_pack(x.x, x.y));
-              f1 = f2_mul(f1, f2_pack(x.z, x.w));
-              acc[16 * half + 2 * c4] = f2_fma(f0, ws2, acc[16 * half + 2 * c4]);
-              acc[16 * half + 2 * c4 + 1] = f2_fma(f1, ws2, acc[16 * half + 2 * c4 + 1]);
-            }
+              for (int i = 0; i < 16; i++)
+                if (tl.m0 + kEpiCols * h + 16 * (c + 1) + i < a.M)
+                  a.dots[((size_t)g * a.M + tl.m0 + kEpiCols * h + 16 * (c + 1) + i) * seg_n + n] =
+                      (int32_t)rB[i];
+            if (c == 0 || !last)
+              tmem_wait_ld();
           }
-          tmem_st32_fill(tq + b * kTN, kBiasBits);
-          tmem_st32_fill(tq + b * kTN + 32, kBiasBits);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0)
-            mbar_arrive(&tempty[b]);
         }
         __syncwarp();
         if (lane == 0)
-          mbar_arrive(&empty[slot]);
+          mbar_arrive(&xempty[xslot]);
       }
-      if (a.dots)
+      if (DOTS)
         continue;
       // ---- write the tile: thread = weight row n, 64 tokens ----
-      const int mbase = tl.m0 + 64 * h;
+      const int mbase = tl.m0 + kEpiCols * h;
       if (tl.swiglu) {
-        if (w3row) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            float lo, hi;
-            f2_unpack(acc[i], lo, hi);
-            xch[(64 * h + 2 * i) * 64 + (row - kTM / 2)] = lo;
-            xch[(64 * h + 2 * i + 1) * 64 + (row - kTM / 2)] = hi;
-          }
-        }
-        bar_sync_epi(kBarXchFull);
-        if (!w3row && row_ok) {
-#pragma unroll
-          for (int i = 0; i < 32; i++) {
-            float lo, hi;
-            f2_unpack(acc[i], lo, hi);
-            const int m = mbase + 2 * i;
+        for (int i = 0; i < kEpiCols / 2; i++) {
+          float lo, hi, glo, ghi;
+          f2_unpack(acc[i], lo, hi);
+          glo = __shfl_down_sync(0xffffffffu, lo, 16);
+          ghi = __shfl_down_sync(0xffffffffu, hi, 16);
+          const int m = mbase + 2 * i;
+          if (!w3row && row_ok) {
             if (m < a.M)
-              sg.c[(size_t)m * sg.ldc + n] = silu_gate_dev(lo, xch[(64 * h + 2 * i) * 64 + row]);
+              seg_c[(size_t)m * seg_ldc + n] = silu_gate_dev(lo, glo);
             if (m + 1 < a.M)
-              sg.c[(size_t)(m + 1) * sg.ldc + n] = silu_gate_dev(hi, xch[(64 * h + 2 * i + 1) * 64 + row]);
+              seg_c[(size_t)(m + 1) * seg_ldc + n] = silu_gate_dev(hi, ghi);
           }
         }
-        bar_sync_epi(kBarXchFree);
       } else if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
+        for (int i = 0; i < kEpiCols / 2; i++) {
           float lo, hi;
           f2_unpack(acc[i], lo, hi);
           const int m = mbase + 2 * i;
-          float *c0 = sg.c + (size_t)m * sg.ldc + n;
+          float *c0 = seg_c + (size_t)m * seg_ldc + n;
           if (m < a.M)
-            *c0 = sg.kind == KC_ADD ? __fadd_rn(*c0, lo) : lo;
+            *c0 = seg_kind == KC_ADD ? __fadd_rn(*c0, lo) : lo;
           if (m + 1 < a.M)
-            c0[sg.ldc] = sg.kind == KC_ADD ? __fadd_rn(c0[sg.ldc], hi) : hi;
+            c0[seg_ldc] = seg_kind == KC_ADD ? __fadd_rn(c0[seg_ldc], hi) : hi;
         }
       }
     }
@@ -398,8 +419,8 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
     if (swiglu) {
       if (s != 0 || nseg != 1)
         return -1;  // the SwiGLU pair is a segment of its own (the reference's engine issues it alone)
-      if (!kc_tmap_2d(&mp.w[0], segs[s].wq, 1, K, segs[s].n, K, 128, kTM / 2, true) ||
-          !kc_tmap_2d(&mp.w3, segs[s].w3q, 1, K, segs[s].n, K, 128, kTM / 2, true))
+      if (!kc_tmap_2d(&mp.w[0], segs[s].wq, 1, K, segs[s].n, K, 128, 16, true) ||
+          !kc_tmap_2d(&mp.w3, segs[s].w3q, 1, K, segs[s].n, K, 128, 16, true))
         return -1;
     } else if (!kc_tmap_2d(&mp.w[s], segs[s].wq, 1, K, segs[s].n, K, 128, kTM, true)) {
       return -1;
@@ -411,12 +432,13 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
   if (!kc_tmap_2d(&mp.x, xq, 1, K, M, K, 128, kTN, true) ||
       !kc_tmap_2d(&mp.xs, xsT, 4, ldt, groups, (uint64_t)ldt * 4, kTN, 2, false))
     return -1;
-  const size_t smem = (size_t)kStages * kStageBytes + kXchBytes + 256 + 1024;
+  const size_t smem = kSmemBytes;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_q8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemm_q8_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemm_q8_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set[dev] = true;
   }
   const int sms = kc_device_sms();
@@ -430,5 +452,14 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
   attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel, mp, a) == cudaSuccess ? 0 : -2;
+  const cudaError_t e = dots ? cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<true>, mp, a)
+                             : cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<false>, mp, a);
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, gemm_q8_tc_kernel<false>);
+    fprintf(stderr, "gemm_q8_tc_kernel launch: %s (regs %d, threads %d, max threads %d, smem %zu + static %zu)\n",
+            cudaGetErrorString(e), fa.numRegs, kThreads, fa.maxThreadsPerBlock, smem, fa.sharedSizeBytes);
+    return -2;
+  }
+  return 0;
 }
