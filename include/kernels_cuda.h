@@ -120,6 +120,18 @@ int k_gemm_q8_backend_test(Q8GemmBackend backend, const int8_t *xq, const float 
  * from row-major weights wq[n][k] instead of an AMX-packed copy. Returns 0 when unsupported. */
 int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, const int8_t *wq, int n);
 
+/* ---- k_gemm_q8 without device allocation (no counterpart in the reference) -------------------------------------- */
+/* Same arguments and results as k_gemm_q8, but the tensor-core path stages its transposed activation scales in a
+ * fixed array compiled into the library (K_GEMM_Q8_NOALLOC_MAX_SCALES floats, 4 MiB, one per device) instead of a
+ * buffer it allocates: (k / gs) * round_up(m, 4) must not exceed that, or the call is rejected. The first call on a
+ * device looks the array's address up (cudaGetSymbolAddress, with that device current), so make it once during setup.
+ * Nothing needs to start at zero: every call rewrites the whole part of the array it reads. Calls on one device share
+ * the array, so two calls in flight at once (different streams or threads) race; issue them on one stream.
+ * Returns 0 on success, -1 when the arguments are rejected (kc_last_error says why, under KC_FAIL_RETURN). */
+#define K_GEMM_Q8_NOALLOC_MAX_SCALES (1 << 20)
+int k_gemm_q8_noalloc(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
+                      int count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -67,6 +67,8 @@ _SIGNATURES = {
     "k_gemm_q8_backend_test": (_c.c_int, [_c.c_int, _i8p, _f32p, _c.c_int, _c.c_int, _c.c_int,
                                           _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_gemm_q8_dots_test": (_c.c_int, [_c.c_void_p, _i8p, _c.c_int, _c.c_int, _c.c_int, _i8p, _c.c_int]),
+    "k_gemm_q8_noalloc": (_c.c_int, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment),
+                                     _c.c_int]),
     "k_rmsnorm": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_float]),
     "k_rmsnorm_rows": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_int, _c.c_float]),
     "k_rmsnorm_q8_rows": (None, [_i8p, _f32p, _f32p, _f32p, _c.c_size_t, _f32p, _c.c_int, _c.c_int, _c.c_float,
@@ -233,6 +235,13 @@ def k_gemm_q8_backend_test(backend, xq, xs, m, k, gs, segs):
 
 def k_gemm_q8_dots_test(dots, xq, m, k, gs, wq, n):
     return _call("k_gemm_q8_dots_test", _ptr(dots), _ptr(xq), m, k, gs, _ptr(wq), n)
+
+
+def k_gemm_q8_noalloc(xq, xs, m, k, gs, segs):
+    """k_gemm_q8 with its scale scratch in the library's fixed device array; raises KernelError when rejected."""
+    arr, count = _segments(segs)
+    if _call("k_gemm_q8_noalloc", _ptr(xq), _ptr(xs), m, k, gs, arr, count) != 0:
+        raise KernelError("k_gemm_q8_noalloc rejected its arguments")
 
 
 def k_rmsnorm(out, x, weight, size, eps):

@@ -351,6 +351,62 @@ int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, c
   return kc_launch_gemm_tc(&seg, 1, xq, scratch, m, k, dots, tl_stream) == 0 ? 1 : 0;
 }
 
+// ---- k_gemm_q8 without device allocation --------------------------------------------------------------------------
+
+// Who needs it: a serving process that hands all of HBM to its weights and KV cache at start-up has no room left for a
+// buffer the GEMM would grow on first use, and a caller on a latency-bound path cannot afford the device-wide
+// synchronisation cudaMalloc / cudaFree bring. The transposed scales therefore live in this fixed array of the
+// library's device image (4 MiB per device); every call overwrites the [K/64][round_up(m, 4)] prefix it reads.
+static __device__ __align__(256) float noalloc_scales[K_GEMM_Q8_NOALLOC_MAX_SCALES];
+
+static float *noalloc_scales_address() {
+  static float *addr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    kc_fail("k_gemm_q8_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scales);
+    if (e != cudaSuccess) {
+      kc_fail("k_gemm_q8_noalloc: cannot resolve the scale array on device %d: %s", dev, cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<float *>(p);
+  }
+  return addr[dev];
+}
+
+int k_gemm_q8_noalloc(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
+                      int count) {
+  if (!gemm_args_ok("k_gemm_q8_noalloc", xq, xs, m, k, gs, segments, count))
+    return -1;
+  if (m == 0 || k == 0)
+    return 0;
+  const Q8GemmBackend backend = pick(xq, m, k, gs, segments, count);
+  if (backend == Q8_GEMM_GPU_DP4A) {  // one GEMV launch per row: no scratch at all
+    kc_clear_error();
+    gemm_rows_dp4a(xq, xs, m, k, gs, segments, count);
+    return kc_last_error()[0] ? -1 : 0;
+  }
+  const size_t need = kc_gemm_xst_floats(m, k / gs);
+  if (need > (size_t)K_GEMM_Q8_NOALLOC_MAX_SCALES) {
+    kc_fail("k_gemm_q8_noalloc: m=%d k=%d needs %zu scale floats, above the fixed %d", m, k, need,
+            K_GEMM_Q8_NOALLOC_MAX_SCALES);
+    return -1;
+  }
+  float *xsT = noalloc_scales_address();
+  if (!xsT)
+    return -1;
+  KcGemmSeg segs[GEMM_MAX_SEGMENTS];
+  to_kc_segs(segments, count, segs);
+  if (!launched(kc_launch_transpose_scales(xsT, xs, m, k / gs, tl_stream), "k_gemm_q8_noalloc") ||
+      !launched(kc_launch_gemm_tc(segs, count, xq, xsT, m, k, nullptr, tl_stream), "k_gemm_q8_noalloc"))
+    return -1;
+  return 0;
+}
+
 // ---- supporting kernels -------------------------------------------------------------------------------------------
 
 void k_rmsnorm_rows(float *out, const float *x, const float *weight, int rows, int size, float epsilon) {
