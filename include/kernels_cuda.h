@@ -80,6 +80,9 @@ void kc_clear_error(void);
  * quantizer, 2 = a bounded wait timed out, 4 = bad arguments), or -1 for a CUDA error. In KC_FAIL_EXIT mode a
  * nonzero result fails like the reference ("nonfinite activation during INT8 quantization"). */
 int kc_status(void);
+/* Applies the fail() policy to a message from a caller of this library (the GPU engine): exit under KC_FAIL_EXIT,
+ * else record it for kc_last_error. */
+void kc_fail_message(const char *message);
 
 /* ---- quantizer (include/kernels.h:110, include/gemm.h:130) ------------------------------------------------------- */
 void k_quantize(int8_t *q, float *s, const float *x, int n, int gs);
@@ -111,6 +114,60 @@ void k_rope_apply_rows(float *q, size_t q_stride, float *k, size_t k_stride, con
  * pair on the reference's AVX-512 ISA. */
 void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t ldx, const float *weight, int rows,
                        int size, float epsilon, int gs);
+
+/* ---- K/V cache and attention (include/kernels.h:126-179) --------------------------------------------------------- */
+/* The cache is the reference's head-major layout (LLAMA_KV_LAYOUT=head, its default): one layer's K or V cache is
+ * [n_kv_heads][seq_len][head_dim] fp32. AttentionWork holds the split-K partials and merge counters in device memory
+ * (the reference keeps the partials in host memory and has no counters); `memory` passed to k_attention_init_rows is
+ * device memory of k_attention_bytes_rows bytes, or NULL to let the call allocate it (k_attention_free releases only
+ * what it allocated). Attention agrees with the reference's within fp32 rounding (split-K merge order), and a row of a
+ * batch is bitwise the same row computed alone. `att` is the reference's host scratch and is ignored. */
+typedef struct {
+  float *partial;
+  int *counters;
+  int max_chunks, n_heads, n_kv_heads, head_dim, seq_len, rows;
+  int external;
+  size_t capacity;
+} AttentionWork;
+void k_kv_strides(int n_kv_heads, int head_dim, int seq_len, size_t *pos_stride, size_t *head_base);
+void k_kv_store(float *cache, const float *src, size_t src_ld, int pos0, int count, int n_kv_heads, int head_dim,
+                int seq_len);
+size_t k_attention_bytes_rows(int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows);
+void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows,
+                           void *memory);
+void k_attention_free(AttentionWork *work);
+void k_attention_kv(float *out, const float *q, const float *key_cache, const float *value_cache, float *att,
+                    AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int position);
+void k_attention_batch_kv(float *out, const float *q, const float *key_cache, const float *value_cache, float *att,
+                          AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int pos0, int m);
+
+/* ---- GPU engine steps (no counterpart in the reference, whose engine does these inline on the host) -------------- */
+/* Fused k_rope_apply_rows + two k_kv_store calls (src/tp.c:549-556): rows r of q (stride q_ld) and k (stride kv_ld)
+ * rotated at position (*position if non-NULL, else pos0) + r with table [seq_len][2 * head_dim] (k_rope_table rows);
+ * q rotated in place, rotated k and v (stride kv_ld) stored into the caches. Reading the position from device memory
+ * lets a captured decode step replay at every position. */
+void k_rope_kv_store_rows(float *q, size_t q_ld, const float *k, const float *v, size_t kv_ld, float *key_cache,
+                          float *value_cache, const float *table, const int *position, int pos0, int rows, int n_heads,
+                          int n_kv_heads, int head_dim, int seq_len);
+/* k_attention_batch_kv whose output is also quantized for the Wo product (k_quantize_rows fused, src/tp.c:562),
+ * oq/os may be NULL; with a device `position` the rows are at *position + r. */
+void k_attention_q8_rows(float *out, int8_t *oq, float *os, const float *q, const float *key_cache,
+                         const float *value_cache, AttentionWork *work, int n_heads, int n_kv_heads, int head_dim,
+                         int seq_len, const int *position, int pos0, int rows, int gs);
+/* x[r][i] = q[tok][i] * s[(tok * dim + i) / gs] for tok = tokens[r] (device), src/tp.c:395-396. */
+void k_embed_q8_rows(float *x, const int *tokens, K8Weight embed, int rows, int dim, int gs, int vocab);
+void k_add(float *x, const float *y, size_t n); /* x += y */
+/* Greedy sampling on the device: *key = a 64-bit key whose unsigned maximum over all shards (an NCCL max all-reduce)
+ * is the first maximum (sample_argmax, src/sampler.c:9-23); logits[i] has vocabulary index offset + i. */
+void k_argmax_key(unsigned long long *key, const float *logits, int n, int offset);
+/* token = index in *key; out[*step] = token (out may be NULL); *token = token; ++*step; ++*position. */
+void k_greedy_advance(int *out, int *step, int *token, int *position, const unsigned long long *key);
+/* Seeded N(0, std) benchmark weights quantized like k_quantize: rows [row0, row0 + rows) x columns [col0, col0 + cols)
+ * of a [*][full_cols] tensor numbered `tensor`, into q [rows][cols] and s [rows][cols / gs]; every element is a
+ * function of (seed, tensor, row, column) only, so a shard equals the same slice of the whole tensor. gs 32..256. */
+void k_random_q8(int8_t *q, float *s, int rows, int cols, size_t row0, size_t col0, size_t full_cols,
+                 unsigned long long seed, unsigned long long tensor, float std, int gs);
+void k_fill(float *x, size_t n, float value);
 
 /* ---- test hooks (include/testing.h:67-69) ------------------------------------------------------------------------ */
 /* One named backend; returns 0 when it is not compiled in (the CPU rungs). */

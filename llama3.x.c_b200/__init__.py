@@ -40,6 +40,14 @@ class GemmQ8Segment(ctypes.Structure):
                 ("pw", ctypes.c_void_p), ("pw3", ctypes.c_void_p), ("n", ctypes.c_int), ("kind", ctypes.c_int)]
 
 
+class AttentionWork(ctypes.Structure):
+    """include/kernels_cuda.h: split-K partials and merge counters in device memory."""
+    _fields_ = [("partial", ctypes.c_void_p), ("counters", ctypes.c_void_p), ("max_chunks", ctypes.c_int),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("seq_len", ctypes.c_int), ("rows", ctypes.c_int), ("external", ctypes.c_int),
+                ("capacity", ctypes.c_size_t)]
+
+
 # Every symbol include/kernels_cuda.h declares, with its ctypes signature (restype, argtypes).
 _c = ctypes
 _SIGNATURES = {
@@ -76,6 +84,28 @@ _SIGNATURES = {
     "k_rope_apply": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_int, _c.c_int]),
     "k_rope_apply_rows": (None, [_f32p, _c.c_size_t, _f32p, _c.c_size_t, _f32p, _c.c_size_t, _c.c_int, _c.c_int,
                                  _c.c_int, _c.c_int]),
+    "kc_fail_message": (None, [_c.c_char_p]),
+    "k_kv_strides": (None, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
+    "k_kv_store": (None, [_f32p, _f32p, _c.c_size_t, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_attention_bytes_rows": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_attention_init_rows": (None, [_c.POINTER(AttentionWork), _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int,
+                                     _c.c_void_p]),
+    "k_attention_free": (None, [_c.POINTER(AttentionWork)]),
+    "k_attention_kv": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _c.POINTER(AttentionWork), _c.c_int, _c.c_int,
+                              _c.c_int, _c.c_int, _c.c_int]),
+    "k_attention_batch_kv": (None, [_f32p, _f32p, _f32p, _f32p, _f32p, _c.POINTER(AttentionWork), _c.c_int,
+                                    _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_rope_kv_store_rows": (None, [_f32p, _c.c_size_t, _f32p, _f32p, _c.c_size_t, _f32p, _f32p, _f32p, _c.c_void_p,
+                                    _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_attention_q8_rows": (None, [_f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _c.POINTER(AttentionWork), _c.c_int,
+                                   _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int, _c.c_int]),
+    "k_embed_q8_rows": (None, [_f32p, _c.c_void_p, K8Weight, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_add": (None, [_f32p, _f32p, _c.c_size_t]),
+    "k_argmax_key": (None, [_c.c_void_p, _f32p, _c.c_int, _c.c_int]),
+    "k_greedy_advance": (None, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p]),
+    "k_random_q8": (None, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_size_t, _c.c_size_t, _c.c_size_t, _c.c_ulonglong,
+                           _c.c_ulonglong, _c.c_float, _c.c_int]),
+    "k_fill": (None, [_f32p, _c.c_size_t, _c.c_float]),
 }
 
 
@@ -302,3 +332,58 @@ def gemm(xq, xs, wq, ws, gs, kind=GEMM_STORE, c=None, w3=None, backend=None):
     elif not k_gemm_q8_backend_test(backend, xq, xs, m, k, gs, [seg]):
         raise KernelError(f"backend {backend} is not compiled in")
     return c
+
+
+# ---- engine kernels (device tensors in, nothing allocated here) ------------------------------------------------------
+
+def attention_work(n_heads, n_kv_heads, head_dim, seq_len, rows=1):
+    """k_attention_init_rows with library-allocated device memory; release with k_attention_free."""
+    w = AttentionWork()
+    _call("k_attention_init_rows", ctypes.byref(w), n_heads, n_kv_heads, head_dim, seq_len, rows, None)
+    return w
+
+
+def k_attention_free(work):
+    _call("k_attention_free", ctypes.byref(work))
+
+
+def k_attention_kv(out, q, kc, vc, work, n_heads, n_kv_heads, head_dim, seq_len, position):
+    _call("k_attention_kv", _ptr(out), _ptr(q), _ptr(kc), _ptr(vc), None, ctypes.byref(work), n_heads, n_kv_heads,
+          head_dim, seq_len, position)
+
+
+def k_attention_batch_kv(out, q, kc, vc, work, n_heads, n_kv_heads, head_dim, seq_len, pos0, m):
+    _call("k_attention_batch_kv", _ptr(out), _ptr(q), _ptr(kc), _ptr(vc), None, ctypes.byref(work), n_heads,
+          n_kv_heads, head_dim, seq_len, pos0, m)
+
+
+def k_attention_q8_rows(out, oq, os_, q, kc, vc, work, n_heads, n_kv_heads, head_dim, seq_len, position, pos0, rows,
+                        gs):
+    _call("k_attention_q8_rows", _ptr(out), _ptr(oq), _ptr(os_), _ptr(q), _ptr(kc), _ptr(vc), ctypes.byref(work),
+          n_heads, n_kv_heads, head_dim, seq_len, _ptr(position) if position is not None else None, pos0, rows, gs)
+
+
+def k_kv_store(cache, src, src_ld, pos0, count, n_kv_heads, head_dim, seq_len):
+    _call("k_kv_store", _ptr(cache), _ptr(src), src_ld, pos0, count, n_kv_heads, head_dim, seq_len)
+
+
+def k_rope_kv_store_rows(q, q_ld, k, v, kv_ld, kc, vc, table, position, pos0, rows, n_heads, n_kv_heads, head_dim,
+                         seq_len):
+    _call("k_rope_kv_store_rows", _ptr(q), q_ld, _ptr(k), _ptr(v), kv_ld, _ptr(kc), _ptr(vc), _ptr(table),
+          _ptr(position) if position is not None else None, pos0, rows, n_heads, n_kv_heads, head_dim, seq_len)
+
+
+def k_embed_q8_rows(x, tokens, embed, rows, dim, gs, vocab):
+    _call("k_embed_q8_rows", _ptr(x), _ptr(tokens), K8Weight(_ptr(embed[0]), _ptr(embed[1])), rows, dim, gs, vocab)
+
+
+def k_argmax_key(key, logits, n, offset):
+    _call("k_argmax_key", _ptr(key), _ptr(logits), n, offset)
+
+
+def k_greedy_advance(out, step, token, position, key):
+    _call("k_greedy_advance", _ptr(out), _ptr(step), _ptr(token), _ptr(position), _ptr(key))
+
+
+def k_random_q8(q, s, rows, cols, row0, col0, full_cols, seed, tensor, std, gs):
+    _call("k_random_q8", _ptr(q), _ptr(s), rows, cols, row0, col0, full_cols, seed, tensor, std, gs)

@@ -22,7 +22,7 @@ bool pdl_on = true;
 
 }  // namespace
 
-static bool kc_fail(const char *format, ...) {
+bool kc_fail(const char *format, ...) {
   va_list args;
   va_start(args, format);
   vsnprintf(tl_error, sizeof(tl_error), format, args);
@@ -58,6 +58,8 @@ int kc_device_sms() {
 
 bool kc_pdl_enabled() { return pdl_on; }
 
+cudaStream_t kc_stream() { return tl_stream; }
+
 extern "C" {
 
 void kernels_init(void) {
@@ -88,6 +90,8 @@ void kc_set_fail_mode(int mode) { fail_mode = mode == KC_FAIL_RETURN ? KC_FAIL_R
 const char *kc_last_error(void) { return tl_error; }
 
 void kc_clear_error(void) { tl_error[0] = 0; }
+
+void kc_fail_message(const char *message) { kc_fail("%s", message); }
 
 int kc_status(void) {
   cudaError_t e = cudaStreamSynchronize(tl_stream);

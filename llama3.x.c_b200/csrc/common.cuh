@@ -102,7 +102,7 @@ __device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t *bar, unsigned 
 }
 
 // 1-D bulk copy global -> shared through the TMA unit, completing `bytes` of transaction count on `bar`.
-// dst and src 16-byte aligned, bytes a multiple of 16. No multicast.
+// dst and src 16-byte aligned, bytes a multiple of 16; the destination is this CTA's shared memory only.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
@@ -111,7 +111,7 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
 }
 
 // 2-D tiled TMA load of the box at (x, y) (x in elements of the innermost dimension; x * element size must be a
-// multiple of 16 bytes) into shared memory, completing its bytes on `bar`. No multicast.
+// multiple of 16 bytes) into shared memory, completing its bytes on `bar` (this CTA only).
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -120,7 +120,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
       : "memory");
 }
 
-// 3-D tiled TMA load of the box at (x, y, z) into shared memory, completing its bytes on `bar`. No multicast.
+// 3-D tiled TMA load of the box at (x, y, z) into shared memory, completing its bytes on `bar` (this CTA only).
 __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, int y, int z, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "

@@ -19,6 +19,10 @@ struct KcGemvSeg {
 };
 
 int kc_device_sms();
+// The calling thread's stream (kernels_set_stream) and the fail() policy of the C-ABI (kc_set_fail_mode): records the
+// message, exits under KC_FAIL_EXIT, returns false under KC_FAIL_RETURN.
+cudaStream_t kc_stream();
+bool kc_fail(const char *format, ...);
 // Programmatic dependent launch of the kernels that support it (kernels_set_pdl; on by default).
 bool kc_pdl_enabled();
 

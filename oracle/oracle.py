@@ -280,3 +280,37 @@ def seeded_q8_matrix(rows, cols, gs, seed, std=0.02):
 
 def env_threads():
     return int(os.environ.get("LLAMA_THREADS", os.cpu_count() or 1))
+
+
+class RefAttentionWork(ctypes.Structure):
+    """The reference's AttentionWork (include/kernels.h:127-132)."""
+    _fields_ = [("partial", ctypes.c_void_p), ("max_chunks", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("workers", ctypes.c_int), ("external", ctypes.c_int),
+                ("capacity", ctypes.c_size_t)]
+
+
+def ref_attention(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, seq_len, position, isa=KERNELS_AVX512):
+    """The reference's decode attention on the head-major cache [n_kv][seq][hd] (k_attention_layout with
+    pos_stride = head_dim, head_base = seq_len * head_dim, what k_attention_kv runs by default, src/attention.c:1434-1442),
+    serial (no team)."""
+    L = ref()
+    L.k_attention_init.argtypes = [ctypes.POINTER(RefAttentionWork), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_int]
+    L.k_attention_free.argtypes = [ctypes.POINTER(RefAttentionWork)]
+    L.k_attention_layout.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.POINTER(RefAttentionWork)] + \
+        [ctypes.c_int] * 5 + [ctypes.c_size_t, ctypes.c_size_t]
+    if not ref_select(isa):
+        raise RuntimeError("instruction set unavailable")
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(key_cache, np.float32)
+    vc = np.ascontiguousarray(value_cache, np.float32)
+    out = np.zeros(n_heads * head_dim, np.float32)
+    att = np.zeros(n_heads * seq_len, np.float32)
+    work = RefAttentionWork()
+    L.k_attention_init(ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len)
+    L.k_attention_layout(_p(out, _f32p), _p(q, _f32p), _p(kc, _f32p), _p(vc, _f32p), _p(att, _f32p),
+                         ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len, position, head_dim,
+                         seq_len * head_dim)
+    L.k_attention_free(ctypes.byref(work))
+    ref_select(KERNELS_SCALAR)
+    return out

@@ -22,6 +22,12 @@ def load_package():
     return mod
 
 
+def load_engine():
+    """The engine mirror, llama3.x.c_b200/engine.py, as llama3x_b200.engine."""
+    load_package()
+    return importlib.import_module("llama3x_b200.engine")
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
 

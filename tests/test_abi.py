@@ -23,10 +23,14 @@ def test_headers_declare_functions():
     assert {"k_quantize", "k_matmul_q8", "k_gemm_q8", "kc_status"} <= names
 
 
+def library_for(header):
+    mod = load_package()
+    return mod.LIB_PATH.parent / ("libllama3x_engine.so" if header.name == "engine_cuda.h" else "libllama3x_cuda.so")
+
+
 @pytest.mark.parametrize("header", HEADERS, ids=lambda p: p.name)
 def test_library_exports_every_declared_symbol(header):
-    mod = load_package()
-    lib = ctypes.CDLL(str(mod.LIB_PATH))
+    lib = ctypes.CDLL(str(library_for(header)))
     missing = [n for n in sorted(declared(header)) if not hasattr(lib, n)]
     assert not missing, f"{header.name}: not exported: {missing}"
 
@@ -35,6 +39,40 @@ def test_python_mirror_binds_the_kernel_header():
     mod = load_package()
     mod.load()
     assert set(mod.exported_symbols()) == declared(ROOT / "include" / "kernels_cuda.h")
+
+
+def test_python_mirror_binds_the_engine_and_device_headers():
+    from conftest import load_engine
+    eng = load_engine()
+    eng.load_library()
+    assert set(eng.ENGINE_SIGNATURES) == declared(ROOT / "include" / "engine_cuda.h")
+    assert set(eng.DEVICE_SIGNATURES) == declared(ROOT / "include" / "device_cuda.h")
+    lib = ctypes.CDLL(str(eng.ENGINE_LIB_PATH))
+    assert ctypes.c_int.in_dll(lib, "engine_q8").value == 1
+
+
+def test_engine_precision_and_layouts():
+    from conftest import load_engine
+    eng = load_engine()
+    lib = eng.load_library()
+    assert lib.engine_precision() == b"int8"
+    # Config and Model keep the reference's x86-64 layout (include/runtime.h:9-17, 86-97): format at byte 28, name at
+    # 88, Config 216 bytes, Model.implementation at 216, Model 272 bytes.
+    assert eng.Config.format.offset == 28 and eng.Config.name.offset == 88 and ctypes.sizeof(eng.Config) == 216
+    assert eng.Model.implementation.offset == 216 and ctypes.sizeof(eng.Model) == 272
+
+
+def test_c_header_layout_matches(tmp_path):
+    """The C header's structs have the same layout as the Python mirror (compiled here with gcc)."""
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "engine_cuda.h"\n'
+                   'int main(void) { printf("%zu %zu %zu %zu\\n", sizeof(Config), offsetof(Config, name), '
+                   'offsetof(Model, implementation), sizeof(Model)); return 0; }\n')
+    import subprocess
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    assert subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split() == \
+        ["216", "88", "216", "272"]
 
 
 def test_name_is_null_before_init():
