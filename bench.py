@@ -1,18 +1,22 @@
 #!/usr/bin/env python
-"""Benchmark of the Q8_0 W8A8 hot path on B200 (one JSON line on rank 0).
+"""Benchmark of the Q8_0 W8A8 path on B200: one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemv|gemm]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N   (N = 2, 4, 8)
 
-Workloads (seeded synthetic data, weights quantized with the reference's Q8_0 rule):
-  gemv   config 0: one step = the fused activation quantize + the decode GEMV y = W x, W 8192 x 2048 (gs 64).
-         Inputs rotate through enough weight copies to exceed L2 (126 MB) three times over, so every step streams W
-         from HBM.
-  gemm   config 1: one step = quantize X [T x 4096] + the prefill GEMM against W1 [14336 x 4096], T = 2048.
+Workloads (seeded synthetic data, random-init weights of the named architecture, Q8_0 gs 64):
+  8b    config 3 (default): Llama-3.1-8B architecture (dim 4096, hidden 14336, 32 layers, 32/8 heads, vocab 128256,
+        context 8192, untied classifier). One step = one request through engine_generate: a 2048-token uniform-random
+        prompt batch-prefilled, then 256 tokens greedy-decoded. Tensor parallel over the N GPUs (one request, one
+        token stream: strong scaling). value = decode tok/s; prefill tok/s rides along.
+  1b    config 2: Llama-3.2-1B architecture (tied classifier), 128-token prompt, 256 tokens.
+  gemv  config 0 kernel alone: quantize + GEMV 8192 x 2048 (for profiling; not the headline).
 
---impl reference times the reference's own CPU implementation (oracle/_ref, compiled from its sources) of the same
-step on all host cores, through its own API (k_quantize + k_matmul_q8 / k_gemm_q8 on a worker team of every core).
-Multi-GPU (torchrun): every rank runs an independent replica of the step (the kernel-level workloads do not shard);
-value is the sum over ranks, timed as the max over ranks.
+The weights (8.5 GB at 8B) exceed L2 many times over, so every decode step streams them from HBM.
+
+--impl reference times the reference's own CPU engine (oracle/_ref/libllama_ref_engine.so, built from its sources:
+engine_forward_batch + engine_forward) on all host cores, on the same architecture written as a seeded checkpoint,
+each step a bounded sample (a 128-token prefill and 8 decode tokens). Under torchrun only rank 0 runs it.
 """
 import argparse
 import ctypes
@@ -30,6 +34,15 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Q8_0 8B decode tok/s & prefill tok/s at 1/2/4/8 B200; GEMV HBM GB/s %"
 L2_BYTES = 126 * 1024 * 1024
 
+ARCH = {
+    "8b": dict(dim=4096, hidden_dim=14336, n_layers=32, n_heads=32, n_kv_heads=8, vocab_size=128256, seq_len=8192,
+               shared=False),
+    "1b": dict(dim=2048, hidden_dim=8192, n_layers=16, n_heads=32, n_kv_heads=8, vocab_size=128256, seq_len=2048,
+               shared=True),
+}
+REQUEST = {"8b": (2048, 256), "1b": (128, 256)}  # prompt tokens, generated tokens
+REF_SAMPLE = (128, 8)  # the reference's bounded per-step sample: prompt tokens, decode tokens
+
 
 def load_package():
     import importlib.util
@@ -44,25 +57,30 @@ def load_package():
     return mod
 
 
+def load_engine():
+    import importlib
+    load_package()
+    return importlib.import_module("llama3x_b200.engine")
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
 
 
 class Clocks:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
 
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.path = Path("/tmp") / f"llama3x_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
@@ -97,20 +115,21 @@ class Clocks:
             for n, v in zip(names, f[3:7]):
                 if v.lower() == "active":
                     reasons.add(n)
+        self.path.unlink(missing_ok=True)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
 
 
-def dist_setup(args):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
+        import datetime
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -131,147 +150,202 @@ def max_over_ranks(world, v):
     return float(t.item())
 
 
-# ---- workloads --------------------------------------------------------------------------------------------------
+def prompt_tokens(n, vocab, seed=3):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
 
-def gemv_workload(kc, torch, d=8192, n=2048, gs=64):
+
+# ---- the dominant kernel: the decode GEMV, timed alone ------------------------------------------------------------
+
+def gemv_roofline(kc, torch, rows, cols, gs=64, launches=60, swiglu=True):
+    """The SwiGLU decode GEMV (W1 and W3, `rows` x `cols` each, the largest per-layer weight stream) on enough rotating
+    weight copies to exceed L2 three times, each launch bracketed by CUDA events inside one captured graph.
+    Returns (algorithmic bytes per launch, mean launch microseconds)."""
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
-    w = torch.randn((d, n), generator=g, device="cuda") * 0.02
-    wq, ws = kc.quantize(w, gs)
-    del w
-    wbytes = wq.numel() + ws.numel() * 4
+    mats = []
+    for _ in range(2 if swiglu else 1):
+        w = torch.randn((rows, cols), generator=g, device="cuda") * 0.02
+        mats.append(kc.quantize(w, gs))
+        del w
+    wbytes = sum(q.numel() + s.numel() * 4 for q, s in mats)
     copies = max(2, -(-3 * L2_BYTES // wbytes))
-    W = [(wq.clone(), ws.clone()) for _ in range(copies)]
-    g.manual_seed(1)
-    x = torch.randn(n, generator=g, device="cuda")
-    xq = torch.empty(n, dtype=torch.int8, device="cuda")
-    xs = torch.empty(n // gs, device="cuda")
-    y = torch.empty(d, device="cuda")
-    alg_bytes = d * n + d * (n // gs) * 4 + n + (n // gs) * 4 + d * 4
+    W = [[(q.clone(), s.clone()) for q, s in mats] for _ in range(copies)]
+    x = torch.randn(cols, generator=g, device="cuda")
+    xq, xs = kc.quantize(x, gs)
+    y = torch.empty(rows, device="cuda")
+    alg = wbytes + cols + (cols // gs) * 4 + rows * 4
 
-    def step(i, ev=None):
-        kc.k_quantize(xq, xs, x, n, gs)
-        a, b = W[i % copies]
-        if ev:
-            ev[0].record()
-        kc.k_matmul_q8(y, xq, xs, a, b, n, d, gs)
-        if ev:
-            ev[1].record()
+    def launch(i):
+        m = W[i % copies]
+        if swiglu:
+            kc.gemv(xq, xs, m[0][0], m[0][1], gs, kind=kc.K_SWIGLU, out=y, w3=m[1])
+        else:
+            kc.gemv(xq, xs, m[0][0], m[0][1], gs, out=y)
 
-    # end-to-end: pinned host x in, pinned host y out, through the public API
-    xh = torch.randn(n, generator=torch.Generator().manual_seed(1)).pin_memory()
-    yh = torch.empty(d).pin_memory()
-
-    def step_e2e(i):
-        x.copy_(xh, non_blocking=True)
-        step(i)
-        yh.copy_(y, non_blocking=True)
-
-    return dict(step=step, step_e2e=step_e2e, launches=2, alg_bytes=alg_bytes, unit="GB/s",
-                per_step_units=alg_bytes / 1e9, workload=f"config0 GEMV {d}x{n} gs{gs} (+ fused-quantize launch)",
-                kernel="gemv_q8_kernel", h2d=n * 4, d2h=d * 4, copies=copies, dtype="int8 x int8 -> int32 -> f32",
-                shape=dict(d=d, n=n, gs=gs))
-
-
-def cpu_reference_gemv(seconds=5.0, d=8192, n=2048, gs=64):
-    """The reference's k_matmul_q8 (LLAMA_KERNELS=auto: AVX-512 VNNI where the CPU has it) on a team of every core."""
-    from oracle import oracle as O
-    L = O.ref()
-    L.kernels_backend_init()
-    isa = O.KERNELS_AVX512 if O.ref_select(O.KERNELS_AVX512) else O.KERNELS_SCALAR
-    O.ref_select(isa)
-    wq, ws = O.seeded_q8_matrix(d, n, gs, 0)
-    copies = max(2, -(-512 * 2**20 // (wq.nbytes + ws.nbytes)))  # rotate past the host caches (gemm_bench --cold-mib)
-    W = [(wq.copy(), ws.copy()) for _ in range(copies)]
-    xq, xs = O.quantize(np.random.default_rng(1).standard_normal(n).astype(np.float32), gs)
-    out = np.empty(d, np.float32)
-    inp = O.K8Input(O._p(xq, O._i8p), O._p(xs, O._f32p), None)
-    ws_ = [O.K8Weight(O._p(a, O._i8p), O._p(b, O._f32p)) for a, b in W]
-    for i in range(3):
-        L.k_matmul_q8(O._p(out, O._f32p), ctypes.byref(inp), ws_[i % copies], n, d, gs)
-    calls, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        L.k_matmul_q8(O._p(out, O._f32p), ctypes.byref(inp), ws_[calls % copies], n, d, gs)
-        calls += 1
-    dt = time.perf_counter() - t0
-    gb = calls * (d * n + d * (n // gs) * 4 + n + (n // gs) * 4 + d * 4) / 1e9
-    return {"value": gb / dt, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
-            "sample": f"{calls} calls of k_matmul_q8 {d}x{n} ({'avx512' if isa else 'scalar'}) over {dt:.1f} s, "
-                      f"{copies} rotating weight copies"}
-
-
-def run_ours(args):
-    import torch
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    kc = load_package()
-    kc.init()
-    wl = gemv_workload(kc, torch)
-    hbm, bf16, peak_kind = peaks()
-    stream = torch.cuda.current_stream()
-    K = args.steps
-    for i in range(args.warmup):
-        wl["step"](i)
+    for i in range(5):
+        launch(i)
     kc.status()
-    # The K steps are captured once into a CUDA graph and replayed: the timed region is then GPU-bound (the kernels'
-    # own time), not bound by Python's per-call launch overhead. External event nodes bracket every hot-path kernel.
-    K = args.steps
     evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-           for _ in range(K)]
+           for _ in range(launches)]
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        for i in range(K):
-            wl["step"](i, evs[i])
+        for i in range(launches):
+            evs[i][0].record()
+            launch(i)
+            evs[i][1].record()
+    graph.replay()
+    torch.cuda.synchronize()
     graph.replay()
     torch.cuda.synchronize()
     kc.status()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with Clocks(local) as clocks:
-        start.record(stream)
-        graph.replay()
-        stop.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    kc.status()
-    ms = max_over_ranks(world, start.elapsed_time(stop))
-    kernel_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
-    value = world * K * wl["per_step_units"] / (ms / 1e3)
+    us = float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
     del graph
-    # end-to-end through the public API with host buffers (plain calls, host launch overhead included)
-    for i in range(args.warmup):
-        wl["step_e2e"](i)
-    torch.cuda.synchronize()
+    return alg, us
+
+
+# ---- the reference's CPU engine -----------------------------------------------------------------------------------
+
+def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
+    """The reference's Q8 engine (engine_forward_batch for the prompt, engine_forward per decode token, greedy) on all
+    host cores. Returns the dict of a cpu_baseline entry plus prefill tok/s."""
+    from oracle import model_file
+    from oracle import oracle as O
+    lib_path = O.HERE / "_ref" / "libllama_ref_engine.so"
+    if not lib_path.exists():
+        return {"unavailable": "oracle/_ref/libllama_ref_engine.so was not built (make -C oracle where the reference "
+                               "sources exist)"}
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("LLAMA_THREADS", str(cores))
+    a = ARCH[arch]
+    shm = Path("/dev/shm")
+    base = shm if shm.exists() and os.statvfs(shm).f_bavail * os.statvfs(shm).f_frsize > 24 * 2**30 else Path("/tmp")
+    t0 = time.perf_counter()
+    path = model_file.write_random_checkpoint(base / f"llama3x_bench_{arch}.bin", **a, seed=1)
+    gen_s = time.perf_counter() - t0
+    eng = load_engine()  # only for the layout-compatible Model struct (include/runtime.h); no GPU code is called
+    L = ctypes.CDLL(str(lib_path))
+    MP = ctypes.POINTER(eng.Model)
+    L.engine_load_context.argtypes = [MP, ctypes.c_char_p, ctypes.c_int]
+    L.engine_forward.argtypes = [MP, ctypes.c_int, ctypes.c_int]
+    L.engine_forward.restype = ctypes.POINTER(ctypes.c_float)
+    L.engine_forward_batch.argtypes = [MP, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.engine_forward_batch.restype = ctypes.POINTER(ctypes.c_float)
+    L.engine_free.argtypes = [MP]
+    model = eng.Model()
+    t0 = time.perf_counter()
+    L.engine_load_context(ctypes.byref(model), os.fsencode(str(path)), prompt_len + decode_len)
+    load_s = time.perf_counter() - t0
+    V = a["vocab_size"]
+    prompt = prompt_tokens(prompt_len, V)
+    arr = (ctypes.c_int * prompt_len)(*prompt.tolist())
+    pre, dec = [], []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        logits = L.engine_forward_batch(ctypes.byref(model), arr, prompt_len, 0, eng.LOGITS_LAST)
+        t1 = time.perf_counter()
+        tok = int(np.argmax(np.ctypeslib.as_array(logits, (V,))))
+        for j in range(decode_len):
+            logits = L.engine_forward(ctypes.byref(model), tok, prompt_len + j)
+            tok = int(np.argmax(np.ctypeslib.as_array(logits, (V,))))
+        t2 = time.perf_counter()
+        if i >= warmup:
+            pre.append(t1 - t0)
+            dec.append(t2 - t1)
+    L.engine_free(ctypes.byref(model))
+    decode = decode_len * len(dec) / sum(dec)
+    prefill = prompt_len * len(pre) / sum(pre)
+    return {"value": round(decode, 3), "unit": "tok/s", "cores": int(os.environ["LLAMA_THREADS"]), "kind": "reference",
+            "prefill_tok_s": round(prefill, 2),
+            "sample": f"reference engine (engine_forward_batch + engine_forward, LLAMA_KERNELS=auto) on the {arch} "
+                      f"architecture: {steps} x ({prompt_len}-token prefill + {decode_len} greedy decode tokens); "
+                      f"checkpoint written in {gen_s:.0f} s, loaded in {load_s:.0f} s"}
+
+
+# ---- our engine ---------------------------------------------------------------------------------------------------
+
+def run_engine(args):
+    import torch
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    kc = load_package()
+    eng = load_engine()
+    a = ARCH[args.workload]
+    P, D = REQUEST[args.workload]
+    nccl_id = eng.share_comm_id(rank, world) if world > 1 else None
+    t0 = time.perf_counter()
+    m = eng.Engine.random(**a, seed=1, context=a["seq_len"], tp=(rank, world, local, nccl_id) if world > 1 else None)
+    init_s = time.perf_counter() - t0
+    prompt = prompt_tokens(P, a["vocab_size"])
+    for _ in range(args.warmup):
+        m.generate(prompt, D)
     barrier(world)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(K):
-        wl["step_e2e"](i)
-    t1.record(stream)
     torch.cuda.synchronize()
+    m.stats_reset()
+    with Clocks(local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tokens = m.generate(prompt, D)
+        wall = time.perf_counter() - t0
+    st = m.stats()
     barrier(world)
-    kc.status()
-    e2e_ms = max_over_ranks(world, t0.elapsed_time(t1))
-    e2e = world * K * wl["per_step_units"] / (e2e_ms / 1e3)
-    achieved = wl["alg_bytes"] / (kernel_ms / 1e3) / 1e9
+    prefill_ms = max_over_ranks(world, st["prefill_ms"])
+    decode_ms = max_over_ranks(world, st["decode_ms"])
+    wall = max_over_ranks(world, wall)
+    decode = st["decode_tokens"] / (decode_ms / 1e3)
+    prefill = st["prefill_tokens"] / (prefill_ms / 1e3)
+
+    # End to end through the reference-facing API with host buffers: engine_forward per token (the token and position
+    # go host -> device, the vocabulary's logits come back to the host), host argmax, as probe-int8 generate does.
+    E = 32
+    logits = m.forward_batch(prompt, 0, eng.LOGITS_LAST)
+    tok = int(np.argmax(logits))
+    for j in range(3):
+        m.forward(tok, P + j)
+    barrier(world)
+    t0 = time.perf_counter()
+    for j in range(E):
+        tok = int(np.argmax(m.forward(tok, P + j)))
+    e2e_s = max_over_ranks(world, time.perf_counter() - t0)
+    m.close()
+
+    # The dominant kernel alone: the SwiGLU decode GEMV of this rank's W1/W3 shard.
+    hbm, peak_kind = peaks()
+    rows = a["hidden_dim"] // world
+    alg, us = gemv_roofline(kc, torch, rows, a["dim"])
+    achieved = alg / (us / 1e6) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"gemv_swiglu_{rows}x{a['dim']}")
+    weights = sum(v for v in weight_bytes(a, world).values())
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": wl["unit"], "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": wl["workload"], "l2": f"inputs rotate over {wl['copies']} weight copies (> 3x L2)",
-                   "parallelism": f"replicas x{world}", **wl["shape"]},
-        "e2e": {"value": round(e2e, 2), "unit": wl["unit"], "h2d_bytes_per_step": wl["h2d"],
-                "d2h_bytes_per_step": wl["d2h"]},
+        "metric": METRIC, "value": round(decode, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round((prefill_ms + decode_ms) / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)",
+        "data": "synthetic: seeded random-init Q8_0 weights N(0,0.02), uniform-random prompt ids",
+        "config": {"workload": f"config {3 if args.workload == '8b' else 2}: {args.workload.upper()} architecture, "
+                               f"{P}-token prefill + {D} greedy tokens per step",
+                   "model": f"llama-{args.workload}-arch", **{k: a[k] for k in ("dim", "hidden_dim", "n_layers",
+                                                                                "n_heads", "n_kv_heads", "vocab_size")},
+                   "context": a["seq_len"], "global_batch": 1, "seq_len": P + D,
+                   "parallelism": f"tp{world}", "l2": f"weights {weights / 1e9:.2f} GB per GPU >> L2"},
+        "prefill_tok_s": round(prefill, 1), "decode_tok_s": round(decode, 2),
+        "decode_ms_per_token": round(decode_ms / max(1, st["decode_tokens"]), 4),
+        "decode_weight_gbs": round(weights / (decode_ms / max(1, st["decode_tokens"]) / 1e3) / 1e9, 1),
+        "wall_s": round(wall, 3), "init_s": round(init_s, 2), "tokens_last_step": len(tokens),
+        "e2e": {"value": round(E / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4 * a["vocab_size"],
+                "path": "engine_forward per token (host token in, host logits out, host argmax)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": wl["kernel"],
-                     "kernel_us": round(kernel_ms * 1e3, 3), "peak_source": f"{peak_kind} hbm_gbs"},
-        "gpu_launches": wl["launches"] * K,
+                     "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "kernel": f"gemv_q8 SwiGLU {rows}x{a['dim']} x2 (decode W1/W3)", "kernel_us": round(us, 3),
+                     "alg_bytes_per_launch": alg, "peak_source": f"{peak_kind} hbm_gbs"},
+        "gpu_launches": int(st["kernel_launches"]),
         "clocks": clocks.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_reference_gemv(seconds=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = reference_engine_sample(args.workload, steps=1, warmup=1, prompt_len=REF_SAMPLE[0],
+                                                       decode_len=REF_SAMPLE[1])
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -279,45 +353,73 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def weight_bytes(a, world, gs=64):
+    d, h, L, V = a["dim"], a["hidden_dim"], a["n_layers"], a["vocab_size"]
+    kv = d // a["n_heads"] * a["n_kv_heads"]
+
+    def q8(n):
+        return n + n // gs * 4
+
+    layer = (2 * q8(d * d) + 2 * q8(d * kv) + 3 * q8(d * h)) // world
+    return {"layers": L * layer, "classifier": q8(V * d) // world}
+
+
+# ---- the reference arm --------------------------------------------------------------------------------------------
+
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    from oracle import oracle as O
-    if not O.ref_available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libllama_ref.so was not built "
-                                                              "(make -C oracle where the reference sources exist)"}))
+    wl = args.workload if args.workload in ARCH else "8b"
+    r = reference_engine_sample(wl, steps=args.steps, warmup=args.warmup, prompt_len=REF_SAMPLE[0],
+                                decode_len=REF_SAMPLE[1])
+    if "unavailable" in r:
+        print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}), flush=True)
         return
-    res = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_reference_gemv(seconds=max(0.5, args.cpu_seconds / max(1, args.steps)))
-        if i >= args.warmup:
-            res.append(r)
-    v = float(np.mean([r["value"] for r in res]))
-    line = {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": "GB/s", "n_gpus": 0,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
-            "data": "synthetic", "config": {"workload": "config0 GEMV 8192x2048 gs64"},
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": res[-1]["cores"], "kind": "reference",
-                             "sample": res[-1]["sample"]},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    a = ARCH[wl]
+    line = {"metric": METRIC, "impl": "reference", "value": r["value"], "unit": "tok/s", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"config {3 if wl == '8b' else 2}: {wl.upper()} architecture on the host cores, "
+                                   f"bounded sample per step", "model": f"llama-{wl}-arch",
+                       **{k: a[k] for k in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size")},
+                       "global_batch": 1, "parallelism": "cpu"},
+            "prefill_tok_s": r["prefill_tok_s"], "decode_tok_s": r["value"],
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ---- config 0 kernel alone (profiling) ----------------------------------------------------------------------------
+
+def run_gemv(args):
+    import torch
+    kc = load_package()
+    kc.init()
+    hbm, peak_kind = peaks()
+    alg, us = gemv_roofline(kc, torch, 8192, 2048, launches=args.steps, swiglu=False)
+    gbs = alg / (us / 1e6) / 1e9
+    print(json.dumps({"metric": "config 0 GEMV HBM GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "kernel_us": round(us, 3),
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                   "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs"}}), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=5.0)
+    ap.add_argument("--workload", choices=["8b", "1b", "gemv"], default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "gemv":
+        run_gemv(args)
     else:
-        run_ours(args)
+        run_engine(args)
 
 
 if __name__ == "__main__":

@@ -75,6 +75,16 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
 int engine_save(Model *model, const char *path);
 /* The engine's CUDA stream (cudaStream_t), for timing with events on it. */
 void *engine_stream(Model *model);
+/* What engine_generate did since the model was set up or engine_stats_reset: device time of its prefill (the prompt
+ * through the last chunk's classifier and the first argmax) and of its decode steps (CUDA events on the engine's
+ * stream), the positions each processed, and the kernels of this library it launched (CUDA-graph replays included). */
+typedef struct {
+  double prefill_ms, decode_ms;
+  long long prefill_tokens, decode_tokens;
+  long long kernel_launches;
+} EngineStats;
+void engine_stats(Model *model, EngineStats *out);
+void engine_stats_reset(Model *model);
 
 #ifdef __cplusplus
 }

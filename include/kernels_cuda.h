@@ -83,6 +83,9 @@ int kc_status(void);
 /* Applies the fail() policy to a message from a caller of this library (the GPU engine): exit under KC_FAIL_EXIT,
  * else record it for kc_last_error. */
 void kc_fail_message(const char *message);
+/* Kernels this library has launched in this process since it was loaded, counted at each successful launch call (no
+ * counterpart in the reference). A CUDA-graph replay launches its captured kernels without calling in here. */
+unsigned long long kc_launch_count(void);
 
 /* ---- quantizer (include/kernels.h:110, include/gemm.h:130) ------------------------------------------------------- */
 void k_quantize(int8_t *q, float *s, const float *x, int n, int gs);
@@ -117,14 +120,13 @@ void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t l
 
 /* ---- K/V cache and attention (include/kernels.h:126-179) --------------------------------------------------------- */
 /* The cache is the reference's head-major layout (LLAMA_KV_LAYOUT=head, its default): one layer's K or V cache is
- * [n_kv_heads][seq_len][head_dim] fp32. AttentionWork holds the split-K partials and merge counters in device memory
- * (the reference keeps the partials in host memory and has no counters); `memory` passed to k_attention_init_rows is
- * device memory of k_attention_bytes_rows bytes, or NULL to let the call allocate it (k_attention_free releases only
- * what it allocated). Attention agrees with the reference's within fp32 rounding (split-K merge order), and a row of a
+ * [n_kv_heads][seq_len][head_dim] fp32. AttentionWork holds the split-K partials in device memory (the reference keeps
+ * them in host memory); head_dim 32, 64 or 128, at most 8 query heads per KV head. `memory` passed to
+ * k_attention_init_rows is device memory of k_attention_bytes_rows bytes, or NULL to let the call allocate it
+ * (k_attention_free releases only what it allocated). Attention agrees with the reference's within fp32 rounding (split-K merge order), and a row of a
  * batch is bitwise the same row computed alone. `att` is the reference's host scratch and is ignored. */
 typedef struct {
   float *partial;
-  int *counters;
   int max_chunks, n_heads, n_kv_heads, head_dim, seq_len, rows;
   int external;
   size_t capacity;
@@ -157,11 +159,12 @@ void k_attention_q8_rows(float *out, int8_t *oq, float *os, const float *q, cons
 /* x[r][i] = q[tok][i] * s[(tok * dim + i) / gs] for tok = tokens[r] (device), src/tp.c:395-396. */
 void k_embed_q8_rows(float *x, const int *tokens, K8Weight embed, int rows, int dim, int gs, int vocab);
 void k_add(float *x, const float *y, size_t n); /* x += y */
-/* Greedy sampling on the device: *key = a 64-bit key whose unsigned maximum over all shards (an NCCL max all-reduce)
- * is the first maximum (sample_argmax, src/sampler.c:9-23); logits[i] has vocabulary index offset + i. */
+/* Greedy sampling on the device: folds into *key (which must hold 0 or an earlier key) a 64-bit key whose unsigned
+ * maximum over all shards (an NCCL max all-reduce) is the first maximum (sample_argmax, src/sampler.c:9-23);
+ * logits[i] has vocabulary index offset + i. */
 void k_argmax_key(unsigned long long *key, const float *logits, int n, int offset);
-/* token = index in *key; out[*step] = token (out may be NULL); *token = token; ++*step; ++*position. */
-void k_greedy_advance(int *out, int *step, int *token, int *position, const unsigned long long *key);
+/* token = index in *key; out[*step] = token (out may be NULL); *token = token; ++*step; ++*position; *key = 0. */
+void k_greedy_advance(int *out, int *step, int *token, int *position, unsigned long long *key);
 /* Seeded N(0, std) benchmark weights quantized like k_quantize: rows [row0, row0 + rows) x columns [col0, col0 + cols)
  * of a [*][full_cols] tensor numbered `tensor`, into q [rows][cols] and s [rows][cols / gs]; every element is a
  * function of (seed, tensor, row, column) only, so a shard equals the same slice of the whole tensor. gs 32..256. */

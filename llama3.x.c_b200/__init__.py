@@ -41,8 +41,8 @@ class GemmQ8Segment(ctypes.Structure):
 
 
 class AttentionWork(ctypes.Structure):
-    """include/kernels_cuda.h: split-K partials and merge counters in device memory."""
-    _fields_ = [("partial", ctypes.c_void_p), ("counters", ctypes.c_void_p), ("max_chunks", ctypes.c_int),
+    """include/kernels_cuda.h: split-K partials in device memory."""
+    _fields_ = [("partial", ctypes.c_void_p), ("max_chunks", ctypes.c_int),
                 ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
                 ("seq_len", ctypes.c_int), ("rows", ctypes.c_int), ("external", ctypes.c_int),
                 ("capacity", ctypes.c_size_t)]
@@ -85,6 +85,7 @@ _SIGNATURES = {
     "k_rope_apply_rows": (None, [_f32p, _c.c_size_t, _f32p, _c.c_size_t, _f32p, _c.c_size_t, _c.c_int, _c.c_int,
                                  _c.c_int, _c.c_int]),
     "kc_fail_message": (None, [_c.c_char_p]),
+    "kc_launch_count": (_c.c_ulonglong, []),
     "k_kv_strides": (None, [_c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
     "k_kv_store": (None, [_f32p, _f32p, _c.c_size_t, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
     "k_attention_bytes_rows": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),

@@ -6,6 +6,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/kernels_cuda.h"
 #include "common.cuh"
 #include "kernels_cuda_internal.h"
@@ -34,9 +36,15 @@ bool kc_fail(const char *format, ...) {
   return false;
 }
 
+static std::atomic<unsigned long long> launch_counter{0};
+
+void kc_count_launch() { launch_counter.fetch_add(1, std::memory_order_relaxed); }
+
 static bool launched(int rc, const char *what) {
-  if (rc == 0)
+  if (rc == 0) {
+    kc_count_launch();
     return true;
+  }
   if (rc == -1)
     return kc_fail("%s: shape not supported by the sm_100a kernels", what);
   return kc_fail("%s: CUDA launch failed: %s", what, cudaGetErrorString(cudaGetLastError()));
@@ -92,6 +100,8 @@ const char *kc_last_error(void) { return tl_error; }
 void kc_clear_error(void) { tl_error[0] = 0; }
 
 void kc_fail_message(const char *message) { kc_fail("%s", message); }
+
+unsigned long long kc_launch_count(void) { return launch_counter.load(std::memory_order_relaxed); }
 
 int kc_status(void) {
   cudaError_t e = cudaStreamSynchronize(tl_stream);

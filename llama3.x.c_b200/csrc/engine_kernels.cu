@@ -13,6 +13,7 @@
 //  - greedy sampling: the first maximum wins (sample_argmax, src/sampler.c:9-23)
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <string.h>
 
 #include "../../include/kernels_cuda.h"
@@ -23,6 +24,8 @@ namespace {
 
 __global__ void embed_kernel(float *x, const int *tokens, const int8_t *q, const float *s, int rows, int dim, int gs,
                              int vocab) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)rows * dim)
     return;
@@ -41,6 +44,8 @@ __global__ void embed_kernel(float *x, const int *tokens, const int8_t *q, const
 __global__ void rope_store_kernel(float *q, long long q_ld, const float *k, const float *v, long long kv_ld, float *kc,
                                   float *vc, const float *table, const int *pos_dev, int pos0, int rows, int n_heads,
                                   int n_kv, int hd, int seq) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int half = hd / 2;
   const int per_row = (n_heads + n_kv) * half + n_kv * hd;  // rotations of q, k, then copies of v
   const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -76,6 +81,8 @@ __global__ void rope_store_kernel(float *q, long long q_ld, const float *k, cons
 // Plain k_kv_store: count rows of n_kv * hd floats (stride src_ld) to positions pos0.. of the head-major cache.
 __global__ void kv_store_kernel(float *cache, const float *src, long long src_ld, int pos0, int count, int n_kv, int hd,
                                 int seq) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = n_kv * hd;
   if (id >= (long long)count * per_row)
@@ -86,162 +93,331 @@ __global__ void kv_store_kernel(float *cache, const float *src, long long src_ld
 }
 
 constexpr int kAttnThreads = 256;
-constexpr int kAttnChunk = 128;  // positions per split
-constexpr int kMaxGqa = 8;       // query heads per KV head handled by one CTA
-constexpr int kMaxHd = 256;
+constexpr int kAttnChunk = 64;     // positions per split: split c covers [64 c, 64 c + 64), whatever the row
+constexpr int kMaxGqa = 8;         // query heads per KV head
+constexpr int kMaxHd = 128;
+constexpr int kPrefillRows = 16;   // query rows per prefill CTA (they share its K/V chunk)
+constexpr int kDecodeStages = 1;   // K/V chunk buffers of a decode CTA: one, so two CTAs fit per SM
 
-// One CTA per (KV head g, split s, query row r): the kv_mul query heads of g against positions
-// [s * chunk, min(pos + 1, (s + 1) * chunk)). Writes (max, sum, weighted V) partials; the last CTA of (g, r) to finish
-// merges the splits and writes the output, quantized in gs-groups too when oq is set ((kv_mul * hd) % gs == 0).
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
-    float *out, long long out_ld, int8_t *oq, float *os, const float *q, long long q_ld, const float *kc,
-    const float *vc, const int *pos_dev, int pos0, int n_kv, int kv_mul, int hd, int seq, int max_splits, float *part,
-    int *counters, int gs) {
-  __shared__ float qs[kMaxGqa * kMaxHd];
-  __shared__ float sc[kMaxGqa][kAttnChunk];
-  __shared__ float red[kMaxGqa][2];
-  __shared__ int last;
-  const int g = blockIdx.x, s = blockIdx.y, r = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = kAttnThreads / 32;
-  const int pos = (pos_dev ? *pos_dev : pos0) + r;
-  const int npos = pos + 1;
-  const int nsplit = (npos + kAttnChunk - 1) / kAttnChunk;
-  const int t0 = s * kAttnChunk, t1 = min(npos, t0 + kAttnChunk);
-  const int nq = kv_mul;
+// Dynamic shared memory of the attention kernels: `stages` buffers of one chunk's K and V rows (filled by bulk copies),
+// the row's query heads, the chunk's scores, the position-group partial sums of P.V, per-head (max, sum) and one copy
+// barrier per stage.
+struct AttnSmem {
+  float *K[2], *V[2];  // stage buffers (both entries alias stage 0 when there is one stage)
+  float *qs, *sc, *pv, *red;
+  uint64_t *bar;
+};
+
+__host__ __device__ inline size_t attn_smem_bytes(int hd, int stages) {
+  return ((size_t)stages * 2 * kAttnChunk * hd + kMaxGqa * kMaxHd + kMaxGqa * kAttnChunk + kAttnThreads * kMaxGqa +
+          2 * kMaxGqa) * sizeof(float) + kDecodeStages * sizeof(uint64_t);
+}
+
+__device__ inline AttnSmem attn_smem(int hd, int stages) {
+  extern __shared__ __align__(16) float attn_dyn[];
+  AttnSmem m;
+  float *p = attn_dyn;
+  for (int i = 0; i < 2; i++) {
+    m.K[i] = p;
+    m.V[i] = p + kAttnChunk * hd;
+    if (i + 1 < stages)
+      p += 2 * kAttnChunk * hd;
+  }
+  p += 2 * kAttnChunk * hd;
+  m.qs = p;
+  m.sc = m.qs + kMaxGqa * kMaxHd;
+  m.pv = m.sc + kMaxGqa * kAttnChunk;
+  m.red = m.pv + kAttnThreads * kMaxGqa;
+  m.bar = reinterpret_cast<uint64_t *>(m.red + 2 * kMaxGqa);  // every size above is a multiple of 2 floats
+  return m;
+}
+
+// Thread 0 issues the bulk copies of rows [t0, t0 + n) of KV head g's K and V (contiguous in the head-major cache)
+// into stage `st`, completing on that stage's barrier.
+__device__ inline void issue_chunk(const AttnSmem &m, int st, const float *kc, const float *vc, int g, int seq, int hd,
+                                   int t0, int n) {
+  const unsigned bytes = (unsigned)n * hd * sizeof(float);
+  mbar_arrive_expect_tx(m.bar + st, 2 * bytes);
+  bulk_g2s(st ? m.K[1] : m.K[0], kc + ((long long)g * seq + t0) * hd, bytes, m.bar + st);
+  bulk_g2s(st ? m.V[1] : m.V[0], vc + ((long long)g * seq + t0) * hd, bytes, m.bar + st);
+}
+
+// Bounded wait for a stage, with the same outcome in every thread of the CTA.
+__device__ inline bool wait_chunk(const AttnSmem &m, int st, unsigned parity) {
+  return __syncthreads_and(mbar_wait_bounded(m.bar + st, parity));
+}
+
+// One row's partial over the first n_t positions of the chunk in K/V: per query head h of the KV head,
+// pdst[h] = (max score, sum of exp(score - max), sum of exp(score - max) v). The arithmetic order depends only on
+// (n_t, nq, hd) and the position within the chunk; decode and prefill both come through here, so a row's result does
+// not depend on which kernel ran it.
+__device__ inline void chunk_partial(const AttnSmem &m, const float *K, const float *V, const float *qg, int n_t,
+                                     int nq, int hd, float *pdst) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float scale = sqrtf((float)hd);
-  const long long stride = hd + 2;
-  float *pbase = part + (((long long)r * n_kv + g) * max_splits) * nq * stride;
-  if (s < nsplit && pos < seq) {
-    for (int i = tid; i < nq * hd; i += kAttnThreads)
-      qs[i] = q[r * q_ld + (long long)g * nq * hd + i];
-    __syncthreads();
-    const float *kh = kc + (long long)g * seq * hd;
-    const float *vh = vc + (long long)g * seq * hd;
-    // Scores: warp per position, lanes across head_dim.
-    for (int t = t0 + warp; t < t1; t += nw) {
-      const float *kt = kh + (long long)t * hd;
-      float acc[kMaxGqa];
+  const int stride = hd + 2, hd4 = hd / 4;
+  for (int i = tid; i < nq * hd; i += kAttnThreads)
+    m.qs[i] = qg[i];
+  __syncthreads();
+  // Scores: a thread per (head, position); the float4 index is rotated by the position so the 32 lanes of a warp hit
+  // 32 different banks, and four partial sums give the FMA chain independent links.
+  for (int pair = tid; pair < nq * kAttnChunk; pair += kAttnThreads) {
+    const int h = pair / kAttnChunk, p = pair - h * kAttnChunk;
+    if (p < n_t) {
+      const float4 *k4 = reinterpret_cast<const float4 *>(K + p * hd);
+      const float4 *q4 = reinterpret_cast<const float4 *>(m.qs + h * hd);
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+      int j = p % hd4;
+#pragma unroll 4
+      for (int i = 0; i < hd4; i++) {
+        const float4 kv = k4[j], qv = q4[j];
+        a0 = fmaf(qv.x, kv.x, a0);
+        a1 = fmaf(qv.y, kv.y, a1);
+        a2 = fmaf(qv.z, kv.z, a2);
+        a3 = fmaf(qv.w, kv.w, a3);
+        j = j + 1 == hd4 ? 0 : j + 1;
+      }
+      m.sc[h * kAttnChunk + p] = ((a0 + a1) + (a2 + a3)) / scale;
+    }
+  }
+  __syncthreads();
+  // Chunk max and exp-sum per head (warp per head, two positions per lane).
+  for (int h = warp; h < nq; h += kAttnThreads / 32) {
+    float *sch = m.sc + h * kAttnChunk;
+    const float s0 = lane < n_t ? sch[lane] : -INFINITY, s1 = lane + 32 < n_t ? sch[lane + 32] : -INFINITY;
+    float mx = fmaxf(s0, s1);
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e0 = lane < n_t ? expf(s0 - mx) : 0.0f, e1 = lane + 32 < n_t ? expf(s1 - mx) : 0.0f;
+    if (lane < n_t)
+      sch[lane] = e0;
+    if (lane + 32 < n_t)
+      sch[lane + 32] = e1;
+    float l = e0 + e1;
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0)
+      m.red[2 * h] = mx, m.red[2 * h + 1] = l;
+  }
+  __syncthreads();
+  // Weighted values: a thread per (position group, dim) accumulates every head of its dim over its group's positions
+  // (nq independent chains); the groups' sums are added in group order.
+  const int groups = kAttnThreads / hd, grp = tid / hd, d = tid - grp * hd;
+  if (grp < groups) {
+    const int per = (n_t + groups - 1) / groups, t0 = grp * per, t1 = min(n_t, t0 + per);
+    float acc[kMaxGqa];
+#pragma unroll
+    for (int h = 0; h < kMaxGqa; h++)
+      acc[h] = 0.0f;
+    for (int t = t0; t < t1; t++) {
+      const float v = V[t * hd + d];
 #pragma unroll
       for (int h = 0; h < kMaxGqa; h++)
-        acc[h] = 0.0f;
-      for (int i = lane; i < hd; i += 32) {
-        const float kv = kt[i];
-#pragma unroll
-        for (int h = 0; h < kMaxGqa; h++)
-          if (h < nq)
-            acc[h] = fmaf(qs[h * hd + i], kv, acc[h]);
-      }
-#pragma unroll
-      for (int h = 0; h < kMaxGqa; h++) {
-        if (h >= nq)
-          break;
-        float d = acc[h];
-#pragma unroll
-        for (int o = 16; o; o >>= 1)
-          d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == 0)
-          sc[h][t - t0] = d / scale;
-      }
+        if (h < nq)
+          acc[h] = fmaf(m.sc[h * kAttnChunk + t], v, acc[h]);
     }
-    __syncthreads();
-    // Chunk max and exp-sum per query head (warp h).
-    if (warp < nq) {
-      float m = -INFINITY;
-      for (int t = lane; t < t1 - t0; t += 32)
-        m = fmaxf(m, sc[warp][t]);
 #pragma unroll
-      for (int o = 16; o; o >>= 1)
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float l = 0.0f;
-      for (int t = lane; t < t1 - t0; t += 32) {
-        const float e = expf(sc[warp][t] - m);
-        sc[warp][t] = e;
-        l += e;
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1)
-        l += __shfl_xor_sync(0xffffffffu, l, o);
-      if (lane == 0)
-        red[warp][0] = m, red[warp][1] = l;
-    }
-    __syncthreads();
-    // Weighted values: thread per (head, dim), coalesced along dim.
-    for (int i = tid; i < nq * hd; i += kAttnThreads) {
-      const int h = i / hd, d = i - h * hd;
-      float acc = 0.0f;
-      for (int t = t0; t < t1; t++)
-        acc = fmaf(sc[h][t - t0], vh[(long long)t * hd + d], acc);
-      pbase[((long long)s * nq + h) * stride + 2 + d] = acc;
-    }
-    if (tid < nq) {
-      pbase[((long long)s * nq + tid) * stride] = red[tid][0];
-      pbase[((long long)s * nq + tid) * stride + 1] = red[tid][1];
-    }
-  } else if (pos >= seq && s == 0 && tid == 0) {
-    kc_raise(KC_ERR_BAD_ARGS);
+    for (int h = 0; h < kMaxGqa; h++)
+      if (h < nq)
+        m.pv[(grp * kMaxGqa + h) * hd + d] = acc[h];
   }
-  // The last CTA of (g, r) merges; every CTA of the grid's y extent counts in, including those past nsplit.
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int done = atomicAdd(&counters[r * n_kv + g], 1);
-    last = done == (int)gridDim.y - 1;
-  }
-  __syncthreads();
-  if (!last)
-    return;
-  __threadfence();
-  if (tid == 0)
-    counters[r * n_kv + g] = 0;  // ready for the next launch
-  if (pos >= seq)
-    return;
   __syncthreads();
   for (int i = tid; i < nq * hd; i += kAttnThreads) {
-    const int h = i / hd, d = i - h * hd;
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; sp++)
-      M = fmaxf(M, __ldcg(pbase + ((long long)sp * nq + h) * stride));
-    float L = 0.0f, O = 0.0f;
-    for (int sp = 0; sp < nsplit; sp++) {
-      const float *pp = pbase + ((long long)sp * nq + h) * stride;
-      const float w = expf(__ldcg(pp) - M);
-      L = fmaf(__ldcg(pp + 1), w, L);
-      O = fmaf(__ldcg(pp + 2 + d), w, O);
-    }
-    qs[i] = O / L;
+    const int h = i / hd, dd = i - h * hd;
+    float sum = m.pv[h * hd + dd];
+    for (int g2 = 1; g2 < groups; g2++)
+      sum += m.pv[(g2 * kMaxGqa + h) * hd + dd];
+    pdst[h * stride + 2 + dd] = sum;
+  }
+  if (tid < nq) {
+    pdst[tid * stride] = m.red[2 * tid];
+    pdst[tid * stride + 1] = m.red[2 * tid + 1];
+  }
+  __syncthreads();  // qs, sc, pv and red are reused next
+}
+
+// Decode: gridDim.y CTAs per (KV head g, row r); CTA y takes chunks y, y + gridDim.y, ... and writes each chunk's
+// partial; attention_combine_kernel merges them.
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
+    const float *q, long long q_ld, const float *kc, const float *vc, const int *pos_dev, int pos0, int n_kv, int nq,
+    int hd, int seq, int max_splits, float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const AttnSmem m = attn_smem(hd, kDecodeStages);
+  const int g = blockIdx.x, y = blockIdx.y, r = blockIdx.z, tid = threadIdx.x, step = gridDim.y;
+  const int pos = (pos_dev ? *pos_dev : pos0) + r;
+  const bool valid = pos >= 0 && pos < seq;
+  const int npos = pos + 1, nsplit = (npos + kAttnChunk - 1) / kAttnChunk;
+  const int stride = hd + 2;
+  float *pbase = part + ((long long)r * n_kv + g) * max_splits * nq * stride;
+  if (tid == 0) {
+    for (int i = 0; i < kDecodeStages; i++)
+      mbar_init(m.bar + i, 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  float *orow = out + r * out_ld + (long long)g * nq * hd;
-  for (int i = tid; i < nq * hd; i += kAttnThreads)
-    orow[i] = qs[i];
-  if (oq) {
-    // Quantize this KV head's nq * hd outputs in gs-groups (k_quantize's rule), warp per group.
-    const int groups = nq * hd / gs;
-    int8_t *qrow = oq + r * out_ld + (long long)g * nq * hd;
-    float *srow = os + r * (out_ld / gs) + (long long)g * nq * hd / gs;
-    for (int grp = warp; grp < groups; grp += nw) {
-      float mx = 0.0f;
-      int bad = 0;
-      for (int i = lane; i < gs; i += 32) {
-        const float v = qs[grp * gs + i];
-        bad |= !isfinite(v);
-        mx = fmaxf(mx, fabsf(v));
+  if (!valid) {
+    if (y == 0 && tid == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+  } else if (y < nsplit) {
+    const float *qg = q + r * q_ld + (long long)g * nq * hd;
+    if (tid == 0)
+      issue_chunk(m, 0, kc, vc, g, seq, hd, y * kAttnChunk, min(npos - y * kAttnChunk, kAttnChunk));
+    int k = 0, issued = 1;
+    for (int c = y; c < nsplit; c += step, k++) {
+      const int st = k % kDecodeStages, next = c + step;
+      const bool more = next < nsplit;
+      if (kDecodeStages > 1 && more && tid == 0)  // the other stage's chunk is done: load the next one meanwhile
+        issue_chunk(m, (k + 1) % kDecodeStages, kc, vc, g, seq, hd, next * kAttnChunk,
+                    min(npos - next * kAttnChunk, kAttnChunk));
+      issued += kDecodeStages > 1 && more;
+      if (!wait_chunk(m, st, (k / kDecodeStages) & 1)) {
+        for (int j = k; j < issued; j++)  // let every copy in flight land (bounded) before leaving
+          mbar_wait_bounded(m.bar + j % kDecodeStages, (j / kDecodeStages) & 1);
+        break;
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1)
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (__any_sync(0xffffffffu, bad) && lane == 0)
-        kc_raise(KC_ERR_NONFINITE);
-      const float scl = __fdiv_rn(mx, 127.0f);
-      if (lane == 0)
-        srow[grp] = scl;
-      for (int i = lane; i < gs; i += 32)
-        qrow[grp * gs + i] = (int8_t)quantize_value(qs[grp * gs + i], scl);
+      chunk_partial(m, st ? m.K[1] : m.K[0], st ? m.V[1] : m.V[0], qg, min(npos - c * kAttnChunk, kAttnChunk), nq,
+                    hd, pbase + (long long)c * nq * stride);
+      if (kDecodeStages == 1 && more && tid == 0)  // one stage: its buffer is free once the math above is done
+        issue_chunk(m, 0, kc, vc, g, seq, hd, next * kAttnChunk, min(npos - next * kAttnChunk, kAttnChunk));
+      issued += kDecodeStages == 1 && more;
     }
   }
 }
 
+// Prefill: one CTA per (KV head g, split s, block of kPrefillRows rows): the chunk is loaded once and every row of the
+// block whose causal range reaches it computes its partial from shared memory. attention_combine_kernel merges.
+__global__ void __launch_bounds__(kAttnThreads) attention_prefill_kernel(
+    const float *q, long long q_ld, const float *kc, const float *vc, const int *pos_dev, int pos0, int rows,
+    int n_kv, int nq, int hd, int seq, int max_splits, float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const AttnSmem m = attn_smem(hd, 1);
+  const int g = blockIdx.x, s = blockIdx.y, r0 = blockIdx.z * kPrefillRows, tid = threadIdx.x;
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int r1 = min(rows, r0 + kPrefillRows);
+  const int t0 = s * kAttnChunk;
+  const int last_pos = min(base + r1 - 1, seq - 1);  // the block's longest causal range
+  if (t0 > last_pos || base + r0 < 0)
+    return;
+  if (tid == 0) {
+    mbar_init(m.bar, 1);
+    fence_mbar_init();
+    issue_chunk(m, 0, kc, vc, g, seq, hd, t0, min(last_pos + 1 - t0, kAttnChunk));
+  }
+  __syncthreads();  // the barrier is initialized before anyone waits on it
+  if (!wait_chunk(m, 0, 0)) {
+    mbar_wait_bounded(m.bar, 0);
+    return;
+  }
+  const int stride = hd + 2;
+  for (int r = r0; r < r1; r++) {
+    const int pos = base + r;
+    if (pos >= seq || pos + 1 <= t0)
+      continue;
+    chunk_partial(m, m.K[0], m.V[0], q + r * q_ld + (long long)g * nq * hd, min(pos + 1 - t0, kAttnChunk), nq, hd,
+                  part + (((long long)r * n_kv + g) * max_splits + s) * nq * stride);
+  }
+}
+
+constexpr int kCombineGroups = kAttnThreads / 32;  // split groups, a warp each
+constexpr int kCombineDims = 64;                    // outputs per CTA (at most): two per lane
+
+// Merges a row's chunk partials for one query head and a block of min(hd, 64) dims: one CTA per (head, dim block,
+// row). The splits are cut into kCombineGroups contiguous groups of ceil(nsplit / kCombineGroups); warp k sums its
+// group in split order (weights exp(max_s - max)), then the groups are added in group order, so the result depends
+// only on the partials, never on which kernel wrote them. With oq set and a block of exactly gs dims, the block is
+// also quantized (k_quantize's rule) as one group.
+__global__ void __launch_bounds__(kAttnThreads) attention_combine_kernel(
+    float *out, long long out_ld, int8_t *oq, float *os, const int *pos_dev, int pos0, int n_kv, int nq, int hd,
+    int seq, int max_splits, const float *part, int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float po[kCombineGroups][kCombineDims], pl[kCombineGroups], red[kCombineGroups], vo[kCombineDims];
+  const int dims = hd < kCombineDims ? hd : kCombineDims, blocks = hd / dims;
+  const int h = blockIdx.x / blocks, d0 = (blockIdx.x - h * blocks) * dims, r = blockIdx.y;
+  const int g = h / nq, hh = h - g * nq, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pos = (pos_dev ? *pos_dev : pos0) + r;
+  if (pos < 0 || pos >= seq) {
+    if (blockIdx.x == 0 && tid == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+    return;
+  }
+  const int stride = hd + 2, nsplit = (pos + kAttnChunk) / kAttnChunk;
+  const long long sstep = (long long)nq * stride;  // from split s to split s + 1
+  const float *pb = part + (((long long)r * n_kv + g) * max_splits * nq + hh) * stride;
+  // The maximum over the splits (order-independent).
+  float mx = -INFINITY;
+  for (int s = tid; s < nsplit; s += kAttnThreads)
+    mx = fmaxf(mx, __ldcg(pb + s * sstep));
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0)
+    red[warp] = mx;
+  __syncthreads();
+  float M = red[0];
+  for (int k = 1; k < kCombineGroups; k++)
+    M = fmaxf(M, red[k]);
+  // Warp k: its group of splits, in order.
+  const int per = (nsplit + kCombineGroups - 1) / kCombineGroups;
+  const int s0 = warp * per, s1 = min(nsplit, s0 + per);
+  float a0 = 0.0f, a1 = 0.0f, l = 0.0f;
+#pragma unroll 4
+  for (int s = s0; s < s1; s++) {
+    const float *ps = pb + s * sstep;
+    const float w = expf(__ldcg(ps) - M);
+    l = fmaf(__ldcg(ps + 1), w, l);
+    a0 = fmaf(__ldcg(ps + 2 + d0 + lane), w, a0);
+    if (dims > 32)
+      a1 = fmaf(__ldcg(ps + 2 + d0 + 32 + lane), w, a1);
+  }
+  po[warp][lane] = a0;
+  if (dims > 32)
+    po[warp][32 + lane] = a1;
+  if (lane == 0)
+    pl[warp] = l;
+  __syncthreads();
+  if (tid < dims) {
+    float O = po[0][tid], L = pl[0];
+    for (int k = 1; k < kCombineGroups; k++) {
+      O += po[k][tid];
+      L += pl[k];
+    }
+    const float v = O / L;
+    out[r * out_ld + (long long)h * hd + d0 + tid] = v;
+    vo[tid] = v;
+  }
+  if (!oq || dims != gs)
+    return;
+  __syncthreads();
+  if (warp == 0) {
+    const float v0 = vo[lane], v1 = dims > 32 ? vo[32 + lane] : 0.0f;
+    const int bad = !isfinite(v0) || !isfinite(v1);
+    float amax = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (__any_sync(0xffffffffu, bad)) {
+      if (lane == 0)
+        kc_raise(KC_ERR_NONFINITE);
+      return;
+    }
+    const float scl = __fdiv_rn(amax, 127.0f);
+    const long long e0 = r * out_ld + (long long)h * hd + d0;
+    if (lane == 0)
+      os[e0 / gs] = scl;
+    oq[e0 + lane] = (int8_t)quantize_value(v0, scl);
+    if (dims > 32)
+      oq[e0 + 32 + lane] = (int8_t)quantize_value(v1, scl);
+  }
+}
+
 __global__ void add_kernel(float *x, const float *y, long long n) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n)
     x[i] = __fadd_rn(x[i], y[i]);
@@ -254,12 +430,18 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)b << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)idx);
 }
 
-__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
+  return a > b ? a : b;
+}
 
+// Each CTA reduces its share of the logits to one key and folds it into *key with a 64-bit atomic maximum (the
+// caller leaves *key at 0 beforehand: a fresh buffer, or k_greedy_advance's reset).
 __global__ void argmax_kernel(unsigned long long *key, const float *logits, int n, int offset) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ unsigned long long best[32];
   unsigned long long k = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     k = umax64(k, argmax_key(logits[i], i + offset));
 #pragma unroll
   for (int o = 16; o; o >>= 1)
@@ -270,14 +452,17 @@ __global__ void argmax_kernel(unsigned long long *key, const float *logits, int 
   if (threadIdx.x == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); w++)
       k = umax64(k, best[w]);
-    *key = umax64(best[0], k);
+    atomicMax(key, umax64(best[0], k));
   }
 }
 
 // Greedy step bookkeeping on the device: token = index of *key; out[*step] = token; *token_in = token (the next
-// step's input); *step += 1; *position += 1.
-__global__ void greedy_advance_kernel(int *out, int *step, int *token_in, int *position, const unsigned long long *key) {
+// step's input); *step += 1; *position += 1; *key = 0 for the next argmax.
+__global__ void greedy_advance_kernel(int *out, int *step, int *token_in, int *position, unsigned long long *key) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int idx = (int)(0xFFFFFFFFu - (unsigned)(*key & 0xFFFFFFFFull));
+  *key = 0;
   if (out)
     out[*step] = idx;
   *token_in = idx;
@@ -304,6 +489,8 @@ __device__ __forceinline__ float seeded_normal(uint64_t seed, uint64_t tensor, u
 __global__ void random_q8_kernel(int8_t *q, float *s, int rows, int cols, long long row0, long long col0,
                                  long long full_cols, unsigned long long seed, unsigned long long tensor, float std,
                                  int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = cols / gs;
   const long long gid = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
@@ -334,6 +521,8 @@ __global__ void random_q8_kernel(int8_t *q, float *s, int rows, int cols, long l
 }
 
 __global__ void fill_kernel(float *x, long long n, float v) {
+  pdl_wait();
+  pdl_launch_dependents();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n)
     x[i] = v;
@@ -343,25 +532,46 @@ inline unsigned blocks_for(long long n, int t) { return (unsigned)((n + t - 1) /
 
 bool launched(const char *what) {
   const cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess)
+  if (e == cudaSuccess) {
+    kc_count_launch();
     return true;
+  }
   return kc_fail("%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
 }
 
 int max_splits_for(int seq) { return (seq + kAttnChunk - 1) / kAttnChunk; }
 
 bool attention_shape_ok(const char *name, const AttentionWork *w, int n_heads, int n_kv, int hd, int seq) {
-  if (!w || !w->partial || !w->counters)
+  if (!w || !w->partial)
     return kc_fail("%s: attention work is not initialized", name);
-  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kMaxGqa || hd <= 0 || hd > kMaxHd || hd % 2)
-    return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d", name, n_heads, n_kv, hd);
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kMaxGqa || hd <= 0 || hd > kMaxHd || hd % 4)
+    return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d (head_dim a multiple of 4 up to %d, at most "
+                   "%d query heads per KV head)", name, n_heads, n_kv, hd, kMaxHd, kMaxGqa);
   if (n_heads != w->n_heads || n_kv != w->n_kv_heads || hd != w->head_dim || seq != w->seq_len)
     return kc_fail("%s: shape differs from the one the work was initialized for", name);
   return true;
 }
 
-// Runs `rows` query rows in waves of the work's row capacity. With device positions (graph replay) the grid covers
-// every split of the context and all rows go in one wave.
+// The kernels' dynamic shared-memory limit, raised once per device to what the largest head dimension needs (a limit
+// set per call would let a smaller head dimension lower it under a larger one).
+bool attention_smem_ready() {
+  static bool done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64)
+    return false;
+  if (!done[dev]) {
+    const int decode = (int)attn_smem_bytes(kMaxHd, kDecodeStages), single = (int)attn_smem_bytes(kMaxHd, 1);
+    if (cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode) ||
+        cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, single))
+      return false;
+    done[dev] = true;
+  }
+  return true;
+}
+
+// One decode row: the split CTAs merge by themselves. Several rows: the row-blocked prefill kernel, then the merge
+// kernel, in waves of the work's row capacity. Device positions (graph replay) size the grid for the whole context.
 bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, float *os, const float *q,
                     long long q_ld, const float *kc, const float *vc, AttentionWork *w, int n_heads, int n_kv, int hd,
                     int seq, const int *pos_dev, int pos0, int rows, int gs) {
@@ -373,18 +583,42 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
     return kc_fail("%s: positions %d..%d outside the context of %d", name, pos0, pos0 + rows - 1, seq);
   if (pos_dev && rows > w->rows)
     return kc_fail("%s: device positions need all %d rows in one wave (work holds %d)", name, rows, w->rows);
-  const int max_splits = max_splits_for(seq);
+  if (!attention_smem_ready())
+    return kc_fail("%s: cannot reserve %zu bytes of shared memory", name, attn_smem_bytes(hd, kDecodeStages));
+  if (hd % 32 || kAttnThreads % hd)
+    return kc_fail("%s: head_dim %d must be 32, 64 or 128", name, hd);
+  const int max_splits = max_splits_for(seq), nq = n_heads / n_kv;
+  // Decode CTAs per (KV head, row): one wave of the GPU at two CTAs per SM, never more than the context has chunks.
+  int ctas = 2 * kc_device_sms() / n_kv;
+  ctas = ctas < 8 ? 8 : ctas;
+  // The combine kernel quantizes its block when the block is exactly one quantization group; else a separate pass.
+  const int dims = hd < kCombineDims ? hd : kCombineDims;
+  const bool fused_q = oq && dims == gs;
   for (int r0 = 0; r0 < rows; r0 += w->rows) {
     const int n = rows - r0 < w->rows ? rows - r0 : w->rows;
     const int splits = pos_dev ? max_splits : max_splits_for(pos0 + r0 + n);
-    dim3 grid(n_kv, splits, n);
-    attention_kernel<<<grid, kAttnThreads, 0, kc_stream()>>>(
-        out + r0 * out_ld, out_ld, oq ? oq + r0 * out_ld : nullptr, oq ? os + r0 * (out_ld / gs) : nullptr,
-        q + r0 * q_ld, q_ld, kc, vc, pos_dev, pos0 + r0, n_kv, n_heads / n_kv, hd, seq, max_splits, w->partial,
-        w->counters, gs);
+    if (n == 1)
+      kc_launch_pdl(attention_decode_kernel, dim3(n_kv, ctas < splits ? ctas : splits, 1), kAttnThreads,
+                    attn_smem_bytes(hd, kDecodeStages), kc_stream(), q + r0 * q_ld, q_ld, kc, vc, pos_dev, pos0 + r0,
+                    n_kv, nq, hd, seq, max_splits, w->partial);
+    else
+      kc_launch_pdl(attention_prefill_kernel, dim3(n_kv, splits, (n + kPrefillRows - 1) / kPrefillRows), kAttnThreads,
+                    attn_smem_bytes(hd, 1), kc_stream(), q + r0 * q_ld, q_ld, kc, vc, pos_dev, pos0 + r0, n, n_kv, nq,
+                    hd, seq, max_splits, w->partial);
+    if (!launched(name))
+      return false;
+    kc_launch_pdl(attention_combine_kernel, dim3(n_heads * (hd / dims), n), kAttnThreads, 0, kc_stream(),
+                  out + r0 * out_ld, out_ld, fused_q ? oq + r0 * out_ld : nullptr,
+                  fused_q ? os + r0 * (out_ld / gs) : nullptr, pos_dev, pos0 + r0, n_kv, nq, hd, seq, max_splits,
+                  w->partial, gs);
     if (!launched(name))
       return false;
   }
+  if (oq && !fused_q &&
+      kc_launch_quantize_rows(oq, os, out, out_ld, rows, n_heads * hd, gs, kc_stream()) == 0)
+    kc_count_launch();
+  else if (oq && !fused_q)
+    return kc_fail("%s: CUDA launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
   return true;
 }
 
@@ -410,8 +644,8 @@ void k_kv_store(float *cache, const float *src, size_t src_ld, int pos0, int cou
   const long long total = (long long)count * n_kv_heads * head_dim;
   if (!total)
     return;
-  kv_store_kernel<<<blocks_for(total, 256), 256, 0, kc_stream()>>>(cache, src, (long long)src_ld, pos0, count,
-                                                                   n_kv_heads, head_dim, seq_len);
+  kc_launch_pdl(kv_store_kernel, blocks_for(total, 256), 256, 0, kc_stream(), cache, src, (long long)src_ld, pos0,
+      count, n_kv_heads, head_dim, seq_len);
   launched("k_kv_store");
 }
 
@@ -427,20 +661,27 @@ void k_rope_kv_store_rows(float *q, size_t q_ld, const float *k, const float *v,
   const long long total = (long long)rows * ((n_heads + n_kv_heads) * (head_dim / 2) + n_kv_heads * head_dim);
   if (!total)
     return;
-  rope_store_kernel<<<blocks_for(total, 256), 256, 0, kc_stream()>>>(q, (long long)q_ld, k, v, (long long)kv_ld,
-                                                                      key_cache, value_cache, table, position, pos0,
-                                                                      rows, n_heads, n_kv_heads, head_dim, seq_len);
+  kc_launch_pdl(rope_store_kernel, blocks_for(total, 256), 256, 0, kc_stream(), q, (long long)q_ld, k, v,
+      (long long)kv_ld, key_cache, value_cache, table, position, pos0, rows, n_heads, n_kv_heads, head_dim, seq_len);
   launched("k_rope_kv_store_rows");
 }
 
 // ---- attention ----------------------------------------------------------------------------------------------------
 
+// Rows of split-K partials the work holds: the rows asked for, capped by a 512 MiB budget (longer batches run in
+// waves), never less than one.
+static int attention_work_rows(int n_heads, int head_dim, int seq_len, int rows) {
+  const size_t per_row = (size_t)n_heads * max_splits_for(seq_len) * (head_dim + 2) * sizeof(float);
+  const size_t fit = ((size_t)512 << 20) / per_row;
+  return (int)(fit < 1 ? 1 : fit < (size_t)rows ? fit : (size_t)rows);
+}
+
 size_t k_attention_bytes_rows(int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows) {
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || seq_len <= 0 || rows <= 0)
     return 0;
+  rows = attention_work_rows(n_heads, head_dim, seq_len, rows);
   const size_t partial = (size_t)rows * n_heads * max_splits_for(seq_len) * (head_dim + 2) * sizeof(float);
-  const size_t counters = (size_t)rows * n_kv_heads * sizeof(int);
-  return ((partial + 255) & ~(size_t)255) + counters;
+  return partial;
 }
 
 void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows,
@@ -451,6 +692,7 @@ void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int
     kc_fail("k_attention_init_rows: invalid shape");
     return;
   }
+  rows = attention_work_rows(n_heads, head_dim, seq_len, rows);
   char *base = static_cast<char *>(memory);
   int external = 1;
   if (!base) {
@@ -462,13 +704,7 @@ void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int
     external = 0;
   }
   const size_t partial = (size_t)rows * n_heads * max_splits_for(seq_len) * (head_dim + 2) * sizeof(float);
-  const size_t counters_at = (partial + 255) & ~(size_t)255;
-  if (cudaMemsetAsync(base + counters_at, 0, (size_t)rows * n_kv_heads * sizeof(int), kc_stream()) != cudaSuccess) {
-    cudaGetLastError();
-    kc_fail("k_attention_init_rows: cannot clear the merge counters");
-  }
   work->partial = reinterpret_cast<float *>(base);
-  work->counters = reinterpret_cast<int *>(base + counters_at);
   work->max_chunks = max_splits_for(seq_len);
   work->n_heads = n_heads;
   work->n_kv_heads = n_kv_heads;
@@ -519,15 +755,15 @@ void k_embed_q8_rows(float *x, const int *tokens, K8Weight embed, int rows, int 
   }
   if (!rows)
     return;
-  embed_kernel<<<blocks_for((long long)rows * dim, 256), 256, 0, kc_stream()>>>(x, tokens, embed.q, embed.s, rows,
-                                                                                 dim, gs, vocab);
+  kc_launch_pdl(embed_kernel, blocks_for((long long)rows * dim, 256), 256, 0, kc_stream(), x, tokens, embed.q, embed.s,
+      rows, dim, gs, vocab);
   launched("k_embed_q8_rows");
 }
 
 void k_add(float *x, const float *y, size_t n) {
   if (!n)
     return;
-  add_kernel<<<blocks_for((long long)n, 256), 256, 0, kc_stream()>>>(x, y, (long long)n);
+  kc_launch_pdl(add_kernel, blocks_for((long long)n, 256), 256, 0, kc_stream(), x, y, (long long)n);
   launched("k_add");
 }
 
@@ -536,12 +772,14 @@ void k_argmax_key(unsigned long long *key, const float *logits, int n, int offse
     kc_fail("k_argmax_key: empty logits");
     return;
   }
-  argmax_kernel<<<1, 1024, 0, kc_stream()>>>(key, logits, n, offset);
+  const int blocks = (n + 4 * 256 - 1) / (4 * 256);
+  kc_launch_pdl(argmax_kernel, blocks < 2 * kc_device_sms() ? blocks : 2 * kc_device_sms(), 256, 0, kc_stream(), key,
+      logits, n, offset);
   launched("k_argmax_key");
 }
 
-void k_greedy_advance(int *out, int *step, int *token, int *position, const unsigned long long *key) {
-  greedy_advance_kernel<<<1, 1, 0, kc_stream()>>>(out, step, token, position, key);
+void k_greedy_advance(int *out, int *step, int *token, int *position, unsigned long long *key) {
+  kc_launch_pdl(greedy_advance_kernel, 1, 1, 0, kc_stream(), out, step, token, position, key);
   launched("k_greedy_advance");
 }
 
@@ -557,15 +795,15 @@ void k_random_q8(int8_t *q, float *s, int rows, int cols, size_t row0, size_t co
   const long long warps = (long long)rows * (cols / gs);
   if (!warps)
     return;
-  random_q8_kernel<<<blocks_for(warps, 8), 256, 0, kc_stream()>>>(q, s, rows, cols, (long long)row0, (long long)col0,
-                                                                   (long long)full_cols, seed, tensor, std, gs);
+  kc_launch_pdl(random_q8_kernel, blocks_for(warps, 8), 256, 0, kc_stream(), q, s, rows, cols, (long long)row0,
+      (long long)col0, (long long)full_cols, seed, tensor, std, gs);
   launched("k_random_q8");
 }
 
 void k_fill(float *x, size_t n, float value) {
   if (!n)
     return;
-  fill_kernel<<<blocks_for((long long)n, 256), 256, 0, kc_stream()>>>(x, (long long)n, value);
+  kc_launch_pdl(fill_kernel, blocks_for((long long)n, 256), 256, 0, kc_stream(), x, (long long)n, value);
   launched("k_fill");
 }
 

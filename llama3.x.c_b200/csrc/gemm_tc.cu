@@ -355,6 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
 
 // xs [M][groups] -> xsT [groups][ldt] (ldt >= M, a multiple of 4 so the TMA row stride is 16-byte aligned).
 __global__ void transpose_scales_kernel(float *xsT, const float *xs, int M, int groups, int ldt) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= groups * ldt)
     return;
@@ -371,7 +373,7 @@ int kc_launch_transpose_scales(float *xsT, const float *xs, int M, int groups, c
   const long long total = (long long)groups * ldt;
   if (total == 0)
     return 0;
-  transpose_scales_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(xsT, xs, M, groups, ldt);
+  kc_launch_pdl(transpose_scales_kernel, (unsigned)((total + 255) / 256), 256, 0, stream, xsT, xs, M, groups, ldt);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

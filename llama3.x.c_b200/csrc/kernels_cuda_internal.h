@@ -23,8 +23,29 @@ int kc_device_sms();
 // message, exits under KC_FAIL_EXIT, returns false under KC_FAIL_RETURN.
 cudaStream_t kc_stream();
 bool kc_fail(const char *format, ...);
+// Counts one successful kernel launch for kc_launch_count.
+void kc_count_launch();
 // Programmatic dependent launch of the kernels that support it (kernels_set_pdl; on by default).
 bool kc_pdl_enabled();
+
+// Launches `kernel` on `stream` with programmatic dependent launch allowed (kernels_set_pdl): it may be scheduled
+// while the previous kernel in the stream drains, so every kernel launched this way starts with griddepcontrol.wait
+// (pdl_wait) before it touches memory another kernel wrote or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t kc_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // Returns 0 on launch, -1 for a shape the kernel does not support, -2 on a launch error.
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,

@@ -22,6 +22,8 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 __global__ void quantize_rows_kernel(int8_t *q, float *s, const float *x, long long ldx, int m, int n, int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = n / gs;
   const long long gid = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
@@ -50,16 +52,88 @@ __global__ void quantize_rows_kernel(int8_t *q, float *s, const float *x, long l
     qg[i] = (int8_t)quantize_value(xg[i], scale);
 }
 
-constexpr int kNormThreads = 256;
-constexpr int kMaxValuesPerLane = 8;  // fused quantize: gs <= 256
+// gs = 64 (the checkpoints' group size): a warp quantizes kQuantGroupsPerWarp groups, each lane a float2 of every
+// group, all loads in flight before the first reduction; per element the arithmetic is quantize_rows_kernel's.
+constexpr int kQuantGroupsPerWarp = 4;
 
+__global__ void quantize_rows64_kernel(int8_t *q, float *s, const float *x, long long ldx, int m, int n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = n / 64;
+  const long long total = (long long)m * groups;
+  const long long g0 = ((long long)blockIdx.x * (blockDim.x >> 5) + warp) * kQuantGroupsPerWarp;
+  float2 v[kQuantGroupsPerWarp];
+#pragma unroll
+  for (int k = 0; k < kQuantGroupsPerWarp; k++) {
+    const long long gid = g0 + k;
+    if (gid < total) {
+      const long long row = gid / groups, g = gid - row * groups;
+      v[k] = *reinterpret_cast<const float2 *>(x + row * ldx + g * 64 + 2 * lane);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kQuantGroupsPerWarp; k++) {
+    const long long gid = g0 + k;
+    if (gid >= total)
+      break;
+    const long long row = gid / groups, g = gid - row * groups;
+    const int bad = !isfinite(v[k].x) || !isfinite(v[k].y);
+    if (__any_sync(0xffffffffu, bad)) {
+      if (lane == 0)
+        kc_raise(KC_ERR_NONFINITE);
+      continue;
+    }
+    const float mx = warp_max(fmaxf(fabsf(v[k].x), fabsf(v[k].y)));
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (lane == 0)
+      s[row * groups + g] = scale;
+    char2 c;
+    c.x = (signed char)quantize_value(v[k].x, scale);
+    c.y = (signed char)quantize_value(v[k].y, scale);
+    *reinterpret_cast<char2 *>(q + row * n + g * 64 + 2 * lane) = c;
+  }
+}
+
+constexpr int kNormThreads = 256;
+constexpr int kMaxValuesPerLane = 8;    // fused quantize: gs <= 256
+constexpr int kNormStagedMax = 16384;   // sizes whose row and weights are staged in shared memory (128 KB)
+
+// Copies n floats (global, any alignment) to shared memory with all threads; 16-byte vector loads when aligned, so a
+// row's loads are all in flight at once instead of trickling through a dependent chain.
+__device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
+  if ((((uintptr_t)src) & 15) == 0 && (n & 3) == 0) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll 4
+    for (int j = threadIdx.x; j < n / 4; j += kNormThreads)
+      d4[j] = s4[j];
+  } else {
+    for (int j = threadIdx.x; j < n; j += kNormThreads)
+      dst[j] = src[j];
+  }
+}
+
+// One CTA per row. With STAGED the row and the weights are first copied to shared memory (2 * size floats of dynamic
+// shared memory); without, they are read from global memory (sizes beyond kNormStagedMax).
+template <bool STAGED>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_t *q, float *s, const float *x,
                                                                 const float *w, int size, long long ldx, float eps,
                                                                 int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float norm_dyn[];
   __shared__ float lanes[64];
   __shared__ float inv;
   const int tid = threadIdx.x, row = blockIdx.x;
   const float *xr = x + row * ldx;
+  if (STAGED) {
+    stage_row(norm_dyn, xr, size);
+    stage_row(norm_dyn + size, w, size);
+    __syncthreads();
+    xr = norm_dyn;
+    w = norm_dyn + size;
+  }
   if (tid < 64) {
     float a = 0.0f;
     int j = 0;
@@ -135,6 +209,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_
 
 __global__ void rope_rows_kernel(float *q, long long q_stride, float *k, long long k_stride, const float *table,
                                  long long table_stride, int rows, int n_heads, int n_kv_heads, int head_dim) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int half = head_dim / 2;
   const int per_row = (n_heads + n_kv_heads) * half;
   const long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -166,7 +242,14 @@ int kc_launch_quantize_rows(int8_t *q, float *s, const float *x, long long ldx, 
   if (groups == 0)
     return 0;
   const int warps = 8;
-  quantize_rows_kernel<<<(unsigned)((groups + warps - 1) / warps), warps * 32, 0, stream>>>(q, s, x, ldx, m, n, gs);
+  if (gs == 64 && ((uintptr_t)x & 7) == 0 && (ldx & 1) == 0 && ((uintptr_t)q & 1) == 0) {
+    const long long per_block = (long long)warps * kQuantGroupsPerWarp;
+    kc_launch_pdl(quantize_rows64_kernel, (unsigned)((groups + per_block - 1) / per_block), warps * 32, 0, stream, q,
+                  s, x, ldx, m, n);
+  } else {
+    kc_launch_pdl(quantize_rows_kernel, (unsigned)((groups + warps - 1) / warps), warps * 32, 0, stream, q, s, x, ldx,
+                  m, n, gs);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -176,7 +259,21 @@ int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const flo
     return 0;
   if (q && (gs <= 0 || gs > 32 * kMaxValuesPerLane || size % gs))
     return -1;
-  rmsnorm_kernel<<<rows, kNormThreads, 0, stream>>>(out, q, s, x, w, size, ldx, eps, gs);
+  if (size <= kNormStagedMax) {
+    static int attr_bytes[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int bytes = 2 * size * (int)sizeof(float);
+    if (dev >= 0 && dev < 64 && bytes > attr_bytes[dev]) {
+      if (cudaFuncSetAttribute(rmsnorm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               2 * kNormStagedMax * (int)sizeof(float)) != cudaSuccess)
+        return -2;
+      attr_bytes[dev] = 2 * kNormStagedMax * (int)sizeof(float);
+    }
+    kc_launch_pdl(rmsnorm_kernel<true>, rows, kNormThreads, bytes, stream, out, q, s, x, w, size, ldx, eps, gs);
+  } else {
+    kc_launch_pdl(rmsnorm_kernel<false>, rows, kNormThreads, 0, stream, out, q, s, x, w, size, ldx, eps, gs);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -186,7 +283,7 @@ int kc_launch_rope_rows(float *q, long long q_stride, float *k, long long k_stri
   long long total = (long long)rows * (n_heads + n_kv_heads) * (head_dim / 2);
   if (total == 0)
     return 0;
-  rope_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(q, q_stride, k, k_stride, table,
+  kc_launch_pdl(rope_rows_kernel, (unsigned)((total + 255) / 256), 256, 0, stream, q, q_stride, k, k_stride, table,
                                                                           table_stride, rows, n_heads, n_kv_heads,
                                                                           head_dim);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -34,6 +34,12 @@ class Model(ctypes.Structure):
                 ("prefill_gemm", ctypes.c_int), ("prefill_kernel", ctypes.c_char_p), ("prefill_bf16", ctypes.c_int)]
 
 
+class EngineStats(ctypes.Structure):
+    """include/engine_cuda.h"""
+    _fields_ = [("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double), ("prefill_tokens", ctypes.c_longlong),
+                ("decode_tokens", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong)]
+
+
 LOGITS_NONE, LOGITS_LAST, LOGITS_ALL = 0, 1, 2
 COMM_ID_BYTES = 128
 
@@ -55,6 +61,8 @@ ENGINE_SIGNATURES = {
     "engine_generate": (_c.c_int, [_MP, _IP, _c.c_int, _c.c_int, _IP]),
     "engine_save": (_c.c_int, [_MP, _c.c_char_p]),
     "engine_stream": (_c.c_void_p, [_MP]),
+    "engine_stats": (None, [_MP, _c.POINTER(EngineStats)]),
+    "engine_stats_reset": (None, [_MP]),
 }
 ENGINE_DATA = ["engine_q8"]
 DEVICE_SIGNATURES = {
@@ -227,6 +235,14 @@ class Engine:
         if n < 0:
             raise _kc().KernelError("engine_generate failed")
         return list(out[:n])
+
+    def stats(self):
+        st = EngineStats()
+        self.lib.engine_stats(self._m, ctypes.byref(st))
+        return {f: getattr(st, f) for f, _ in EngineStats._fields_}
+
+    def stats_reset(self):
+        self.lib.engine_stats_reset(self._m)
 
     def save(self, path):
         if self.lib.engine_save(self._m, os.fsencode(str(path))) != 0:

@@ -61,6 +61,11 @@ typedef struct {
   int *staging; /* pinned: token uploads [max_batch], then the scalar uploads at staging + max_batch */
   void *stream, *comm;
   void *graph_logits, *graph_greedy;
+  unsigned long long graph_logits_kernels, graph_greedy_kernels; /* kernels captured in each graph */
+  long long captured, replayed; /* launch-count corrections: captured calls do not run, replays bypass the count */
+  unsigned long long launches_base;
+  void *ev[3];
+  EngineStats stats;
 } Engine;
 
 static int last_gs; /* engine_group_size: the group size of the last model set up */
@@ -244,6 +249,8 @@ static int allocate_state(Engine *e) {
   e->step_dev = dev_alloc(sizeof(int));
   e->key_dev = dev_alloc(sizeof(unsigned long long));
   e->staging = kd_host_alloc((B + 16) * sizeof(int));
+  for (int i = 0; i < 3; i++)
+    e->ev[i] = kd_event_create();
   if (failed())
     return -1;
   k_attention_init_rows(&e->attn, e->hl, e->kl, e->hd, e->context, e->max_batch < 256 ? e->max_batch : 256, NULL);
@@ -294,6 +301,7 @@ static int connect(Engine *e) {
 
 static void publish(Model *model, Engine *e) {
   last_gs = e->gs;
+  e->launches_base = kc_launch_count();
   model->config = e->c;
   model->max_batch = e->max_batch;
   const char *logits = getenv("LLAMA_PREFILL_LOGITS");
@@ -684,12 +692,13 @@ static void decode_greedy_step(Engine *e) {
   k_greedy_advance(e->gen_dev, e->step_dev, e->tokens_dev, e->pos_dev, e->key_dev);
 }
 
-static int run_step(Engine *e, void **graph, void (*step)(Engine *)) {
+static int run_step(Engine *e, void **graph, unsigned long long *kernels, void (*step)(Engine *)) {
   if (!e->graphs) {
     step(e);
     return failed() ? -1 : 0;
   }
   if (!*graph) {
+    unsigned long long before = kc_launch_count();
     if (kd_capture_begin())
       return -1;
     step(e);
@@ -699,7 +708,10 @@ static int run_step(Engine *e, void **graph, void (*step)(Engine *)) {
       return -1;
     }
     *graph = g;
+    *kernels = kc_launch_count() - before;
+    e->captured += (long long)*kernels;
   }
+  e->replayed += (long long)*kernels;
   return kd_graph_launch(*graph);
 }
 
@@ -732,7 +744,7 @@ float *engine_forward(Model *model, int token, int position) {
   scalars[1] = position;
   kd_copy(e->tokens_dev, &scalars[0], sizeof(int));
   kd_copy(e->pos_dev, &scalars[1], sizeof(int));
-  if (run_step(e, &e->graph_logits, decode_logits_step))
+  if (run_step(e, &e->graph_logits, &e->graph_logits_kernels, decode_logits_step))
     return NULL;
   copy_logits_host(e, e->logits_host, e->logits_dev, e->gather_dev);
   if (kd_sync() || kc_status() || failed())
@@ -874,6 +886,8 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
     if (!e->gen_dev)
       return -1;
   }
+  kernels_set_stream(e->stream);
+  kd_event_record(e->ev[0]);
   for (int i = 0; i < count; i += e->max_batch) {
     int n = count - i < e->max_batch ? count - i : e->max_batch;
     if (prefill(e, prompt + i, n, i, i + n == count ? LOGITS_LAST : LOGITS_NONE))
@@ -889,9 +903,11 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
   if (e->S > 1)
     kd_allreduce_max_u64(e->comm, e->key_dev, 1);
   k_greedy_advance(e->gen_dev, e->step_dev, e->tokens_dev, e->pos_dev, e->key_dev);
+  kd_event_record(e->ev[1]);
   for (int i = 1; i < steps; i++)
-    if (run_step(e, &e->graph_greedy, decode_greedy_step))
+    if (run_step(e, &e->graph_greedy, &e->graph_greedy_kernels, decode_greedy_step))
       return -1;
+  kd_event_record(e->ev[2]);
   int *tokens = malloc((size_t)steps * sizeof(int));
   if (!tokens)
     return efail("engine_generate: out of host memory");
@@ -899,6 +915,10 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
     free(tokens);
     return -1;
   }
+  e->stats.prefill_ms += kd_event_ms(e->ev[0], e->ev[1]);
+  e->stats.decode_ms += kd_event_ms(e->ev[1], e->ev[2]);
+  e->stats.prefill_tokens += count;
+  e->stats.decode_tokens += steps - 1;
   int n = 0;
   for (; n < steps; n++) {
     out[n] = tokens[n];
@@ -917,6 +937,24 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
 int engine_max_batch(const Model *model) { return model->max_batch; }
 const char *engine_precision(void) { return "int8"; }
 int engine_group_size(void) { return last_gs; }
+
+void engine_stats(Model *model, EngineStats *out) {
+  Engine *e = model->implementation;
+  memset(out, 0, sizeof(*out));
+  if (!e)
+    return;
+  *out = e->stats;
+  out->kernel_launches = (long long)(kc_launch_count() - e->launches_base) - e->captured + e->replayed;
+}
+
+void engine_stats_reset(Model *model) {
+  Engine *e = model->implementation;
+  if (!e)
+    return;
+  memset(&e->stats, 0, sizeof(e->stats));
+  e->launches_base = kc_launch_count();
+  e->captured = e->replayed = 0;
+}
 
 void *engine_stream(Model *model) {
   Engine *e = model->implementation;
@@ -1008,6 +1046,8 @@ void engine_free(Model *model) {
   kd_sync();
   kd_graph_free(e->graph_logits);
   kd_graph_free(e->graph_greedy);
+  for (int i = 0; i < 3; i++)
+    kd_event_free(e->ev[i]);
   if (e->layers)
     for (int l = 0; l < e->c.n_layers; l++) {
       Layer *y = &e->layers[l];

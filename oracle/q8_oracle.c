@@ -6,6 +6,7 @@
 #include "q8_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 int orc_quantize(int8_t *q, float *s, const float *x, int n, int gs) {
@@ -201,4 +202,30 @@ void orc_rope_apply(float *q, float *k, const float *table, int n_heads, int n_k
         k[i + 1] = a * s + b * c;
       }
     }
+}
+
+static uint64_t orc_mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+void orc_random_q8(int8_t *q, float *s, size_t row0, size_t rows, size_t cols, int gs, uint64_t seed,
+                   uint64_t tensor, float std) {
+  /* Box-Muller pairs: elements 2i and 2i + 1 of a row share one hash pair (r cos t, r sin t). */
+  float *row = malloc((cols + 1) * sizeof(float));
+  if (!row)
+    return;
+  for (size_t r = 0; r < rows; r++) {
+    for (size_t c = 0; c < cols; c += 2) {
+      uint64_t h1 = orc_mix64(seed ^ orc_mix64(tensor * 0x9E3779B97F4A7C15ull + ((row0 + r) * cols + c) / 2));
+      uint64_t h2 = orc_mix64(h1 + 0x632BE59BD9B4E019ull);
+      float u1 = ((float)(h1 >> 40) + 1.0f) * (1.0f / 16777217.0f), u2 = (float)(h2 >> 40) * (1.0f / 16777216.0f);
+      float radius = std * sqrtf(-2.0f * logf(u1)), angle = 6.2831853f * u2;
+      row[c] = radius * cosf(angle);
+      row[c + 1] = radius * sinf(angle);
+    }
+    orc_quantize(q + r * cols, s + r * (cols / gs), row, (int)cols, gs);
+  }
+  free(row);
 }

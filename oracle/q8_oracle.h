@@ -59,3 +59,9 @@ void orc_rope_apply(float *q, float *k, const float *table, int n_heads, int n_k
 #endif
 
 #endif
+
+/* Seeded N(0, std) values by element index (SplitMix64 finalizer feeding Box-Muller in double precision), rows
+ * [row0, row0 + rows) of a [*][cols] tensor numbered `tensor`, quantized with orc_quantize's rule into q [rows][cols]
+ * and s [rows][cols / gs]. Used to write benchmark-size checkpoints for the reference's CPU engine. */
+void orc_random_q8(int8_t *q, float *s, size_t row0, size_t rows, size_t cols, int gs, uint64_t seed,
+                   uint64_t tensor, float std);
