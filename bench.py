@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the Q8_0 W8A8 path on B200: one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv|ffn]
+                    [--profile-request] [--no-cpu-baseline]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N   (N = 2, 4, 8)
 
 Workloads (seeded synthetic data, random-init weights of the named architecture, Q8_0 gs 64):
@@ -11,6 +12,10 @@ Workloads (seeded synthetic data, random-init weights of the name
         token stream: strong scaling). value = decode tok/s; prefill tok/s rides along.
   1b    config 2: Llama-3.2-1B architecture (tied classifier), 128-token prompt, 256 tokens.
   gemv  config 0 kernel alone: quantize + GEMV 8192 x 2048 (for profiling; not the headline).
+  ffn   the dominant decode kernel alone: the 8B SwiGLU GEMV (W1 and W3, 14336 x 4096 each) on rotating weights.
+
+--profile-request (8b / 1b) runs one short request (the prefill and 4 greedy tokens) and nothing else, for an ncu launch
+list of every kernel the request launches.
 
 The weights (8.5 GB at 8B) exceed L2 many times over, so every decode step streams them from HBM.
 
@@ -263,6 +268,16 @@ def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
 
 # ---- our engine ---------------------------------------------------------------------------------------------------
 
+def run_profile_request(args):
+    """One request (prefill + 4 greedy tokens) on the workload's model, nothing timed: an ncu launch list target."""
+    eng = load_engine()
+    a = ARCH[args.workload]
+    P, _ = REQUEST[args.workload]
+    with eng.Engine.random(**a, seed=1, context=a["seq_len"]) as m:
+        tokens = m.generate(prompt_tokens(P, a["vocab_size"]), 4)
+    print(json.dumps({"profile_request": args.workload, "prompt": P, "tokens": tokens}), flush=True)
+
+
 def run_engine(args):
     import torch
     world, rank, local = dist_setup()
@@ -313,10 +328,12 @@ def run_engine(args):
     rows = a["hidden_dim"] // world
     alg, us = gemv_roofline(kc, torch, rows, a["dim"])
     achieved = alg / (us / 1e6) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
+    traffic = None  # DRAM bytes per launch from the ncu capture of this kernel at this shape, when one is committed
+    tf = ROOT / "profiles" / f"gemv_swiglu_{rows}x{a['dim']}_full.txt"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get(f"gemv_swiglu_{rows}x{a['dim']}")
+        for line in tf.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1].split()[0])
     weights = sum(v for v in weight_bytes(a, world).values())
     line = {
         "metric": METRIC, "value": round(decode, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -396,9 +413,14 @@ def run_gemv(args):
     kc = load_package()
     kc.init()
     hbm, peak_kind = peaks()
-    alg, us = gemv_roofline(kc, torch, 8192, 2048, launches=args.steps, swiglu=False)
+    if args.workload == "ffn":
+        alg, us = gemv_roofline(kc, torch, 14336, 4096, launches=args.steps, swiglu=True)
+        name = "8B SwiGLU decode GEMV (W1, W3 14336 x 4096) HBM GB/s"
+    else:
+        alg, us = gemv_roofline(kc, torch, 8192, 2048, launches=args.steps, swiglu=False)
+        name = "config 0 GEMV HBM GB/s"
     gbs = alg / (us / 1e6) / 1e9
-    print(json.dumps({"metric": "config 0 GEMV HBM GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+    print(json.dumps({"metric": name, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
                       "steps": args.steps, "warmup": args.warmup, "kernel_us": round(us, 3),
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                    "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs"}}), flush=True)
@@ -410,14 +432,17 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["8b", "1b", "gemv"], default="8b")
+    ap.add_argument("--workload", choices=["8b", "1b", "gemv", "ffn"], default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-request", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "gemv":
+    elif args.workload in ("gemv", "ffn"):
         run_gemv(args)
+    elif args.profile_request:
+        run_profile_request(args)
     else:
         run_engine(args)
 

@@ -135,3 +135,24 @@ def test_invalid_inputs_fail_like_the_reference(eng, files):
         assert m.forward(1, 0).shape == (512,)  # still usable
     with pytest.raises(kc.KernelError, match="requested context exceeds"):
         eng.Engine.load(files["tiny"], context=257)
+
+
+PROBE_GPU = HERE.parent / "oracle" / "_ref" / "probe-gpu"
+
+
+@pytest.mark.skipif(not PROBE_GPU.exists(), reason="oracle/_ref/probe-gpu is built where the reference sources exist")
+@pytest.mark.parametrize("name", ["tiny", "wide"])
+def test_reference_probe_driver_runs_the_gpu_engine(files, name):
+    """The reference's own tests/probe.c, linked against libllama3x_engine.so instead of its engine (the drop-in at
+    include/runtime.h:98-116), reproduces the reference's greedy tokens and per-position logits."""
+    import subprocess
+    p = GOLDEN[f"{name}_prompt"]
+    out = subprocess.run([str(PROBE_GPU), "generate", str(files[name]), "64", *map(str, p)], capture_output=True,
+                         check=True, timeout=300).stdout
+    assert same_tokens(name, [int(t) for t in out.split()])
+    stable = int(GOLDEN[f"{name}_stable"])
+    raw = subprocess.run([str(PROBE_GPU), str(files[name]), *map(str, p[:stable])], capture_output=True, check=True,
+                         timeout=300).stdout
+    logits = np.frombuffer(raw, np.float32).reshape(stable, -1)
+    for i in range(stable):
+        assert close(logits[i], GOLDEN[f"{name}_logits"][i]), f"position {i}"
