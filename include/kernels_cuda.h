@@ -101,6 +101,15 @@ void k_matmul_q8_ld(float *out, const K8Input *x, const K8Weight *w, size_t ld, 
 void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, const K8Weight *w3, size_t ld, int n,
                            int d, int gs);
 
+/* The decode GEMV with its input prepared inside the kernel (no reference counterpart): x holds n fp32 activations,
+ * RMS-normalized with `weight` and `epsilon` first when weight is not NULL (k_rmsnorm_q8_rows' arithmetic), then
+ * quantized in gs-groups (k_quantize's rule) by every CTA into its own shared memory, while the first weight stages
+ * stream in. Bitwise the pair k_rmsnorm_q8_rows (or k_quantize) + k_matmul_q8*, in one launch. The 1-3 segments share
+ * one kind: GEMM_STORE, GEMM_ADD, GEMM_PARTIAL (rows `n` of c from w) or GEMM_SWIGLU (one segment, w and w3); weight
+ * rows have stride ld. gs 16..256, a power of two. */
+void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
+                       const GemmQ8Segment *segments, int count);
+
 /* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count);
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count);

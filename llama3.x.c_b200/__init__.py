@@ -71,6 +71,8 @@ _SIGNATURES = {
     "k_matmul_q8_swiglu_ld": (None, [_f32p, _c.POINTER(K8Input), _c.POINTER(K8Weight), _c.POINTER(K8Weight),
                                      _c.c_size_t, _c.c_int, _c.c_int, _c.c_int]),
     "k_gemm_q8": (None, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
+    "k_matmul_q8_fused": (None, [_f32p, _f32p, _c.c_float, _c.c_size_t, _c.c_int, _c.c_int,
+                                 _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_gemm_q8_pick": (_c.c_int, [_c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_gemm_q8_backend_test": (_c.c_int, [_c.c_int, _i8p, _f32p, _c.c_int, _c.c_int, _c.c_int,
                                           _c.POINTER(GemmQ8Segment), _c.c_int]),
@@ -252,6 +254,12 @@ def _segments(segs):
 def k_gemm_q8(xq, xs, m, k, gs, segs):
     arr, count = _segments(segs)
     _call("k_gemm_q8", _ptr(xq), _ptr(xs), m, k, gs, arr, count)
+
+
+def k_matmul_q8_fused(x, weight, eps, ld, n, gs, segs):
+    """The decode GEMV on fp32 activations: RMSNorm (weight not None) + quantize inside the kernel."""
+    arr, count = _segments(segs)
+    _call("k_matmul_q8_fused", _ptr(x), _ptr(weight), eps, ld, n, gs, arr, count)
 
 
 def k_gemm_q8_pick(gs, segs):

@@ -212,6 +212,39 @@ void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, con
   gemv("k_matmul_q8_swiglu_ld", &s, 1, x, ld, n, gs, KC_SWIGLU);
 }
 
+void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
+                       const GemmQ8Segment *segments, int count) {
+  const char *name = "k_matmul_q8_fused";
+  if (!x) {
+    kc_fail("%s: missing activations", name);
+    return;
+  }
+  if (count < 1 || count > GEMM_MAX_SEGMENTS) {
+    kc_fail("%s: needs 1..%d segments, got %d", name, GEMM_MAX_SEGMENTS, count);
+    return;
+  }
+  if (gs <= 0 || n <= 0 || n % gs || ld < (size_t)n || ld % (size_t)gs) {
+    kc_fail("%s: invalid shape n=%d ld=%zu gs=%d", name, n, ld, gs);
+    return;
+  }
+  KcGemvSeg segs[GEMM_MAX_SEGMENTS];
+  int kind = -1;
+  for (int i = 0; i < count; i++) {
+    const GemmQ8Segment &g = segments[i];
+    const int k = g.kind == GEMM_STORE ? KC_STORE : g.kind == GEMM_ADD ? KC_ADD : g.kind == GEMM_PARTIAL ? KC_PARTIAL
+                  : g.kind == GEMM_SWIGLU ? KC_SWIGLU : -1;
+    if (k < 0 || (kind >= 0 && k != kind) || (k == KC_SWIGLU && (count != 1 || !g.w3.q || !g.w3.s)) || g.n < 0 ||
+        !weight_ok(name, g.w)) {
+      kc_fail("%s: segments need one kind (a SwiGLU pair alone), weights and non-negative rows", name);
+      return;
+    }
+    kind = k;
+    segs[i] = KcGemvSeg{g.c, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
+  }
+  launched(kc_launch_gemv_f32(segs, count, KcGemvAct{x, weight, epsilon}, n, (long long)ld, gs, kind, tl_stream),
+           name);
+}
+
 // ---- batched prefill GEMM -----------------------------------------------------------------------------------------
 
 static int kc_kind_of(GemmKind k) {

@@ -163,6 +163,41 @@ __device__ __forceinline__ float silu_gate_dev(float value, float gate) {
   return __fmul_rn(value, gate);
 }
 
+// RMSNorm's sum of squares in the reference's AVX-512 order (src/kernels_simd.c:136-161): 64 lanes, lane l
+// accumulating x[l], x[64 + l], ... with FMAs, a 16-lane tail for sizes that are not a multiple of 64. Call from
+// threads 0..63; returns lane l's partial.
+__device__ __forceinline__ float rms_lane_sum(const float *x, int size, int l) {
+  float a = 0.0f;
+  int j = 0;
+#pragma unroll 8
+  for (; j + 64 <= size; j += 64)
+    a = __fmaf_rn(x[j + l], x[j + l], a);
+  if (l < 16)
+    for (; j < size; j += 16)
+      if (j + l < size)
+        a = __fmaf_rn(x[j + l], x[j + l], a);
+  return a;
+}
+
+// The 64 lane partials reduced in the reference's order ((a0 + a1) + (a2 + a3) per 16-lane group, then GCC's
+// reduce_add_ps tree), divided by size, plus epsilon: 1 / sqrtf of that (one thread).
+__device__ __forceinline__ float rms_inverse(const float *lanes, int size, float eps) {
+  float v[16], t8[8], t4[4];
+  for (int l = 0; l < 16; l++)
+    v[l] = __fadd_rn(__fadd_rn(lanes[l], lanes[16 + l]), __fadd_rn(lanes[32 + l], lanes[48 + l]));
+  for (int l = 0; l < 8; l++)
+    t8[l] = __fadd_rn(v[8 + l], v[l]);
+  for (int l = 0; l < 4; l++)
+    t4[l] = __fadd_rn(t8[4 + l], t8[l]);
+  float ss = __fadd_rn(__fadd_rn(t4[0], t4[2]), __fadd_rn(t4[1], t4[3]));
+  ss = __fdiv_rn(ss, (float)size);
+  ss = __fadd_rn(ss, eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(ss));
+}
+
+// One normalized value: weight * (inv * x), the reference's rounding steps.
+__device__ __forceinline__ float rms_apply(float x, float w, float inv) { return __fmul_rn(w, __fmul_rn(inv, x)); }
+
 // k_quantize's per-value rule (src/gemv.c:617-621): q = (int8)roundf(clamp(x / scale, -127, 127)), 0 when scale == 0.
 __device__ __forceinline__ int quantize_value(float x, float scale) {
   float v = scale == 0.0f ? 0.0f : __fdiv_rn(x, scale);

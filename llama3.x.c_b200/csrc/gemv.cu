@@ -58,11 +58,19 @@ struct __align__(64) GemvMaps {
   CUtensorMap s3map;
 };
 
+// Activation modes: the int8 values and scales as given, or fp32 values quantized (and first RMS-normalized) by every
+// CTA into its shared memory.
+enum { kActQ8 = 0, kActQuantize = 1, kActNormQuantize = 2 };
+
 struct GemvArgs {
   GemvSegDev seg[3];
   int nseg;
   const int8_t *xq;
   const float *xs;
+  const float *xf;     // kActQuantize / kActNormQuantize: fp32 activations
+  const float *normw;  // kActNormQuantize: RMSNorm weights
+  float eps;
+  int act;
   int n;        // inputs (K)
   int gs;
   int kind;     // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU
@@ -189,6 +197,73 @@ __device__ __forceinline__ int group_dot(const uint8_t *buf, const int8_t *xrow,
   return dot;
 }
 
+// The activation of the fused modes, built by all threads while the first weight stages stream in: x (and the norm
+// weights) staged into shared memory, RMSNorm (the k_rmsnorm_q8_rows arithmetic: rms_lane_sum, rms_inverse,
+// rms_apply) when asked, then each gs-group quantized by k_quantize's rule into XQ / XS. Bitwise the separate kernels'
+// result. scratch: 65 floats (the chain buffers, unused until the main loop).
+__device__ __forceinline__ void prepare_activation(const GemvArgs &a, int8_t *XQ, float *XS, float *XF, float *scratch,
+                                                   int gs) {
+  const int tid = threadIdx.x, lane = tid & 31, n = a.n;
+  const bool norm = a.act == kActNormQuantize;
+  float *NW = XF + n;
+  const bool vec = ((uintptr_t)a.xf & 15) == 0 && (!norm || ((uintptr_t)a.normw & 15) == 0) && (n & 3) == 0;
+  if (vec) {
+    for (int i = tid; i < n / 4; i += kThreads) {
+      reinterpret_cast<float4 *>(XF)[i] = __ldg(reinterpret_cast<const float4 *>(a.xf) + i);
+      if (norm)
+        reinterpret_cast<float4 *>(NW)[i] = __ldg(reinterpret_cast<const float4 *>(a.normw) + i);
+    }
+  } else {
+    for (int i = tid; i < n; i += kThreads) {
+      XF[i] = __ldg(a.xf + i);
+      if (norm)
+        NW[i] = __ldg(a.normw + i);
+    }
+  }
+  __syncthreads();
+  if (norm) {
+    if (tid < 64)
+      scratch[tid] = rms_lane_sum(XF, n, tid);
+    __syncthreads();
+    if (tid == 0)
+      scratch[64] = rms_inverse(scratch, n, a.eps);
+    __syncthreads();
+  }
+  const float inv = norm ? scratch[64] : 1.0f;
+  // Four lanes per group, each taking every fourth value (gs / 4 of them), the walk rotated by the group's place in
+  // the warp so the 32 lanes read 32 different banks; the group max comes from two shuffles. The max is
+  // order-independent and each value is quantized on its own, so the mapping does not change a bit of the result.
+  const int per = gs / 4, sub = lane & 3, g8 = (lane >> 2) & 7;
+  const int groups = n / gs, slots = (groups + 7) / 8 * 32;  // 8 groups per warp-sized slot
+  for (int t = tid; t < slots; t += kThreads) {
+    const int grp = (t >> 5) * 8 + g8;
+    const bool live = grp < groups;
+    const float *xg = XF + grp * gs, *wg = NW + grp * gs;
+    float mx = 0.0f;
+    int bad = 0;
+    if (live)
+      for (int i = 0; i < per; i++) {
+        const int j = (4 * (i + g8) + sub) & (gs - 1);
+        const float v = norm ? rms_apply(xg[j], wg[j], inv) : xg[j];
+        bad |= !isfinite(v);
+        mx = fmaxf(mx, fabsf(v));
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (!live)
+      continue;
+    if (bad)
+      kc_raise(KC_ERR_NONFINITE);
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (sub == 0)
+      XS[grp] = scale;
+    for (int i = 0; i < per; i++) {
+      const int j = (4 * (i + g8) + sub) & (gs - 1);
+      XQ[grp * gs + j] = (int8_t)quantize_value(norm ? rms_apply(xg[j], wg[j], inv) : xg[j], scale);
+    }
+  }
+}
+
 template <int GS>
 __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -233,10 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
                   &bars[i]);
   }
   pdl_wait();
-  for (int i = tid; i < n / 16; i += kThreads)
-    reinterpret_cast<int4 *>(XQ)[i] = __ldg(reinterpret_cast<const int4 *>(a.xq) + i);
-  for (int i = tid; i < n / gs; i += kThreads)
-    XS[i] = __ldg(a.xs + i);
+  if (a.act == kActQ8) {
+    for (int i = tid; i < n / 16; i += kThreads)
+      reinterpret_cast<int4 *>(XQ)[i] = __ldg(reinterpret_cast<const int4 *>(a.xq) + i);
+    for (int i = tid; i < n / gs; i += kThreads)
+      XS[i] = __ldg(a.xs + i);
+  } else {
+    prepare_activation(a, XQ, XS, reinterpret_cast<float *>(XQ + ((n + 15) & ~15)), T, gs);
+  }
   __syncthreads();
 
   if (warp < kDotWarps) {
@@ -398,9 +477,10 @@ __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, Gem
   }
 }
 
-size_t smem_bytes(int n, int gs, int stage_bytes, int depth) {
+// act_floats: fp32 staging of the fused activation modes (n, or 2n with the norm weights).
+size_t smem_bytes(int n, int gs, int stage_bytes, int depth, int act_floats) {
   return (size_t)depth * stage_bytes + 128 + (size_t)2 * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
-         (size_t)((n + 15) & ~15) + 1024;
+         (size_t)((n + 15) & ~15) + (size_t)act_floats * 4 + 1024;
 }
 
 bool encode_weight(CUtensorMap *wmap, CUtensorMap *smap, const int8_t *wq, const float *ws, int rows, int n,
@@ -433,28 +513,42 @@ static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, con
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
-static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
-                      int kind, cudaStream_t stream, int grid_limit);
+static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
+                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit);
 
 // Host launcher (argument validation is the C-ABI layer's job): the TMA kernel where the shape allows it, else the
 // general rung.
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
                    int kind, cudaStream_t stream, int grid_limit) {
-  int rc = launch_tma(segs, nseg, xq, xs, n, ld, gs, kind, stream, grid_limit);
+  int rc = launch_tma(segs, nseg, xq, xs, nullptr, n, ld, gs, kind, stream, grid_limit);
   if (rc == -1)
     rc = launch_generic(segs, nseg, xq, xs, n, ld, gs, kind, stream);
   return rc;
 }
 
-static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
-                      int kind, cudaStream_t stream, int grid_limit) {
+// The fused-activation GEMV: the TMA kernel only (-1 when the shape does not fit it).
+int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
+                       cudaStream_t stream) {
+  return launch_tma(segs, nseg, nullptr, nullptr, &act, n, ld, gs, kind, stream, 0);
+}
+
+static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
+                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit) {
   thread_local GemvMaps M;
   GemvArgs A;
   memset(&M, 0, sizeof(M));
   memset(&A, 0, sizeof(A));
   if (gs < 16 || gs > kChunk || (gs & (gs - 1)) || n % gs || ld % gs || ld < n || ((ld / gs) * 4) % 16 ||
-      ((uintptr_t)xq & 15))
+      ((uintptr_t)xq & 15) || (act && gs > 256))
     return -1;
+  int act_floats = 0;
+  if (act) {
+    A.xf = act->x;
+    A.normw = act->norm;
+    A.eps = act->eps;
+    A.act = act->norm ? kActNormQuantize : kActQuantize;
+    act_floats = act->norm ? 2 * n : n;
+  }
   const bool swiglu = kind == KC_SWIGLU;
   const int box_rows = swiglu ? kTileRows / 2 : kTileRows;
   int units = 0;
@@ -503,14 +597,15 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
 #ifndef KC_GEMV_MAX_DEPTH
 #define KC_GEMV_MAX_DEPTH 4
 #endif
-  const size_t budget = KC_GEMV_SMEM_BUDGET;
-  if (smem_bytes(n, gs, A.stage_bytes, 2) > budget)
+  // The fused modes may use the rest of the 227 KB for their fp32 staging rather than give up pipeline depth.
+  const size_t budget = act ? 226 * 1024 : KC_GEMV_SMEM_BUDGET;
+  if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
     return -1;
   int depth = 2;
-  while (depth < KC_GEMV_MAX_DEPTH && smem_bytes(n, gs, A.stage_bytes, depth + 1) <= budget)
+  while (depth < KC_GEMV_MAX_DEPTH && smem_bytes(n, gs, A.stage_bytes, depth + 1, act_floats) <= budget)
     depth++;
   A.depth = depth;
-  const size_t smem = smem_bytes(n, gs, A.stage_bytes, depth);
+  const size_t smem = smem_bytes(n, gs, A.stage_bytes, depth, act_floats);
   const int sms = kc_device_sms();
   int grid = units < sms ? units : sms;
   if (grid_limit > 0 && grid > grid_limit)

@@ -51,6 +51,16 @@ cudaError_t kc_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
                    int kind, cudaStream_t stream, int grid_limit);
 
+// fp32 input of the fused GEMV: x (n values), the RMSNorm weights (nullptr: quantize only) and epsilon. Every CTA
+// normalizes and quantizes x itself into shared memory, bitwise as kc_launch_rmsnorm / kc_launch_quantize_rows.
+struct KcGemvAct {
+  const float *x;
+  const float *norm;
+  float eps;
+};
+int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
+                       cudaStream_t stream);
+
 // One GEMM segment (GemmQ8Segment without the AMX-packed copies), kind in KC_* terms.
 struct KcGemmSeg {
   float *c;

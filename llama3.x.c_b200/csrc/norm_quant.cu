@@ -134,37 +134,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_
     xr = norm_dyn;
     w = norm_dyn + size;
   }
-  if (tid < 64) {
-    float a = 0.0f;
-    int j = 0;
-    for (; j + 64 <= size; j += 64)
-      a = __fmaf_rn(xr[j + tid], xr[j + tid], a);
-    if (tid < 16)
-      for (; j < size; j += 16)
-        if (j + tid < size)
-          a = __fmaf_rn(xr[j + tid], xr[j + tid], a);
-    lanes[tid] = a;
-  }
+  if (tid < 64)
+    lanes[tid] = rms_lane_sum(xr, size, tid);
   __syncthreads();
-  if (tid == 0) {
-    float v[16], t8[8], t4[4];
-    for (int l = 0; l < 16; l++)
-      v[l] = __fadd_rn(__fadd_rn(lanes[l], lanes[16 + l]), __fadd_rn(lanes[32 + l], lanes[48 + l]));
-    for (int l = 0; l < 8; l++)
-      t8[l] = __fadd_rn(v[8 + l], v[l]);
-    for (int l = 0; l < 4; l++)
-      t4[l] = __fadd_rn(t8[4 + l], t8[l]);
-    float ss = __fadd_rn(__fadd_rn(t4[0], t4[2]), __fadd_rn(t4[1], t4[3]));
-    ss = __fdiv_rn(ss, (float)size);
-    ss = __fadd_rn(ss, eps);
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(ss));
-  }
+  if (tid == 0)
+    inv = rms_inverse(lanes, size, eps);
   __syncthreads();
   const float ss = inv;
   if (!q) {
     float *orow = out + (long long)row * size;
     for (int j = tid; j < size; j += kNormThreads)
-      orow[j] = __fmul_rn(w[j], __fmul_rn(ss, xr[j]));
+      orow[j] = rms_apply(xr[j], w[j], ss);
     return;
   }
   const int warp = tid >> 5, lane = tid & 31, groups = size / gs;
@@ -176,7 +156,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_
       int i = lane + 32 * t;
       if (i < gs) {
         int j = g * gs + i;
-        o[t] = __fmul_rn(w[j], __fmul_rn(ss, xr[j]));
+        o[t] = rms_apply(xr[j], w[j], ss);
         mx = fmaxf(mx, fabsf(o[t]));
       }
     }

@@ -639,17 +639,27 @@ static void residual_reduce(Engine *e, int rows) {
   k_add(e->x, e->partial, n);
 }
 
-/* One token at the position in e->pos_dev (device), its id in e->tokens_dev[0]: everything up to the local logits. */
+static GemmQ8Segment segment(float *c, int ldc, Q8 w, Q8 w3, int n, GemmKind kind) {
+  GemmQ8Segment g = {c, ldc, k8(w), k8(w3), NULL, NULL, n, kind};
+  return g;
+}
+
+/* One token at the position in e->pos_dev (device), its id in e->tokens_dev[0]: everything up to the local logits.
+ * The RMSNorm + quantize before QKV, W1/W3 and the classifier, and the quantize before W2, run inside those GEMVs
+ * (k_matmul_q8_fused), bitwise the separate kernels the batched path uses. */
 static void decode_layers(Engine *e) {
   const Config *p = &e->c;
   int dim = p->dim, gs = e->gs;
-  K8Input in = {e->xq, e->xs, NULL}, att = {e->aq, e->as, NULL}, hid = {e->hq, e->hs, NULL};
+  Q8 none = {NULL, NULL};
+  K8Input att = {e->aq, e->as, NULL};
   k_embed_q8_rows(e->x, e->tokens_dev, k8(e->embed), 1, dim, gs, p->vocab_size);
   for (int l = 0; l < p->n_layers; l++) {
     Layer *y = &e->layers[l];
     float *kc = e->key_cache + (size_t)l * e->layer_kv, *vc = e->value_cache + (size_t)l * e->layer_kv;
-    k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, y->rms_att, 1, dim, p->norm_eps, gs);
-    k_matmul_q8_qkv(e->q, e->k, e->v, &in, k8(y->wq), k8(y->wk), k8(y->wv), dim, e->ql, e->kvl, gs);
+    GemmQ8Segment qkv[3] = {segment(e->q, e->ql, y->wq, none, e->ql, GEMM_STORE),
+                            segment(e->k, e->kvl, y->wk, none, e->kvl, GEMM_STORE),
+                            segment(e->v, e->kvl, y->wv, none, e->kvl, GEMM_STORE)};
+    k_matmul_q8_fused(e->x, y->rms_att, p->norm_eps, dim, dim, gs, qkv, 3);
     k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
                          e->context);
     k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
@@ -661,19 +671,16 @@ static void decode_layers(Engine *e) {
       k_matmul_q8_ld(e->partial, &att, &wo, e->ql, e->ql, dim, gs, K_PARTIAL);
       residual_reduce(e, 1);
     }
-    k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, y->rms_ffn, 1, dim, p->norm_eps, gs);
-    k_matmul_q8_swiglu(e->hb, &in, k8(y->w1), k8(y->w3), dim, e->hid_l, gs);
-    k_quantize(e->hq, e->hs, e->hb, e->hid_l, gs);
-    if (e->S == 1) {
-      k_matmul_q8_add(e->x, &hid, k8(y->w2), e->hid_l, dim, gs);
-    } else {
-      K8Weight w2 = k8(y->w2);
-      k_matmul_q8_ld(e->partial, &hid, &w2, e->hid_l, e->hid_l, dim, gs, K_PARTIAL);
+    GemmQ8Segment up = segment(e->hb, e->hid_l, y->w1, y->w3, e->hid_l, GEMM_SWIGLU);
+    k_matmul_q8_fused(e->x, y->rms_ffn, p->norm_eps, dim, dim, gs, &up, 1);
+    GemmQ8Segment down = segment(e->S == 1 ? e->x : e->partial, dim, y->w2, none, dim,
+                                 e->S == 1 ? GEMM_ADD : GEMM_PARTIAL);
+    k_matmul_q8_fused(e->hb, NULL, 0.0f, e->hid_l, e->hid_l, gs, &down, 1);
+    if (e->S > 1)
       residual_reduce(e, 1);
-    }
   }
-  k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, e->rms_final, 1, dim, p->norm_eps, gs);
-  k_matmul_q8(e->logits_dev, &in, k8(e->cls), dim, e->vl, gs);
+  GemmQ8Segment cls = segment(e->logits_dev, e->vl, e->cls, none, e->vl, GEMM_STORE);
+  k_matmul_q8_fused(e->x, e->rms_final, p->norm_eps, dim, dim, gs, &cls, 1);
 }
 
 /* The decode step that hands logits to the host: every rank's shard gathered into gather_dev. */

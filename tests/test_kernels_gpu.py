@@ -360,3 +360,85 @@ def test_k_gemm_q8_picks_tensor_cores_for_batches(kc, oracle):
     c = kc.gemm(dev(xq), dev(xs), dev(wq), dev(ws), gs)
     kc.status()
     assert (bits(host(c)) == bits(oracle.gemm(xq, xs, wq, ws, gs))).all()
+
+
+# ---- the fused-input GEMV (k_matmul_q8_fused): RMSNorm / quantize inside the kernel ----------------------------------
+
+@pytest.mark.parametrize("n", [512, 2048, 4096])
+def test_fused_norm_qkv_bitwise(kc, oracle, n):
+    """RMSNorm + quantize + 3-segment GEMV in one launch equals k_rmsnorm_q8_rows + k_matmul_q8_qkv and the oracle."""
+    gs, dq, dkv = 64, n, n // 4
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    mats = [oracle.seeded_q8_matrix(r, n, gs, 100 + i) for i, r in enumerate((dq, dkv, dkv))]
+    dm = [(dev(a), dev(b)) for a, b in mats]
+    fused = [torch.zeros(r, device="cuda") for r in (dq, dkv, dkv)]
+    segs = [kc.segment(o, m) for o, m in zip(fused, dm)]
+    kc.k_matmul_q8_fused(dev(x), dev(w), 1e-5, n, n, gs, segs)
+    q = torch.empty(n, dtype=torch.int8, device="cuda")
+    s = torch.empty(n // gs, device="cuda")
+    kc.k_rmsnorm_q8_rows(q, s, None, dev(x), n, dev(w), 1, n, 1e-5, gs)
+    apart = [torch.zeros(r, device="cuda") for r in (dq, dkv, dkv)]
+    kc.k_matmul_q8_qkv(*apart, q, s, *dm, n, dq, dkv, gs)
+    kc.status()
+    rq, rs = oracle.quantize(oracle.rmsnorm(x, w, 1e-5), gs)
+    for f, a, (wq, ws) in zip(fused, apart, mats):
+        assert (bits(host(f)) == bits(host(a))).all()
+        assert (bits(host(f)) == bits(oracle.gemm(rq, rs, wq, ws, gs)[0])).all()
+
+
+def test_fused_norm_swiglu_and_quantize_add_bitwise(kc, oracle):
+    gs, n, hidden = 64, 4096, 14336
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(n).astype(np.float32)
+    w = np.ones(n, np.float32)
+    w1, w3 = oracle.seeded_q8_matrix(hidden, n, gs, 1), oracle.seeded_q8_matrix(hidden, n, gs, 3)
+    hb = torch.zeros(hidden, device="cuda")
+    kc.k_matmul_q8_fused(dev(x), dev(w), 1e-5, n, n, gs,
+                         [kc.segment(hb, (dev(w1[0]), dev(w1[1])), kc.GEMM_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))])
+    q = torch.empty(n, dtype=torch.int8, device="cuda")
+    s = torch.empty(n // gs, device="cuda")
+    kc.k_rmsnorm_q8_rows(q, s, None, dev(x), n, dev(w), 1, n, 1e-5, gs)
+    ref = kc.gemv(q, s, dev(w1[0]), dev(w1[1]), gs, kind=kc.K_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))
+    kc.status()
+    assert (bits(host(hb)) == bits(host(ref))).all()
+    # The down projection on fp32 input (quantize only), accumulated into a residual.
+    w2 = oracle.seeded_q8_matrix(n, hidden, gs, 5)
+    base = rng.standard_normal(n).astype(np.float32)
+    res_f, res_a = dev(base), dev(base)
+    kc.k_matmul_q8_fused(hb, None, 0.0, hidden, hidden, gs, [kc.segment(res_f, (dev(w2[0]), dev(w2[1])), kc.GEMM_ADD)])
+    hq, hs = kc.quantize(hb, gs)
+    kc.gemv(hq, hs, dev(w2[0]), dev(w2[1]), gs, kind=kc.K_ADD, out=res_a)
+    kc.status()
+    assert (bits(host(res_f)) == bits(host(res_a))).all()
+    rq, rs = oracle.quantize(host(hb), gs)
+    assert (bits(host(res_f)) == bits(oracle.gemm(rq, rs, *w2, gs, kind=oracle.ADD, c=base[None])[0])).all()
+
+
+def test_fused_partial_on_a_column_slice(kc, oracle):
+    """A tensor-parallel W2 shard: PARTIAL over a column slice (row stride ld > n) on fp32 input."""
+    gs, rows, full, n, c0 = 64, 256, 1024, 256, 512
+    wq, ws = oracle.seeded_q8_matrix(rows, full, gs, 9)
+    x = np.random.default_rng(3).standard_normal(n).astype(np.float32)
+    out = torch.zeros(rows, device="cuda")
+    wd = (dev(wq)[:, c0:], dev(ws)[:, c0 // gs:])
+    seg = kc.GemmQ8Segment()
+    seg.c, seg.ldc, seg.n, seg.kind = kc._ptr(out), rows, rows, kc.GEMM_PARTIAL
+    seg.w = kc.K8Weight(kc._ptr(wd[0]), kc._ptr(wd[1]))
+    seg._tensors = (out,) + wd
+    kc.k_matmul_q8_fused(dev(x), None, 0.0, full, n, gs, [seg])
+    kc.status()
+    rq, rs = oracle.quantize(x, gs)
+    ref = oracle.gemm(rq, rs, np.ascontiguousarray(wq[:, c0:c0 + n]), np.ascontiguousarray(ws[:, c0 // gs:(c0 + n) // gs]),
+                      gs)[0]
+    assert (bits(host(out)) == bits(ref)).all()
+
+
+def test_fused_rejects_mixed_kinds(kc, oracle):
+    wq, ws = oracle.seeded_q8_matrix(64, 256, 64, 1)
+    a, b = torch.zeros(64, device="cuda"), torch.zeros(64, device="cuda")
+    x = torch.zeros(256, device="cuda")
+    with pytest.raises(kc.KernelError, match="one kind"):
+        kc.k_matmul_q8_fused(x, None, 0.0, 256, 256, 64, [kc.segment(a, (dev(wq), dev(ws))),
+                                                           kc.segment(b, (dev(wq), dev(ws)), kc.GEMM_ADD)])
