@@ -110,6 +110,32 @@ void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, con
 void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
                        const GemmQ8Segment *segments, int count);
 
+/* The decode GEMV followed by work its last CTA does once, after every CTA's outputs are in memory (no reference
+ * counterpart): a kernel boundary saved between a GEMV and the small step the next one needs.
+ *   K_TAIL_QUANTIZE:        k_quantize(q, s, x, n, gs), e.g. of the SwiGLU output the GEMV just wrote;
+ *   K_TAIL_NORM_QUANTIZE:   k_rmsnorm_q8_rows(q, s, NULL, x, n, weight, 1, n, epsilon, gs), e.g. of the residual the
+ *                           GEMV just added into (the next layer's input);
+ *   K_TAIL_ROPE_KV_STORE:   k_rope_kv_store_rows on the three segments' outputs (q, k, v) at *position.
+ * Bitwise the separate kernels. The input is the usual K8Input and the segments share one kind (as
+ * k_matmul_q8_fused). Tail GEMVs in flight on two streams of one device at once race on the kernel's completion
+ * counter. */
+typedef enum { K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE } KernelTailKind;
+typedef struct {
+  KernelTailKind kind;
+  const float *x;      /* (NORM_)QUANTIZE: n values, and the RMSNorm weights and epsilon */
+  const float *weight;
+  float epsilon;
+  int8_t *q;
+  float *s;
+  int n;
+  const float *rope_table; /* ROPE_KV_STORE: [seq_len][2 * head_dim], the position in device memory, the caches */
+  const int *position;
+  float *key_cache, *value_cache;
+  int n_heads, n_kv_heads, head_dim, seq_len;
+} KernelTail;
+void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Segment *segments, int count,
+                      const KernelTail *tail);
+
 /* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count);
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count);

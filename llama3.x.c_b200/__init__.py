@@ -40,6 +40,18 @@ class GemmQ8Segment(ctypes.Structure):
                 ("pw", ctypes.c_void_p), ("pw3", ctypes.c_void_p), ("n", ctypes.c_int), ("kind", ctypes.c_int)]
 
 
+class KernelTail(ctypes.Structure):
+    """include/kernels_cuda.h: work the decode GEMV's last CTA does once."""
+    _fields_ = [("kind", ctypes.c_int), ("x", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("epsilon", ctypes.c_float),
+                ("q", ctypes.c_void_p), ("s", ctypes.c_void_p), ("n", ctypes.c_int), ("rope_table", ctypes.c_void_p),
+                ("position", ctypes.c_void_p), ("key_cache", ctypes.c_void_p), ("value_cache", ctypes.c_void_p),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("seq_len", ctypes.c_int)]
+
+
+K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE = 0, 1, 2, 3
+
+
 class AttentionWork(ctypes.Structure):
     """include/kernels_cuda.h: split-K partials in device memory."""
     _fields_ = [("partial", ctypes.c_void_p), ("max_chunks", ctypes.c_int),
@@ -73,6 +85,8 @@ _SIGNATURES = {
     "k_gemm_q8": (None, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_matmul_q8_fused": (None, [_f32p, _f32p, _c.c_float, _c.c_size_t, _c.c_int, _c.c_int,
                                  _c.POINTER(GemmQ8Segment), _c.c_int]),
+    "k_matmul_q8_tail": (None, [_c.POINTER(K8Input), _c.c_size_t, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment),
+                                _c.c_int, _c.POINTER(KernelTail)]),
     "k_gemm_q8_pick": (_c.c_int, [_c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_gemm_q8_backend_test": (_c.c_int, [_c.c_int, _i8p, _f32p, _c.c_int, _c.c_int, _c.c_int,
                                           _c.POINTER(GemmQ8Segment), _c.c_int]),
@@ -260,6 +274,13 @@ def k_matmul_q8_fused(x, weight, eps, ld, n, gs, segs):
     """The decode GEMV on fp32 activations: RMSNorm (weight not None) + quantize inside the kernel."""
     arr, count = _segments(segs)
     _call("k_matmul_q8_fused", _ptr(x), _ptr(weight), eps, ld, n, gs, arr, count)
+
+
+def k_matmul_q8_tail(xq, xs, ld, n, gs, segs, tail):
+    """The decode GEMV on int8 input, then `tail` (a KernelTail) done once by its last CTA."""
+    arr, count = _segments(segs)
+    inp = _input(xq, xs)
+    _call("k_matmul_q8_tail", ctypes.byref(inp), ld, n, gs, arr, count, ctypes.byref(tail))
 
 
 def k_gemm_q8_pick(gs, segs):

@@ -212,15 +212,29 @@ void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, con
   gemv("k_matmul_q8_swiglu_ld", &s, 1, x, ld, n, gs, KC_SWIGLU);
 }
 
+// Segments of one kind as KcGemvSeg; false (and fail()) otherwise.
+static bool gemv_segments(const char *name, const GemmQ8Segment *segments, int count, KcGemvSeg *segs, int *kind) {
+  if (count < 1 || count > GEMM_MAX_SEGMENTS)
+    return kc_fail("%s: needs 1..%d segments, got %d", name, GEMM_MAX_SEGMENTS, count);
+  *kind = -1;
+  for (int i = 0; i < count; i++) {
+    const GemmQ8Segment &g = segments[i];
+    const int k = g.kind == GEMM_STORE ? KC_STORE : g.kind == GEMM_ADD ? KC_ADD : g.kind == GEMM_PARTIAL ? KC_PARTIAL
+                  : g.kind == GEMM_SWIGLU ? KC_SWIGLU : -1;
+    if (k < 0 || (*kind >= 0 && k != *kind) || (k == KC_SWIGLU && (count != 1 || !g.w3.q || !g.w3.s)) || g.n < 0 ||
+        !weight_ok(name, g.w))
+      return kc_fail("%s: segments need one kind (a SwiGLU pair alone), weights and non-negative rows", name);
+    *kind = k;
+    segs[i] = KcGemvSeg{g.c, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
+  }
+  return true;
+}
+
 void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
                        const GemmQ8Segment *segments, int count) {
   const char *name = "k_matmul_q8_fused";
   if (!x) {
     kc_fail("%s: missing activations", name);
-    return;
-  }
-  if (count < 1 || count > GEMM_MAX_SEGMENTS) {
-    kc_fail("%s: needs 1..%d segments, got %d", name, GEMM_MAX_SEGMENTS, count);
     return;
   }
   if (gs <= 0 || n <= 0 || n % gs || ld < (size_t)n || ld % (size_t)gs) {
@@ -229,20 +243,52 @@ void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_
   }
   KcGemvSeg segs[GEMM_MAX_SEGMENTS];
   int kind = -1;
-  for (int i = 0; i < count; i++) {
-    const GemmQ8Segment &g = segments[i];
-    const int k = g.kind == GEMM_STORE ? KC_STORE : g.kind == GEMM_ADD ? KC_ADD : g.kind == GEMM_PARTIAL ? KC_PARTIAL
-                  : g.kind == GEMM_SWIGLU ? KC_SWIGLU : -1;
-    if (k < 0 || (kind >= 0 && k != kind) || (k == KC_SWIGLU && (count != 1 || !g.w3.q || !g.w3.s)) || g.n < 0 ||
-        !weight_ok(name, g.w)) {
-      kc_fail("%s: segments need one kind (a SwiGLU pair alone), weights and non-negative rows", name);
-      return;
-    }
-    kind = k;
-    segs[i] = KcGemvSeg{g.c, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
-  }
+  if (!gemv_segments(name, segments, count, segs, &kind))
+    return;
   launched(kc_launch_gemv_f32(segs, count, KcGemvAct{x, weight, epsilon}, n, (long long)ld, gs, kind, tl_stream),
            name);
+}
+
+void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Segment *segments, int count,
+                      const KernelTail *tail) {
+  const char *name = "k_matmul_q8_tail";
+  KcGemvSeg segs[GEMM_MAX_SEGMENTS];
+  int kind = -1;
+  if (!gemv_shape_ok(name, x, ld, n, gs) || !gemv_segments(name, segments, count, segs, &kind))
+    return;
+  if (!tail) {
+    kc_fail("%s: missing tail", name);
+    return;
+  }
+  KcGemvTail t = {};
+  t.kind = tail->kind;
+  if (tail->kind == K_TAIL_QUANTIZE || tail->kind == K_TAIL_NORM_QUANTIZE) {
+    if (!tail->x || !tail->q || !tail->s || tail->n <= 0 || tail->n % gs ||
+        (tail->kind == K_TAIL_NORM_QUANTIZE && !tail->weight)) {
+      kc_fail("%s: the quantize tail needs x, q, s, a whole number of %d-groups and (to normalize) weights", name, gs);
+      return;
+    }
+    t.x = tail->x, t.w = tail->weight, t.eps = tail->epsilon, t.q = tail->q, t.s = tail->s, t.n = tail->n;
+  } else if (tail->kind == K_TAIL_ROPE_KV_STORE) {
+    if (count != 3 || kind != KC_STORE || !tail->rope_table || !tail->position || !tail->key_cache ||
+        !tail->value_cache || tail->head_dim <= 0 || tail->head_dim % 2 || tail->n_kv_heads <= 0 ||
+        segments[0].n != tail->n_heads * tail->head_dim || segments[1].n != tail->n_kv_heads * tail->head_dim ||
+        segments[2].n != tail->n_kv_heads * tail->head_dim) {
+      kc_fail("%s: the RoPE tail needs the q, k, v segments (STORE) of its heads, the table, position and caches", name);
+      return;
+    }
+    t.qv = segments[0].c, t.kv = segments[1].c, t.vv = segments[2].c;
+    t.kcache = tail->key_cache, t.vcache = tail->value_cache, t.table = tail->rope_table, t.pos = tail->position;
+    t.nh = tail->n_heads, t.nkv = tail->n_kv_heads, t.hd = tail->head_dim, t.seq = tail->seq_len;
+  } else if (tail->kind != K_TAIL_NONE) {
+    kc_fail("%s: invalid tail kind %d", name, (int)tail->kind);
+    return;
+  }
+  if (t.kind == KC_TAIL_NONE) {
+    launched(kc_launch_gemv(segs, count, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
+    return;
+  }
+  launched(kc_launch_gemv_tail(segs, count, x->q, x->s, n, (long long)ld, gs, kind, t, tl_stream), name);
 }
 
 // ---- batched prefill GEMM -----------------------------------------------------------------------------------------

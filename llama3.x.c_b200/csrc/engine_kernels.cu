@@ -328,10 +328,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_flash_kernel(
       kc_raise(KC_ERR_BAD_ARGS);
     return;
   }
-  // Query v = (row - r0) * nq + h.
-  for (int i = tid; i < kFlashQ * HD; i += kAttnThreads) {
-    const int v = i / HD, d = i - v * HD;
-    Q[i] = v < nv ? q[(r0 + v / nq) * q_ld + (long long)(g * nq + v % nq) * HD + d] : 0.0f;
+  // Query v = (row - r0) * nq + h: a row's nq heads are contiguous. 16-byte loads, 8 in flight per thread.
+  {
+    constexpr int per4 = kFlashQ * HD / 4, B = 8;
+    for (int base = tid; base < per4; base += kAttnThreads * B) {
+      float4 r[B];
+#pragma unroll
+      for (int b = 0; b < B; b++) {
+        const int i = base + b * kAttnThreads, v = i / (HD / 4), d4 = i - v * (HD / 4);
+        r[b] = i < per4 && v < nv ? reinterpret_cast<const float4 *>(q + (r0 + v / nq) * q_ld +
+                                                                      (long long)(g * nq + v % nq) * HD)[d4]
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (base + b * kAttnThreads < per4)
+          reinterpret_cast<float4 *>(Q)[base + b * kAttnThreads] = r[b];
+    }
   }
   if (tid < kFlashQ)
     rowm[tid] = -INFINITY, rowl[tid] = 0.0f;

@@ -20,7 +20,7 @@
 // stage. Dot warps and the chain warp hand the buffers over with named barriers; no CTA-wide barrier sits in the loop.
 //
 // Launch overlap: the kernel lets its dependent start at once (griddepcontrol.launch_dependents) and issues its first
-// weight stages before waiting on the kernel it depends on (griddepcontrol.wait), so under programmatic dependent
+// weight stage before waiting on the kernel it depends on (griddepcontrol.wait), so under programmatic dependent
 // launch the weight stream overlaps the previous kernel's tail. Activations and outputs are touched only after the
 // wait.
 #include <cuda.h>
@@ -32,13 +32,21 @@
 
 namespace {
 
+#ifndef KC_GEMV_MIN_BLOCKS
+#define KC_GEMV_MIN_BLOCKS 1
+#endif
 constexpr int kDotWarps = 8;
 constexpr int kThreads = (kDotWarps + 1) * 32;  // 8 dot warps + 1 chain/producer warp
 constexpr int kTileRows = 32;                   // physical weight rows per sub-tile (one per lane)
-constexpr int kChunk = 1024;                    // K bytes per stage
+#ifndef KC_GEMV_CHUNK
+#define KC_GEMV_CHUNK 1024
+#endif
+constexpr int kChunk = KC_GEMV_CHUNK;           // K bytes per stage
 constexpr int kBoxCols = 128;                   // bytes per 128B-swizzled box row
 constexpr int kBoxes = kChunk / kBoxCols;
 constexpr int kWeightStage = kTileRows * kChunk;
+constexpr int kFastGroups = kChunk / 64;            // groups of a full chunk at gs 64
+constexpr int kWarpGroups = kFastGroups / kDotWarps;  // ... of them per dot warp
 // Named barriers (0 is __syncthreads): T_FULL + b / T_EMPTY + b for the two chain buffers b.
 constexpr int kBarTFull = 1, kBarTEmpty = 3;
 
@@ -71,6 +79,7 @@ struct GemvArgs {
   const float *normw;  // kActNormQuantize: RMSNorm weights
   float eps;
   int act;
+  KcGemvTail tail;     // work the last CTA to finish does once (kind 0: none)
   int n;        // inputs (K)
   int gs;
   int kind;     // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU
@@ -130,11 +139,30 @@ __device__ __forceinline__ bool lane_active(bool swiglu, int lane, int cnt) {
   return swiglu ? (lane & 15) < cnt : lane < cnt;
 }
 
-__device__ __forceinline__ void bar_sync_named(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+// Named barriers with immediate ids: a register id makes ptxas reserve all 16 of the CTA's barriers, and the SM's
+// barrier pool then holds one CTA of this kernel at a time.
+template <int ID>
+__device__ __forceinline__ void bar_sync_id() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(kThreads) : "memory");
 }
-__device__ __forceinline__ void bar_arrive_named(int id, int count) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+template <int ID>
+__device__ __forceinline__ void bar_arrive_id() {
+  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(kThreads) : "memory");
+}
+// Barrier `base` or `base + 1`, picked by the stage's parity.
+template <int BASE>
+__device__ __forceinline__ void bar_sync_named(int parity) {
+  if (parity)
+    bar_sync_id<BASE + 1>();
+  else
+    bar_sync_id<BASE>();
+}
+template <int BASE>
+__device__ __forceinline__ void bar_arrive_named(int parity) {
+  if (parity)
+    bar_arrive_id<BASE + 1>();
+  else
+    bar_arrive_id<BASE>();
 }
 
 // Stage layout: the weights of one 32-row sub-tile (two 16-row halves, w1 then w3, for SwiGLU) as 8 K-blocks of
@@ -197,39 +225,56 @@ __device__ __forceinline__ int group_dot(const uint8_t *buf, const int8_t *xrow,
   return dot;
 }
 
-// The activation of the fused modes, built by all threads while the first weight stages stream in: x (and the norm
-// weights) staged into shared memory, RMSNorm (the k_rmsnorm_q8_rows arithmetic: rms_lane_sum, rms_inverse,
-// rms_apply) when asked, then each gs-group quantized by k_quantize's rule into XQ / XS. Bitwise the separate kernels'
-// result. scratch: 65 floats (the chain buffers, unused until the main loop).
-__device__ __forceinline__ void prepare_activation(const GemvArgs &a, int8_t *XQ, float *XS, float *XF, float *scratch,
-                                                   int gs) {
-  const int tid = threadIdx.x, lane = tid & 31, n = a.n;
-  const bool norm = a.act == kActNormQuantize;
-  float *NW = XF + n;
-  const bool vec = ((uintptr_t)a.xf & 15) == 0 && (!norm || ((uintptr_t)a.normw & 15) == 0) && (n & 3) == 0;
-  if (vec) {
-    for (int i = tid; i < n / 4; i += kThreads) {
-      reinterpret_cast<float4 *>(XF)[i] = __ldg(reinterpret_cast<const float4 *>(a.xf) + i);
-      if (norm)
-        reinterpret_cast<float4 *>(NW)[i] = __ldg(reinterpret_cast<const float4 *>(a.normw) + i);
+// Copies n floats from global to shared memory with all the CTA's threads, each keeping kStageBatch 16-byte loads in
+// flight before its first store (a load-then-store loop would wait one memory round trip per element). L2-coherent
+// loads (ld.global.cg) when `coherent`: the data may have been written by other CTAs of this very launch.
+constexpr int kStageBatch = 8;
+
+__device__ __forceinline__ void stage_floats(float *dst, const float *src, int n, bool coherent) {
+  const int tid = threadIdx.x;
+  if (((uintptr_t)src & 15) == 0 && (n & 3) == 0) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+    const int n4 = n / 4;
+    for (int base = tid; base < n4; base += kThreads * kStageBatch) {
+      float4 r[kStageBatch];
+#pragma unroll
+      for (int b = 0; b < kStageBatch; b++) {
+        const int i = base + b * kThreads;
+        if (i < n4)
+          r[b] = coherent ? __ldcg(s4 + i) : __ldg(s4 + i);
+      }
+#pragma unroll
+      for (int b = 0; b < kStageBatch; b++) {
+        const int i = base + b * kThreads;
+        if (i < n4)
+          d4[i] = r[b];
+      }
     }
   } else {
-    for (int i = tid; i < n; i += kThreads) {
-      XF[i] = __ldg(a.xf + i);
-      if (norm)
-        NW[i] = __ldg(a.normw + i);
+    for (int base = tid; base < n; base += kThreads * kStageBatch) {
+      float r[kStageBatch];
+#pragma unroll
+      for (int b = 0; b < kStageBatch; b++) {
+        const int i = base + b * kThreads;
+        if (i < n)
+          r[b] = coherent ? __ldcg(src + i) : __ldg(src + i);
+      }
+#pragma unroll
+      for (int b = 0; b < kStageBatch; b++) {
+        const int i = base + b * kThreads;
+        if (i < n)
+          dst[i] = r[b];
+      }
     }
   }
-  __syncthreads();
-  if (norm) {
-    if (tid < 64)
-      scratch[tid] = rms_lane_sum(XF, n, tid);
-    __syncthreads();
-    if (tid == 0)
-      scratch[64] = rms_inverse(scratch, n, a.eps);
-    __syncthreads();
-  }
-  const float inv = norm ? scratch[64] : 1.0f;
+}
+
+// Quantizes the n staged values XF (RMS-normalized first with NW and inv when norm) in gs-groups by k_quantize's rule
+// into q / s (shared or global memory), with all the CTA's threads.
+__device__ __forceinline__ void quantize_staged(const float *XF, const float *NW, float inv, bool norm, int8_t *q,
+                                                float *s, int n, int gs) {
+  const int tid = threadIdx.x, lane = tid & 31;
   // Four lanes per group, each taking every fourth value (gs / 4 of them), the walk rotated by the group's place in
   // the warp so the 32 lanes read 32 different banks; the group max comes from two shuffles. The max is
   // order-independent and each value is quantized on its own, so the mapping does not change a bit of the result.
@@ -256,16 +301,115 @@ __device__ __forceinline__ void prepare_activation(const GemvArgs &a, int8_t *XQ
       kc_raise(KC_ERR_NONFINITE);
     const float scale = __fdiv_rn(mx, 127.0f);
     if (sub == 0)
-      XS[grp] = scale;
+      s[grp] = scale;
     for (int i = 0; i < per; i++) {
       const int j = (4 * (i + g8) + sub) & (gs - 1);
-      XQ[grp * gs + j] = (int8_t)quantize_value(norm ? rms_apply(xg[j], wg[j], inv) : xg[j], scale);
+      q[grp * gs + j] = (int8_t)quantize_value(norm ? rms_apply(xg[j], wg[j], inv) : xg[j], scale);
     }
   }
 }
 
+// The activation of the fused modes, built by all threads while the first weight stages stream in: x (and the norm
+// weights) staged into shared memory, RMSNorm (the k_rmsnorm_q8_rows arithmetic: rms_lane_sum, rms_inverse,
+// rms_apply) when asked, then each gs-group quantized by k_quantize's rule into XQ / XS. Bitwise the separate kernels'
+// result. scratch: 65 floats (the chain buffers, unused until the main loop).
+__device__ __forceinline__ void prepare_activation(const GemvArgs &a, int8_t *XQ, float *XS, float *XF, float *scratch,
+                                                   int gs) {
+  const int tid = threadIdx.x, n = a.n;
+  const bool norm = a.act == kActNormQuantize;
+  float *NW = XF + n;
+  stage_floats(XF, a.xf, n, false);
+  if (norm)
+    stage_floats(NW, a.normw, n, false);
+  __syncthreads();
+  if (norm) {
+    if (tid < 64)
+      scratch[tid] = rms_lane_sum(XF, n, tid);
+    __syncthreads();
+    if (tid == 0)
+      scratch[64] = rms_inverse(scratch, n, a.eps);
+    __syncthreads();
+  }
+  quantize_staged(XF, NW, norm ? scratch[64] : 1.0f, norm, XQ, XS, n, gs);
+}
+
+// Completion counter of the tail GEMVs: every CTA adds one when its outputs are written; the one that makes it
+// gridDim.x runs the tail and puts it back to zero for the next launch.
+__device__ unsigned kc_gemv_tail_counter;
+
+// The tail job (see KcGemvTail), by all the threads of the last CTA, with `scratch` (the CTA's stage buffers, free
+// once its main loop is done) for staging.
+__device__ void run_tail(const KcGemvTail &t, float *scratch, int gs) {
+  const int tid = threadIdx.x;
+  if (t.kind == KC_TAIL_ROPE_KV_STORE) {
+    // k_rope_kv_store_rows for one row at *pos (rope_store_kernel's arithmetic).
+    const int pos = *t.pos, half = t.hd / 2;
+    if (pos < 0 || pos >= t.seq) {
+      if (tid == 0)
+        kc_raise(KC_ERR_BAD_ARGS);
+      return;
+    }
+    const float *tb = t.table + (long long)pos * 2 * t.hd;
+    const int nq = t.nh * t.hd, nkv = t.nkv * t.hd;
+    float *Qs = scratch, *Ks = Qs + nq, *Vs = Ks + nkv;
+    stage_floats(Qs, t.qv, nq, true);
+    stage_floats(Ks, t.kv, nkv, true);
+    stage_floats(Vs, t.vv, nkv, true);
+    __syncthreads();
+    const int rot = (t.nh + t.nkv) * half;
+    for (int p = tid; p < rot + nkv; p += kThreads) {
+      if (p < rot) {
+        const bool is_k = p >= t.nh * half;
+        const int pp = is_k ? p - t.nh * half : p, h = pp / half, j = 2 * (pp - h * half);
+        const float *src = (is_k ? Ks : Qs) + h * t.hd + j;
+        const float c = tb[j], sn = tb[t.hd + j + 1];
+        const float a = src[0], b = src[1];
+        const float o0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+        const float o1 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+        float *dst = is_k ? t.kcache + ((long long)h * t.seq + pos) * t.hd + j : t.qv + h * t.hd + j;
+        dst[0] = o0, dst[1] = o1;
+      } else {
+        const int i = p - rot, h = i / t.hd, d = i - h * t.hd;
+        t.vcache[((long long)h * t.seq + pos) * t.hd + d] = Vs[i];
+      }
+    }
+    return;
+  }
+  // (RMSNorm +) quantize t.x: staged through shared memory as the fused-input prologue does (same arithmetic).
+  const bool norm = t.kind == KC_TAIL_NORM_QUANTIZE;
+  float *XF = scratch, *NW = scratch + t.n, *lanes = NW + (norm ? t.n : 0);
+  stage_floats(XF, t.x, t.n, true);
+  if (norm)
+    stage_floats(NW, t.w, t.n, false);
+  __syncthreads();
+  if (norm) {
+    if (tid < 64)
+      lanes[tid] = rms_lane_sum(XF, t.n, tid);
+    __syncthreads();
+    if (tid == 0)
+      lanes[64] = rms_inverse(lanes, t.n, t.eps);
+    __syncthreads();
+  }
+  quantize_staged(XF, NW, norm ? lanes[64] : 1.0f, norm, t.q, t.s, t.n, gs);
+}
+
+// Counts this CTA's outputs in; the CTA that completes the count runs the tail. `flag`: one int of shared memory.
+__device__ __forceinline__ void finish_tail(const GemvArgs &a, float *scratch, int *flag) {
+  __threadfence();  // this CTA's output writes, visible before the count says so
+  __syncthreads();
+  if (threadIdx.x == 0)
+    *flag = atomicAdd(&kc_gemv_tail_counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!*flag)
+    return;
+  __threadfence();
+  run_tail(a.tail, scratch, a.gs);
+  if (threadIdx.x == 0)
+    kc_gemv_tail_counter = 0;
+}
+
 template <int GS>
-__global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // The 128-byte swizzle is a function of the address bits, so the stages start on a 1024-byte boundary.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -274,8 +418,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, c = blockIdx.x;
   const int u0 = a.units * c / G, u1 = a.units * (c + 1) / G;  // units * grid < 2^31 (checked on the host)
-  if (u1 <= u0)
+  if (u1 <= u0) {
+    if (a.tail.kind)
+      finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem));
     return;
+  }
   const Plan plan = make_plan(a, u0, u1, swiglu ? 4 : 5);
   const int nchunks = a.nchunks, depth = a.depth, stage_bytes = a.stage_bytes, n = a.n;
   const int S = (plan.nsub[0] + plan.nsub[1] + plan.nsub[2]) * nchunks;
@@ -301,12 +448,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == kDotWarps) {
-    // Weights do not depend on the previous kernel: start streaming them before waiting for it.
-    for (int i = 0; i < depth && i < S; i++)
-      issue_stage(m, gpc, a.kblock, subtile(plan, i / nchunks), i % nchunks, swiglu, lane, stages + i * stage_bytes,
-                  &bars[i]);
-  }
+  // Weights do not depend on the previous kernel: the first stage streams in before waiting for it. The others are
+  // issued once the activation loads are on their way, so those few kilobytes do not queue behind the whole
+  // prefetch on the way into this SM.
+  if (warp == kDotWarps && S > 0)
+    issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &bars[0]);
   pdl_wait();
   if (a.act == kActQ8) {
     for (int i = tid; i < n / 16; i += kThreads)
@@ -316,6 +462,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   } else {
     prepare_activation(a, XQ, XS, reinterpret_cast<float *>(XQ + ((n + 15) & ~15)), T, gs);
   }
+  if (warp == kDotWarps)
+    for (int i = 1; i < depth && i < S; i++)
+      issue_stage(m, gpc, a.kblock, subtile(plan, i / nchunks), i % nchunks, swiglu, lane, stages + i * stage_bytes,
+                  &bars[i]);
   __syncthreads();
 
   if (warp < kDotWarps) {
@@ -327,20 +477,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
       if (!*abort_flag && !mbar_wait_bounded(&bars[slot], phase))
         *abort_flag = 1;
       if (i >= 2)
-        bar_sync_named(kBarTEmpty + (i & 1), kThreads);
+        bar_sync_named<kBarTEmpty>(i & 1);
       const uint8_t *buf = stages + slot * stage_bytes;
       float *Tb = T + (i & 1) * gpc * kTileRows;
       const int groups = min(gpc, (n - chunk * kChunk) / gs);
       if (lane_active(swiglu, lane, t.cnt)) {
         const int8_t *xrow = XQ + chunk * kChunk;
         const float *xsc = XS + chunk * gpc;
-        if (GS == 64 && groups == 16) {
-          // Both of this warp's groups at once: 8 independent dp4a chains in flight.
-          const int g0 = warp, g1 = warp + kDotWarps;
-          const int d0 = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g0, gs) : group_dot<GS, 32>(buf, xrow, lane, g0, gs);
-          const int d1 = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g1, gs) : group_dot<GS, 32>(buf, xrow, lane, g1, gs);
-          Tb[g0 * kTileRows + lane] = __fmul_rn(__int2float_rn(d0), xsc[g0]);
-          Tb[g1 * kTileRows + lane] = __fmul_rn(__int2float_rn(d1), xsc[g1]);
+        if (GS == 64 && groups == kFastGroups) {
+          // All of this warp's groups at once: 4 independent dp4a chains per group in flight.
+          int d[kWarpGroups];
+#pragma unroll
+          for (int j = 0; j < kWarpGroups; j++)
+            d[j] = swiglu ? group_dot<GS, 16>(buf, xrow, lane, warp + j * kDotWarps, gs)
+                          : group_dot<GS, 32>(buf, xrow, lane, warp + j * kDotWarps, gs);
+#pragma unroll
+          for (int j = 0; j < kWarpGroups; j++)
+            Tb[(warp + j * kDotWarps) * kTileRows + lane] =
+                __fmul_rn(__int2float_rn(d[j]), xsc[warp + j * kDotWarps]);
         } else {
           for (int g = warp; g < groups; g += kDotWarps) {
             const int d = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g, gs) : group_dot<GS, 32>(buf, xrow, lane, g, gs);
@@ -348,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
           }
         }
       }
-      bar_arrive_named(kBarTFull + (i & 1), kThreads);
+      bar_arrive_named<kBarTFull>(i & 1);
       if (++slot == depth)
         slot = 0, phase ^= 1u;
       if (++chunk == nchunks)
@@ -361,24 +515,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
     int nchunk = depth % nchunks, nsub = depth / nchunks;  // chunk and sub-tile of stage i + depth
     for (int i = 0; i < S; i++) {
       const Sub t = subtile(plan, sub);
-      bar_sync_named(kBarTFull + (i & 1), kThreads);
+      bar_sync_named<kBarTFull>(i & 1);
       const float *Tb = T + (i & 1) * gpc * kTileRows;
       const float *wsr = reinterpret_cast<const float *>(stages + slot * stage_bytes + kWeightStage) + lane * gpc;
       const int groups = min(gpc, (n - chunk * kChunk) / gs);
-      if (GS == 64 && groups == 16 && lane_active(swiglu, lane, t.cnt)) {
-        // Load the chunk's 16 scaled dots and 16 weight scales first, then run the 16 dependent FMAs.
-        float tv[16], wv[16];
+      if (GS == 64 && groups == kFastGroups && lane_active(swiglu, lane, t.cnt)) {
+        // 16 groups at a time: their scaled dots and weight scales loaded first, then the 16 dependent FMAs.
 #pragma unroll
-        for (int g = 0; g < 16; g += 4) {
-          float4 w4 = *reinterpret_cast<const float4 *>(wsr + g);
-          wv[g] = w4.x, wv[g + 1] = w4.y, wv[g + 2] = w4.z, wv[g + 3] = w4.w;
+        for (int h = 0; h < kFastGroups; h += 16) {
+          float tv[16], wv[16];
+#pragma unroll
+          for (int g = 0; g < 16; g += 4) {
+            float4 w4 = *reinterpret_cast<const float4 *>(wsr + h + g);
+            wv[g] = w4.x, wv[g + 1] = w4.y, wv[g + 2] = w4.z, wv[g + 3] = w4.w;
+          }
+#pragma unroll
+          for (int g = 0; g < 16; g++)
+            tv[g] = Tb[(h + g) * kTileRows + lane];
+#pragma unroll
+          for (int g = 0; g < 16; g++)
+            acc = __fmaf_rn(tv[g], wv[g], acc);
         }
-#pragma unroll
-        for (int g = 0; g < 16; g++)
-          tv[g] = Tb[g * kTileRows + lane];
-#pragma unroll
-        for (int g = 0; g < 16; g++)
-          acc = __fmaf_rn(tv[g], wv[g], acc);
       } else if (lane_active(swiglu, lane, t.cnt)) {
         for (int g = 0; g < groups; g += 4) {
           float4 w4 = *reinterpret_cast<const float4 *>(wsr + g);
@@ -416,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
       if (++nchunk == nchunks)
         nchunk = 0, nsub++;
       if (i + 2 < S)
-        bar_arrive_named(kBarTEmpty + (i & 1), kThreads);
+        bar_arrive_named<kBarTEmpty>(i & 1);
       if (++slot == depth)
         slot = 0;
       if (++chunk == nchunks)
@@ -429,6 +586,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (*abort_flag && tid == 0)
     for (int j = max(0, *issued - depth); j < *issued; j++)
       mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
+  if (a.tail.kind) {
+    __syncthreads();
+    finish_tail(a, reinterpret_cast<float *>(stages), const_cast<int *>(abort_flag) + 2);
+  }
 }
 
 // The general rung, for shapes the TMA kernel cannot describe (group sizes below 16 or not a power of two, scale rows
@@ -514,7 +675,8 @@ static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, con
 }
 
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
-                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit);
+                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit,
+                      const KcGemvTail *tail = nullptr);
 
 // Host launcher (argument validation is the C-ABI layer's job): the TMA kernel where the shape allows it, else the
 // general rung.
@@ -526,6 +688,11 @@ int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const floa
   return rc;
 }
 
+int kc_launch_gemv_tail(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld,
+                        int gs, int kind, const KcGemvTail &tail, cudaStream_t stream) {
+  return launch_tma(segs, nseg, xq, xs, nullptr, n, ld, gs, kind, stream, 0, &tail);
+}
+
 // The fused-activation GEMV: the TMA kernel only (-1 when the shape does not fit it).
 int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
                        cudaStream_t stream) {
@@ -533,7 +700,7 @@ int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, in
 }
 
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
-                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit) {
+                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit, const KcGemvTail *tail) {
   thread_local GemvMaps M;
   GemvArgs A;
   memset(&M, 0, sizeof(M));
@@ -597,8 +764,13 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
 #ifndef KC_GEMV_MAX_DEPTH
 #define KC_GEMV_MAX_DEPTH 4
 #endif
+#ifndef KC_GEMV_FUSED_BUDGET
+#define KC_GEMV_FUSED_BUDGET (226 * 1024)
+#endif
   // The fused modes may use the rest of the 227 KB for their fp32 staging rather than give up pipeline depth.
-  const size_t budget = act ? 226 * 1024 : KC_GEMV_SMEM_BUDGET;
+  size_t budget = act ? KC_GEMV_FUSED_BUDGET : KC_GEMV_SMEM_BUDGET;
+  if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
+    budget = 226 * 1024;
   if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
     return -1;
   int depth = 2;
@@ -606,6 +778,17 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     depth++;
   A.depth = depth;
   const size_t smem = smem_bytes(n, gs, A.stage_bytes, depth, act_floats);
+  if (tail) {
+    // The tail stages its vector (and the norm weights) in the stage buffers.
+    const int tail_floats = tail->kind == KC_TAIL_NORM_QUANTIZE   ? 2 * tail->n + 65
+                            : tail->kind == KC_TAIL_QUANTIZE      ? tail->n
+                            : tail->kind == KC_TAIL_ROPE_KV_STORE ? (tail->nh + 2 * tail->nkv) * tail->hd
+                                                                  : 0;
+    if ((size_t)tail_floats * 4 > (size_t)depth * A.stage_bytes || (tail->kind <= KC_TAIL_NORM_QUANTIZE &&
+                                                                    tail->kind && (tail->n % gs || gs > 256)))
+      return -1;
+    A.tail = *tail;
+  }
   const int sms = kc_device_sms();
   int grid = units < sms ? units : sms;
   if (grid_limit > 0 && grid > grid_limit)
@@ -617,6 +800,10 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   if (dev < 64 && !attr_set[dev][variant]) {
     cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+#ifdef KC_GEMV_CARVEOUT
+    cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, KC_GEMV_CARVEOUT);
+#endif
     attr_set[dev][variant] = true;
   }
   cudaLaunchConfig_t cfg = {};

@@ -50,6 +50,30 @@ cudaError_t kc_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 // Returns 0 on launch, -1 for a shape the kernel does not support, -2 on a launch error.
 int kc_launch_gemv(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
                    int kind, cudaStream_t stream, int grid_limit);
+// The same with a tail (the TMA kernel only; -1 when the shape does not fit it). Concurrent tail GEMVs on different
+// streams of one device race on the kernel's completion counter.
+int kc_launch_gemv_tail(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld,
+                        int gs, int kind, const struct KcGemvTail &tail, cudaStream_t stream);
+
+// Work the last CTA of a decode GEMV does once, after every CTA's outputs are in memory: quantize (or RMS-normalize
+// and quantize) an fp32 vector, e.g. the residual the GEMV just added into, for the next GEMV; or rotate the q and k
+// rows the three QKV segments produced and store k and v into the K/V cache at *pos. Arithmetic as the separate
+// kernels (k_quantize, k_rmsnorm_q8_rows, k_rope_kv_store_rows), bitwise.
+enum { KC_TAIL_NONE = 0, KC_TAIL_QUANTIZE = 1, KC_TAIL_NORM_QUANTIZE = 2, KC_TAIL_ROPE_KV_STORE = 3 };
+struct KcGemvTail {
+  int kind;
+  const float *x, *w;  // (NORM_)QUANTIZE: the vector [n] and the RMSNorm weights
+  float eps;
+  int8_t *q;
+  float *s;
+  int n;
+  float *qv, *kv;      // ROPE_KV_STORE: q [nh * hd] rotated in place, k [nkv * hd], v [nkv * hd]
+  const float *vv;
+  float *kcache, *vcache;
+  const float *table;  // [seq][2 * hd]
+  const int *pos;
+  int nh, nkv, hd, seq;
+};
 
 // fp32 input of the fused GEMV: x (n values), the RMSNorm weights (nullptr: quantize only) and epsilon. Every CTA
 // normalizes and quantizes x itself into shared memory, bitwise as kc_launch_rmsnorm / kc_launch_quantize_rows.

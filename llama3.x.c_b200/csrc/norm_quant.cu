@@ -99,18 +99,36 @@ constexpr int kNormThreads = 256;
 constexpr int kMaxValuesPerLane = 8;    // fused quantize: gs <= 256
 constexpr int kNormStagedMax = 16384;   // sizes whose row and weights are staged in shared memory (128 KB)
 
-// Copies n floats (global, any alignment) to shared memory with all threads; 16-byte vector loads when aligned, so a
-// row's loads are all in flight at once instead of trickling through a dependent chain.
+// Copies n floats (global, any alignment) to shared memory with all threads, each keeping 8 loads in flight before
+// its first store (a load-then-store loop would wait one memory round trip per element).
 __device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
+  constexpr int B = 8;
   if ((((uintptr_t)src) & 15) == 0 && (n & 3) == 0) {
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     float4 *d4 = reinterpret_cast<float4 *>(dst);
-#pragma unroll 4
-    for (int j = threadIdx.x; j < n / 4; j += kNormThreads)
-      d4[j] = s4[j];
+    for (int base = threadIdx.x; base < n / 4; base += kNormThreads * B) {
+      float4 r[B];
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (base + b * kNormThreads < n / 4)
+          r[b] = s4[base + b * kNormThreads];
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (base + b * kNormThreads < n / 4)
+          d4[base + b * kNormThreads] = r[b];
+    }
   } else {
-    for (int j = threadIdx.x; j < n; j += kNormThreads)
-      dst[j] = src[j];
+    for (int base = threadIdx.x; base < n; base += kNormThreads * B) {
+      float r[B];
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (base + b * kNormThreads < n)
+          r[b] = src[base + b * kNormThreads];
+#pragma unroll
+      for (int b = 0; b < B; b++)
+        if (base + b * kNormThreads < n)
+          dst[base + b * kNormThreads] = r[b];
+    }
   }
 }
 

@@ -442,3 +442,78 @@ def test_fused_rejects_mixed_kinds(kc, oracle):
     with pytest.raises(kc.KernelError, match="one kind"):
         kc.k_matmul_q8_fused(x, None, 0.0, 256, 256, 64, [kc.segment(a, (dev(wq), dev(ws))),
                                                            kc.segment(b, (dev(wq), dev(ws)), kc.GEMM_ADD)])
+
+
+# ---- the tail GEMV (k_matmul_q8_tail): the next step's small work done once by the last CTA -------------------------
+
+def _tail(kc, kind, **kw):
+    t = kc.KernelTail()
+    t.kind = kind
+    for k, v in kw.items():
+        setattr(t, k, kc._ptr(v) if hasattr(v, "data_ptr") else v)
+    return t
+
+
+def test_tail_norm_quantize_after_add_bitwise(kc, oracle):
+    """Wo-like: x += W a, then the next GEMV's input rmsnorm+quantize(x) by the last CTA; three calls in a row."""
+    gs, n, d = 64, 4096, 4096
+    rng = np.random.default_rng(21)
+    wq, ws = oracle.seeded_q8_matrix(d, n, gs, 21)
+    nw = dev((1 + 0.1 * rng.standard_normal(d)).astype(np.float32))
+    x = dev(rng.standard_normal(d).astype(np.float32))
+    x_ref = x.clone()
+    for step in range(3):
+        a = rng.standard_normal(n).astype(np.float32)
+        aq, as_ = kc.quantize(dev(a), gs)
+        q = torch.empty(d, dtype=torch.int8, device="cuda")
+        s = torch.empty(d // gs, device="cuda")
+        tail = _tail(kc, kc.K_TAIL_NORM_QUANTIZE, x=x, weight=nw, epsilon=1e-5, q=q, s=s, n=d)
+        kc.k_matmul_q8_tail(aq, as_, n, n, gs, [kc.segment(x, (dev(wq), dev(ws)), kc.GEMM_ADD)], tail)
+        kc.gemv(aq, as_, dev(wq), dev(ws), gs, kind=kc.K_ADD, out=x_ref)
+        rq = torch.empty(d, dtype=torch.int8, device="cuda")
+        rs = torch.empty(d // gs, device="cuda")
+        kc.k_rmsnorm_q8_rows(rq, rs, None, x_ref, d, nw, 1, d, 1e-5, gs)
+        kc.status()
+        assert (bits(host(x)) == bits(host(x_ref))).all(), step
+        assert (host(q) == host(rq)).all() and (bits(host(s)) == bits(host(rs))).all(), step
+
+
+def test_tail_quantize_after_swiglu_bitwise(kc, oracle):
+    gs, n, hidden = 64, 4096, 14336
+    rng = np.random.default_rng(22)
+    w1, w3 = oracle.seeded_q8_matrix(hidden, n, gs, 1), oracle.seeded_q8_matrix(hidden, n, gs, 2)
+    xq, xs = kc.quantize(dev(rng.standard_normal(n).astype(np.float32)), gs)
+    hb = torch.zeros(hidden, device="cuda")
+    hq = torch.empty(hidden, dtype=torch.int8, device="cuda")
+    hs = torch.empty(hidden // gs, device="cuda")
+    tail = _tail(kc, kc.K_TAIL_QUANTIZE, x=hb, q=hq, s=hs, n=hidden)
+    seg = kc.segment(hb, (dev(w1[0]), dev(w1[1])), kc.GEMM_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))
+    kc.k_matmul_q8_tail(xq, xs, n, n, gs, [seg], tail)
+    ref = kc.gemv(xq, xs, dev(w1[0]), dev(w1[1]), gs, kind=kc.K_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))
+    rq, rs = kc.quantize(ref, gs)
+    kc.status()
+    assert (bits(host(hb)) == bits(host(ref))).all()
+    assert (host(hq) == host(rq)).all() and (bits(host(hs)) == bits(host(rs))).all()
+
+
+@pytest.mark.parametrize("nh,nkv,hd", [(32, 8, 128), (8, 4, 32)])
+def test_tail_rope_kv_store_bitwise(kc, oracle, nh, nkv, hd):
+    gs, n, seq, pos = 64, nh * hd, 64, 37
+    rng = np.random.default_rng(nh)
+    mats = [oracle.seeded_q8_matrix(r, n, gs, 30 + i) for i, r in enumerate((nh * hd, nkv * hd, nkv * hd))]
+    dm = [(dev(a), dev(b)) for a, b in mats]
+    xq, xs = kc.quantize(dev(rng.standard_normal(n).astype(np.float32)), gs)
+    table = dev(np.stack([oracle.rope_table(p, hd, 500000.0) for p in range(seq)]))
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    outs = [torch.zeros(r, device="cuda") for r in (nh * hd, nkv * hd, nkv * hd)]
+    kcache, vcache = torch.zeros((nkv, seq, hd), device="cuda"), torch.zeros((nkv, seq, hd), device="cuda")
+    tail = _tail(kc, kc.K_TAIL_ROPE_KV_STORE, rope_table=table, position=p, key_cache=kcache, value_cache=vcache,
+                 n_heads=nh, n_kv_heads=nkv, head_dim=hd, seq_len=seq)
+    kc.k_matmul_q8_tail(xq, xs, n, n, gs, [kc.segment(o, m) for o, m in zip(outs, dm)], tail)
+    ref = [torch.zeros(r, device="cuda") for r in (nh * hd, nkv * hd, nkv * hd)]
+    kc.k_matmul_q8_qkv(*ref, xq, xs, *dm, n, nh * hd, nkv * hd, gs)
+    rk, rv = torch.zeros_like(kcache), torch.zeros_like(vcache)
+    kc.k_rope_kv_store_rows(ref[0], nh * hd, ref[1], ref[2], nkv * hd, rk, rv, table, p, 0, 1, nh, nkv, hd, seq)
+    kc.status()
+    assert (bits(host(outs[0])) == bits(host(ref[0]))).all()
+    assert torch.equal(kcache, rk) and torch.equal(vcache, rv)
