@@ -107,20 +107,31 @@ void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, con
  * stream in. Bitwise the pair k_rmsnorm_q8_rows (or k_quantize) + k_matmul_q8*, in one launch. The 1-3 segments share
  * one kind: GEMM_STORE, GEMM_ADD, GEMM_PARTIAL (rows `n` of c from w) or GEMM_SWIGLU (one segment, w and w3); weight
  * rows have stride ld. gs 16..256, a power of two. */
+typedef struct KernelTail KernelTail;
+/* `tail` (may be NULL) as for k_matmul_q8_tail below. */
 void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
-                       const GemmQ8Segment *segments, int count);
+                       const GemmQ8Segment *segments, int count, const KernelTail *tail);
 
 /* The decode GEMV followed by work its last CTA does once, after every CTA's outputs are in memory (no reference
  * counterpart): a kernel boundary saved between a GEMV and the small step the next one needs.
  *   K_TAIL_QUANTIZE:        k_quantize(q, s, x, n, gs), e.g. of the SwiGLU output the GEMV just wrote;
  *   K_TAIL_NORM_QUANTIZE:   k_rmsnorm_q8_rows(q, s, NULL, x, n, weight, 1, n, epsilon, gs), e.g. of the residual the
  *                           GEMV just added into (the next layer's input);
- *   K_TAIL_ROPE_KV_STORE:   k_rope_kv_store_rows on the three segments' outputs (q, k, v) at *position.
+ *   K_TAIL_ROPE_KV_STORE:   k_rope_kv_store_rows on the three segments' outputs (q, k, v) at *position;
+ *   K_TAIL_QUANTIZE_OUTPUT: k_quantize(q, s, c, n, gs) of the GEMV's own output (one GEMM_STORE or GEMM_SWIGLU segment
+ *                           of n rows, n % gs == 0, n / gs <= 65536), not by the last CTA but by each CTA for the
+ *                           groups its rows complete (a per-group counter), so the quantization adds no serial step.
  * Bitwise the separate kernels. The input is the usual K8Input and the segments share one kind (as
  * k_matmul_q8_fused). Tail GEMVs in flight on two streams of one device at once race on the kernel's completion
- * counter. */
-typedef enum { K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE } KernelTailKind;
-typedef struct {
+ * counters. */
+typedef enum {
+  K_TAIL_NONE,
+  K_TAIL_QUANTIZE,
+  K_TAIL_NORM_QUANTIZE,
+  K_TAIL_ROPE_KV_STORE,
+  K_TAIL_QUANTIZE_OUTPUT
+} KernelTailKind;
+struct KernelTail {
   KernelTailKind kind;
   const float *x;      /* (NORM_)QUANTIZE: n values, and the RMSNorm weights and epsilon */
   const float *weight;
@@ -132,7 +143,7 @@ typedef struct {
   const int *position;
   float *key_cache, *value_cache;
   int n_heads, n_kv_heads, head_dim, seq_len;
-} KernelTail;
+};
 void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Segment *segments, int count,
                       const KernelTail *tail);
 

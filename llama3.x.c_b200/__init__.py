@@ -49,7 +49,7 @@ class KernelTail(ctypes.Structure):
                 ("seq_len", ctypes.c_int)]
 
 
-K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE = 0, 1, 2, 3
+K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE, K_TAIL_QUANTIZE_OUTPUT = 0, 1, 2, 3, 4
 
 
 class AttentionWork(ctypes.Structure):
@@ -84,7 +84,7 @@ _SIGNATURES = {
                                      _c.c_size_t, _c.c_int, _c.c_int, _c.c_int]),
     "k_gemm_q8": (None, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
     "k_matmul_q8_fused": (None, [_f32p, _f32p, _c.c_float, _c.c_size_t, _c.c_int, _c.c_int,
-                                 _c.POINTER(GemmQ8Segment), _c.c_int]),
+                                 _c.POINTER(GemmQ8Segment), _c.c_int, _c.c_void_p]),
     "k_matmul_q8_tail": (None, [_c.POINTER(K8Input), _c.c_size_t, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment),
                                 _c.c_int, _c.POINTER(KernelTail)]),
     "k_gemm_q8_pick": (_c.c_int, [_c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
@@ -270,10 +270,12 @@ def k_gemm_q8(xq, xs, m, k, gs, segs):
     _call("k_gemm_q8", _ptr(xq), _ptr(xs), m, k, gs, arr, count)
 
 
-def k_matmul_q8_fused(x, weight, eps, ld, n, gs, segs):
-    """The decode GEMV on fp32 activations: RMSNorm (weight not None) + quantize inside the kernel."""
+def k_matmul_q8_fused(x, weight, eps, ld, n, gs, segs, tail=None):
+    """The decode GEMV on fp32 activations: RMSNorm (weight not None) + quantize inside the kernel; `tail` an optional
+    KernelTail."""
     arr, count = _segments(segs)
-    _call("k_matmul_q8_fused", _ptr(x), _ptr(weight), eps, ld, n, gs, arr, count)
+    _call("k_matmul_q8_fused", _ptr(x), _ptr(weight), eps, ld, n, gs, arr, count,
+          ctypes.addressof(tail) if tail is not None else None)
 
 
 def k_matmul_q8_tail(xq, xs, ld, n, gs, segs, tail):

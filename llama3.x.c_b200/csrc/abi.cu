@@ -230,8 +230,43 @@ static bool gemv_segments(const char *name, const GemmQ8Segment *segments, int c
   return true;
 }
 
+// The C-ABI tail as the kernel's, checked against the segments; false (kc_fail) when it does not fit them.
+static bool tail_from(const char *name, const KernelTail *tail, const GemmQ8Segment *segments, int count, int kind,
+                      int gs, KcGemvTail *t) {
+  *t = KcGemvTail{};
+  if (!tail)
+    return true;
+  t->kind = tail->kind;
+  if (tail->kind == K_TAIL_QUANTIZE || tail->kind == K_TAIL_NORM_QUANTIZE) {
+    if (!tail->x || !tail->q || !tail->s || tail->n <= 0 || tail->n % gs ||
+        (tail->kind == K_TAIL_NORM_QUANTIZE && !tail->weight))
+      return kc_fail("%s: the quantize tail needs x, q, s, a whole number of %d-groups and (to normalize) weights",
+                     name, gs);
+    t->x = tail->x, t->w = tail->weight, t->eps = tail->epsilon, t->q = tail->q, t->s = tail->s, t->n = tail->n;
+  } else if (tail->kind == K_TAIL_ROPE_KV_STORE) {
+    if (count != 3 || kind != KC_STORE || !tail->rope_table || !tail->position || !tail->key_cache ||
+        !tail->value_cache || tail->head_dim <= 0 || tail->head_dim % 2 || tail->n_kv_heads <= 0 ||
+        segments[0].n != tail->n_heads * tail->head_dim || segments[1].n != tail->n_kv_heads * tail->head_dim ||
+        segments[2].n != tail->n_kv_heads * tail->head_dim)
+      return kc_fail("%s: the RoPE tail needs the q, k, v segments (STORE) of its heads, the table, position and caches",
+                     name);
+    t->qv = segments[0].c, t->kv = segments[1].c, t->vv = segments[2].c;
+    t->kcache = tail->key_cache, t->vcache = tail->value_cache, t->table = tail->rope_table, t->pos = tail->position;
+    t->nh = tail->n_heads, t->nkv = tail->n_kv_heads, t->hd = tail->head_dim, t->seq = tail->seq_len;
+  } else if (tail->kind == K_TAIL_QUANTIZE_OUTPUT) {
+    if (count != 1 || (kind != KC_STORE && kind != KC_SWIGLU) || !tail->q || !tail->s || segments[0].n % gs ||
+        segments[0].n / gs > (1 << 16))
+      return kc_fail("%s: the output quantizer needs one STORE or SWIGLU segment of whole %d-groups (at most 65536) "
+                     "and q, s", name, gs);
+    t->q = tail->q, t->s = tail->s, t->n = segments[0].n;
+  } else if (tail->kind != K_TAIL_NONE) {
+    return kc_fail("%s: invalid tail kind %d", name, (int)tail->kind);
+  }
+  return true;
+}
+
 void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
-                       const GemmQ8Segment *segments, int count) {
+                       const GemmQ8Segment *segments, int count, const KernelTail *tail) {
   const char *name = "k_matmul_q8_fused";
   if (!x) {
     kc_fail("%s: missing activations", name);
@@ -243,9 +278,11 @@ void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_
   }
   KcGemvSeg segs[GEMM_MAX_SEGMENTS];
   int kind = -1;
-  if (!gemv_segments(name, segments, count, segs, &kind))
+  KcGemvTail t;
+  if (!gemv_segments(name, segments, count, segs, &kind) || !tail_from(name, tail, segments, count, kind, gs, &t))
     return;
-  launched(kc_launch_gemv_f32(segs, count, KcGemvAct{x, weight, epsilon}, n, (long long)ld, gs, kind, tl_stream),
+  launched(kc_launch_gemv_f32(segs, count, KcGemvAct{x, weight, epsilon}, n, (long long)ld, gs, kind, tl_stream,
+                              t.kind ? &t : nullptr),
            name);
 }
 
@@ -260,30 +297,9 @@ void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Se
     kc_fail("%s: missing tail", name);
     return;
   }
-  KcGemvTail t = {};
-  t.kind = tail->kind;
-  if (tail->kind == K_TAIL_QUANTIZE || tail->kind == K_TAIL_NORM_QUANTIZE) {
-    if (!tail->x || !tail->q || !tail->s || tail->n <= 0 || tail->n % gs ||
-        (tail->kind == K_TAIL_NORM_QUANTIZE && !tail->weight)) {
-      kc_fail("%s: the quantize tail needs x, q, s, a whole number of %d-groups and (to normalize) weights", name, gs);
-      return;
-    }
-    t.x = tail->x, t.w = tail->weight, t.eps = tail->epsilon, t.q = tail->q, t.s = tail->s, t.n = tail->n;
-  } else if (tail->kind == K_TAIL_ROPE_KV_STORE) {
-    if (count != 3 || kind != KC_STORE || !tail->rope_table || !tail->position || !tail->key_cache ||
-        !tail->value_cache || tail->head_dim <= 0 || tail->head_dim % 2 || tail->n_kv_heads <= 0 ||
-        segments[0].n != tail->n_heads * tail->head_dim || segments[1].n != tail->n_kv_heads * tail->head_dim ||
-        segments[2].n != tail->n_kv_heads * tail->head_dim) {
-      kc_fail("%s: the RoPE tail needs the q, k, v segments (STORE) of its heads, the table, position and caches", name);
-      return;
-    }
-    t.qv = segments[0].c, t.kv = segments[1].c, t.vv = segments[2].c;
-    t.kcache = tail->key_cache, t.vcache = tail->value_cache, t.table = tail->rope_table, t.pos = tail->position;
-    t.nh = tail->n_heads, t.nkv = tail->n_kv_heads, t.hd = tail->head_dim, t.seq = tail->seq_len;
-  } else if (tail->kind != K_TAIL_NONE) {
-    kc_fail("%s: invalid tail kind %d", name, (int)tail->kind);
+  KcGemvTail t;
+  if (!tail_from(name, tail, segments, count, kind, gs, &t))
     return;
-  }
   if (t.kind == KC_TAIL_NONE) {
     launched(kc_launch_gemv(segs, count, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
     return;

@@ -393,6 +393,54 @@ __device__ void run_tail(const KcGemvTail &t, float *scratch, int gs) {
   quantize_staged(XF, NW, norm ? lanes[64] : 1.0f, norm, t.q, t.s, t.n, gs);
 }
 
+// Per-group completion counters of KC_TAIL_QUANTIZE_OUTPUT: each CTA adds the rows it wrote to every gs-group they
+// touch; the CTA that brings a group to gs quantizes it and puts the counter back to zero for the next launch.
+constexpr int kMaxOutputGroups = 1 << 16;
+__device__ unsigned kc_gemv_group_counter[kMaxOutputGroups];
+
+// KC_TAIL_QUANTIZE_OUTPUT for output rows [r0, r1) of `out`, which this CTA has written: count them in, then quantize
+// (k_quantize's rule, one warp per group) each group this CTA completed. `flags`: shared scratch, one int per group
+// the range touches.
+__device__ void quantize_output_groups(const KcGemvTail &t, const float *out, int r0, int r1, int gs, int *flags) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g0 = r0 / gs, ng = (r1 - 1) / gs - g0 + 1;
+  __threadfence();  // this CTA's outputs, visible before the counts say so
+  __syncthreads();
+  for (int i = tid; i < ng; i += kThreads) {
+    const int g = g0 + i, lo = max(r0, g * gs), hi = min(r1, (g + 1) * gs);
+    flags[i] = atomicAdd(&kc_gemv_group_counter[g], (unsigned)(hi - lo)) + (unsigned)(hi - lo) == (unsigned)gs;
+  }
+  __syncthreads();
+  for (int i = warp; i < ng; i += kThreads / 32) {
+    if (!flags[i])
+      continue;
+    const int g = g0 + i;
+    __threadfence();  // the other CTAs' rows of the group, counted in before the count completed
+    float mx = 0.0f;
+    int bad = 0;
+    for (int j = lane; j < gs; j += 32) {
+      const float v = __ldcg(out + (long long)g * gs + j);
+      bad |= !isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (__any_sync(0xffffffffu, bad)) {
+      if (lane == 0)
+        kc_raise(KC_ERR_NONFINITE);
+    } else {
+      const float scale = __fdiv_rn(mx, 127.0f);
+      if (lane == 0)
+        t.s[g] = scale;
+      for (int j = lane; j < gs; j += 32)
+        t.q[(long long)g * gs + j] = (int8_t)quantize_value(__ldcg(out + (long long)g * gs + j), scale);
+    }
+    if (lane == 0)
+      kc_gemv_group_counter[g] = 0;
+  }
+}
+
 // Counts this CTA's outputs in; the CTA that completes the count runs the tail. `flag`: one int of shared memory.
 __device__ __forceinline__ void finish_tail(const GemvArgs &a, float *scratch, int *flag) {
   __threadfence();  // this CTA's output writes, visible before the count says so
@@ -419,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
   const int G = gridDim.x, c = blockIdx.x;
   const int u0 = a.units * c / G, u1 = a.units * (c + 1) / G;  // units * grid < 2^31 (checked on the host)
   if (u1 <= u0) {
-    if (a.tail.kind)
+    if (a.tail.kind && a.tail.kind != KC_TAIL_QUANTIZE_OUTPUT)
       finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem));
     return;
   }
@@ -586,7 +634,10 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
   if (*abort_flag && tid == 0)
     for (int j = max(0, *issued - depth); j < *issued; j++)
       mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
-  if (a.tail.kind) {
+  if (a.tail.kind == KC_TAIL_QUANTIZE_OUTPUT) {
+    __syncthreads();
+    quantize_output_groups(a.tail, out0, u0, u1, gs, reinterpret_cast<int *>(stages));
+  } else if (a.tail.kind) {
     __syncthreads();
     finish_tail(a, reinterpret_cast<float *>(stages), const_cast<int *>(abort_flag) + 2);
   }
@@ -695,8 +746,8 @@ int kc_launch_gemv_tail(const KcGemvSeg *segs, int nseg, const int8_t *xq, const
 
 // The fused-activation GEMV: the TMA kernel only (-1 when the shape does not fit it).
 int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
-                       cudaStream_t stream) {
-  return launch_tma(segs, nseg, nullptr, nullptr, &act, n, ld, gs, kind, stream, 0);
+                       cudaStream_t stream, const KcGemvTail *tail) {
+  return launch_tma(segs, nseg, nullptr, nullptr, &act, n, ld, gs, kind, stream, 0, tail);
 }
 
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
@@ -786,6 +837,11 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
                                                                   : 0;
     if ((size_t)tail_floats * 4 > (size_t)depth * A.stage_bytes || (tail->kind <= KC_TAIL_NORM_QUANTIZE &&
                                                                     tail->kind && (tail->n % gs || gs > 256)))
+      return -1;
+    // The output quantizer: one STORE or SwiGLU segment of whole groups, within the counters.
+    if (tail->kind == KC_TAIL_QUANTIZE_OUTPUT &&
+        (nseg != 1 || (kind != KC_STORE && kind != KC_SWIGLU) || segs[0].d % gs || segs[0].d / gs > kMaxOutputGroups ||
+         !tail->q || !tail->s))
       return -1;
     A.tail = *tail;
   }

@@ -59,7 +59,10 @@ int kc_launch_gemv_tail(const KcGemvSeg *segs, int nseg, const int8_t *xq, const
 // and quantize) an fp32 vector, e.g. the residual the GEMV just added into, for the next GEMV; or rotate the q and k
 // rows the three QKV segments produced and store k and v into the K/V cache at *pos. Arithmetic as the separate
 // kernels (k_quantize, k_rmsnorm_q8_rows, k_rope_kv_store_rows), bitwise.
-enum { KC_TAIL_NONE = 0, KC_TAIL_QUANTIZE = 1, KC_TAIL_NORM_QUANTIZE = 2, KC_TAIL_ROPE_KV_STORE = 3 };
+// KC_TAIL_QUANTIZE_OUTPUT is not a last-CTA job: the GEMV's own output (one segment) is quantized in gs-groups, each
+// by the CTA whose rows complete it.
+enum { KC_TAIL_NONE = 0, KC_TAIL_QUANTIZE = 1, KC_TAIL_NORM_QUANTIZE = 2, KC_TAIL_ROPE_KV_STORE = 3,
+       KC_TAIL_QUANTIZE_OUTPUT = 4 };
 struct KcGemvTail {
   int kind;
   const float *x, *w;  // (NORM_)QUANTIZE: the vector [n] and the RMSNorm weights
@@ -83,7 +86,7 @@ struct KcGemvAct {
   float eps;
 };
 int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
-                       cudaStream_t stream);
+                       cudaStream_t stream, const struct KcGemvTail *tail = nullptr);
 
 // One GEMM segment (GemmQ8Segment without the AMX-packed copies), kind in KC_* terms.
 struct KcGemmSeg {

@@ -645,13 +645,20 @@ static GemmQ8Segment segment(float *c, int ldc, Q8 w, Q8 w3, int n, GemmKind kin
 }
 
 /* One token at the position in e->pos_dev (device), its id in e->tokens_dev[0]: everything up to the local logits.
- * The RMSNorm + quantize before QKV, W1/W3 and the classifier, and the quantize before W2, run inside those GEMVs
- * (k_matmul_q8_fused), bitwise the separate kernels the batched path uses. */
+ * The RMSNorm + quantize before QKV, W1/W3 and the classifier run inside those GEMVs (k_matmul_q8_fused), and the
+ * SwiGLU GEMV quantizes its own output for W2 (K_TAIL_QUANTIZE_OUTPUT): bitwise the separate kernels the batched
+ * path uses. */
 static void decode_layers(Engine *e) {
   const Config *p = &e->c;
   int dim = p->dim, gs = e->gs;
   Q8 none = {NULL, NULL};
-  K8Input att = {e->aq, e->as, NULL};
+  K8Input att = {e->aq, e->as, NULL}, hid = {e->hq, e->hs, NULL};
+  /* The SwiGLU GEMV quantizes its output for W2 itself, each group by the CTA that completes it. */
+  KernelTail quant_hidden;
+  memset(&quant_hidden, 0, sizeof(quant_hidden));
+  quant_hidden.kind = K_TAIL_QUANTIZE_OUTPUT;
+  quant_hidden.q = e->hq;
+  quant_hidden.s = e->hs;
   k_embed_q8_rows(e->x, e->tokens_dev, k8(e->embed), 1, dim, gs, p->vocab_size);
   for (int l = 0; l < p->n_layers; l++) {
     Layer *y = &e->layers[l];
@@ -659,7 +666,7 @@ static void decode_layers(Engine *e) {
     GemmQ8Segment qkv[3] = {segment(e->q, e->ql, y->wq, none, e->ql, GEMM_STORE),
                             segment(e->k, e->kvl, y->wk, none, e->kvl, GEMM_STORE),
                             segment(e->v, e->kvl, y->wv, none, e->kvl, GEMM_STORE)};
-    k_matmul_q8_fused(e->x, y->rms_att, p->norm_eps, dim, dim, gs, qkv, 3);
+    k_matmul_q8_fused(e->x, y->rms_att, p->norm_eps, dim, dim, gs, qkv, 3, NULL);
     k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
                          e->context);
     k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
@@ -672,15 +679,15 @@ static void decode_layers(Engine *e) {
       residual_reduce(e, 1);
     }
     GemmQ8Segment up = segment(e->hb, e->hid_l, y->w1, y->w3, e->hid_l, GEMM_SWIGLU);
-    k_matmul_q8_fused(e->x, y->rms_ffn, p->norm_eps, dim, dim, gs, &up, 1);
-    GemmQ8Segment down = segment(e->S == 1 ? e->x : e->partial, dim, y->w2, none, dim,
-                                 e->S == 1 ? GEMM_ADD : GEMM_PARTIAL);
-    k_matmul_q8_fused(e->hb, NULL, 0.0f, e->hid_l, e->hid_l, gs, &down, 1);
+    k_matmul_q8_fused(e->x, y->rms_ffn, p->norm_eps, dim, dim, gs, &up, 1, &quant_hidden);
+    K8Weight w2 = k8(y->w2);
+    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &hid, &w2, e->hid_l, e->hid_l, dim, gs,
+                   e->S == 1 ? K_ADD : K_PARTIAL);
     if (e->S > 1)
       residual_reduce(e, 1);
   }
   GemmQ8Segment cls = segment(e->logits_dev, e->vl, e->cls, none, e->vl, GEMM_STORE);
-  k_matmul_q8_fused(e->x, e->rms_final, p->norm_eps, dim, dim, gs, &cls, 1);
+  k_matmul_q8_fused(e->x, e->rms_final, p->norm_eps, dim, dim, gs, &cls, 1, NULL);
 }
 
 /* The decode step that hands logits to the host: every rank's shard gathered into gather_dev. */

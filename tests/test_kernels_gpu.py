@@ -496,6 +496,52 @@ def test_tail_quantize_after_swiglu_bitwise(kc, oracle):
     assert (host(hq) == host(rq)).all() and (bits(host(hs)) == bits(host(rs))).all()
 
 
+@pytest.mark.parametrize("hidden", [14336, 1792, 192])
+def test_output_quantizer_after_fused_swiglu_bitwise(kc, oracle, hidden):
+    """The decode FFN's first GEMV as the engine runs it: RMSNorm + quantize of x inside the kernel, SwiGLU, and its
+    output quantized for W2 group by group by the CTAs that complete each group (K_TAIL_QUANTIZE_OUTPUT). Equal to
+    k_rmsnorm_q8_rows + the SwiGLU GEMV + k_quantize bitwise; three calls in a row (the counters reset), shapes with
+    many rows per CTA, a TP shard, and fewer rows than CTAs."""
+    gs, n = 64, 4096
+    rng = np.random.default_rng(hidden)
+    w1, w3 = oracle.seeded_q8_matrix(hidden, n, gs, 3), oracle.seeded_q8_matrix(hidden, n, gs, 4)
+    nw = dev((1 + 0.1 * rng.standard_normal(n)).astype(np.float32))
+    seg_w = ((dev(w1[0]), dev(w1[1])), (dev(w3[0]), dev(w3[1])))
+    for step in range(3):
+        x = dev(rng.standard_normal(n).astype(np.float32))
+        hb = torch.zeros(hidden, device="cuda")
+        hq = torch.empty(hidden, dtype=torch.int8, device="cuda")
+        hs = torch.empty(hidden // gs, device="cuda")
+        tail = _tail(kc, kc.K_TAIL_QUANTIZE_OUTPUT, q=hq, s=hs)
+        kc.k_matmul_q8_fused(x, nw, 1e-5, n, n, gs, [kc.segment(hb, seg_w[0], kc.GEMM_SWIGLU, w3=seg_w[1])], tail)
+        xq = torch.empty(n, dtype=torch.int8, device="cuda")
+        xs = torch.empty(n // gs, device="cuda")
+        kc.k_rmsnorm_q8_rows(xq, xs, None, x, n, nw, 1, n, 1e-5, gs)
+        ref = kc.gemv(xq, xs, *seg_w[0], gs, kind=kc.K_SWIGLU, w3=seg_w[1])
+        rq, rs = kc.quantize(ref, gs)
+        kc.status()
+        assert (bits(host(hb)) == bits(host(ref))).all(), step
+        assert (host(hq) == host(rq)).all() and (bits(host(hs)) == bits(host(rs))).all(), step
+
+
+def test_output_quantizer_store_segment_bitwise(kc, oracle):
+    """K_TAIL_QUANTIZE_OUTPUT on a STORE GEMV with int8 input, group size 32, rows that do not split evenly."""
+    gs, n, d = 32, 2048, 4096 + 5 * 32
+    rng = np.random.default_rng(23)
+    wq, ws = oracle.seeded_q8_matrix(d, n, gs, 23)
+    xq, xs = kc.quantize(dev(rng.standard_normal(n).astype(np.float32)), gs)
+    out = torch.zeros(d, device="cuda")
+    q = torch.empty(d, dtype=torch.int8, device="cuda")
+    s = torch.empty(d // gs, device="cuda")
+    kc.k_matmul_q8_tail(xq, xs, n, n, gs, [kc.segment(out, (dev(wq), dev(ws)))], _tail(kc, kc.K_TAIL_QUANTIZE_OUTPUT,
+                                                                                       q=q, s=s))
+    ref = kc.gemv(xq, xs, dev(wq), dev(ws), gs)
+    rq, rs = kc.quantize(ref, gs)
+    kc.status()
+    assert (bits(host(out)) == bits(host(ref))).all()
+    assert (host(q) == host(rq)).all() and (bits(host(s)) == bits(host(rs))).all()
+
+
 @pytest.mark.parametrize("nh,nkv,hd", [(32, 8, 128), (8, 4, 32)])
 def test_tail_rope_kv_store_bitwise(kc, oracle, nh, nkv, hd):
     gs, n, seq, pos = 64, nh * hd, 64, 37
