@@ -52,6 +52,16 @@ int kd_allreduce_max_u64(void *comm, unsigned long long *buf, size_t count);
 int kd_allgather_f32(void *comm, const float *send, float *recv, size_t count); /* recv: count floats per rank */
 void kd_comm_free(void *comm);
 
+/* Peer-memory all-reduce for one short vector (the decode step's residual partials), one kernel per call: every rank
+ * pushes its partial over NVLink into every rank's receive buffer (CUDA IPC mappings, so all ranks are processes on
+ * one node with peer access between every pair of GPUs, as NVSwitch gives) and waits, bounded, for the others'; then
+ * x[i] += sum of the partials in rank order, identical on every rank. kd_peer_init is collective over `comm` (it
+ * exchanges the IPC handles once); every rank must then make the same kd_peer_allreduce_add calls in the same order.
+ * n <= max_floats. A peer that does not arrive within the wait limit raises the kernel error flag (kc_status). */
+void *kd_peer_init(void *comm, int rank, int world, size_t max_floats);
+int kd_peer_allreduce_add(void *peer, float *x, const float *partial, size_t n);
+void kd_peer_free(void *peer);
+
 #ifdef __cplusplus
 }
 #endif

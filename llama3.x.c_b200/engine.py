@@ -93,6 +93,9 @@ DEVICE_SIGNATURES = {
     "kd_allreduce_max_u64": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_size_t]),
     "kd_allgather_f32": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
     "kd_comm_free": (None, [_c.c_void_p]),
+    "kd_peer_init": (_c.c_void_p, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_size_t]),
+    "kd_peer_allreduce_add": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
+    "kd_peer_free": (None, [_c.c_void_p]),
 }
 
 _engine = None

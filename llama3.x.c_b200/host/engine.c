@@ -60,6 +60,7 @@ typedef struct {
   unsigned long long *key_dev;
   int *staging; /* pinned: token uploads [max_batch], then the scalar uploads at staging + max_batch */
   void *stream, *comm;
+  void *peer; /* peer-memory all-reduce of the decode residual (kd_peer_*), or NULL for NCCL */
   void *graph_logits, *graph_greedy;
   unsigned long long graph_logits_kernels, graph_greedy_kernels; /* kernels captured in each graph */
   long long captured, replayed; /* launch-count corrections: captured calls do not run, replays bypass the count */
@@ -296,7 +297,16 @@ static int connect(Engine *e) {
   if (e->S == 1)
     return 0;
   e->comm = kd_comm_init(e->rank, e->S, tp_request.id);
-  return e->comm ? 0 : -1;
+  if (!e->comm)
+    return -1;
+  /* The decode step's two residual reductions per layer go through peer memory unless LLAMA_PEER_ALLREDUCE=0. */
+  const char *peer = getenv("LLAMA_PEER_ALLREDUCE");
+  if (!(peer && !strcmp(peer, "0"))) {
+    e->peer = kd_peer_init(e->comm, e->rank, e->S, (size_t)e->c.dim);
+    if (!e->peer)
+      return -1;
+  }
+  return 0;
 }
 
 static void publish(Model *model, Engine *e) {
@@ -635,6 +645,10 @@ void engine_init_random(Model *model, const Config *config, int group_size, unsi
 
 static void residual_reduce(Engine *e, int rows) {
   size_t n = (size_t)rows * e->c.dim;
+  if (rows == 1 && e->peer) {
+    kd_peer_allreduce_add(e->peer, e->x, e->partial, n);
+    return;
+  }
   kd_allreduce_sum_f32(e->comm, e->partial, n);
   k_add(e->x, e->partial, n);
 }
@@ -1099,6 +1113,7 @@ void engine_free(Model *model) {
   kd_host_free(e->logits_host);
   kd_host_free(e->batch_logits_host);
   kd_host_free(e->staging);
+  kd_peer_free(e->peer);
   kd_comm_free(e->comm);
   kernels_set_stream(NULL);
   kd_stream_free(e->stream);

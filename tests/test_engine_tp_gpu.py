@@ -24,8 +24,10 @@ from test_engine_gpu import same_tokens  # noqa: E402
 GOLDEN = np.load(HERE / "golden" / "engine_golden.npz")
 
 
-def _rank(rank, world, nccl_id, path, prompt, out):
+def _rank(rank, world, nccl_id, path, prompt, out, peer=True):
     try:
+        import os
+        os.environ["LLAMA_PEER_ALLREDUCE"] = "1" if peer else "0"
         from conftest import load_engine
         eng = load_engine()
         with eng.Engine.load(path, tp=(rank, world, rank, nccl_id)) as m:
@@ -36,12 +38,12 @@ def _rank(rank, world, nccl_id, path, prompt, out):
         out.put((rank, None, None, repr(e)))
 
 
-def run_ranks(world, path, prompt):
+def run_ranks(world, path, prompt, peer=True):
     from conftest import load_engine
     nccl_id = load_engine().comm_unique_id()
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nccl_id, str(path), prompt, out)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nccl_id, str(path), prompt, out, peer)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -63,12 +65,13 @@ def small(tmp_path_factory):
     return models.write_model(tmp_path_factory.mktemp("tp") / "small.bin", "small")
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_tensor_parallel_matches_reference_and_one_gpu(small, world):
+@pytest.mark.parametrize("world,peer", [(2, True), (4, True), (8, True), (2, False)])
+def test_tensor_parallel_matches_reference_and_one_gpu(small, world, peer):
+    """peer: the decode residual reduced through peer memory (kd_peer_allreduce_add, the default) or NCCL."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     prompt = GOLDEN["small_prompt"]
-    results = run_ranks(world, small, prompt)
+    results = run_ranks(world, small, prompt, peer)
     from conftest import load_engine
     eng = load_engine()
     with eng.Engine.load(small) as m:
