@@ -48,7 +48,12 @@ constexpr int kWeightStage = kTileRows * kChunk;
 constexpr int kFastGroups = kChunk / 64;            // groups of a full chunk at gs 64
 constexpr int kWarpGroups = kFastGroups / kDotWarps;  // ... of them per dot warp
 // Named barriers (0 is __syncthreads): T_FULL + b / T_EMPTY + b for the two chain buffers b.
-constexpr int kBarTFull = 1, kBarTEmpty = 3;
+#ifndef KC_GEMV_TBUF
+#define KC_GEMV_TBUF 2
+#endif
+constexpr int kTBuf = KC_GEMV_TBUF;  // chain buffers: how many stages the dot warps may run ahead of the chain warp
+constexpr int kBarTFull = 1, kBarTEmpty = 1 + kTBuf;
+static_assert(kTBuf >= 2 && kTBuf <= 4, "chain buffers");
 
 struct GemvSegDev {
   float *out;
@@ -149,20 +154,24 @@ template <int ID>
 __device__ __forceinline__ void bar_arrive_id() {
   asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(kThreads) : "memory");
 }
-// Barrier `base` or `base + 1`, picked by the stage's parity.
+// Barrier BASE + idx (idx < kTBuf), with the id an immediate in every branch.
 template <int BASE>
-__device__ __forceinline__ void bar_sync_named(int parity) {
-  if (parity)
-    bar_sync_id<BASE + 1>();
-  else
-    bar_sync_id<BASE>();
+__device__ __forceinline__ void bar_sync_named(int idx) {
+  switch (idx) {
+    case 0: bar_sync_id<BASE>(); break;
+    case 1: bar_sync_id<BASE + 1>(); break;
+    case 2: if (kTBuf > 2) bar_sync_id<BASE + (kTBuf > 2 ? 2 : 0)>(); break;
+    default: if (kTBuf > 3) bar_sync_id<BASE + (kTBuf > 3 ? 3 : 0)>(); break;
+  }
 }
 template <int BASE>
-__device__ __forceinline__ void bar_arrive_named(int parity) {
-  if (parity)
-    bar_arrive_id<BASE + 1>();
-  else
-    bar_arrive_id<BASE>();
+__device__ __forceinline__ void bar_arrive_named(int idx) {
+  switch (idx) {
+    case 0: bar_arrive_id<BASE>(); break;
+    case 1: bar_arrive_id<BASE + 1>(); break;
+    case 2: if (kTBuf > 2) bar_arrive_id<BASE + (kTBuf > 2 ? 2 : 0)>(); break;
+    default: if (kTBuf > 3) bar_arrive_id<BASE + (kTBuf > 3 ? 3 : 0)>(); break;
+  }
 }
 
 // Stage layout: the weights of one 32-row sub-tile (two 16-row halves, w1 then w3, for SwiGLU) as 8 K-blocks of
@@ -485,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
   volatile int *abort_flag = reinterpret_cast<int *>(tail + 8 * 8);
   volatile int *issued = reinterpret_cast<int *>(tail + 8 * 8 + 4);
   float *T = reinterpret_cast<float *>(tail + 128);
-  float *XS = T + 2 * gpc * kTileRows;
+  float *XS = T + kTBuf * gpc * kTileRows;
   int8_t *XQ = reinterpret_cast<int8_t *>(XS + ((n / gs + 3) & ~3));
 
   if (tid == 0) {
@@ -524,10 +533,10 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
       const Sub t = subtile(plan, sub);
       if (!*abort_flag && !mbar_wait_bounded(&bars[slot], phase))
         *abort_flag = 1;
-      if (i >= 2)
-        bar_sync_named<kBarTEmpty>(i & 1);
+      if (i >= kTBuf)
+        bar_sync_named<kBarTEmpty>(i % kTBuf);
       const uint8_t *buf = stages + slot * stage_bytes;
-      float *Tb = T + (i & 1) * gpc * kTileRows;
+      float *Tb = T + (i % kTBuf) * gpc * kTileRows;
       const int groups = min(gpc, (n - chunk * kChunk) / gs);
       if (lane_active(swiglu, lane, t.cnt)) {
         const int8_t *xrow = XQ + chunk * kChunk;
@@ -550,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
           }
         }
       }
-      bar_arrive_named<kBarTFull>(i & 1);
+      bar_arrive_named<kBarTFull>(i % kTBuf);
       if (++slot == depth)
         slot = 0, phase ^= 1u;
       if (++chunk == nchunks)
@@ -563,8 +572,8 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
     int nchunk = depth % nchunks, nsub = depth / nchunks;  // chunk and sub-tile of stage i + depth
     for (int i = 0; i < S; i++) {
       const Sub t = subtile(plan, sub);
-      bar_sync_named<kBarTFull>(i & 1);
-      const float *Tb = T + (i & 1) * gpc * kTileRows;
+      bar_sync_named<kBarTFull>(i % kTBuf);
+      const float *Tb = T + (i % kTBuf) * gpc * kTileRows;
       const float *wsr = reinterpret_cast<const float *>(stages + slot * stage_bytes + kWeightStage) + lane * gpc;
       const int groups = min(gpc, (n - chunk * kChunk) / gs);
       if (GS == 64 && groups == kFastGroups && lane_active(swiglu, lane, t.cnt)) {
@@ -620,8 +629,8 @@ __global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(c
       }
       if (++nchunk == nchunks)
         nchunk = 0, nsub++;
-      if (i + 2 < S)
-        bar_arrive_named<kBarTEmpty>(i & 1);
+      if (i + kTBuf < S)
+        bar_arrive_named<kBarTEmpty>(i % kTBuf);
       if (++slot == depth)
         slot = 0;
       if (++chunk == nchunks)
@@ -691,7 +700,7 @@ __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, Gem
 
 // act_floats: fp32 staging of the fused activation modes (n, or 2n with the norm weights).
 size_t smem_bytes(int n, int gs, int stage_bytes, int depth, int act_floats) {
-  return (size_t)depth * stage_bytes + 128 + (size_t)2 * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
+  return (size_t)depth * stage_bytes + 128 + (size_t)kTBuf * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
          (size_t)((n + 15) & ~15) + (size_t)act_floats * 4 + 1024;
 }
 

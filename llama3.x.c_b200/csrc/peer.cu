@@ -18,6 +18,7 @@
 // x[i] + (((p_0 + p_1) + p_2) + ...). Every rank computes the same sum in the same order, so the replicated residual
 // stays identical across ranks. Nothing here waits on another CTA of the same GPU.
 #include <cuda_runtime.h>
+#include <stdio.h>
 #include <string.h>
 
 #include "../../include/device_cuda.h"
@@ -99,11 +100,14 @@ struct PeerState {
   size_t max_floats;
 };
 
+// Set-up failures of the optional peer path (an IPC mapping the node does not allow, say) are reported on stderr
+// and leave the caller on NCCL; they do not go through the library's fail() policy.
 bool cuda_ok(cudaError_t e, const char *what) {
   if (e == cudaSuccess)
     return true;
   cudaGetLastError();
-  return kc_fail("%s: %s", what, cudaGetErrorString(e));
+  fprintf(stderr, "%s: %s (the peer-memory all-reduce is off; NCCL reduces instead)\n", what, cudaGetErrorString(e));
+  return false;
 }
 
 }  // namespace
@@ -144,26 +148,38 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
   cudaIpcMemHandle_t mine, all[kPeerMax];
   static_assert(sizeof(cudaIpcMemHandle_t) % sizeof(float) == 0, "IPC handle size");
   constexpr size_t hf = sizeof(cudaIpcMemHandle_t) / sizeof(float);
+  memset(&mine, 0, sizeof(mine));
   float *xchg = nullptr;
+  if (!cuda_ok(cudaMalloc(&xchg, (world + 1) * sizeof(cudaIpcMemHandle_t)), "kd_peer_init: cudaMalloc")) {
+    delete s;
+    return nullptr;
+  }
+  // Local set-up; a failure here still takes part in the exchange below (with an all-zero handle), so that no rank
+  // is left waiting in the collective. The engine then agrees on NCCL with the others.
   bool ok = cuda_ok(cudaMalloc(&s->base, recv_bytes), "kd_peer_init: cudaMalloc") &&
             cuda_ok(cudaMalloc(&s->args.epoch, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
             cuda_ok(cudaMemset(s->base, 0, recv_bytes), "kd_peer_init: cudaMemset") &&
             cuda_ok(cudaMemset(s->args.epoch, 0, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
             // Zeroed before any peer can learn the handle: a peer's first store lands after this.
             cuda_ok(cudaDeviceSynchronize(), "kd_peer_init: synchronize") &&
-            cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle") &&
-            cuda_ok(cudaMalloc(&xchg, (world + 1) * sizeof(cudaIpcMemHandle_t)), "kd_peer_init: cudaMalloc") &&
-            cuda_ok(cudaMemcpy(xchg + world * hf, &mine, sizeof(mine), cudaMemcpyHostToDevice), "kd_peer_init: copy");
+            cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle");
+  if (!ok)
+    memset(&mine, 0, sizeof(mine));
   // Every rank's handle to every rank, through the NCCL communicator (on the calling thread's stream).
-  ok = ok && kd_allgather_f32(comm, xchg + world * hf, xchg, hf) == 0 &&
-       cuda_ok(cudaStreamSynchronize(kc_stream()), "kd_peer_init: synchronize") &&
-       cuda_ok(cudaMemcpy(all, xchg, world * sizeof(cudaIpcMemHandle_t), cudaMemcpyDeviceToHost), "kd_peer_init: copy");
-  if (xchg)
-    cudaFree(xchg);
+  const bool exchanged =
+      cuda_ok(cudaMemcpy(xchg + world * hf, &mine, sizeof(mine), cudaMemcpyHostToDevice), "kd_peer_init: copy") &&
+      kd_allgather_f32(comm, xchg + world * hf, xchg, hf) == 0 &&  // NCCL failures do go through fail()
+      cuda_ok(cudaStreamSynchronize(kc_stream()), "kd_peer_init: synchronize") &&
+      cuda_ok(cudaMemcpy(all, xchg, world * sizeof(cudaIpcMemHandle_t), cudaMemcpyDeviceToHost), "kd_peer_init: copy");
+  cudaFree(xchg);
+  ok = ok && exchanged;
+  static const cudaIpcMemHandle_t none = {};
   for (int p = 0; ok && p < world; p++) {
     char *b = nullptr;
     if (p == rank) {
       b = static_cast<char *>(s->base);
+    } else if (!memcmp(&all[p], &none, sizeof(none))) {
+      ok = false;  // that rank's set-up failed
     } else {
       void *m = nullptr;
       ok = cuda_ok(cudaIpcOpenMemHandle(&m, all[p], cudaIpcMemLazyEnablePeerAccess), "kd_peer_init: cudaIpcOpenMemHandle");

@@ -293,20 +293,37 @@ static Engine *engine_create(Model *model) {
   return e;
 }
 
+/* 1 on every rank if every rank has its peer path, else 0 everywhere (the others release theirs). A max all-reduce of
+ * "this rank lacks it" over NCCL, through the engine's device scratch key. */
+static int agree_on_peer(Engine *e) {
+  unsigned long long lack = e->peer ? 0 : 1, *d = (unsigned long long *)kd_malloc(sizeof(lack));
+  if (!d)
+    return -1;
+  int rc = kd_copy(d, &lack, sizeof(lack)) || kd_allreduce_max_u64(e->comm, d, 1) || kd_copy(&lack, d, sizeof(lack)) ||
+           kd_sync();
+  kd_free(d);
+  if (rc)
+    return -1;
+  if (lack && e->peer) {
+    kd_peer_free(e->peer);
+    e->peer = NULL;
+  }
+  return 0;
+}
+
 static int connect(Engine *e) {
   if (e->S == 1)
     return 0;
   e->comm = kd_comm_init(e->rank, e->S, tp_request.id);
   if (!e->comm)
     return -1;
-  /* The decode step's two residual reductions per layer go through peer memory unless LLAMA_PEER_ALLREDUCE=0. */
+  /* The decode step's two residual reductions per layer go through peer memory unless LLAMA_PEER_ALLREDUCE=0, or the
+   * node does not allow the mapping (kd_peer_init says so on stderr and returns NULL): then NCCL reduces. Every rank
+   * takes the same path: a rank whose set-up failed tells the others through one small all-reduce. */
   const char *peer = getenv("LLAMA_PEER_ALLREDUCE");
-  if (!(peer && !strcmp(peer, "0"))) {
+  if (!(peer && !strcmp(peer, "0")))
     e->peer = kd_peer_init(e->comm, e->rank, e->S, (size_t)e->c.dim);
-    if (!e->peer)
-      return -1;
-  }
-  return 0;
+  return agree_on_peer(e);
 }
 
 static void publish(Model *model, Engine *e) {
