@@ -14,7 +14,9 @@
  * Weight layout is the checkpoint's: values row-major [rows][ld] int8 (ld a multiple of gs), scales [rows][ld / gs]
  * fp32. Weight values, weight scales and activations passed to the GEMV/GEMM must be 16-byte aligned, and ld / gs a
  * multiple of 4 (cudaMalloc'd buffers with the reference's shapes satisfy this). The supported group sizes are the
- * powers of two 16..256 (the checkpoints use 64); W8A32 inputs (K8Input.q == NULL) are refused. */
+ * powers of two 16..256 (the checkpoints use 64); other group sizes take a slower general kernel.
+ * W8A32 (K8Input.q == NULL, fp32 activations in f) runs on every k_matmul_q8* entry point, bitwise the reference's
+ * AVX-512 kernel (dots_q8f_body, src/gemv.c:141-180) when gs % 16 == 0 and its portable loop otherwise. */
 #ifndef LLAMA3X_KERNELS_CUDA_H
 #define LLAMA3X_KERNELS_CUDA_H
 

@@ -215,6 +215,9 @@ def k_quantize_rows(q, s, x, ldx, m, n, gs):
 
 
 def _input(xq, xs):
+    """K8Input: int8 values xq and scales xs (W8A8), or fp32 activations in xq with xs None (W8A32: q NULL, f set)."""
+    if xs is None and xq is not None and str(getattr(xq, "dtype", "")) in ("torch.float32", "float32"):
+        return K8Input(None, None, _ptr(xq))
     return K8Input(_ptr(xq), _ptr(xs), None)
 
 

@@ -140,9 +140,16 @@ void k_quantize(int8_t *q, float *s, const float *x, int n, int gs) { k_quantize
 
 // ---- decode GEMV --------------------------------------------------------------------------------------------------
 
+// W8A8 input (q, s) or, with q NULL, W8A32 (f), as the reference's K8Input (include/kernels.h:101-109).
+static bool gemv_input_ok(const char *name, const K8Input *x) {
+  if (!x || (x->q ? !x->s : !x->f))
+    return kc_fail("%s: the input needs int8 values and scales, or (W8A32) fp32 activations", name);
+  return true;
+}
+
 static bool gemv_shape_ok(const char *name, const K8Input *x, size_t ld, int n, int gs) {
-  if (!x || !x->q || !x->s)
-    return kc_fail("%s: W8A32 activations (K8Input.q == NULL) are not supported by the sm_100a backend", name);
+  if (!gemv_input_ok(name, x))
+    return false;
   if (gs <= 0)
     return kc_fail("%s: invalid group size %d", name, gs);
   if (n < 0 || n % gs)
@@ -170,6 +177,10 @@ static void gemv(const char *name, const KcGemvSeg *segs, int nseg, const K8Inpu
     if (!weight_ok(name, K8Weight{segs[i].wq, segs[i].ws}) ||
         (kind == KC_SWIGLU && !weight_ok(name, K8Weight{segs[i].w3q, segs[i].w3s})))
       return;
+  }
+  if (!x->q) {  // W8A32
+    launched(kc_launch_gemv_w8a32(segs, nseg, x->f, n, (long long)ld, gs, kind, tl_stream), name);
+    return;
   }
   launched(kc_launch_gemv(segs, nseg, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
 }
@@ -293,6 +304,10 @@ void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Se
   int kind = -1;
   if (!gemv_shape_ok(name, x, ld, n, gs) || !gemv_segments(name, segments, count, segs, &kind))
     return;
+  if (!x->q) {
+    kc_fail("%s: a tail GEMV needs int8 activations (W8A8)", name);
+    return;
+  }
   if (!tail) {
     kc_fail("%s: missing tail", name);
     return;

@@ -715,6 +715,77 @@ bool encode_weight(CUtensorMap *wmap, CUtensorMap *smap, const int8_t *wq, const
 
 }  // namespace
 
+// W8A32 (K8Input.q NULL: fp32 activations x against the int8 weights), bitwise the reference on both of its paths.
+// AVX (gs % 16 == 0): its AVX-512 kernel dots_q8f_body (src/gemv.c:141-180). Each of the 16 vector lanes is a lane of
+// a half-warp, one output row per half-warp: lane l sums columns c + l into ga and c + 16 + l into gb over each
+// 32-column step of a group (a last 16 columns, when gs % 32 == 16, into ga), then acc = fma(ga + gb, ws[g], acc); the
+// row is the 16 accumulators reduced in _mm512_reduce_add_ps's tree (pairs 8, 4, 2, 1 lanes apart).
+// Otherwise: its portable loop (src/gemv.c:427-436), one thread per row: per group the products added in column order,
+// then val += group * ws, no fused multiply-add.
+// For SwiGLU each row is computed for w1 and for w3 and combined with silu_gate. The activations are read through the
+// read-only cache: every row of the CTA reads the same ones.
+template <bool AVX>
+__global__ void __launch_bounds__(256) gemv_q8f_kernel(GemvSegDev s0, GemvSegDev s1, GemvSegDev s2,
+                                                        const int8_t *wq0, const int8_t *wq1, const int8_t *wq2,
+                                                        const float *ws0, const float *ws1, const float *ws2,
+                                                        const int8_t *w3q, const float *w3s, int nseg, const float *x,
+                                                        int n, long long ld, int gs, int kind, int units) {
+  pdl_wait();
+  const int per_cta = AVX ? (int)blockDim.x / 16 : (int)blockDim.x;
+  const int l = AVX ? (int)(threadIdx.x & 15) : 0;
+  const int unit = blockIdx.x * per_cta + (AVX ? (int)(threadIdx.x >> 4) : (int)threadIdx.x);
+  if (!AVX && unit >= units)
+    return;
+  const int u = unit < units ? unit : units - 1;  // AVX: a half-warp past the end computes a real row, stores nothing
+  int s = (nseg > 1 && u >= s1.unit0) ? 1 : 0;
+  if (nseg > 2 && u >= s2.unit0)
+    s = 2;
+  const GemvSegDev seg = s == 0 ? s0 : s == 1 ? s1 : s2;
+  const long long row = u - seg.unit0, sld = ld / gs;
+  const int groups = n / gs;
+  float res[2] = {0.0f, 0.0f};
+  for (int pass = 0; pass < (kind == KC_SWIGLU ? 2 : 1); pass++) {
+    const int8_t *w = (pass ? w3q : s == 0 ? wq0 : s == 1 ? wq1 : wq2) + row * ld;
+    const float *sc = (pass ? w3s : s == 0 ? ws0 : s == 1 ? ws1 : ws2) + row * sld;
+    float acc = 0.0f;
+    if (AVX) {
+      for (int g = 0; g < groups; g++) {
+        const long long b = (long long)g * gs;
+        float ga = 0.0f, gb = 0.0f;
+        int c = 0;
+        for (; c + 32 <= gs; c += 32) {
+          ga = __fmaf_rn((float)w[b + c + l], __ldg(x + b + c + l), ga);
+          gb = __fmaf_rn((float)w[b + c + 16 + l], __ldg(x + b + c + 16 + l), gb);
+        }
+        for (; c < gs; c += 16)
+          ga = __fmaf_rn((float)w[b + c + l], __ldg(x + b + c + l), ga);
+        acc = __fmaf_rn(__fadd_rn(ga, gb), __ldg(sc + g), acc);
+      }
+#pragma unroll
+      for (int o = 8; o; o >>= 1)
+        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, o, 16));
+    } else {
+      for (int g = 0; g < groups; g++) {
+        const long long b = (long long)g * gs;
+        float group = 0.0f;
+        for (int k = 0; k < gs; k++)
+          group = __fadd_rn(group, __fmul_rn((float)w[b + k], __ldg(x + b + k)));
+        acc = __fadd_rn(acc, __fmul_rn(group, __ldg(sc + g)));
+      }
+    }
+    res[pass] = acc;
+  }
+  if (unit < units && l == 0) {
+    float *out = seg.out + row;
+    if (kind == KC_SWIGLU)
+      *out = silu_gate_dev(res[0], res[1]);
+    else if (kind == KC_ADD)
+      *out = __fadd_rn(*out, res[0]);
+    else
+      *out = res[0];
+  }
+}
+
 static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, int n, long long ld,
                           int gs, int kind, cudaStream_t stream) {
   GemvSegDev d[3] = {};
@@ -737,6 +808,31 @@ static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, con
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
                       long long ld, int gs, int kind, cudaStream_t stream, int grid_limit,
                       const KcGemvTail *tail = nullptr);
+
+// The W8A32 GEMV (see gemv_q8f_kernel): 16 rows per 256-thread CTA on the AVX order, 256 on the portable one.
+int kc_launch_gemv_w8a32(const KcGemvSeg *segs, int nseg, const float *x, int n, long long ld, int gs, int kind,
+                         cudaStream_t stream) {
+  GemvSegDev d[3] = {};
+  const int8_t *wq[3] = {};
+  const float *ws[3] = {};
+  int units = 0;
+  for (int s = 0; s < nseg; s++) {
+    d[s].out = segs[s].out, d[s].d = segs[s].d, d[s].unit0 = units;
+    wq[s] = segs[s].wq, ws[s] = segs[s].ws;
+    units += segs[s].d;
+  }
+  if (units == 0 || n == 0)
+    return 0;
+  if (gs % 16 == 0)
+    gemv_q8f_kernel<true><<<(units + 15) / 16, 256, 0, stream>>>(d[0], d[1], d[2], wq[0], wq[1], wq[2], ws[0], ws[1],
+                                                                 ws[2], segs[0].w3q, segs[0].w3s, nseg, x, n, ld, gs,
+                                                                 kind, units);
+  else
+    gemv_q8f_kernel<false><<<(units + 255) / 256, 256, 0, stream>>>(d[0], d[1], d[2], wq[0], wq[1], wq[2], ws[0],
+                                                                    ws[1], ws[2], segs[0].w3q, segs[0].w3s, nseg, x, n,
+                                                                    ld, gs, kind, units);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
 
 // Host launcher (argument validation is the C-ABI layer's job): the TMA kernel where the shape allows it, else the
 // general rung.

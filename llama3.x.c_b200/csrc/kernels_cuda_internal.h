@@ -85,6 +85,9 @@ struct KcGemvAct {
   const float *norm;
   float eps;
 };
+// W8A32: fp32 activations against int8 weights, the reference's orders (0, or -2 on a launch error).
+int kc_launch_gemv_w8a32(const KcGemvSeg *segs, int nseg, const float *x, int n, long long ld, int gs, int kind,
+                         cudaStream_t stream);
 int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, int n, long long ld, int gs, int kind,
                        cudaStream_t stream, const struct KcGemvTail *tail = nullptr);
 

@@ -61,6 +61,8 @@ typedef struct {
   int *staging; /* pinned: token uploads [max_batch], then the scalar uploads at staging + max_batch */
   void *stream, *comm;
   void *peer; /* peer-memory all-reduce of the decode residual (kd_peer_*), or NULL for NCCL */
+  int w8a32;  /* LLAMA_Q8_ACTIVATIONS=fp32: fp32 activations against the int8 weights, one row per forward */
+  float *xb;  /* W8A32: the normalized row the projections read */
   void *graph_logits, *graph_greedy;
   unsigned long long graph_logits_kernels, graph_greedy_kernels; /* kernels captured in each graph */
   long long captured, replayed; /* launch-count corrections: captured calls do not run, replays bypass the count */
@@ -69,7 +71,8 @@ typedef struct {
   EngineStats stats;
 } Engine;
 
-static int last_gs; /* engine_group_size: the group size of the last model set up */
+static int last_gs;    /* engine_group_size: the group size of the last model set up */
+static int last_w8a32; /* engine_precision: whether that model runs W8A32 */
 
 static struct {
   int rank, world, device, set;
@@ -222,6 +225,17 @@ static int prefill_batch_from_env(int context) {
   return count < context ? (int)count : context;
 }
 
+/* LLAMA_Q8_ACTIVATIONS as the reference reads it (src/engine.c:132-135): int8 (the default, W8A8) or fp32 (W8A32). */
+static int activations_from_env(void) {
+  const char *a = getenv("LLAMA_Q8_ACTIVATIONS");
+  if (a && *a && strcmp(a, "int8") && strcmp(a, "fp32"))
+    return efail("LLAMA_Q8_ACTIVATIONS must be int8 or fp32");
+  return a && !strcmp(a, "fp32");
+}
+
+/* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. */
+static int max_batch_for(const Engine *e) { return e->w8a32 ? 1 : prefill_batch_from_env(e->context); }
+
 /* Device buffers sized for the context and the batch. */
 static int allocate_state(Engine *e) {
   const Config *p = &e->c;
@@ -242,6 +256,7 @@ static int allocate_state(Engine *e) {
   e->as = dev_alloc(B * (e->ql / e->gs) * sizeof(float));
   e->hq = dev_alloc(B * e->hid_l);
   e->hs = dev_alloc(B * (e->hid_l / e->gs) * sizeof(float));
+  e->xb = e->w8a32 ? dev_alloc(B * dim * sizeof(float)) : NULL;
   e->logits_dev = dev_alloc((size_t)e->vmax * sizeof(float));
   e->gather_dev = e->S > 1 ? dev_alloc((size_t)e->vmax * e->S * sizeof(float)) : NULL;
   e->logits_host = kd_host_alloc((size_t)p->vocab_size * sizeof(float));
@@ -328,6 +343,7 @@ static int connect(Engine *e) {
 
 static void publish(Model *model, Engine *e) {
   last_gs = e->gs;
+  last_w8a32 = e->w8a32;
   e->launches_base = kc_launch_count();
   model->config = e->c;
   model->max_batch = e->max_batch;
@@ -567,8 +583,8 @@ void engine_load_context(Model *model, const char *path, int context) {
   e->context = context ? context : (p.seq_len < DEFAULT_CONTEXT_CAP ? p.seq_len : DEFAULT_CONTEXT_CAP);
   e->c.seq_len = e->context;
   model->file_bytes = bytes;
-  if (plan(e) || (e->max_batch = prefill_batch_from_env(e->context)) < 0 || connect(e) || allocate_state(e) ||
-      load_weights(e, base, bytes)) {
+  if ((e->w8a32 = activations_from_env()) < 0 || plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) ||
+      allocate_state(e) || load_weights(e, base, bytes)) {
     munmap(base, bytes);
     engine_free(model);
     return;
@@ -601,7 +617,8 @@ void engine_init_random(Model *model, const Config *config, int group_size, unsi
   e->gs = group_size;
   e->context = context ? context : p.seq_len;
   e->c.seq_len = e->context;
-  if (plan(e) || (e->max_batch = prefill_batch_from_env(e->context)) < 0 || connect(e) || allocate_state(e)) {
+  if ((e->w8a32 = activations_from_env()) < 0 || plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) ||
+      allocate_state(e)) {
     engine_free(model);
     return;
   }
@@ -675,11 +692,46 @@ static GemmQ8Segment segment(float *c, int ldc, Q8 w, Q8 w3, int n, GemmKind kin
   return g;
 }
 
+/* The W8A32 token (forward_q8 with fp32 activations, src/tp.c:379-436): every projection reads the fp32 vector itself
+ * (the normalized row, the attention output, the SwiGLU output), nothing is quantized. */
+static void decode_layers_w8a32(Engine *e) {
+  const Config *p = &e->c;
+  int dim = p->dim, gs = e->gs;
+  K8Input xin = {NULL, NULL, e->xb}, ain = {NULL, NULL, e->att}, hin = {NULL, NULL, e->hb};
+  k_embed_q8_rows(e->x, e->tokens_dev, k8(e->embed), 1, dim, gs, p->vocab_size);
+  for (int l = 0; l < p->n_layers; l++) {
+    Layer *y = &e->layers[l];
+    float *kc = e->key_cache + (size_t)l * e->layer_kv, *vc = e->value_cache + (size_t)l * e->layer_kv;
+    k_rmsnorm(e->xb, e->x, y->rms_att, dim, p->norm_eps);
+    k_matmul_q8_qkv(e->q, e->k, e->v, &xin, k8(y->wq), k8(y->wk), k8(y->wv), dim, e->ql, e->kvl, gs);
+    k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
+                         e->context);
+    k_attention_q8_rows(e->att, NULL, NULL, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
+                        1, gs);
+    K8Weight wo = k8(y->wo), w2 = k8(y->w2);
+    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &ain, &wo, e->ql, e->ql, dim, gs, e->S == 1 ? K_ADD : K_PARTIAL);
+    if (e->S > 1)
+      residual_reduce(e, 1);
+    k_rmsnorm(e->xb, e->x, y->rms_ffn, dim, p->norm_eps);
+    k_matmul_q8_swiglu(e->hb, &xin, k8(y->w1), k8(y->w3), dim, e->hid_l, gs);
+    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &hin, &w2, e->hid_l, e->hid_l, dim, gs,
+                   e->S == 1 ? K_ADD : K_PARTIAL);
+    if (e->S > 1)
+      residual_reduce(e, 1);
+  }
+  k_rmsnorm(e->xb, e->x, e->rms_final, dim, p->norm_eps);
+  k_matmul_q8(e->logits_dev, &xin, k8(e->cls), dim, e->vl, gs);
+}
+
 /* One token at the position in e->pos_dev (device), its id in e->tokens_dev[0]: everything up to the local logits.
  * The RMSNorm + quantize before QKV, W1/W3 and the classifier run inside those GEMVs (k_matmul_q8_fused), and the
  * SwiGLU GEMV quantizes its own output for W2 (K_TAIL_QUANTIZE_OUTPUT): bitwise the separate kernels the batched
  * path uses. */
 static void decode_layers(Engine *e) {
+  if (e->w8a32) {
+    decode_layers_w8a32(e);
+    return;
+  }
   const Config *p = &e->c;
   int dim = p->dim, gs = e->gs;
   Q8 none = {NULL, NULL};
@@ -865,6 +917,17 @@ static int prefill(Engine *e, const int *tokens, int count, int pos0, LogitsWant
   kernels_set_stream(e->stream);
   if (kd_sync()) /* the previous chunk's upload may still be queued on the stream */
     return -1;
+  if (e->w8a32) {
+    /* W8A32 prefills one row per call (count == 1 == max_batch) through the decode step, as the reference runs it
+     * per token; the step leaves that row's logits in logits_dev. Its own staging slots: engine_generate writes
+     * staging[max_batch..+1] right after the last of these calls, while the copies below may still be queued. */
+    int *scalars = e->staging + e->max_batch + 2;
+    scalars[0] = tokens[0];
+    scalars[1] = pos0;
+    kd_copy(e->tokens_dev, &scalars[0], sizeof(int));
+    kd_copy(e->pos_dev, &scalars[1], sizeof(int));
+    return run_step(e, &e->graph_logits, &e->graph_logits_kernels, decode_logits_step) || failed() ? -1 : 0;
+  }
   memcpy(e->staging, tokens, (size_t)count * sizeof(int));
   kd_copy(e->tokens_dev, e->staging, (size_t)count * sizeof(int));
   prefill_layers(e, count, pos0);
@@ -896,7 +959,10 @@ float *engine_forward_batch(Model *model, const int *tokens, int count, int pos0
         return NULL;
     }
     /* Per row as the reference (src/tp.c:608-621); rows are classified as one GEMM, bitwise the per-row GEMV. */
-    classify_rows(e, 0, count, e->batch_logits_dev);
+    if (e->w8a32)  /* the one row's local logits, from the decode step */
+      kd_copy(e->batch_logits_dev, e->logits_dev, (size_t)e->vl * sizeof(float));
+    else
+      classify_rows(e, 0, count, e->batch_logits_dev);
     for (int i = 0; i < count; i++) {
       const float *row = e->batch_logits_dev + (size_t)i * e->vl;
       if (e->S > 1) {
@@ -980,7 +1046,7 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
 /* ---- misc ---------------------------------------------------------------------------------------------------------- */
 
 int engine_max_batch(const Model *model) { return model->max_batch; }
-const char *engine_precision(void) { return "int8"; }
+const char *engine_precision(void) { return last_w8a32 ? "int8_q8_0_w8a32" : "int8_q8_0"; }
 int engine_group_size(void) { return last_gs; }
 
 void engine_stats(Model *model, EngineStats *out) {
@@ -1115,7 +1181,7 @@ void engine_free(Model *model) {
   kd_free(e->value_cache);
   kd_free(e->rope);
   float *bufs[] = {e->x, e->q, e->k, e->v, e->att, e->hb, e->partial, e->xs, e->as, e->hs, e->logits_dev,
-                   e->gather_dev, e->batch_logits_dev};
+                   e->gather_dev, e->batch_logits_dev, e->xb};
   for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++)
     kd_free(bufs[i]);
   kd_free(e->xq);

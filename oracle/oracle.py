@@ -48,6 +48,9 @@ def lib():
         L.orc_quantize_rows.restype = ctypes.c_int
         L.orc_group_dots.argtypes = [_i32p, _i8p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i8p, ctypes.c_size_t,
                                      ctypes.c_int]
+        for name in ("orc_gemv_f32_avx512_order", "orc_gemv_f32_scalar"):
+            getattr(L, name).argtypes = [_f32p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int]
         L.orc_gemv_scalar.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int]
         L.orc_gemm_amx_order.argtypes = [_f32p, ctypes.c_int, _i8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -97,6 +100,19 @@ def gemv_scalar(xq, xs, wq, ws, gs):
     out = np.empty(d, np.float32)
     lib().orc_gemv_scalar(_p(out, _f32p), _p(xq, _i8p), _p(xs, _f32p), _p(wq, _i8p), _p(ws, _f32p), ld, xq.shape[-1],
                           d, gs)
+    return out
+
+
+def gemv_f32(x, wq, ws, gs):
+    """W8A32 (fp32 activations): the reference's AVX-512 order (dots_q8f_body, src/gemv.c:141-180) when gs % 16 == 0,
+    else its portable loop (src/gemv.c:427-436); one activation row, d rows of weights."""
+    x = np.ascontiguousarray(x, np.float32)
+    wq = np.ascontiguousarray(wq, np.int8)
+    ws = np.ascontiguousarray(ws, np.float32)
+    d, ld = wq.shape
+    out = np.empty(d, np.float32)
+    f = lib().orc_gemv_f32_avx512_order if gs % 16 == 0 else lib().orc_gemv_f32_scalar
+    f(_p(out, _f32p), _p(x, _f32p), _p(wq, _i8p), _p(ws, _f32p), ld, x.shape[-1], d, gs)
     return out
 
 
@@ -232,6 +248,21 @@ def ref_gemv(xq, xs, wq, ws, gs, isa=KERNELS_SCALAR):
         raise RuntimeError("instruction set unavailable")
     inp = K8Input(_p(xq, _i8p), _p(xs, _f32p), None)
     ref().k_matmul_q8(_p(out, _f32p), ctypes.byref(inp), K8Weight(_p(wq, _i8p), _p(ws, _f32p)), n, d, gs)
+    return out
+
+
+def ref_gemv_f32(x, wq, ws, gs, isa=KERNELS_AVX512):
+    """The reference's k_matmul_q8 on fp32 activations (W8A32: K8Input.q NULL, f = x)."""
+    x = np.ascontiguousarray(x, np.float32)
+    wq = np.ascontiguousarray(wq, np.int8)
+    ws = np.ascontiguousarray(ws, np.float32)
+    d, n = wq.shape
+    out = np.empty(d, np.float32)
+    if not ref_select(isa):
+        raise RuntimeError("instruction set unavailable")
+    inp = K8Input(None, None, _p(x, _f32p))
+    ref().k_matmul_q8(_p(out, _f32p), ctypes.byref(inp), K8Weight(_p(wq, _i8p), _p(ws, _f32p)), n, d, gs)
+    ref_select(KERNELS_SCALAR)
     return out
 
 

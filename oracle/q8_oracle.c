@@ -134,6 +134,59 @@ static float reduce16(const float *a) {
   return t2[0] + t2[1];
 }
 
+void orc_gemv_f32_avx512_order(float *out, const float *x, const int8_t *wq, const float *ws, size_t ld, int n, int d,
+                               int gs) {
+  /* W8A32 (fp32 activations), dots_q8f_body (src/gemv.c:141-180), the reference's path when gs % 16 == 0: per row 16
+   * lanes; per group two lane sums ga (columns c + l) and gb (c + 16 + l) over 32-column steps, a 16-column tail into
+   * ga, then acc[l] = fma(ga[l] + gb[l], ws[g], acc[l]); the row is the 16 lanes reduced as _mm512_reduce_add_ps. */
+  size_t scale_ld = ld / (size_t)gs;
+  for (int r = 0; r < d; r++) {
+    const int8_t *w = wq + (size_t)r * ld;
+    const float *sc = ws + (size_t)r * scale_ld;
+    float acc[16];
+    memset(acc, 0, sizeof(acc));
+    for (int g = 0; g < n / gs; g++) {
+      float ga[16], gb[16];
+      memset(ga, 0, sizeof(ga));
+      memset(gb, 0, sizeof(gb));
+      int c = 0;
+      for (; c + 32 <= gs; c += 32) {
+        size_t off = (size_t)g * gs + c;
+        for (int l = 0; l < 16; l++) {
+          ga[l] = fmaf((float)w[off + l], x[off + l], ga[l]);
+          gb[l] = fmaf((float)w[off + 16 + l], x[off + 16 + l], gb[l]);
+        }
+      }
+      for (; c < gs; c += 16) {
+        size_t off = (size_t)g * gs + c;
+        for (int l = 0; l < 16; l++)
+          ga[l] = fmaf((float)w[off + l], x[off + l], ga[l]);
+      }
+      for (int l = 0; l < 16; l++)
+        acc[l] = fmaf(ga[l] + gb[l], sc[g], acc[l]);
+    }
+    out[r] = reduce16(acc);
+  }
+}
+
+void orc_gemv_f32_scalar(float *out, const float *x, const int8_t *wq, const float *ws, size_t ld, int n, int d,
+                         int gs) {
+  /* W8A32 on q8_dots' portable loop (src/gemv.c:427-436): per group the products summed in column order, then
+   * val += group * ws (no fused multiply-add: the reference builds without -march). */
+  size_t scale_ld = ld / (size_t)gs;
+  for (int r = 0; r < d; r++) {
+    const int8_t *w = wq + (size_t)r * ld;
+    float val = 0.0f;
+    for (int j = 0; j <= n - gs; j += gs) {
+      float group = 0.0f;
+      for (int k = 0; k < gs; k++)
+        group += (float)w[j + k] * x[j + k];
+      val += group * ws[(size_t)r * scale_ld + j / gs];
+    }
+    out[r] = val;
+  }
+}
+
 void orc_rmsnorm_avx512_order(float *o, const float *x, const float *w, int size, float eps) {
   /* src/kernels_simd.c:136-161 */
   float a[4][16];

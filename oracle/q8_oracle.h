@@ -40,6 +40,10 @@ void orc_gemm_amx_order(float *c, int ldc, const int8_t *xq, const float *xs, in
                         const float *ws, const int8_t *w3q, const float *w3s, size_t ldw, int n, int kind);
 
 /* silu_gate (src/gemv.c:246-250). */
+/* W8A32 GEMV (fp32 activations x, int8 weights): the reference's AVX-512 order (gs % 16 == 0) and its portable loop. */
+void orc_gemv_f32_avx512_order(float *out, const float *x, const int8_t *wq, const float *ws, size_t ld, int n, int d,
+                               int gs);
+void orc_gemv_f32_scalar(float *out, const float *x, const int8_t *wq, const float *ws, size_t ld, int n, int d, int gs);
 float orc_silu_gate(float value, float gate);
 
 /* rmsnorm_eps, the scalar order (src/kernels.c:8-21). */

@@ -11,6 +11,7 @@ Cases (all small; numpy PCG64 seeds below):
   amx_*           k_gemm_q8 on the AMX-INT8 backend (amx_q8_chunk, src/gemm.c:554-610) + its exact int32 group dots
                   (k_gemm_q8_amx_dots_test)
   rms_*           k_rmsnorm on the AVX-512 ISA (src/kernels_simd.c:136-161) and the scalar one (src/kernels.c:8-21)
+  gemvf_*         k_matmul_q8 on fp32 activations (W8A32), AVX-512 ISA for gs % 16 == 0, else scalar
 """
 import sys
 from pathlib import Path
@@ -68,6 +69,14 @@ def main():
         out.update({f"rms_{n}_x": x, f"rms_{n}_w": w,
                     f"rms_{n}_avx512": O.ref_rmsnorm(x, w, 1e-5, O.KERNELS_AVX512),
                     f"rms_{n}_scalar": O.ref_rmsnorm(x, w, 1e-5, O.KERNELS_SCALAR)})
+    # W8A32 (fp32 activations, K8Input.q NULL): k_matmul_q8 on the AVX-512 ISA (dots_q8f_body, src/gemv.c:141-180)
+    # for gs % 16 == 0, else the portable loop (src/gemv.c:427-436).
+    for d, n, gs in [(37, 1024, 64), (16, 512, 32), (20, 256, 16), (9, 384, 128), (8, 96, 48), (6, 40, 2)]:
+        wq, ws = O.seeded_q8_matrix(d, n, gs, seed=d + n)
+        x = (rng.standard_normal(n) * rng.uniform(0.1, 5)).astype(np.float32)
+        isa = O.KERNELS_AVX512 if gs % 16 == 0 else O.KERNELS_SCALAR
+        key = f"gemvf_{d}_{n}_{gs}"
+        out.update({key + "_wq": wq, key + "_ws": ws, key + "_x": x, key + "_y": O.ref_gemv_f32(x, wq, ws, gs, isa)})
     path = Path(__file__).with_name("q8_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({path.stat().st_size} bytes, {len(out)} arrays)")

@@ -55,7 +55,7 @@ def test_engine_precision_and_layouts():
     from conftest import load_engine
     eng = load_engine()
     lib = eng.load_library()
-    assert lib.engine_precision() == b"int8"
+    assert lib.engine_precision() == b"int8_q8_0"  # the reference's name (src/engine.c:191-195) before any W8A32 load
     # Config and Model keep the reference's x86-64 layout (include/runtime.h:9-17, 86-97): format at byte 28, name at
     # 88, Config 216 bytes, Model.implementation at 216, Model 272 bytes.
     assert eng.Config.format.offset == 28 and eng.Config.name.offset == 88 and ctypes.sizeof(eng.Config) == 216

@@ -81,6 +81,32 @@ def test_logits_match_reference_at_stable_positions(eng, files, name):
         assert close(m.forward_batch(p, 0, eng.LOGITS_LAST), GOLDEN[f"{name}_batch"])
 
 
+@pytest.mark.parametrize("name", ["tiny", "small"])
+def test_w8a32_matches_reference(eng, files, name, monkeypatch):
+    """LLAMA_Q8_ACTIVATIONS=fp32 (W8A32: every projection reads fp32 activations, nothing is quantized; one row per
+    forward): the reference's W8A32 logits at its stable positions (1e-5 of the largest |logit|) and its greedy tokens
+    over its W8A32 horizon (same near-tie rule), the reference's precision name and batch size."""
+    monkeypatch.setenv("LLAMA_Q8_ACTIVATIONS", "fp32")
+    stable = int(GOLDEN[f"{name}_w8a32_stable"])
+    p = GOLDEN[f"{name}_prompt"]
+    with eng.Engine.load(files[name]) as m:
+        assert eng.load_library().engine_precision() == b"int8_q8_0_w8a32"
+        assert m.model.max_batch == 1
+        for i, t in enumerate(p[:stable]):
+            assert close(m.forward(t, i), GOLDEN[f"{name}_w8a32_logits"][i]), f"position {i}"
+        assert close(m.forward_batch(p[stable - 1:stable], stable - 1, eng.LOGITS_ALL)[0],
+                     GOLDEN[f"{name}_w8a32_logits"][stable - 1])
+    with eng.Engine.load(files[name]) as m:
+        tokens = m.generate(p, 64)
+    want = GOLDEN[f"{name}_w8a32_generate"].tolist()
+    horizon = int(GOLDEN[f"{name}_w8a32_horizon"])
+    first = next((i for i, (a, b) in enumerate(zip(tokens, want)) if a != b), min(len(tokens), len(want)))
+    assert first >= horizon or GOLDEN[f"{name}_w8a32_margin"][first] < NEAR_TIE, (first, horizon)
+    monkeypatch.setenv("LLAMA_Q8_ACTIVATIONS", "bf16")
+    with pytest.raises(eng._kc().KernelError, match="LLAMA_Q8_ACTIVATIONS must be int8 or fp32"):
+        eng.Engine.load(files[name])
+
+
 @pytest.mark.parametrize("name", ["tiny", "wide"])
 def test_batch_rows_match_single_positions(eng, files, name):
     """A batched prefill (flash attention) against the same positions forwarded one at a time (split-K attention): the

@@ -188,6 +188,66 @@ def test_gemv_swiglu(kc, oracle, d, n):
     assert ulp_diff(host(out), ref).max() <= 2
 
 
+# ---- W8A32 (K8Input.q NULL, fp32 activations): the reference's AVX-512 order (gs % 16 == 0) and portable loop ----
+W8A32_SHAPES = [(37, 1024, 64), (16, 512, 32), (20, 256, 16), (9, 384, 128), (8, 96, 48), (6, 40, 2),
+                (4096, 4096, 64), (33, 14336, 64), (1000, 2048, 256), (3, 64, 8)]
+
+
+@pytest.mark.parametrize("d,n,gs", W8A32_SHAPES)
+def test_w8a32_gemv_bitwise(kc, oracle, d, n, gs):
+    wq, ws = oracle.seeded_q8_matrix(d, n, gs, d + 3 * n)
+    x = (np.random.default_rng(d).standard_normal(n) * 2).astype(np.float32)
+    y = kc.gemv(dev(x), None, dev(wq), dev(ws), gs)
+    kc.status()
+    assert (bits(host(y)) == bits(oracle.gemv_f32(x, wq, ws, gs))).all()
+
+
+def test_w8a32_golden(kc):
+    """The reference's own W8A32 outputs (tests/golden/q8_golden.npz, gemvf_*), bitwise."""
+    keys = sorted({k[:-2] for k in GOLDEN.files if k.startswith("gemvf_") and k.endswith("_y")})
+    assert keys
+    for k in keys:
+        gs = int(k.split("_")[-1])
+        y = kc.gemv(dev(GOLDEN[k + "_x"]), None, dev(GOLDEN[k + "_wq"]), dev(GOLDEN[k + "_ws"]), gs)
+        kc.status()
+        assert (bits(host(y)) == bits(GOLDEN[k + "_y"])).all(), k
+
+
+@pytest.mark.parametrize("gs", [64, 8])
+def test_w8a32_epilogues(kc, oracle, gs):
+    """ADD, PARTIAL on a column slice with a row stride, three QKV segments and SwiGLU, on fp32 activations."""
+    rng = np.random.default_rng(gs)
+    d, n = 96, 512
+    wq, ws = oracle.seeded_q8_matrix(d, n, gs, 41)
+    x = rng.standard_normal(n).astype(np.float32)
+    base = rng.standard_normal(d).astype(np.float32)
+    out = dev(base)
+    kc.gemv(dev(x), None, dev(wq), dev(ws), gs, kind=kc.K_ADD, out=out)
+    kc.status()
+    assert (bits(host(out)) == bits(base + oracle.gemv_f32(x, wq, ws, gs))).all()
+    # Column slice [col0, col0 + m) of rows with stride ld.
+    col0, m = 128, 256
+    part = torch.zeros(d, device="cuda")
+    wt, st = dev(wq), dev(ws)
+    kc.k_matmul_q8_ld(part, dev(x[col0:col0 + m]), None, wt[:, col0:], st[:, col0 // gs:], n, m, d, gs, kc.K_PARTIAL)
+    kc.status()
+    ref = oracle.gemv_f32(x[col0:col0 + m], np.ascontiguousarray(wq[:, col0:col0 + m]),
+                          np.ascontiguousarray(ws[:, col0 // gs:(col0 + m) // gs]), gs)
+    assert (bits(host(part)) == bits(ref)).all()
+    mats = [oracle.seeded_q8_matrix(r, n, gs, 50 + i) for i, r in enumerate((64, 32, 32))]
+    outs = [torch.zeros(r, device="cuda") for r in (64, 32, 32)]
+    kc.k_matmul_q8_qkv(*outs, dev(x), None, *[(dev(a), dev(b)) for a, b in mats], n, 64, 32, gs)
+    kc.status()
+    for o, (a, b) in zip(outs, mats):
+        assert (bits(host(o)) == bits(oracle.gemv_f32(x, a, b, gs))).all()
+    w3q, w3s = oracle.seeded_q8_matrix(d, n, gs, 42)
+    sw = kc.gemv(dev(x), None, dev(wq), dev(ws), gs, kind=kc.K_SWIGLU, w3=(dev(w3q), dev(w3s)))
+    kc.status()
+    a1, a3 = oracle.gemv_f32(x, wq, ws, gs), oracle.gemv_f32(x, w3q, w3s, gs)
+    ref = np.array([oracle.lib().orc_silu_gate(float(p), float(q)) for p, q in zip(a1, a3)], np.float32)
+    assert ulp_diff(host(sw), ref).max() <= 2
+
+
 def test_gemv_config0_full_size_properties(kc, oracle):
     # Config 0 (8192 x 2048, N(0, 0.02) weights, N(0, 1) activations): bitwise against the oracle, and linear in the
     # activation scales (doubling every xs doubles y exactly: the rescale multiplies by a power of two).

@@ -46,6 +46,18 @@ def test_gemv_scalar_golden(oracle, d, n):
 AMX_CASES = [(1, 40, 512), (7, 48, 1024), (33, 32, 256)]
 
 
+W8A32_CASES = [(37, 1024, 64), (16, 512, 32), (20, 256, 16), (9, 384, 128), (8, 96, 48), (6, 40, 2)]
+
+
+@pytest.mark.parametrize("d,n,gs", W8A32_CASES)
+def test_gemv_f32_golden(oracle, d, n, gs):
+    """W8A32: the reference's k_matmul_q8 on fp32 activations (its AVX-512 lane order for gs % 16 == 0, its portable
+    loop for gs 2), bitwise."""
+    k = f"gemvf_{d}_{n}_{gs}"
+    y = oracle.gemv_f32(GOLDEN[k + "_x"], GOLDEN[k + "_wq"], GOLDEN[k + "_ws"], gs)
+    assert (bits(y) == bits(GOLDEN[k + "_y"])).all()
+
+
 @pytest.mark.parametrize("m,d,k", AMX_CASES)
 def test_gemm_amx_order_golden(oracle, m, d, k):
     key = f"amx_{m}_{d}_{k}"
