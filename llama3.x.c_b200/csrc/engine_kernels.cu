@@ -561,6 +561,78 @@ __global__ void __launch_bounds__(kAttnThreads) attention_combine_kernel(
   }
 }
 
+// Attention for the shapes the split and flash kernels do not take (head_dim not 32, 64 or 128, or more than
+// kMaxGqa query heads per KV head), such as the reference's own test fixtures (head_dim 2): one CTA per (query head,
+// row) over the row's causal range, the scores in shared memory ([seq] floats). The same softmax as the reference's
+// scalar attention: scores q.k / sqrt(head_dim), their maximum, exp(s - max) and its sum, then the weighted values
+// divided by the sum; it agrees with the reference within fp32 rounding, as the fast kernels do. Slow by design.
+constexpr int kGenericThreads = 256;
+
+__device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  __syncthreads();  // red is reused
+  if (lane == 0)
+    red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int w = 1; w < kGenericThreads / 32; w++)
+    v = is_max ? fmaxf(v, red[w]) : v + red[w];
+  return v;
+}
+
+__global__ void __launch_bounds__(kGenericThreads) attention_generic_kernel(
+    float *out, long long out_ld, const float *q, long long q_ld, const float *kc, const float *vc, const int *pos_dev,
+    int pos0, int nq, int hd, int seq) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ float sc[];  // [seq]
+  __shared__ float red[kGenericThreads / 32];
+  const int h = blockIdx.x, r = blockIdx.y, g = h / nq, tid = threadIdx.x;
+  const int pos = (pos_dev ? *pos_dev : pos0) + r;
+  if (pos < 0 || pos >= seq) {
+    if (h == 0 && tid == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+    return;
+  }
+  const int npos = pos + 1;
+  const float *qh = q + r * q_ld + (long long)h * hd;
+  const float *kh = kc + (long long)g * seq * hd, *vh = vc + (long long)g * seq * hd;
+  const float scale = sqrtf((float)hd);
+  float mx = -INFINITY;
+  for (int t = tid; t < npos; t += kGenericThreads) {
+    float s = 0.0f;
+    for (int d = 0; d < hd; d++)
+      s = fmaf(qh[d], kh[(long long)t * hd + d], s);
+    s /= scale;
+    sc[t] = s;
+    mx = fmaxf(mx, s);
+  }
+  const float M = block_reduce(mx, red, true);
+  float l = 0.0f;
+  for (int t = tid; t < npos; t += kGenericThreads) {
+    const float e = expf(sc[t] - M);
+    sc[t] = e;
+    l += e;
+  }
+  const float L = block_reduce(l, red, false);  // also orders the sc writes above before the reads below
+  for (int d = tid; d < hd; d += kGenericThreads) {
+    float o = 0.0f;
+    for (int t = 0; t < npos; t++)
+      o = fmaf(sc[t], vh[(long long)t * hd + d], o);
+    out[r * out_ld + (long long)h * hd + d] = o / L;
+  }
+}
+
+// Shapes the split-K decode and flash prefill kernels take.
+bool attention_fast_shape(int n_heads, int n_kv, int hd) {
+  return hd % 32 == 0 && hd <= kMaxHd && kAttnThreads % hd == 0 && n_heads / n_kv <= kMaxGqa;
+}
+
 __global__ void add_kernel(float *x, const float *y, long long n) {
   pdl_wait();
   pdl_launch_dependents();
@@ -687,12 +759,15 @@ bool launched(const char *what) {
 
 int max_splits_for(int seq) { return (seq + kAttnChunk - 1) / kAttnChunk; }
 
+// The generic kernel keeps a row's scores in shared memory: contexts up to 48K positions.
+constexpr size_t kGenericMaxSmem = 192 * 1024;
+
 bool attention_shape_ok(const char *name, const AttentionWork *w, int n_heads, int n_kv, int hd, int seq) {
   if (!w || !w->partial)
     return kc_fail("%s: attention work is not initialized", name);
-  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kMaxGqa || hd <= 0 || hd > kMaxHd || hd % 4)
-    return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d (head_dim a multiple of 4 up to %d, at most "
-                   "%d query heads per KV head)", name, n_heads, n_kv, hd, kMaxHd, kMaxGqa);
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || hd <= 0 || seq <= 0 ||
+      (!attention_fast_shape(n_heads, n_kv, hd) && (size_t)seq * sizeof(float) > kGenericMaxSmem))
+    return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d / context %d", name, n_heads, n_kv, hd, seq);
   if (n_heads != w->n_heads || n_kv != w->n_kv_heads || hd != w->head_dim || seq != w->seq_len)
     return kc_fail("%s: shape differs from the one the work was initialized for", name);
   return true;
@@ -734,9 +809,29 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
     return kc_fail("%s: positions %d..%d outside the context of %d", name, pos0, pos0 + rows - 1, seq);
   if (!attention_smem_ready())
     return kc_fail("%s: cannot reserve %zu bytes of shared memory", name, attn_smem_bytes(hd, kDecodeStages));
-  if (hd % 32 || kAttnThreads % hd)
-    return kc_fail("%s: head_dim %d must be 32, 64 or 128", name, hd);
   const int max_splits = max_splits_for(seq), nq = n_heads / n_kv;
+  if (!attention_fast_shape(n_heads, n_kv, hd)) {
+    const size_t smem = (size_t)seq * sizeof(float);
+    static bool generic_attr[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !generic_attr[dev]) {
+      if (cudaFuncSetAttribute(attention_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kGenericMaxSmem) != cudaSuccess)
+        return kc_fail("%s: cannot reserve shared memory for the generic attention", name);
+      generic_attr[dev] = true;
+    }
+    kc_launch_pdl(attention_generic_kernel, dim3(n_heads, rows), kGenericThreads, smem, kc_stream(), out, out_ld, q,
+                  q_ld, kc, vc, pos_dev, pos0, nq, hd, seq);
+    if (!launched(name))
+      return false;
+    if (oq) {
+      if (kc_launch_quantize_rows(oq, os, out, out_ld, rows, n_heads * hd, gs, kc_stream()) != 0)
+        return kc_fail("%s: CUDA launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
+      kc_count_launch();
+    }
+    return true;
+  }
   // Decode CTAs per (KV head, row): one wave of the GPU at two CTAs per SM, never more than the context has chunks.
   int ctas = 2 * kc_device_sms() / n_kv;
   ctas = ctas < 8 ? 8 : ctas;

@@ -62,6 +62,7 @@ typedef struct {
   void *stream, *comm;
   void *peer; /* peer-memory all-reduce of the decode residual (kd_peer_*), or NULL for NCCL */
   int w8a32;  /* LLAMA_Q8_ACTIVATIONS=fp32: fp32 activations against the int8 weights, one row per forward */
+  int fused;  /* the decode step's fused GEMV modes fit these shapes (fused_shapes) */
   float *xb;  /* W8A32: the normalized row the projections read */
   void *graph_logits, *graph_greedy;
   unsigned long long graph_logits_kernels, graph_greedy_kernels; /* kernels captured in each graph */
@@ -233,8 +234,20 @@ static int activations_from_env(void) {
   return a && !strcmp(a, "fp32");
 }
 
+/* The decode step's fused kernels (RMSNorm and quantize inside the GEMV, the output quantizer) run on the TMA GEMV,
+ * which takes group sizes 16..256 that are powers of two and scale rows of whole 16-byte units. Other shapes, such as
+ * the reference's gs 2 test fixtures, take the separate kernels (decode_layers_plain). */
+static int fused_shapes(const Engine *e) {
+  int gs = e->gs, dim = e->c.dim;
+  /* The fused GEMVs read dim inputs (QKV, W1/W3, classifier); the output quantizer cuts hid_l outputs into groups. */
+  return gs >= 16 && gs <= 256 && !(gs & (gs - 1)) && dim % gs == 0 && (dim / gs) % 4 == 0 && e->hid_l % gs == 0;
+}
+
 /* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. */
-static int max_batch_for(const Engine *e) { return e->w8a32 ? 1 : prefill_batch_from_env(e->context); }
+static int max_batch_for(Engine *e) {
+  e->fused = fused_shapes(e); /* plan() has set the shard shapes */
+  return e->w8a32 ? 1 : prefill_batch_from_env(e->context);
+}
 
 /* Device buffers sized for the context and the batch. */
 static int allocate_state(Engine *e) {
@@ -723,6 +736,38 @@ static void decode_layers_w8a32(Engine *e) {
   k_matmul_q8(e->logits_dev, &xin, k8(e->cls), dim, e->vl, gs);
 }
 
+/* The W8A8 token on the separate kernels, for shapes the fused GEMV does not take (fused_shapes): RMSNorm + quantize,
+ * the GEMV, the quantize of the attention and SwiGLU outputs as their own launches (forward_q8, src/tp.c:387-436). */
+static void decode_layers_plain(Engine *e) {
+  const Config *p = &e->c;
+  int dim = p->dim, gs = e->gs;
+  K8Input in = {e->xq, e->xs, NULL}, att = {e->aq, e->as, NULL}, hid = {e->hq, e->hs, NULL};
+  k_embed_q8_rows(e->x, e->tokens_dev, k8(e->embed), 1, dim, gs, p->vocab_size);
+  for (int l = 0; l < p->n_layers; l++) {
+    Layer *y = &e->layers[l];
+    float *kc = e->key_cache + (size_t)l * e->layer_kv, *vc = e->value_cache + (size_t)l * e->layer_kv;
+    k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, y->rms_att, 1, dim, p->norm_eps, gs);
+    k_matmul_q8_qkv(e->q, e->k, e->v, &in, k8(y->wq), k8(y->wk), k8(y->wv), dim, e->ql, e->kvl, gs);
+    k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
+                         e->context);
+    k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
+                        1, gs);
+    K8Weight wo = k8(y->wo), w2 = k8(y->w2);
+    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &att, &wo, e->ql, e->ql, dim, gs, e->S == 1 ? K_ADD : K_PARTIAL);
+    if (e->S > 1)
+      residual_reduce(e, 1);
+    k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, y->rms_ffn, 1, dim, p->norm_eps, gs);
+    k_matmul_q8_swiglu(e->hb, &in, k8(y->w1), k8(y->w3), dim, e->hid_l, gs);
+    k_quantize(e->hq, e->hs, e->hb, e->hid_l, gs);
+    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &hid, &w2, e->hid_l, e->hid_l, dim, gs,
+                   e->S == 1 ? K_ADD : K_PARTIAL);
+    if (e->S > 1)
+      residual_reduce(e, 1);
+  }
+  k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x, dim, e->rms_final, 1, dim, p->norm_eps, gs);
+  k_matmul_q8(e->logits_dev, &in, k8(e->cls), dim, e->vl, gs);
+}
+
 /* One token at the position in e->pos_dev (device), its id in e->tokens_dev[0]: everything up to the local logits.
  * The RMSNorm + quantize before QKV, W1/W3 and the classifier run inside those GEMVs (k_matmul_q8_fused), and the
  * SwiGLU GEMV quantizes its own output for W2 (K_TAIL_QUANTIZE_OUTPUT): bitwise the separate kernels the batched
@@ -730,6 +775,10 @@ static void decode_layers_w8a32(Engine *e) {
 static void decode_layers(Engine *e) {
   if (e->w8a32) {
     decode_layers_w8a32(e);
+    return;
+  }
+  if (!e->fused) {
+    decode_layers_plain(e);
     return;
   }
   const Config *p = &e->c;

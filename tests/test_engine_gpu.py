@@ -81,6 +81,26 @@ def test_logits_match_reference_at_stable_positions(eng, files, name):
         assert close(m.forward_batch(p, 0, eng.LOGITS_LAST), GOLDEN[f"{name}_batch"])
 
 
+def test_reference_fixture_baseline_logits(eng, tmp_path):
+    """The reference's own regression fixture and golden values (tests/golden/ref_fixture.npz: the group-size-2,
+    head_dim-2 checkpoint of its tests/fixtures.py, and the 48 logits of its tests/baseline_logits.json["runq"]),
+    checked as its tests/test_runtime.py:55-70 checks them: rel_tol 2e-5, abs_tol 2e-6. This shape takes the generic
+    attention and the separate RMSNorm/quantize kernels; the batched prefill gives the same rows."""
+    import math
+    fixture = np.load(HERE / "golden" / "ref_fixture.npz")
+    path = tmp_path / "int8.bin"
+    path.write_bytes(fixture["int8_bin"].tobytes())
+    want = fixture["runq"]
+    with eng.Engine.load(path) as m:
+        got = np.concatenate([m.forward(65 + p, p)[:12] for p in range(4)])
+    assert all(math.isclose(a, b, rel_tol=2e-5, abs_tol=2e-6) for a, b in zip(got, want)), (got, want)
+    with eng.Engine.load(path) as m:
+        rows = m.forward_batch([65, 66, 67, 68], 0, eng.LOGITS_ALL)
+        tokens = m.generate([65, 66, 67], 6)
+    assert all(math.isclose(a, b, rel_tol=2e-5, abs_tol=2e-6) for a, b in zip(rows[:, :12].reshape(-1), want))
+    assert len(tokens) >= 1
+
+
 @pytest.mark.parametrize("name", ["tiny", "small"])
 def test_w8a32_matches_reference(eng, files, name, monkeypatch):
     """LLAMA_Q8_ACTIVATIONS=fp32 (W8A32: every projection reads fp32 activations, nothing is quantized; one row per
