@@ -72,6 +72,10 @@ void kernels_set_stream(void *stream);  /* cudaStream_t for this thread's kernel
 /* Programmatic dependent launch for the GEMV/GEMM (on by default): their weight streams start while the previous
  * kernel in the stream finishes. No reference counterpart (a CPU team has no launch latency to hide). */
 void kernels_set_pdl(int on);
+/* The reference's CPU worker-team set-up and teardown (include/kernels.h:29-30): the GPU has no team to build, so both
+ * do nothing; they exist so that callers written for the reference link unchanged. */
+void kernels_backend_init(void);
+void kernels_backend_free(void);
 
 /* ---- error handling (runtime.h fail() analogue) ----------------------------------------------------------------- */
 enum { KC_FAIL_EXIT = 0, KC_FAIL_RETURN = 1 };
@@ -102,6 +106,20 @@ void k_matmul_q8_swiglu(float *out, const K8Input *x, K8Weight w1, K8Weight w3, 
 void k_matmul_q8_ld(float *out, const K8Input *x, const K8Weight *w, size_t ld, int n, int d, int gs, int kind);
 void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, const K8Weight *w3, size_t ld, int n,
                            int d, int gs);
+/* Member `worker` of `workers`' share of k_matmul_q8_ld (include/kernels.h:86-95, 119-120): output rows
+ * [d * worker / workers, d * (worker + 1) / workers), the reference's static Q8 split (src/gemv.c:488-495); the
+ * members' shares together are the full product, bitwise. `claim` is ignored, as the reference ignores it for Q8.
+ * `done`, when not NULL, is called as done(done_ctx, r0, r1) once the share's rows are in memory (this call waits for
+ * the stream), so a caller can start on those rows. */
+typedef void (*RowsDoneFn)(void *ctx, int r0, int r1);
+#ifdef __cplusplus
+typedef int kc_atomic_int; /* the reference's atomic_int, only passed through */
+#else
+#include <stdatomic.h>
+typedef atomic_int kc_atomic_int;
+#endif
+void k_matmul_q8_ld_worker(float *out, const K8Input *x, const K8Weight *w, size_t ld, int n, int d, int gs, int kind,
+                           int worker, int workers, kc_atomic_int *claim, RowsDoneFn done, void *done_ctx);
 
 /* The decode GEMV with its input prepared inside the kernel (no reference counterpart): x holds n fp32 activations,
  * RMS-normalized with `weight` and `epsilon` first when weight is not NULL (k_rmsnorm_q8_rows' arithmetic), then
@@ -148,6 +166,22 @@ struct KernelTail {
 };
 void k_matmul_q8_tail(const K8Input *x, size_t ld, int n, int gs, const GemmQ8Segment *segments, int count,
                       const KernelTail *tail);
+
+/* ---- AMX packing helpers (include/gemm.h:55-67, 136-144) ---------------------------------------------------------- */
+/* The reference's int8 tile layout for its AMX kernels, produced on the host: rows in tiles of 16, K in quads, both
+ * zero-padded (K to 64): dst[((tile * kp / 4 + quad) * 16 + row_in_tile) * 4 + byte] with kp = cols rounded up to 64.
+ * The sm_100a GEMM reads the row-major weights through TMA and never these copies (GemmQ8Segment.pw is ignored); the
+ * helpers exist so that loaders written for the reference link unchanged and get the same bytes. Host memory. */
+size_t s8_vnni_bytes(int rows, int cols);
+void pack_s8_vnni(int8_t *dst, const int8_t *w, int rows, int cols, size_t ld);
+void pack_s8_vnni_tiles(int8_t *dst, const int8_t *w, int rows, int cols, size_t ld, int first, int last);
+typedef struct {
+  int8_t *dst;
+  const int8_t *w;
+  int rows, cols;
+  size_t ld;
+} PackS8;
+void pack_s8_vnni_many(const PackS8 *jobs, int count);
 
 /* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count);

@@ -83,6 +83,15 @@ _SIGNATURES = {
     "k_matmul_q8_swiglu_ld": (None, [_f32p, _c.POINTER(K8Input), _c.POINTER(K8Weight), _c.POINTER(K8Weight),
                                      _c.c_size_t, _c.c_int, _c.c_int, _c.c_int]),
     "k_gemm_q8": (None, [_i8p, _f32p, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment), _c.c_int]),
+    "k_matmul_q8_ld_worker": (None, [_f32p, _c.POINTER(K8Input), _c.POINTER(K8Weight), _c.c_size_t, _c.c_int,
+                                     _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
+                                     _c.c_void_p]),
+    "kernels_backend_init": (None, []),
+    "kernels_backend_free": (None, []),
+    "s8_vnni_bytes": (_c.c_size_t, [_c.c_int, _c.c_int]),
+    "pack_s8_vnni": (None, [_i8p, _i8p, _c.c_int, _c.c_int, _c.c_size_t]),
+    "pack_s8_vnni_tiles": (None, [_i8p, _i8p, _c.c_int, _c.c_int, _c.c_size_t, _c.c_int, _c.c_int]),
+    "pack_s8_vnni_many": (None, [_c.c_void_p, _c.c_int]),
     "k_matmul_q8_fused": (None, [_f32p, _f32p, _c.c_float, _c.c_size_t, _c.c_int, _c.c_int,
                                  _c.POINTER(GemmQ8Segment), _c.c_int, _c.c_void_p]),
     "k_matmul_q8_tail": (None, [_c.POINTER(K8Input), _c.c_size_t, _c.c_int, _c.c_int, _c.POINTER(GemmQ8Segment),
@@ -286,6 +295,28 @@ def k_matmul_q8_tail(xq, xs, ld, n, gs, segs, tail):
     arr, count = _segments(segs)
     inp = _input(xq, xs)
     _call("k_matmul_q8_tail", ctypes.byref(inp), ld, n, gs, arr, count, ctypes.byref(tail))
+
+
+ROWS_DONE = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int, ctypes.c_int)
+
+
+def k_matmul_q8_ld_worker(out, xq, xs, wq, ws, ld, n, d, gs, kind, worker, workers, done=None):
+    """Member `worker` of `workers`' share of k_matmul_q8_ld; done(r0, r1) once its rows are in memory."""
+    inp = _input(xq, xs)
+    w = _weight(wq, ws)
+    cb = ROWS_DONE(lambda ctx, r0, r1: done(r0, r1)) if done else None
+    _call("k_matmul_q8_ld_worker", _ptr(out), ctypes.byref(inp), ctypes.byref(w), ld, n, d, gs, kind, worker, workers,
+          None, ctypes.cast(cb, ctypes.c_void_p) if cb else None, None)
+
+
+def pack_s8_vnni(w, rows, cols, ld):
+    """The reference's AMX tile layout of an int8 matrix (host numpy array in, host numpy array out)."""
+    import numpy as np
+    L = load()  # host code: no device needed
+    out = np.zeros(L.s8_vnni_bytes(rows, cols), np.int8)
+    w = np.ascontiguousarray(w, np.int8)
+    L.pack_s8_vnni(out.ctypes.data_as(ctypes.c_void_p), w.ctypes.data_as(ctypes.c_void_p), rows, cols, ld)
+    return out
 
 
 def k_gemm_q8_pick(gs, segs):

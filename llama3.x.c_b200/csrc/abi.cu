@@ -93,6 +93,9 @@ void kernels_set_stream(void *stream) { tl_stream = static_cast<cudaStream_t>(st
 
 void kernels_set_pdl(int on) { pdl_on = on != 0; }
 
+void kernels_backend_init(void) {}
+void kernels_backend_free(void) {}
+
 void kc_set_fail_mode(int mode) { fail_mode = mode == KC_FAIL_RETURN ? KC_FAIL_RETURN : KC_FAIL_EXIT; }
 
 const char *kc_last_error(void) { return tl_error; }
@@ -221,6 +224,32 @@ void k_matmul_q8_swiglu_ld(float *out, const K8Input *x, const K8Weight *w1, con
                            int d, int gs) {
   KcGemvSeg s = {out, w1->q, w1->s, w3->q, w3->s, d};
   gemv("k_matmul_q8_swiglu_ld", &s, 1, x, ld, n, gs, KC_SWIGLU);
+}
+
+void k_matmul_q8_ld_worker(float *out, const K8Input *x, const K8Weight *w, size_t ld, int n, int d, int gs, int kind,
+                           int worker, int workers, kc_atomic_int *claim, RowsDoneFn done, void *done_ctx) {
+  (void)claim;
+  const char *name = "k_matmul_q8_ld_worker";
+  if (kind != K_STORE && kind != K_ADD && kind != K_PARTIAL) {
+    kc_fail("%s: invalid epilogue kind %d", name, kind);
+    return;
+  }
+  if (workers < 1 || worker < 0 || worker >= workers || d < 0 || !w || gs <= 0) {
+    kc_fail("%s: invalid member %d of %d", name, worker, workers);
+    return;
+  }
+  const int r0 = (int)((long long)d * worker / workers), r1 = (int)((long long)d * (worker + 1) / workers);
+  if (r1 <= r0)
+    return;
+  KcGemvSeg s = {out + r0, w->q + (size_t)r0 * ld, w->s + (size_t)r0 * (ld / (size_t)gs), nullptr, nullptr, r1 - r0};
+  gemv(name, &s, 1, x, ld, n, gs, kind);
+  if (done && !kc_last_error()[0]) {
+    if (cudaStreamSynchronize(tl_stream) != cudaSuccess) {
+      kc_fail("%s: %s", name, cudaGetErrorString(cudaGetLastError()));
+      return;
+    }
+    done(done_ctx, r0, r1);
+  }
 }
 
 // Segments of one kind as KcGemvSeg; false (and fail()) otherwise.
@@ -569,6 +598,39 @@ void k_rope_apply_rows(float *q, size_t q_stride, float *k, size_t k_stride, con
 
 void k_rope_apply(float *q, float *k, const float *table, int n_heads, int n_kv_heads, int head_dim) {
   k_rope_apply_rows(q, 0, k, 0, table, 0, 1, n_heads, n_kv_heads, head_dim);
+}
+
+// ---- AMX packing helpers (host) ------------------------------------------------------------------------------------
+
+size_t s8_vnni_bytes(int rows, int cols) {
+  const size_t r = ((size_t)(rows > 0 ? rows : 0) + 15) / 16 * 16, c = ((size_t)(cols > 0 ? cols : 0) + 63) / 64 * 64;
+  return r * c;
+}
+
+void pack_s8_vnni_tiles(int8_t *dst, const int8_t *w, int rows, int cols, size_t ld, int first, int last) {
+  // The reference's layout (pack_s8_vnni_tiles, src/gemm.c:384-394): tile t holds rows [16 t, 16 t + 16); within it,
+  // K quad k4 (columns 4 k4 .. 4 k4 + 3) is a run of 16 rows x 4 bytes; rows and columns past the matrix are zeros.
+  const size_t kp = ((size_t)cols + 63) / 64 * 64;
+  for (int t = first; t < last; t++) {
+    int8_t *tile = dst + (size_t)t * 16 * kp;
+    for (size_t k4 = 0; k4 < kp / 4; k4++)
+      for (int r = 0; r < 16; r++) {
+        const size_t row = (size_t)t * 16 + r;
+        for (int b = 0; b < 4; b++) {
+          const size_t col = 4 * k4 + b;
+          tile[(k4 * 16 + r) * 4 + b] = row < (size_t)rows && col < (size_t)cols ? w[row * ld + col] : 0;
+        }
+      }
+  }
+}
+
+void pack_s8_vnni(int8_t *dst, const int8_t *w, int rows, int cols, size_t ld) {
+  pack_s8_vnni_tiles(dst, w, rows, cols, ld, 0, (rows + 15) / 16);
+}
+
+void pack_s8_vnni_many(const PackS8 *jobs, int count) {
+  for (int i = 0; i < count; i++)
+    pack_s8_vnni(jobs[i].dst, jobs[i].w, jobs[i].rows, jobs[i].cols, jobs[i].ld);
 }
 
 }  // extern "C"

@@ -12,6 +12,7 @@ Cases (all small; numpy PCG64 seeds below):
                   (k_gemm_q8_amx_dots_test)
   rms_*           k_rmsnorm on the AVX-512 ISA (src/kernels_simd.c:136-161) and the scalar one (src/kernels.c:8-21)
   gemvf_*         k_matmul_q8 on fp32 activations (W8A32), AVX-512 ISA for gs % 16 == 0, else scalar
+  vnni_*          pack_s8_vnni of a 37 x 200 slice (row stride 256)
 """
 import sys
 from pathlib import Path
@@ -77,6 +78,12 @@ def main():
         isa = O.KERNELS_AVX512 if gs % 16 == 0 else O.KERNELS_SCALAR
         key = f"gemvf_{d}_{n}_{gs}"
         out.update({key + "_wq": wq, key + "_ws": ws, key + "_x": x, key + "_y": O.ref_gemv_f32(x, wq, ws, gs, isa)})
+    # The reference's AMX int8 packing (pack_s8_vnni, src/gemm.c:384-398) of a ragged matrix with a row stride.
+    L = O.ref()
+    w = rng.integers(-127, 128, size=(37, 256), dtype=np.int8)
+    packed = np.zeros(L.s8_vnni_bytes(37, 200), np.int8)
+    L.pack_s8_vnni(O._p(packed, O._i8p), O._p(w, O._i8p), 37, 200, 256)
+    out.update(vnni_w=w, vnni_packed=packed)
     path = Path(__file__).with_name("q8_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({path.stat().st_size} bytes, {len(out)} arrays)")

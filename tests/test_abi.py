@@ -78,3 +78,15 @@ def test_c_header_layout_matches(tmp_path):
 def test_name_is_null_before_init():
     mod = load_package()
     assert mod.load().kernels_name() is None
+
+
+def test_pack_s8_vnni_matches_reference_golden():
+    """The reference's AMX tile layout, produced on the host by this library (no device): bitwise the reference's
+    pack_s8_vnni on a ragged slice with a row stride (tests/golden/q8_golden.npz, vnni_*)."""
+    import numpy as np
+    from conftest import load_package
+    kc = load_package()
+    g = np.load(Path(__file__).parent / "golden" / "q8_golden.npz")
+    packed = kc.pack_s8_vnni(g["vnni_w"], 37, 200, 256)
+    assert packed.shape == g["vnni_packed"].shape and (packed == g["vnni_packed"]).all()
+

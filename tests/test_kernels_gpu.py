@@ -188,6 +188,26 @@ def test_gemv_swiglu(kc, oracle, d, n):
     assert ulp_diff(host(out), ref).max() <= 2
 
 
+@pytest.mark.parametrize("workers", [1, 3, 7])
+def test_ld_worker_shares_make_the_full_product(kc, oracle, workers):
+    """k_matmul_q8_ld_worker: every member's static share (src/gemv.c:488-495) together equals k_matmul_q8_ld bitwise,
+    and done(r0, r1) reports each share once its rows are written, covering [0, d) without overlap."""
+    d, ld, n, gs = 100, 512, 512, 64
+    wq, ws, xq, xs = make_case(oracle, d, ld, gs, 61)
+    full = torch.zeros(d, device="cuda")
+    kc.k_matmul_q8_ld(full, dev(xq), dev(xs), dev(wq), dev(ws), ld, n, d, gs, kc.K_STORE)
+    out = torch.zeros(d, device="cuda")
+    ranges = []
+    for w in range(workers):
+        kc.k_matmul_q8_ld_worker(out, dev(xq), dev(xs), dev(wq), dev(ws), ld, n, d, gs, kc.K_STORE, w, workers,
+                                 done=lambda r0, r1: ranges.append((r0, r1, host(out)[r0:r1].copy())))
+    kc.status()
+    assert (bits(host(out)) == bits(host(full))).all()
+    assert [r[:2] for r in ranges] == [(d * w // workers, d * (w + 1) // workers) for w in range(workers)]
+    for r0, r1, rows in ranges:  # the rows were already written when done() ran
+        assert (bits(rows) == bits(host(full)[r0:r1])).all()
+
+
 # ---- W8A32 (K8Input.q NULL, fp32 activations): the reference's AVX-512 order (gs % 16 == 0) and portable loop ----
 W8A32_SHAPES = [(37, 1024, 64), (16, 512, 32), (20, 256, 16), (9, 384, 128), (8, 96, 48), (6, 40, 2),
                 (4096, 4096, 64), (33, 14336, 64), (1000, 2048, 256), (3, 64, 8)]
