@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the Q8_0 W8A8 path on B200: one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv|ffn]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv|ffn|gemm]
                     [--profile-request] [--no-cpu-baseline]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N   (N = 2, 4, 8)
 
@@ -426,13 +426,84 @@ def run_gemv(args):
                                    "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs"}}), flush=True)
 
 
+# ---- config 1: the prefill GEMM alone ---------------------------------------------------------------------------
+
+GEMM_SHAPES = {"up": (14336, 4096), "down": (4096, 14336)}  # (N weight rows, K)
+
+
+def run_gemm(args):
+    """Config 1: k_gemm_q8 (STORE) on the 8B up (14336 x 4096) and down (4096 x 14336) projections at T = 128, 512 and
+    2048 activation rows, each launch timed with CUDA events inside a captured graph, the weights rotating over enough
+    copies to exceed L2 three times. Per shape: int8 TOPS against the binding roof, the int8 tensor peak (taken as
+    twice the measured bf16 GEMM peak, the dense int8/bf16 ratio) or HBM for its bytes, whichever takes longer."""
+    import torch
+    kc = load_package()
+    kc.init()
+    hbm, peak_kind = peaks()
+    pk = ROOT / "MEASURED_PEAKS.json"
+    bf16 = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
+    int8_tops = 2 * bf16
+    gs, shapes = 64, []
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    for name, (N, K) in GEMM_SHAPES.items():
+        w = torch.randn((N, K), generator=g, device="cuda") * 0.02
+        wq, ws = kc.quantize(w, gs)
+        del w
+        wbytes = wq.numel() + ws.numel() * 4
+        copies = max(2, -(-3 * L2_BYTES // wbytes))
+        W = [(wq.clone(), ws.clone()) for _ in range(copies)]
+        for T in (128, 512, 2048):
+            x = torch.randn((T, K), generator=g, device="cuda")
+            xq, xs = kc.quantize(x, gs)
+            c = torch.empty((T, N), device="cuda")
+            launches = max(4, args.steps)
+
+            def launch(i):
+                kc.k_gemm_q8(xq, xs, T, K, gs, [kc.segment(c, W[i % copies])])
+
+            for i in range(args.warmup):
+                launch(i)
+            kc.status()
+            evs = [(torch.cuda.Event(enable_timing=True, external=True),
+                    torch.cuda.Event(enable_timing=True, external=True)) for _ in range(launches)]
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(launches):
+                    evs[i][0].record()
+                    launch(i)
+                    evs[i][1].record()
+            graph.replay()
+            torch.cuda.synchronize()
+            kc.status()
+            us = float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
+            del graph
+            ops = 2.0 * T * N * K
+            nbytes = wbytes + T * K * (1 + 4 / gs) + 4 * T * N
+            t_tensor, t_hbm = ops / (int8_tops * 1e12), nbytes / (hbm * 1e9)
+            bound = "tensor" if t_tensor >= t_hbm else "hbm"
+            tops = ops / (us * 1e-6) / 1e12
+            shapes.append({"shape": f"{name} T={T} N={N} K={K}", "us": round(us, 2), "int8_tops": round(tops, 1),
+                           "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bound": bound,
+                           "frac": round(max(t_tensor, t_hbm) / (us * 1e-6), 4)})
+            del x, xq, xs, c
+        del W, wq, ws
+    head = next(s for s in shapes if s["shape"].startswith("up T=2048"))
+    print(json.dumps({"metric": "config 1 prefill GEMM int8 TOPS (8B up projection, T=2048)", "value": head["int8_tops"],
+                      "unit": "TOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "int8",
+                      "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
+                                "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} "
+                                          "hbm_gbs"},
+                      "shapes": shapes}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["8b", "1b", "gemv", "ffn"], default="8b")
+    ap.add_argument("--workload", choices=["8b", "1b", "gemv", "ffn", "gemm"], default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-request", action="store_true")
     args = ap.parse_args()
@@ -441,6 +512,8 @@ def main():
         run_reference(args)
     elif args.workload in ("gemv", "ffn"):
         run_gemv(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
     elif args.profile_request:
         run_profile_request(args)
     else:
