@@ -32,9 +32,6 @@
 
 namespace {
 
-#ifndef KC_GEMV_MIN_BLOCKS
-#define KC_GEMV_MIN_BLOCKS 1
-#endif
 constexpr int kDotWarps = 8;
 constexpr int kThreads = (kDotWarps + 1) * 32;  // 8 dot warps + 1 chain/producer warp
 constexpr int kTileRows = 32;                   // physical weight rows per sub-tile (one per lane)
@@ -466,7 +463,7 @@ __device__ __forceinline__ void finish_tail(const GemvArgs &a, float *scratch, i
 }
 
 template <int GS>
-__global__ void __launch_bounds__(kThreads, KC_GEMV_MIN_BLOCKS) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // The 128-byte swizzle is a function of the address bits, so the stages start on a 1024-byte boundary.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -920,11 +917,8 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
 #ifndef KC_GEMV_MAX_DEPTH
 #define KC_GEMV_MAX_DEPTH 4
 #endif
-#ifndef KC_GEMV_FUSED_BUDGET
-#define KC_GEMV_FUSED_BUDGET (226 * 1024)
-#endif
   // The fused modes may use the rest of the 227 KB for their fp32 staging rather than give up pipeline depth.
-  size_t budget = act ? KC_GEMV_FUSED_BUDGET : KC_GEMV_SMEM_BUDGET;
+  size_t budget = act ? 226 * 1024 : KC_GEMV_SMEM_BUDGET;
   if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
     budget = 226 * 1024;
   if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
@@ -961,10 +955,6 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   if (dev < 64 && !attr_set[dev][variant]) {
     cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-#ifdef KC_GEMV_CARVEOUT
-    cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
-                         cudaFuncAttributePreferredSharedMemoryCarveout, KC_GEMV_CARVEOUT);
-#endif
     attr_set[dev][variant] = true;
   }
   cudaLaunchConfig_t cfg = {};
