@@ -106,15 +106,18 @@ def test_batch_rows_match_single_rows_and_fused_quantize(kc, oracle):
         assert (host(q8) == wq).all() and (host(sc).view(np.int32) == ws.view(np.int32)).all()
 
 
-def test_device_position_matches_host_position(kc):
-    n_heads, n_kv, hd, seq = 8, 2, 128, 1024
+@pytest.mark.parametrize("n_heads,n_kv,seq", [(8, 2, 1024), (4, 1, 8192), (8, 2, 8192)])
+def test_device_position_matches_host_position(kc, n_heads, n_kv, seq):
+    """Also at the per-rank shapes of the 8B model under tensor parallelism (8 ranks: 4 heads on 1 KV head; 4 ranks:
+    8 on 2) and its full context."""
+    hd = 128
     rng = np.random.default_rng(6)
     q = dev(rng.standard_normal(n_heads * hd, dtype=np.float32))
     kcache = dev(rng.standard_normal((n_kv, seq, hd), dtype=np.float32))
     vcache = dev(rng.standard_normal((n_kv, seq, hd), dtype=np.float32))
     work = kc.attention_work(n_heads, n_kv, hd, seq)
     try:
-        for pos in (0, 130, 1023):
+        for pos in (0, 130, seq - 1):
             a, b = torch.zeros(n_heads * hd, device="cuda"), torch.zeros(n_heads * hd, device="cuda")
             kc.k_attention_kv(a, q, kcache, vcache, work, n_heads, n_kv, hd, seq, pos)
             p = torch.tensor([pos], dtype=torch.int32, device="cuda")
