@@ -10,6 +10,7 @@
 #define LLAMA3X_DEVICE_CUDA_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -57,10 +58,21 @@ void kd_comm_free(void *comm);
  * one node with peer access between every pair of GPUs, as NVSwitch gives) and waits, bounded, for the others'; then
  * x[i] += sum of the partials in rank order, identical on every rank. kd_peer_init is collective over `comm` (it
  * exchanges the IPC handles once); every rank must then make the same kd_peer_allreduce_add calls in the same order.
- * n <= max_floats. A peer that does not arrive within the wait limit raises the kernel error flag (kc_status). */
+ * n <= max_floats. A peer that does not arrive within the wait limit raises the kernel error flag (kc_status).
+ * world 1 (comm may be NULL) is a single rank: no IPC, x += partial, and kd_peer_matmul_q8_add equals
+ * k_matmul_q8_add bitwise. */
 void *kd_peer_init(void *comm, int rank, int world, size_t max_floats);
 int kd_peer_allreduce_add(void *peer, float *x, const float *partial, size_t n);
 void kd_peer_free(void *peer);
+/* The column-sharded Wo / W2 product and its all-reduce in one kernel, as the reference fuses them into one team job
+ * (project_residual / project_reduce_fn, src/tp.c:232-244 and 316-335: a K_PARTIAL share whose rows are flagged to the
+ * exchange as they finish, then added into the residual): x[r] += sum over ranks, in rank order, of row r of this rank's slice (wq [d][ld] int8, ws [d][ld / gs]) times its activations (xq [n], xs [n / gs]),
+ * each rank's product in the AMX order. Bitwise equal to k_matmul_q8_ld(..., K_PARTIAL) followed by
+ * kd_peer_allreduce_add. d <= max_floats of kd_peer_init; gs a power of two in 16..1024 dividing n and ld, with
+ * (ld / gs) a multiple of 4 and 16-byte aligned activations and scale rows, else rejected (-1). Every rank makes the
+ * same calls in the same order, on the same number of SMs. */
+int kd_peer_matmul_q8_add(void *peer, float *x, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                          size_t ld, int n, int d, int gs);
 
 #ifdef __cplusplus
 }

@@ -268,7 +268,8 @@ int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, c
 /* Same arguments and results as k_gemm_q8, but the tensor-core path stages its transposed activation scales in a
  * fixed array compiled into the library (K_GEMM_Q8_NOALLOC_MAX_SCALES floats, 4 MiB, one per device) instead of a
  * buffer it allocates: (k / gs) * round_up(m, 4) must not exceed that, or the call is rejected. The first call on a
- * device looks the array's address up (cudaGetSymbolAddress, with that device current), so make it once during setup.
+ * device looks the array's address up (cudaGetSymbolAddress, with that device current), so make it once during setup,
+ * before any stream capture.
  * Nothing needs to start at zero: every call rewrites the whole part of the array it reads. Calls on one device share
  * the array, so two calls in flight at once (different streams or threads) race; issue them on one stream.
  * Returns 0 on success, -1 when the arguments are rejected (kc_last_error says why, under KC_FAIL_RETURN). */

@@ -26,6 +26,18 @@ __device__ __forceinline__ uint64_t kc_globaltimer() {
 // Every spin in this library gives up after this many nanoseconds and raises KC_ERR_TIMEOUT.
 constexpr uint64_t KC_WAIT_NS = 2000000000ull;
 
+// Slots of the peer reductions: 8-byte {float bits, call number} words written and polled whole, in this GPU's memory
+// or a peer's (CUDA IPC mapping); volatile, so every poll reads memory.
+__device__ __forceinline__ unsigned long long peer_ld_slot(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void peer_st_slot(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

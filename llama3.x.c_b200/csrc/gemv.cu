@@ -84,12 +84,13 @@ struct GemvArgs {
   KcGemvTail tail;     // work the last CTA to finish does once (kind 0: none)
   int n;        // inputs (K)
   int gs;
-  int kind;     // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU
+  int kind;     // KC_STORE / KC_ADD / KC_PARTIAL / KC_SWIGLU / KC_REDUCE_ADD
   int units;    // output rows over all segments
   int nchunks;
   int depth;    // pipeline stages
   int stage_bytes;
   int kblock;   // weight maps are 3-D k-block maps: one TMA instruction per stage (and per w1/w3 half)
+  KcPeerGemv peer;  // KC_REDUCE_ADD: the ranks' slots and this rank's call counters
 };
 
 struct Sub {
@@ -462,6 +463,53 @@ __device__ __forceinline__ void finish_tail(const GemvArgs &a, float *scratch, i
     kc_gemv_tail_counter = 0;
 }
 
+// ---- KC_REDUCE_ADD: the tensor-parallel sum inside the GEMV ------------------------------------------------------
+// Every rank computes the same rows of its own column slice of the weights; the chain warp sends each finished row to
+// every rank as one 8-byte {float bits, call number} store (slot [parity][rank][row] of that rank's region, over
+// NVLink for the peers). Once its own rows are sent, each CTA waits, bounded, until its rows from every rank have
+// arrived in this GPU's region and adds them to the output in rank order: out[r] + (((p_0 + p_1) + p_2) + ...), the
+// order and rounding of kd_peer_allreduce_add after a PARTIAL GEMV, so the replicated residual stays identical on all
+// ranks. The call number seq (this CTA's counter + 1) selects the parity: a rank can only start call seq + 2 after
+// every rank has sent its rows of call seq + 1, which each does only after its call seq kernel finished, so a slot is
+// never overwritten while it is still being read. The CTAs of one GPU never wait on each other.
+__device__ __forceinline__ void push_row(const KcPeerGemv &p, long long par, unsigned seq, int row, float v) {
+  const unsigned long long w = ((unsigned long long)seq << 32) | __float_as_uint(v);
+  const long long off = (par * p.world + p.rank) * p.stride + row;
+#pragma unroll
+  for (int q = 0; q < kPeerMaxRanks; q++)  // static indices: the pointers stay in parameter space
+    if (q < p.world)
+      peer_st_slot(p.slots[q] + off, w);
+}
+
+__device__ __forceinline__ void reduce_rows(const KcPeerGemv &p, float *out, int r0, int r1, long long par,
+                                            unsigned seq) {
+  const unsigned long long *mine = p.slots[0];
+#pragma unroll
+  for (int q = 1; q < kPeerMaxRanks; q++)
+    mine = q == p.rank ? p.slots[q] : mine;
+  mine += par * p.world * p.stride;
+  const uint64_t start = kc_globaltimer();
+  for (int r = r0 + (int)threadIdx.x; r < r1; r += (int)blockDim.x) {
+    float sum = 0.0f;
+    bool ok = true;
+    for (int q = 0; q < p.world && ok; q++) {
+      unsigned long long v = peer_ld_slot(mine + q * p.stride + r);
+      for (unsigned k = 1; (unsigned)(v >> 32) != seq; k++) {
+        if ((k & 63u) == 0 && kc_globaltimer() - start > KC_WAIT_NS) {
+          kc_raise(KC_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        v = peer_ld_slot(mine + q * p.stride + r);
+      }
+      const float f = __uint_as_float((unsigned)v);
+      sum = q == 0 ? f : __fadd_rn(sum, f);
+    }
+    if (ok)
+      out[r] = __fadd_rn(out[r], sum);
+  }
+}
+
 template <int GS>
 __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -475,6 +523,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (u1 <= u0) {
     if (a.tail.kind && a.tail.kind != KC_TAIL_QUANTIZE_OUTPUT)
       finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem));
+    if (a.kind == KC_REDUCE_ADD) {  // no rows, but the call still counts
+      pdl_wait();
+      if (tid == 0)
+        a.peer.epoch[c] += 1u;
+    }
     return;
   }
   const Plan plan = make_plan(a, u0, u1, swiglu ? 4 : 5);
@@ -508,6 +561,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (warp == kDotWarps && S > 0)
     issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &bars[0]);
   pdl_wait();
+  // The counter was written by the previous reducing call, complete once pdl_wait returns.
+  const unsigned seq = a.kind == KC_REDUCE_ADD ? a.peer.epoch[c] + 1u : 0u;
+  const long long par = seq & 1u;
   if (a.act == kActQ8) {
     for (int i = tid; i < n / 16; i += kThreads)
       reinterpret_cast<int4 *>(XQ)[i] = __ldg(reinterpret_cast<const int4 *>(a.xq) + i);
@@ -611,6 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
         } else if (lane < t.cnt) {
           if (a.kind == KC_ADD)
             out[lane] = __fadd_rn(out[lane], acc);
+          else if (a.kind == KC_REDUCE_ADD)
+            push_row(a.peer, par, seq, t.row0 + lane, acc);
           else
             out[lane] = acc;
         }
@@ -640,6 +698,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (*abort_flag && tid == 0)
     for (int j = max(0, *issued - depth); j < *issued; j++)
       mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
+  if (a.kind == KC_REDUCE_ADD) {
+    reduce_rows(a.peer, out0, u0, u1, par, seq);
+    __syncthreads();
+    if (tid == 0)
+      a.peer.epoch[c] = seq;
+  }
   if (a.tail.kind == KC_TAIL_QUANTIZE_OUTPUT) {
     __syncthreads();
     quantize_output_groups(a.tail, out0, u0, u1, gs, reinterpret_cast<int *>(stages));
@@ -804,7 +868,7 @@ static int launch_generic(const KcGemvSeg *segs, int nseg, const int8_t *xq, con
 
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
                       long long ld, int gs, int kind, cudaStream_t stream, int grid_limit,
-                      const KcGemvTail *tail = nullptr);
+                      const KcGemvTail *tail = nullptr, const KcPeerGemv *peer = nullptr);
 
 // The W8A32 GEMV (see gemv_q8f_kernel): 16 rows per 256-thread CTA on the AVX order, 256 on the portable one.
 int kc_launch_gemv_w8a32(const KcGemvSeg *segs, int nseg, const float *x, int n, long long ld, int gs, int kind,
@@ -852,8 +916,16 @@ int kc_launch_gemv_f32(const KcGemvSeg *segs, int nseg, const KcGemvAct &act, in
   return launch_tma(segs, nseg, nullptr, nullptr, &act, n, ld, gs, kind, stream, 0, tail);
 }
 
+// The reducing GEMV: the TMA kernel only (-1 when the shape does not fit it; there is no general rung to fall back
+// to, as every rank must run the same kernel).
+int kc_launch_gemv_reduce(const KcGemvSeg &seg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                          const KcPeerGemv &peer, cudaStream_t stream) {
+  return launch_tma(&seg, 1, xq, xs, nullptr, n, ld, gs, KC_REDUCE_ADD, stream, 0, nullptr, &peer);
+}
+
 static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const float *xs, const KcGemvAct *act, int n,
-                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit, const KcGemvTail *tail) {
+                      long long ld, int gs, int kind, cudaStream_t stream, int grid_limit, const KcGemvTail *tail,
+                      const KcPeerGemv *peer) {
   thread_local GemvMaps M;
   GemvArgs A;
   memset(&M, 0, sizeof(M));
@@ -868,6 +940,12 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     A.eps = act->eps;
     A.act = act->norm ? kActNormQuantize : kActQuantize;
     act_floats = act->norm ? 2 * n : n;
+  }
+  if (kind == KC_REDUCE_ADD) {
+    if (!peer || nseg != 1 || tail || act || segs[0].d <= 0 || segs[0].d > peer->stride || peer->world < 1 ||
+        peer->world > kPeerMaxRanks || peer->rank < 0 || peer->rank >= peer->world || !peer->epoch)
+      return -1;
+    A.peer = *peer;
   }
   const bool swiglu = kind == KC_SWIGLU;
   const int box_rows = swiglu ? kTileRows / 2 : kTileRows;
@@ -948,6 +1026,8 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   int grid = units < sms ? units : sms;
   if (grid_limit > 0 && grid > grid_limit)
     grid = grid_limit;
+  if (kind == KC_REDUCE_ADD)  // one grid size for every call: each CTA's counter counts every call
+    grid = sms < kPeerGemvMaxCtas ? sms : kPeerGemvMaxCtas;
   static bool attr_set[64][2];
   int dev = 0;
   cudaGetDevice(&dev);

@@ -6,8 +6,22 @@
 #include <stdint.h>
 
 // Epilogue kinds, numerically equal to the reference's KernelEpilogue / GemmKind (include/kernels.h:84,
-// include/gemm.h:15-20): STORE, ADD, PARTIAL, SWIGLU.
-enum { KC_STORE = 0, KC_ADD = 1, KC_PARTIAL = 2, KC_SWIGLU = 3 };
+// include/gemm.h:15-20): STORE, ADD, PARTIAL, SWIGLU. KC_REDUCE_ADD (the decode GEMV only) is PARTIAL followed by
+// the tensor-parallel sum over ranks, added into the output: out += sum over ranks of this product, in rank order.
+enum { KC_STORE = 0, KC_ADD = 1, KC_PARTIAL = 2, KC_SWIGLU = 3, KC_REDUCE_ADD = 4 };
+
+// The reducing GEMV's view of the peer state (peer.cu): every rank's slot region [2 parities][world][stride] of
+// 8-byte {float bits, call number} slots as mapped in this process, and this rank's per-CTA call counters. The
+// reducing GEMV always launches min(SMs, kPeerGemvMaxCtas) CTAs, whatever the shape, so every counter advances on
+// every call and all of them hold the number of calls made.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerGemvMaxCtas = 256;
+struct KcPeerGemv {
+  unsigned long long *slots[kPeerMaxRanks];
+  unsigned *epoch;  // [kPeerGemvMaxCtas]
+  long long stride;
+  int rank, world;
+};
 
 struct KcGemvSeg {
   float *out;
@@ -85,6 +99,12 @@ struct KcGemvAct {
   const float *norm;
   float eps;
 };
+// The reducing decode GEMV: one segment (out, wq, ws, d <= peer.stride), int8 activations; out[r] += the sum over
+// ranks, in rank order, of every rank's product row r (0, -1 for a shape the TMA kernel does not take, -2 on a launch
+// error). Every rank must make the same calls in the same order.
+int kc_launch_gemv_reduce(const KcGemvSeg &seg, const int8_t *xq, const float *xs, int n, long long ld, int gs,
+                          const KcPeerGemv &peer, cudaStream_t stream);
+
 // W8A32: fp32 activations against int8 weights, the reference's orders (0, or -2 on a launch error).
 int kc_launch_gemv_w8a32(const KcGemvSeg *segs, int nseg, const float *x, int n, long long ld, int gs, int kind,
                          cudaStream_t stream);

@@ -5,8 +5,10 @@
 // not bandwidth: one kernel per reduction, no library collective.
 //
 // Layout: each rank owns one device allocation, exported with CUDA IPC and mapped by every other rank:
-//   recv [2 parities][world sources][stride] 8-byte slots {float bits, call number}
-// and a private epoch [ctas] (calls completed per CTA; the same on every rank, as every rank makes the same calls).
+//   recv [2 parities][world sources][stride] 8-byte slots {float bits, call number}   (kd_peer_allreduce_add)
+//   gemv [2 parities][world sources][stride] the same, for the reducing GEMV           (kd_peer_matmul_q8_add)
+// and private epochs (calls completed per CTA; the same on every rank, as every rank makes the same calls), one
+// array per user, so that the two kinds of call can interleave in any order.
 // Call number seq = epoch[c] + 1 selects the parity, so a rank can be one call ahead of a peer without overwriting what
 // the peer still reads (a rank reaches call seq + 2 only after every peer has pushed call seq + 1, which each does
 // only after finishing call seq).
@@ -38,16 +40,6 @@ struct PeerArgs {
   int rank, world, ctas;
 };
 
-__device__ __forceinline__ unsigned long long ld_slot(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_slot(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_add_kernel(const PeerArgs a, float *x,
                                                                           const float *partial, int n) {
   pdl_wait();  // the partial comes from the previous kernel
@@ -61,7 +53,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_add_kernel(const 
 #pragma unroll
     for (int p = 0; p < kPeerMax; p++)  // static indices: the pointers stay in parameter space
       if (p < a.world)
-        st_slot(a.recv[p] + (par * a.world + a.rank) * a.stride + i, v);
+        peer_st_slot(a.recv[p] + (par * a.world + a.rank) * a.stride + i, v);
   }
   const unsigned long long *mine = a.recv[0];
 #pragma unroll
@@ -73,14 +65,14 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_add_kernel(const 
   for (int i = lo + tid; i < hi; i += kPeerThreads) {
     float s = 0.0f;
     for (int r = 0; r < a.world && ok; r++) {
-      unsigned long long v = ld_slot(mine + r * a.stride + i);
+      unsigned long long v = peer_ld_slot(mine + r * a.stride + i);
       for (unsigned k = 1; (unsigned)(v >> 32) != seq; k++) {
         if ((k & 63u) == 0 && kc_globaltimer() - start > KC_WAIT_NS) {
           kc_raise(KC_ERR_TIMEOUT);
           ok = false;
           break;
         }
-        v = ld_slot(mine + r * a.stride + i);
+        v = peer_ld_slot(mine + r * a.stride + i);
       }
       const float f = __uint_as_float((unsigned)v);
       s = r == 0 ? f : __fadd_rn(s, f);
@@ -95,6 +87,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_add_kernel(const 
 
 struct PeerState {
   PeerArgs args;
+  KcPeerGemv gemv;           // the reducing GEMV's slots (second half of every rank's allocation) and epochs
   void *base;                // this rank's exported allocation (the slots)
   void *opened[kPeerMax];    // the peers' allocations mapped here
   size_t max_floats;
@@ -125,11 +118,13 @@ void kd_peer_free(void *peer) {
     cudaFree(s->base);
   if (s->args.epoch)
     cudaFree(s->args.epoch);
+  if (s->gemv.epoch)
+    cudaFree(s->gemv.epoch);
   delete s;
 }
 
 void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
-  if (!comm || world < 2 || world > kPeerMax || rank < 0 || rank >= world || max_floats == 0 ||
+  if ((!comm && world > 1) || world < 1 || world > kPeerMax || rank < 0 || rank >= world || max_floats == 0 ||
       max_floats > (1u << 26)) {
     kc_fail("kd_peer_init: invalid arguments (rank %d of %d, %zu floats)", rank, world, max_floats);
     return nullptr;
@@ -145,6 +140,9 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
   s->args.rank = rank;
   s->args.world = world;
   s->args.ctas = ctas;
+  s->gemv.stride = stride;
+  s->gemv.rank = rank;
+  s->gemv.world = world;
   cudaIpcMemHandle_t mine, all[kPeerMax];
   static_assert(sizeof(cudaIpcMemHandle_t) % sizeof(float) == 0, "IPC handle size");
   constexpr size_t hf = sizeof(cudaIpcMemHandle_t) / sizeof(float);
@@ -156,13 +154,25 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
   }
   // Local set-up; a failure here still takes part in the exchange below (with an all-zero handle), so that no rank
   // is left waiting in the collective. The engine then agrees on NCCL with the others.
-  bool ok = cuda_ok(cudaMalloc(&s->base, recv_bytes), "kd_peer_init: cudaMalloc") &&
+  bool ok = cuda_ok(cudaMalloc(&s->base, 2 * recv_bytes), "kd_peer_init: cudaMalloc") &&
             cuda_ok(cudaMalloc(&s->args.epoch, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
-            cuda_ok(cudaMemset(s->base, 0, recv_bytes), "kd_peer_init: cudaMemset") &&
+            cuda_ok(cudaMalloc(&s->gemv.epoch, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
+            cuda_ok(cudaMemset(s->base, 0, 2 * recv_bytes), "kd_peer_init: cudaMemset") &&
             cuda_ok(cudaMemset(s->args.epoch, 0, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
+            cuda_ok(cudaMemset(s->gemv.epoch, 0, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
             // Zeroed before any peer can learn the handle: a peer's first store lands after this.
             cuda_ok(cudaDeviceSynchronize(), "kd_peer_init: synchronize") &&
-            cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle");
+            (world == 1 || cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle"));
+  if (world == 1) {  // one rank: its own slots only, nothing to exchange
+    cudaFree(xchg);
+    s->args.recv[0] = reinterpret_cast<unsigned long long *>(s->base);
+    s->gemv.slots[0] = reinterpret_cast<unsigned long long *>(static_cast<char *>(s->base) + recv_bytes);
+    if (!ok) {
+      kd_peer_free(s);
+      return nullptr;
+    }
+    return s;
+  }
   if (!ok)
     memset(&mine, 0, sizeof(mine));
   // Every rank's handle to every rank, through the NCCL communicator (on the calling thread's stream).
@@ -187,6 +197,7 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
       b = static_cast<char *>(m);
     }
     s->args.recv[p] = reinterpret_cast<unsigned long long *>(b);
+    s->gemv.slots[p] = reinterpret_cast<unsigned long long *>(b ? b + recv_bytes : nullptr);
   }
   if (!ok) {
     kd_peer_free(s);
@@ -206,6 +217,34 @@ int kd_peer_allreduce_add(void *peer, float *x, const float *partial, size_t n) 
   if (e != cudaSuccess) {
     cudaGetLastError();
     kc_fail("kd_peer_allreduce_add: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  kc_count_launch();
+  return 0;
+}
+
+int kd_peer_matmul_q8_add(void *peer, float *x, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                          size_t ld, int n, int d, int gs) {
+  const PeerState *s = static_cast<const PeerState *>(peer);
+  if (!s || !x || !xq || !xs || !wq || !ws || n <= 0 || d <= 0 || (size_t)d > s->max_floats || gs <= 0 ||
+      n % gs || ld < (size_t)n || ld % gs || ld > (size_t)INT32_MAX) {
+    kc_fail("kd_peer_matmul_q8_add: invalid arguments (ld %zu, n %d, d %d, gs %d)", ld, n, d, gs);
+    return -1;
+  }
+  KcGemvSeg seg = {};
+  seg.out = x;
+  seg.wq = wq;
+  seg.ws = ws;
+  seg.d = d;
+  const int rc = kc_launch_gemv_reduce(seg, xq, xs, n, (long long)ld, gs, s->gemv, kc_stream());
+  if (rc == -1) {
+    kc_fail("kd_peer_matmul_q8_add: shape not supported by the reducing GEMV (n %d, gs %d, 16-byte aligned "
+            "activations and scale rows needed)", n, gs);
+    return -1;
+  }
+  if (rc != 0) {
+    const cudaError_t e = cudaGetLastError();
+    kc_fail("kd_peer_matmul_q8_add: %s", cudaGetErrorString(e));
     return -1;
   }
   kc_count_launch();

@@ -96,6 +96,8 @@ DEVICE_SIGNATURES = {
     "kd_peer_init": (_c.c_void_p, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_size_t]),
     "kd_peer_allreduce_add": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
     "kd_peer_free": (None, [_c.c_void_p]),
+    "kd_peer_matmul_q8_add": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                         _c.c_size_t, _c.c_int, _c.c_int, _c.c_int]),
 }
 
 _engine = None

@@ -63,6 +63,7 @@ typedef struct {
   void *peer; /* peer-memory all-reduce of the decode residual (kd_peer_*), or NULL for NCCL */
   int w8a32;  /* LLAMA_Q8_ACTIVATIONS=fp32: fp32 activations against the int8 weights, one row per forward */
   int fused;  /* the decode step's fused GEMV modes fit these shapes (fused_shapes) */
+  int reduce_fused; /* with peer: Wo and W2 reduce inside their GEMV (kd_peer_matmul_q8_add, reduce_shapes) */
   float *xb;  /* W8A32: the normalized row the projections read */
   void *graph_logits, *graph_greedy;
   unsigned long long graph_logits_kernels, graph_greedy_kernels; /* kernels captured in each graph */
@@ -244,8 +245,19 @@ static int fused_shapes(const Engine *e) {
 }
 
 /* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. */
+/* The reducing GEMV is the TMA GEMV on int8 inputs: Wo reads ql of them, W2 hid_l, each a whole number of 4-group
+ * units. It is used with LLAMA_PEER_GEMV=1 (the same on every rank); otherwise the PARTIAL GEMV +
+ * kd_peer_allreduce_add pair reduces. */
+static int reduce_shapes(const Engine *e) {
+  int gs = e->gs;
+  const char *on = getenv("LLAMA_PEER_GEMV");
+  return on && !strcmp(on, "1") && e->fused && e->ql % gs == 0 && (e->ql / gs) % 4 == 0 &&
+         (e->hid_l / gs) % 4 == 0;
+}
+
 static int max_batch_for(Engine *e) {
   e->fused = fused_shapes(e); /* plan() has set the shard shapes */
+  e->reduce_fused = reduce_shapes(e);
   return e->w8a32 ? 1 : prefill_batch_from_env(e->context);
 }
 
@@ -803,8 +815,12 @@ static void decode_layers(Engine *e) {
                          e->context);
     k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
                         1, gs);
+    /* Tensor parallel with the peer path: the shard's product and the sum over ranks in one kernel. */
+    const int reduce_in_gemv = e->S > 1 && e->peer && e->reduce_fused;
     if (e->S == 1) {
       k_matmul_q8_add(e->x, &att, k8(y->wo), e->ql, dim, gs);
+    } else if (reduce_in_gemv) {
+      kd_peer_matmul_q8_add(e->peer, e->x, e->aq, e->as, y->wo.q, y->wo.s, (size_t)e->ql, e->ql, dim, gs);
     } else {
       K8Weight wo = k8(y->wo);
       k_matmul_q8_ld(e->partial, &att, &wo, e->ql, e->ql, dim, gs, K_PARTIAL);
@@ -812,11 +828,15 @@ static void decode_layers(Engine *e) {
     }
     GemmQ8Segment up = segment(e->hb, e->hid_l, y->w1, y->w3, e->hid_l, GEMM_SWIGLU);
     k_matmul_q8_fused(e->x, y->rms_ffn, p->norm_eps, dim, dim, gs, &up, 1, &quant_hidden);
-    K8Weight w2 = k8(y->w2);
-    k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &hid, &w2, e->hid_l, e->hid_l, dim, gs,
-                   e->S == 1 ? K_ADD : K_PARTIAL);
-    if (e->S > 1)
-      residual_reduce(e, 1);
+    if (reduce_in_gemv) {
+      kd_peer_matmul_q8_add(e->peer, e->x, e->hq, e->hs, y->w2.q, y->w2.s, (size_t)e->hid_l, e->hid_l, dim, gs);
+    } else {
+      K8Weight w2 = k8(y->w2);
+      k_matmul_q8_ld(e->S == 1 ? e->x : e->partial, &hid, &w2, e->hid_l, e->hid_l, dim, gs,
+                     e->S == 1 ? K_ADD : K_PARTIAL);
+      if (e->S > 1)
+        residual_reduce(e, 1);
+    }
   }
   GemmQ8Segment cls = segment(e->logits_dev, e->vl, e->cls, none, e->vl, GEMM_STORE);
   k_matmul_q8_fused(e->x, e->rms_final, p->norm_eps, dim, dim, gs, &cls, 1, NULL);

@@ -28,6 +28,7 @@ def _rank(rank, world, nccl_id, path, prompt, out, peer=True):
     try:
         import os
         os.environ["LLAMA_PEER_ALLREDUCE"] = "1" if peer else "0"
+        os.environ["LLAMA_PEER_GEMV"] = "0" if peer == "kernel" else "1"
         from conftest import load_engine
         eng = load_engine()
         with eng.Engine.load(path, tp=(rank, world, rank, nccl_id)) as m:
@@ -65,9 +66,11 @@ def small(tmp_path_factory):
     return models.write_model(tmp_path_factory.mktemp("tp") / "small.bin", "small")
 
 
-@pytest.mark.parametrize("world,peer", [(2, True), (4, True), (8, True), (2, False)])
+@pytest.mark.parametrize("world,peer", [(2, True), (4, True), (8, True), (2, "kernel"), (2, False)])
 def test_tensor_parallel_matches_reference_and_one_gpu(small, world, peer):
-    """peer: the decode residual reduced through peer memory (kd_peer_allreduce_add, the default) or NCCL."""
+    """peer: the decode residual reduced through peer memory (True: inside the Wo / W2 GEMV, LLAMA_PEER_GEMV=1, where
+    the shard shapes allow it, which the small model's do at 2 ranks, else kd_peer_allreduce_add), through
+    kd_peer_allreduce_add after a PARTIAL GEMV ("kernel", LLAMA_PEER_GEMV=0), or through NCCL (False)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     prompt = GOLDEN["small_prompt"]
