@@ -510,7 +510,8 @@ __device__ __forceinline__ void reduce_rows(const KcPeerGemv &p, float *out, int
   }
 }
 
-template <int GS>
+// RED: the KC_REDUCE_ADD instantiation; the others carry none of its code.
+template <int GS, bool RED>
 __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_constant__ GemvMaps m, const GemvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // The 128-byte swizzle is a function of the address bits, so the stages start on a 1024-byte boundary.
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (u1 <= u0) {
     if (a.tail.kind && a.tail.kind != KC_TAIL_QUANTIZE_OUTPUT)
       finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem));
-    if (a.kind == KC_REDUCE_ADD) {  // no rows, but the call still counts
+    if (RED) {  // no rows, but the call still counts
       pdl_wait();
       if (tid == 0)
         a.peer.epoch[c] += 1u;
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
     issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &bars[0]);
   pdl_wait();
   // The counter was written by the previous reducing call, complete once pdl_wait returns.
-  const unsigned seq = a.kind == KC_REDUCE_ADD ? a.peer.epoch[c] + 1u : 0u;
+  const unsigned seq = RED ? a.peer.epoch[c] + 1u : 0u;
   const long long par = seq & 1u;
   if (a.act == kActQ8) {
     for (int i = tid; i < n / 16; i += kThreads)
@@ -667,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
         } else if (lane < t.cnt) {
           if (a.kind == KC_ADD)
             out[lane] = __fadd_rn(out[lane], acc);
-          else if (a.kind == KC_REDUCE_ADD)
+          else if (RED)
             push_row(a.peer, par, seq, t.row0 + lane, acc);
           else
             out[lane] = acc;
@@ -698,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   if (*abort_flag && tid == 0)
     for (int j = max(0, *issued - depth); j < *issued; j++)
       mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
-  if (a.kind == KC_REDUCE_ADD) {
+  if (RED) {
     reduce_rows(a.peer, out0, u0, u1, par, seq);
     __syncthreads();
     if (tid == 0)
@@ -1028,13 +1029,14 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     grid = grid_limit;
   if (kind == KC_REDUCE_ADD)  // one grid size for every call: each CTA's counter counts every call
     grid = sms < kPeerGemvMaxCtas ? sms : kPeerGemvMaxCtas;
-  static bool attr_set[64][2];
+  static bool attr_set[64][4];
   int dev = 0;
   cudaGetDevice(&dev);
-  const int variant = gs == 64 ? 0 : 1;
+  const int variant = (gs == 64 ? 0 : 1) + (kind == KC_REDUCE_ADD ? 2 : 0);
+  void (*const kernels[4])(const GemvMaps, const GemvArgs) = {gemv_q8_kernel<64, false>, gemv_q8_kernel<0, false>,
+                                                              gemv_q8_kernel<64, true>, gemv_q8_kernel<0, true>};
   if (dev < 64 && !attr_set[dev][variant]) {
-    cudaFuncSetAttribute(variant == 0 ? gemv_q8_kernel<64> : gemv_q8_kernel<0>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(kernels[variant], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr_set[dev][variant] = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -1047,7 +1049,6 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = variant == 0 ? cudaLaunchKernelEx(&cfg, gemv_q8_kernel<64>, M, A)
-                               : cudaLaunchKernelEx(&cfg, gemv_q8_kernel<0>, M, A);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[variant], M, A);
   return e == cudaSuccess ? 0 : -2;
 }

@@ -246,12 +246,11 @@ static int fused_shapes(const Engine *e) {
 
 /* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. */
 /* The reducing GEMV is the TMA GEMV on int8 inputs: Wo reads ql of them, W2 hid_l, each a whole number of 4-group
- * units. It is used with LLAMA_PEER_GEMV=1 (the same on every rank); otherwise the PARTIAL GEMV +
- * kd_peer_allreduce_add pair reduces. */
+ * units. LLAMA_PEER_GEMV=0 (the same on every rank) keeps the PARTIAL GEMV + kd_peer_allreduce_add pair instead. */
 static int reduce_shapes(const Engine *e) {
   int gs = e->gs;
-  const char *on = getenv("LLAMA_PEER_GEMV");
-  return on && !strcmp(on, "1") && e->fused && e->ql % gs == 0 && (e->ql / gs) % 4 == 0 &&
+  const char *off = getenv("LLAMA_PEER_GEMV");
+  return !(off && !strcmp(off, "0")) && e->fused && e->ql % gs == 0 && (e->ql / gs) % 4 == 0 &&
          (e->hid_l / gs) % 4 == 0;
 }
 

@@ -68,8 +68,8 @@ def small(tmp_path_factory):
 
 @pytest.mark.parametrize("world,peer", [(2, True), (4, True), (8, True), (2, "kernel"), (2, False)])
 def test_tensor_parallel_matches_reference_and_one_gpu(small, world, peer):
-    """peer: the decode residual reduced through peer memory (True: inside the Wo / W2 GEMV, LLAMA_PEER_GEMV=1, where
-    the shard shapes allow it, which the small model's do at 2 ranks, else kd_peer_allreduce_add), through
+    """peer: the decode residual reduced through peer memory (True, the default: inside the Wo / W2 GEMV where the
+    shard shapes allow it, which the small model's do at 2 ranks, else kd_peer_allreduce_add), through
     kd_peer_allreduce_add after a PARTIAL GEMV ("kernel", LLAMA_PEER_GEMV=0), or through NCCL (False)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
