@@ -103,6 +103,43 @@ bool cuda_ok(cudaError_t e, const char *what) {
   return false;
 }
 
+// A state for `rank` of `world` with this rank's slots (both regions) and call counters allocated and zeroed. *ok is
+// false after a CUDA failure (reported on stderr); the state is returned either way, for the caller to free.
+PeerState *local_state(int rank, int world, size_t max_floats, size_t *recv_bytes, bool *ok) {
+  PeerState *s = new PeerState();
+  memset(s, 0, sizeof(*s));
+  s->max_floats = max_floats;
+  int ctas = (int)((max_floats + kPeerThreads - 1) / kPeerThreads);  // a slot per thread
+  ctas = ctas < 1 ? 1 : ctas > kPeerMaxCtas ? kPeerMaxCtas : ctas;
+  const long long stride = (long long)((max_floats + 31) / 32 * 32);
+  *recv_bytes = (size_t)2 * world * stride * sizeof(unsigned long long);
+  s->args.stride = stride;
+  s->args.rank = rank;
+  s->args.world = world;
+  s->args.ctas = ctas;
+  s->gemv.stride = stride;
+  s->gemv.rank = rank;
+  s->gemv.world = world;
+  const size_t bytes = 2 * *recv_bytes;
+  *ok = cuda_ok(cudaMalloc(&s->base, bytes), "kd_peer_init: cudaMalloc") &&
+        cuda_ok(cudaMalloc(&s->args.epoch, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
+        cuda_ok(cudaMalloc(&s->gemv.epoch, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
+        cuda_ok(cudaMemset(s->base, 0, bytes), "kd_peer_init: cudaMemset") &&
+        cuda_ok(cudaMemset(s->args.epoch, 0, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
+        cuda_ok(cudaMemset(s->gemv.epoch, 0, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
+        // Zeroed before any peer can learn the handle: a peer's first store lands after this.
+        cuda_ok(cudaDeviceSynchronize(), "kd_peer_init: synchronize");
+  return s;
+}
+
+// Every rank's slots are this process's own buffer: the single-rank state, and the test hook's absent peers.
+void map_local(PeerState *s, size_t recv_bytes) {
+  for (int p = 0; p < s->args.world; p++) {
+    s->args.recv[p] = reinterpret_cast<unsigned long long *>(s->base);
+    s->gemv.slots[p] = reinterpret_cast<unsigned long long *>(static_cast<char *>(s->base) + recv_bytes);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -129,50 +166,29 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
     kc_fail("kd_peer_init: invalid arguments (rank %d of %d, %zu floats)", rank, world, max_floats);
     return nullptr;
   }
-  PeerState *s = new PeerState();
-  memset(s, 0, sizeof(*s));
-  s->max_floats = max_floats;
-  int ctas = (int)((max_floats + kPeerThreads - 1) / kPeerThreads);  // a slot per thread
-  ctas = ctas < 1 ? 1 : ctas > kPeerMaxCtas ? kPeerMaxCtas : ctas;
-  const long long stride = (long long)((max_floats + 31) / 32 * 32);
-  const size_t recv_bytes = (size_t)2 * world * stride * sizeof(unsigned long long);
-  s->args.stride = stride;
-  s->args.rank = rank;
-  s->args.world = world;
-  s->args.ctas = ctas;
-  s->gemv.stride = stride;
-  s->gemv.rank = rank;
-  s->gemv.world = world;
+  size_t recv_bytes = 0;
+  bool ok = false;
+  PeerState *s = local_state(rank, world, max_floats, &recv_bytes, &ok);
+  if (world == 1) {  // one rank: its own slots only, nothing to exchange
+    if (!ok) {
+      kd_peer_free(s);
+      return nullptr;
+    }
+    map_local(s, recv_bytes);
+    return s;
+  }
   cudaIpcMemHandle_t mine, all[kPeerMax];
   static_assert(sizeof(cudaIpcMemHandle_t) % sizeof(float) == 0, "IPC handle size");
   constexpr size_t hf = sizeof(cudaIpcMemHandle_t) / sizeof(float);
   memset(&mine, 0, sizeof(mine));
   float *xchg = nullptr;
   if (!cuda_ok(cudaMalloc(&xchg, (world + 1) * sizeof(cudaIpcMemHandle_t)), "kd_peer_init: cudaMalloc")) {
-    delete s;
+    kd_peer_free(s);
     return nullptr;
   }
-  // Local set-up; a failure here still takes part in the exchange below (with an all-zero handle), so that no rank
-  // is left waiting in the collective. The engine then agrees on NCCL with the others.
-  bool ok = cuda_ok(cudaMalloc(&s->base, 2 * recv_bytes), "kd_peer_init: cudaMalloc") &&
-            cuda_ok(cudaMalloc(&s->args.epoch, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
-            cuda_ok(cudaMalloc(&s->gemv.epoch, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMalloc") &&
-            cuda_ok(cudaMemset(s->base, 0, 2 * recv_bytes), "kd_peer_init: cudaMemset") &&
-            cuda_ok(cudaMemset(s->args.epoch, 0, kPeerMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
-            cuda_ok(cudaMemset(s->gemv.epoch, 0, kPeerGemvMaxCtas * sizeof(unsigned)), "kd_peer_init: cudaMemset") &&
-            // Zeroed before any peer can learn the handle: a peer's first store lands after this.
-            cuda_ok(cudaDeviceSynchronize(), "kd_peer_init: synchronize") &&
-            (world == 1 || cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle"));
-  if (world == 1) {  // one rank: its own slots only, nothing to exchange
-    cudaFree(xchg);
-    s->args.recv[0] = reinterpret_cast<unsigned long long *>(s->base);
-    s->gemv.slots[0] = reinterpret_cast<unsigned long long *>(static_cast<char *>(s->base) + recv_bytes);
-    if (!ok) {
-      kd_peer_free(s);
-      return nullptr;
-    }
-    return s;
-  }
+  // A local set-up failure still takes part in the exchange below (with an all-zero handle), so that no rank is left
+  // waiting in the collective. The engine then agrees on NCCL with the others.
+  ok = ok && cuda_ok(cudaIpcGetMemHandle(&mine, s->base), "kd_peer_init: cudaIpcGetMemHandle");
   if (!ok)
     memset(&mine, 0, sizeof(mine));
   // Every rank's handle to every rank, through the NCCL communicator (on the calling thread's stream).
@@ -203,6 +219,22 @@ void *kd_peer_init(void *comm, int rank, int world, size_t max_floats) {
     kd_peer_free(s);
     return nullptr;
   }
+  return s;
+}
+
+void *kd_peer_test_absent(int world, size_t max_floats) {
+  if (world < 2 || world > kPeerMax || max_floats == 0 || max_floats > (1u << 26)) {
+    kc_fail("kd_peer_test_absent: invalid arguments (%d ranks, %zu floats)", world, max_floats);
+    return nullptr;
+  }
+  size_t recv_bytes = 0;
+  bool ok = false;
+  PeerState *s = local_state(0, world, max_floats, &recv_bytes, &ok);
+  if (!ok) {
+    kd_peer_free(s);
+    return nullptr;
+  }
+  map_local(s, recv_bytes);
   return s;
 }
 

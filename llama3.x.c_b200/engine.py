@@ -98,6 +98,7 @@ DEVICE_SIGNATURES = {
     "kd_peer_free": (None, [_c.c_void_p]),
     "kd_peer_matmul_q8_add": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
                                          _c.c_size_t, _c.c_int, _c.c_int, _c.c_int]),
+    "kd_peer_test_absent": (_c.c_void_p, [_c.c_int, _c.c_size_t]),
 }
 
 _engine = None

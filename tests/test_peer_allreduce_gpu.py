@@ -212,3 +212,45 @@ def test_peer_single_rank_reducing_gemv(kc, oracle):
             assert (got.view(np.int32) == want.view(np.int32)).all(), call
     finally:
         lib.kd_peer_free(peer)
+
+
+def test_peer_absent_rank_times_out(kc, oracle):
+    """A rank that never arrives (kd_peer_test_absent: rank 0 of 2, the other rank's slots never written), the GPU form
+    of the reference's exchange-fail tests: the reducing GEMV and the standalone all-reduce each give up after the
+    2 s device wait limit, kc_status reports the timeout, x keeps its value, and the context stays usable."""
+    import ctypes
+    import time
+    from conftest import load_engine
+    lib = load_engine().load_library()
+    kc.status()
+    d, n = 256, 256
+    dev = [torch.from_numpy(v).cuda() for v in gemv_inputs(oracle, 0, 0, d, n)]
+    x0 = dev[0].cpu().numpy()
+    part = torch.ones(d, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    p = [ctypes.c_void_p(t.data_ptr()) for t in dev]
+    peer = lib.kd_peer_test_absent(2, DIM)
+    assert peer, "kd_peer_test_absent failed"
+    try:
+        start = time.monotonic()
+        assert lib.kd_peer_matmul_q8_add(peer, p[0], p[1], p[2], p[3], p[4], n, n, d, 64) == 0
+        with pytest.raises(kc.KernelError, match="timed out"):
+            kc.status()
+        assert lib.kd_peer_allreduce_add(peer, p[0], ctypes.c_void_p(part.data_ptr()), d) == 0
+        with pytest.raises(kc.KernelError, match="timed out"):
+            kc.status()
+        assert time.monotonic() - start < 30
+        assert (dev[0].cpu().numpy().view(np.int32) == x0.view(np.int32)).all()
+    finally:
+        lib.kd_peer_free(peer)
+    # The same context runs the next reduction normally.
+    one = lib.kd_peer_init(None, 0, 1, DIM)
+    assert one, "kd_peer_init failed"
+    try:
+        assert lib.kd_peer_matmul_q8_add(one, p[0], p[1], p[2], p[3], p[4], n, n, d, 64) == 0
+        got = dev[0].cpu().numpy()
+        kc.status()
+    finally:
+        lib.kd_peer_free(one)
+    want = gemv_expected(oracle, 1, 0, d, n)
+    assert (got.view(np.int32) == want.view(np.int32)).all()
