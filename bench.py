@@ -1,8 +1,9 @@
 #!/usr/bin/env python
 """Benchmark of the Q8_0 W8A8 path on B200: one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload 8b|1b|gemv|ffn|gemm]
-                    [--profile-request] [--no-cpu-baseline]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 8b|1b|gemv|ffn|gemm|sweep] [--profile-request] [--no-cpu-baseline]
+                    [--sweep-t 1,2,...] [--sweep-s 1,2,4,8] [--sweep-rows-max 16]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N   (N = 2, 4, 8)
 
 Workloads (seeded synthetic data, random-init weights of the named architecture, Q8_0 gs 64):
@@ -13,6 +14,9 @@ Workloads (seeded synthetic data, random-init weights of the name
   1b    config 2: Llama-3.2-1B architecture (tied classifier), 128-token prompt, 256 tokens.
   gemv  config 0 kernel alone: quantize + GEMV 8192 x 2048 (for profiling; not the headline).
   ffn   the dominant decode kernel alone: the 8B SwiGLU GEMV (W1 and W3, 14336 x 4096 each) on rotating weights.
+  gemm  config 1: the prefill GEMM alone (8B up and down projections, T = 128 / 512 / 2048).
+  sweep config 4: every 8B projection's rank-0 shard at S = 1/2/4/8 times T activation rows, the tensor-core GEMM
+        against one decode GEMV per row, and the crossover T per shard.
 
 --profile-request (8b / 1b) runs one short request (the prefill and 4 greedy tokens) and nothing else, for an ncu launch
 list of every kernel the request launches.
@@ -497,13 +501,129 @@ def run_gemm(args):
                       "shapes": shapes}), flush=True)
 
 
+# ---- config 4: the GEMV -> tensor-core GEMM crossover sweep -------------------------------------------------------
+
+# Every 8B projection as (weight rows N, K, split): "rows" shards split the output rows over S ranks (wq, wk/wv, w1/w3,
+# the classifier), "cols" shards the input columns (wo, w2), as the reference's shard plan does (src/shards.c:223-248).
+SWEEP_PROJECTIONS = {"wq": (4096, 4096, "rows"), "wk/wv": (1024, 4096, "rows"), "wo": (4096, 4096, "cols"),
+                     "w1/w3": (14336, 4096, "rows"), "w2": (4096, 14336, "cols"), "cls": (128256, 4096, "rows")}
+SWEEP_T = (1, 2, 4, 8, 16, 64, 256, 1024, 4096)
+
+
+def timed_graph(torch, launch, warmup, launches):
+    """Mean microseconds of `launch(i)`: warm-up calls, then `launches` calls captured in one graph with a pair of CUDA
+    events around each, replayed once."""
+    for i in range(warmup):
+        launch(i)
+    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+           for _ in range(launches)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(launches):
+            evs[i][0].record()
+            launch(warmup + i)
+            evs[i][1].record()
+    graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    return float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
+
+
+def run_sweep(args):
+    """Config 4 on one GPU: each 8B projection's rank-0 shard at S = 1/2/4/8 (rows N/S for row-split weights, columns
+    K/S for wo and w2; the all-reduce that joins column shards is not part of this figure) times T activation rows.
+    At every T the tensor-core GEMM (k_gemm_q8's Q8_GEMM_GPU_TCGEN05 rung) runs; up to T = --sweep-rows-max the
+    one-GEMV-per-row rung (Q8_GEMM_GPU_DP4A, what k_gemm_q8 takes below its row threshold) runs beside it. Weights
+    rotate over enough copies to exceed L2 three times and the copy index runs on across launches, so every launch
+    reads weights no recent launch touched. The crossover of a shard is the smallest swept T from which the GEMM is
+    faster at every larger T where both ran."""
+    import torch
+    kc = load_package()
+    kc.init()
+    hbm, peak_kind = peaks()
+    pk = ROOT / "MEASURED_PEAKS.json"
+    bf16 = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
+    int8_tops = 2 * bf16
+    ts = [int(t) for t in args.sweep_t.split(",")] if args.sweep_t else list(SWEEP_T)
+    splits = [int(s) for s in args.sweep_s.split(",")]
+    gs, points, crossover = 64, [], {}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    for S in splits:
+        for name, (N, K, split) in SWEEP_PROJECTIONS.items():
+            n, k = (N // S, K) if split == "rows" else (N, K // S)
+            w = torch.randn((n, k), generator=g, device="cuda") * 0.02
+            wq, ws = kc.quantize(w, gs)
+            del w
+            wbytes = wq.numel() + ws.numel() * 4
+            copies = max(2, -(-3 * L2_BYTES // wbytes))
+            W = [(wq.clone(), ws.clone()) for _ in range(copies)]
+            del wq, ws
+            ctr = [0]
+            wins = {}
+            for T in ts:
+                x = torch.randn((T, k), generator=g, device="cuda")
+                xq, xs = kc.quantize(x, gs)
+                del x
+                c = torch.empty((T, n), device="cuda")
+
+                def launch(backend):
+                    def f(_i):
+                        wq_, ws_ = W[ctr[0] % copies]
+                        ctr[0] += 1
+                        if not kc.k_gemm_q8_backend_test(backend, xq, xs, T, k, gs, [kc.segment(c, (wq_, ws_))]):
+                            raise kc.KernelError(f"backend {backend} is not compiled in")
+                    return f
+
+                tc_us = timed_graph(torch, launch(kc.Q8_GEMM_GPU_TCGEN05), args.warmup, args.steps)
+                kc.status()
+                rows_us = None
+                if T <= args.sweep_rows_max:
+                    rows_us = timed_graph(torch, launch(kc.Q8_GEMM_GPU_DP4A), args.warmup, args.steps)
+                    kc.status()
+                    wins[T] = tc_us <= rows_us
+                ops = 2.0 * T * n * k
+                nbytes = wbytes + T * k * (1 + 4 / gs) + 4 * T * n
+                t_tensor, t_hbm = ops / (int8_tops * 1e12), nbytes / (hbm * 1e9)
+                points.append({"proj": name, "S": S, "N": n, "K": k, "T": T, "tc_us": round(tc_us, 2),
+                               "rows_us": None if rows_us is None else round(rows_us, 2),
+                               "tc_tops": round(ops / (tc_us * 1e-6) / 1e12, 1),
+                               "tc_gbs": round(nbytes / (tc_us * 1e-6) / 1e9, 1),
+                               "bound": "tensor" if t_tensor >= t_hbm else "hbm",
+                               "frac": round(max(t_tensor, t_hbm) / (tc_us * 1e-6), 4)})
+                del xq, xs, c
+            cross = None
+            for T in sorted(wins, reverse=True):
+                if not wins[T]:
+                    break
+                cross = T
+            crossover[f"{name} S={S}"] = cross
+            del W
+            torch.cuda.empty_cache()
+    known = [v for v in crossover.values() if v is not None]
+    print(json.dumps({"metric": "config 4 GEMV -> tensor-core GEMM crossover (activation rows), per-rank shards",
+                      "value": max(known) if known else None, "unit": "rows", "higher_is_better": False,
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "int8",
+                      "data": "synthetic: seeded N(0,0.02) weights, N(0,1) activations, Q8_0 gs 64",
+                      "config": {"workload": "config 4: 8B projections x T x S (rank-0 shard shapes on one GPU)",
+                                 "T": ts, "S": splits, "rows_rung_max_T": args.sweep_rows_max,
+                                 "l2": "weights rotate over > 3x L2"},
+                      "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
+                                "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} "
+                                          "hbm_gbs"},
+                      "crossover": crossover, "points": points}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["8b", "1b", "gemv", "ffn", "gemm"], default="8b")
+    ap.add_argument("--workload", choices=["8b", "1b", "gemv", "ffn", "gemm", "sweep"], default="8b")
+    ap.add_argument("--sweep-t", default="", help="sweep: comma-separated activation row counts (default: config 4's)")
+    ap.add_argument("--sweep-s", default="1,2,4,8", help="sweep: comma-separated tensor-parallel splits")
+    ap.add_argument("--sweep-rows-max", type=int, default=16, help="sweep: largest T timed on the per-row GEMV rung")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-request", action="store_true")
     args = ap.parse_args()
@@ -514,6 +634,8 @@ def main():
         run_gemv(args)
     elif args.workload == "gemm":
         run_gemm(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     elif args.profile_request:
         run_profile_request(args)
     else:

@@ -427,7 +427,9 @@ static float *gemm_scratch(size_t floats) {
 }
 
 // Activation rows from which the tensor-core GEMM beats one GEMV launch per row (the reference's k_gemm_q8_pick
-// threshold analogue; measured on B200 with the configuration-4 sweep).
+// threshold analogue). Measured on B200 over every 8B projection shard at 1/2/4/8-way splits: the crossover is 8 for
+// most shards, 4 for the widest (W1/W3, the classifier) and 16 for W2 unsplit. Both rungs give bitwise-equal
+// outputs, so the threshold affects only speed.
 static const int kTcMinRows = 8;
 
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count) {

@@ -19,7 +19,8 @@
 //   warps 2-9   epilogue (warp % 4 = TMEM lane quadrant = 32 weight rows, (warp - 2) / 4 = 64-token half): per
 //               group it reads its 32 x 64 int32 dots in 16-column chunks (each read in flight while the previous
 //               chunk is promoted with packed f32x2 instructions) and releases the buffer once the last chunk is in
-//               registers. Four buffers let the MMA run up to three groups ahead of the promotion.
+//               registers. Four buffers let the MMA run up to three groups ahead of the promotion. Column chunks
+//               past the last token are not promoted (they are never stored).
 // Group promotion: the group's first MMA overwrites its TMEM buffer (no clearing), the epilogue converts each exact
 // int32 dot to float (exact: |dot| <= 64*127^2 < 2^24) and applies mul, fma as packed pairs.
 //
@@ -244,6 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
       const int n = tl.n0 + (tl.swiglu ? 16 * q + (lane & 15) : row);
       const bool row_ok = n < seg_n;
       const float *wsr = (w3row ? a.seg[0].ws3 : seg_ws) + (size_t)min(n, seg_n - 1) * groups;
+      // Token columns of this warp that hold activation rows (warp-uniform). 16-column chunks at or past it are
+      // never stored, so their promotion is skipped: with few tokens the epilogue does only the columns it writes.
+      const int live = a.M - (tl.m0 + kEpiCols * h);
       uint64_t acc[kEpiCols / 2];
 #pragma unroll
       for (int i = 0; i < kEpiCols / 2; i++)
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
 #pragma unroll
           for (int c = 0; c < 4; c += 2) {
             tmem_ld16(tb + 16 * (c + 1), rB);
-            if (promote)
+            if (promote && 16 * c < live)
               promote16(acc + 8 * c, rA, xs + 16 * c, ws2);
             if (dump)
 #pragma unroll
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
                 tmem_ld16(tq + bn * kTN, rA);
               }
             }
-            if (ok_cur && !DOTS)
+            if (ok_cur && !DOTS && 16 * (c + 1) < live)
               promote16(acc + 8 * (c + 1), rB, xs + 16 * (c + 1), ws2);
             if (dump)
 #pragma unroll

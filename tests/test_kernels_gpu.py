@@ -366,7 +366,10 @@ def test_gemm_tc_group_dots_exact(kc, oracle, m, n, k):
     assert (host(dots) == oracle.group_dots(xq, wq, 64)).all()
 
 
-TC_SHAPES = [(128, 128, 256), (33, 48, 1024), (257, 300, 2048), (7, 4096, 4096), (130, 129, 14336)]
+# Partial token tiles skip the promotion of column chunks past the last token: M = 64 fills exactly one of the two
+# 64-column halves, M = 65 puts one token in the second.
+TC_SHAPES = [(128, 128, 256), (33, 48, 1024), (257, 300, 2048), (7, 4096, 4096), (130, 129, 14336), (64, 200, 512),
+             (65, 96, 768)]
 
 
 @pytest.mark.parametrize("m,n,k", TC_SHAPES)
