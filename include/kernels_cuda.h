@@ -184,6 +184,12 @@ typedef struct {
 void pack_s8_vnni_many(const PackS8 *jobs, int count);
 
 /* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
+/* From 8 activation rows on, shapes the tensor-core kernel takes (gs 64, k % 256 == 0, 16-byte aligned operands, a
+ * SwiGLU pair as the only segment) run on it; fewer rows and other shapes run one decode GEMV per row. Both give the
+ * same bits. The tensor-core path stages the transposed activation scales in one buffer per device that the library
+ * grows with cudaMalloc when a call needs more (k_gemm_q8_noalloc uses a fixed array instead). Every call on a device
+ * shares that buffer, so calls on one device must not overlap on the GPU: issue them from one stream, as the
+ * reference's team_run is not reentrant (include/workers.h:26). */
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count);
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count);
 

@@ -244,7 +244,6 @@ static int fused_shapes(const Engine *e) {
   return gs >= 16 && gs <= 256 && !(gs & (gs - 1)) && dim % gs == 0 && (dim / gs) % 4 == 0 && e->hid_l % gs == 0;
 }
 
-/* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. */
 /* The reducing GEMV is the TMA GEMV on int8 inputs: Wo reads ql of them, W2 hid_l, each a whole number of 4-group
  * units. LLAMA_PEER_GEMV=0 (the same on every rank) keeps the PARTIAL GEMV + kd_peer_allreduce_add pair instead. */
 static int reduce_shapes(const Engine *e) {
@@ -254,6 +253,8 @@ static int reduce_shapes(const Engine *e) {
          (e->hid_l / gs) % 4 == 0;
 }
 
+/* Rows per engine_forward_batch: W8A32 never batches (src/engine.c:97-104), else LLAMA_PREFILL_BATCH. Also fixes
+ * which decode kernels the shard shapes allow. */
 static int max_batch_for(Engine *e) {
   e->fused = fused_shapes(e); /* plan() has set the shard shapes */
   e->reduce_fused = reduce_shapes(e);
