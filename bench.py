@@ -12,7 +12,7 @@ Workloads (seeded synthetic data, random-init weights of the name
         prompt batch-prefilled, then 256 tokens greedy-decoded. Tensor parallel over the N GPUs (one request, one
         token stream: strong scaling). value = decode tok/s; prefill tok/s rides along.
   1b    config 2: Llama-3.2-1B architecture (tied classifier), 128-token prompt, 256 tokens.
-  gemv  config 0 kernel alone: quantize + GEMV 8192 x 2048 (for profiling; not the headline).
+  gemv  config 0 kernel alone: the GEMV 8192 x 2048 on activations quantized beforehand (not the headline).
   ffn   the dominant decode kernel alone: the 8B SwiGLU GEMV (W1 and W3, 14336 x 4096 each) on rotating weights.
   gemm  config 1: the prefill GEMM alone (8B up and down projections, T = 128 / 512 / 2048).
   sweep config 4: every 8B projection's rank-0 shard at S = 1/2/4/8 times T activation rows, the tensor-core GEMM
