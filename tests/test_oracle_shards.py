@@ -1,4 +1,4 @@
-"""CPU tests: the properties of the Q8 arithmetic that tensor parallelism relies on, on the oracle at 1/2/4/8-way splits
+"""CPU tests: the properties of the Q8 arithmetic that tensor parallelism relies on, on the oracle at 2/4/8-way splits
 of the 8B shapes. The reference's tests check them for its two sockets:
 - a rank quantizes only its own column slice of an activation, and because the group size divides the slice, that
   equals the slice of the full quantization, bit for bit (tests/kernels.c:517-527);
