@@ -154,7 +154,9 @@ def max_over_ranks(world, v):
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    # NCCL reduces device tensors; a gloo group (the CPU tests of this helper) reduces host tensors.
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
