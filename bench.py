@@ -25,7 +25,9 @@ The weights (8.5 GB at 8B) exceed L2 many times over, so every decode step strea
 
 --impl reference times the reference's own CPU engine (oracle/_ref/libllama_ref_engine.so, built from its sources:
 engine_forward_batch + engine_forward) on all host cores, on the same architecture written as a seeded checkpoint,
-each step a bounded sample (a 128-token prefill and 8 decode tokens). Under torchrun only rank 0 runs it.
+each step a bounded sample (a 128-token prefill and 8 decode tokens). Under torchrun only rank 0 runs it. For the
+gemv, ffn and gemm workloads it runs the reference's own microbenchmark instead (oracle/_ref/gemm-bench, built from
+tests/gemm_bench.c) on the same shapes; those workloads' own lines carry the same figures as cpu_baseline.
 """
 import argparse
 import ctypes
@@ -214,7 +216,7 @@ def gemv_roofline(kc, torch, rows, cols, gs=64, launches=60, swiglu=True):
     return alg, us
 
 
-# ---- the reference's CPU engine -----------------------------------------------------------------------------------
+# ---- the reference's CPU path: its engine, and its kernels alone ---------------------------------------------------
 
 def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
     """The reference's Q8 engine (engine_forward_batch for the prompt, engine_forward per decode token, greedy) on all
@@ -270,6 +272,58 @@ def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
             "sample": f"reference engine (engine_forward_batch + engine_forward, LLAMA_KERNELS=auto) on the {arch} "
                       f"architecture: {steps} x ({prompt_len}-token prefill + {decode_len} greedy decode tokens); "
                       f"checkpoint written in {gen_s:.0f} s, loaded in {load_s:.0f} s"}
+
+
+def reference_kernel_bench(bench_args, reps, kernels="auto"):
+    """The reference's own GEMV/GEMM microbenchmark (tests/gemm_bench.c, compiled from its sources into
+    oracle/_ref/gemm-bench by oracle/Makefile) with `--kernel q8 <bench_args> --reps <reps>` on all host cores and
+    LLAMA_KERNELS=<kernels>. Returns {"cores", "lines", "command"} with its JSON lines, or {"unavailable": why}."""
+    exe = ROOT / "oracle" / "_ref" / "gemm-bench"
+    if not exe.exists():
+        return {"unavailable": "oracle/_ref/gemm-bench was not built (make -C oracle where the reference sources exist)"}
+    env = dict(os.environ, LLAMA_KERNELS=kernels)
+    env.setdefault("LLAMA_THREADS", str(os.cpu_count() or 1))
+    cmd = [str(exe), "--kernel", "q8", *bench_args, "--reps", str(reps)]
+    try:
+        out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference gemm-bench did not finish within 600 s"}
+    if out.returncode:
+        return {"unavailable": f"reference gemm-bench exited {out.returncode}: {out.stderr.strip()[-200:]}"}
+    lines = [json.loads(l) for l in out.stdout.splitlines() if l.startswith("{")]
+    return {"cores": int(env["LLAMA_THREADS"]), "lines": lines,
+            "command": f"LLAMA_KERNELS={kernels} " + " ".join(["gemm-bench", *cmd[1:]])}
+
+
+def reference_gemv_baseline(rows, cols):
+    """cpu_baseline of the decode GEMV: the reference's k_matmul_q8 (gemm-bench --gemv, one activation row, its decode
+    selection LLAMA_KERNELS=auto) on one rows x cols matrix, weights cycled through 512 MiB of copies. GB/s counts the
+    weight values and scales."""
+    r = reference_kernel_bench(["--shapes", f"{rows}x{cols}", "--m", "1", "--gemv", "--cold-mib", "512"], reps=20)
+    if "unavailable" in r:
+        return r
+    line = next((l for l in r["lines"] if l.get("kernel") == "gemv_rows_q8"), None)
+    if line is None:
+        return {"unavailable": "reference gemm-bench printed no gemv_rows_q8 line"}
+    return {"value": line["weight_gbs_median"], "unit": "GB/s", "cores": r["cores"], "kind": "reference",
+            "sample": f"{r['command']} ({line['isa']}): median of {line['reps']} k_matmul_q8 "
+                      f"calls on {rows} x {cols}, {line['median_s'] * 1e6:.1f} us each; weight bytes / time"}
+
+
+def reference_gemm_points(shapes, ts):
+    """The reference's k_gemm_q8 (gemm-bench, STORE) per (N, K, T): {(N, K, T): (median us, int8 TOPS, isa)}, plus the
+    run's core count and command; or {"unavailable": why}. Its fastest W8A8 prefill backend is AMX-INT8, which
+    LLAMA_KERNELS=auto does not select in this tool; hosts without AMX take auto (AVX-512)."""
+    args = ["--shapes", ",".join(f"{n}x{k}" for n, k in shapes), "--m", ",".join(str(t) for t in ts), "--cold-mib",
+            "512"]
+    r = reference_kernel_bench(args, reps=3, kernels="amx")
+    if "unavailable" in r:
+        r = reference_kernel_bench(args, reps=3, kernels="auto")
+    if "unavailable" in r:
+        return r
+    pts = {(l["n"], l["k"], l["m"]): (l["median_s"] * 1e6, l["gflops_median"] / 1e3, l["isa"])
+           for l in r["lines"] if l.get("kernel") == "gemm_q8"}
+    return {"points": pts, "cores": r["cores"], "command": r["command"]}
 
 
 # ---- our engine ---------------------------------------------------------------------------------------------------
@@ -389,8 +443,43 @@ def weight_bytes(a, world, gs=64):
 
 # ---- the reference arm --------------------------------------------------------------------------------------------
 
+def run_reference_kernels(args):
+    """--impl reference for the kernel workloads (gemv, ffn, gemm): the reference's own gemm-bench on the shapes of
+    this arm's line, on every host core. Each figure is the median of a bounded number of calls (20 GEMVs, 3 GEMMs
+    per shape)."""
+    if args.workload == "gemm":
+        metric, unit = GEMM_METRIC, "TOPS"
+        ref = reference_gemm_points(list(GEMM_SHAPES.values()), GEMM_T)
+        if "unavailable" not in ref:
+            _, tops, isa = ref["points"].get((*GEMM_SHAPES["up"], GEMM_T[-1]), (None, None, None))
+            shapes = [{"shape": f"{name} T={t} N={n} K={k}", "cpu_us": round(ref["points"][(n, k, t)][0], 2),
+                       "cpu_tops": round(ref["points"][(n, k, t)][1], 2)}
+                      for name, (n, k) in GEMM_SHAPES.items() for t in GEMM_T if (n, k, t) in ref["points"]]
+            ref = {"value": None if tops is None else round(tops, 2), "unit": unit, "cores": ref["cores"],
+                   "kind": "reference", "shapes": shapes,
+                   "sample": f"{ref['command']} ({isa}): median of 3 k_gemm_q8 calls per shape"}
+    else:
+        metric, unit = GEMV_METRIC[args.workload], "GB/s"
+        ref = reference_gemv_baseline(*GEMV_SHAPES[args.workload])
+    if "unavailable" in ref:
+        print(json.dumps({"impl": "reference", "unavailable": ref["unavailable"]}), flush=True)
+        return
+    line = {"metric": metric, "impl": "reference", "value": ref["value"], "unit": unit, "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: the reference's kernel on the host cores", "parallelism": "cpu"},
+            "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if "shapes" in ref:
+        line["shapes"] = ref["shapes"]
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if args.workload in GEMV_SHAPES or args.workload == "gemm":
+        run_reference_kernels(args)
         return
     wl = args.workload if args.workload in ARCH else "8b"
     r = reference_engine_sample(wl, steps=args.steps, warmup=args.warmup, prompt_len=REF_SAMPLE[0],
@@ -414,27 +503,53 @@ def run_reference(args):
 
 # ---- config 0 kernel alone (profiling) ----------------------------------------------------------------------------
 
+GEMV_SHAPES = {"gemv": (8192, 2048), "ffn": (14336, 4096)}  # (weight rows, K) of one matrix
+GEMV_METRIC = {"gemv": "config 0 GEMV HBM GB/s", "ffn": "8B SwiGLU decode GEMV (W1, W3 14336 x 4096) HBM GB/s"}
+GEMM_METRIC = "config 1 prefill GEMM int8 TOPS (8B up projection, T=2048)"
+
 def run_gemv(args):
     import torch
     kc = load_package()
     kc.init()
     hbm, peak_kind = peaks()
-    if args.workload == "ffn":
-        alg, us = gemv_roofline(kc, torch, 14336, 4096, launches=args.steps, swiglu=True)
-        name = "8B SwiGLU decode GEMV (W1, W3 14336 x 4096) HBM GB/s"
-    else:
-        alg, us = gemv_roofline(kc, torch, 8192, 2048, launches=args.steps, swiglu=False)
-        name = "config 0 GEMV HBM GB/s"
+    rows, cols = GEMV_SHAPES[args.workload]
+    alg, us = gemv_roofline(kc, torch, rows, cols, launches=args.steps, swiglu=args.workload == "ffn")
+    name = GEMV_METRIC[args.workload]
     gbs = alg / (us / 1e6) / 1e9
-    print(json.dumps({"metric": name, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
-                      "steps": args.steps, "warmup": args.warmup, "kernel_us": round(us, 3),
-                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                                   "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs"}}), flush=True)
+    line = {"metric": name, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "kernel_us": round(us, 3),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_source": f"{peak_kind} hbm_gbs"}}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = reference_gemv_baseline(*GEMV_SHAPES[args.workload])
+    print(json.dumps(line), flush=True)
+
+
+# ---- timing of a kernel alone ----------------------------------------------------------------------------------
+
+def timed_graph(torch, launch, warmup, launches):
+    """Mean microseconds of `launch(i)`: warm-up calls, then `launches` calls captured in one graph with a pair of CUDA
+    events around each, replayed once."""
+    for i in range(warmup):
+        launch(i)
+    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+           for _ in range(launches)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(launches):
+            evs[i][0].record()
+            launch(warmup + i)
+            evs[i][1].record()
+    graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    return float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
 
 
 # ---- config 1: the prefill GEMM alone ---------------------------------------------------------------------------
 
 GEMM_SHAPES = {"up": (14336, 4096), "down": (4096, 14336)}  # (N weight rows, K)
+GEMM_T = (128, 512, 2048)
 
 
 def run_gemm(args):
@@ -459,48 +574,50 @@ def run_gemm(args):
         wbytes = wq.numel() + ws.numel() * 4
         copies = max(2, -(-3 * L2_BYTES // wbytes))
         W = [(wq.clone(), ws.clone()) for _ in range(copies)]
-        for T in (128, 512, 2048):
+        for T in GEMM_T:
             x = torch.randn((T, K), generator=g, device="cuda")
             xq, xs = kc.quantize(x, gs)
             c = torch.empty((T, N), device="cuda")
-            launches = max(4, args.steps)
 
             def launch(i):
                 kc.k_gemm_q8(xq, xs, T, K, gs, [kc.segment(c, W[i % copies])])
 
-            for i in range(args.warmup):
-                launch(i)
+            us = timed_graph(torch, launch, args.warmup, max(4, args.steps))
             kc.status()
-            evs = [(torch.cuda.Event(enable_timing=True, external=True),
-                    torch.cuda.Event(enable_timing=True, external=True)) for _ in range(launches)]
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for i in range(launches):
-                    evs[i][0].record()
-                    launch(i)
-                    evs[i][1].record()
-            graph.replay()
-            torch.cuda.synchronize()
-            kc.status()
-            us = float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
-            del graph
             ops = 2.0 * T * N * K
             nbytes = wbytes + T * K * (1 + 4 / gs) + 4 * T * N
             t_tensor, t_hbm = ops / (int8_tops * 1e12), nbytes / (hbm * 1e9)
             bound = "tensor" if t_tensor >= t_hbm else "hbm"
             tops = ops / (us * 1e-6) / 1e12
-            shapes.append({"shape": f"{name} T={T} N={N} K={K}", "us": round(us, 2), "int8_tops": round(tops, 1),
+            shapes.append({"shape": f"{name} T={T} N={N} K={K}", "key": (N, K, T), "us": round(us, 2),
+                           "int8_tops": round(tops, 1),
                            "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bound": bound,
                            "frac": round(max(t_tensor, t_hbm) / (us * 1e-6), 4)})
             del x, xq, xs, c
         del W, wq, ws
-    head = next(s for s in shapes if s["shape"].startswith("up T=2048"))
-    print(json.dumps({"metric": "config 1 prefill GEMM int8 TOPS (8B up projection, T=2048)", "value": head["int8_tops"],
-                      "unit": "TOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "int8",
-                      "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
-                                "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} "
-                                          "hbm_gbs"},
-                      "shapes": shapes}), flush=True)
+    head = next(s for s in shapes if s["key"] == (*GEMM_SHAPES["up"], GEMM_T[-1]))
+    line = {"metric": GEMM_METRIC, "value": head["int8_tops"],
+            "unit": "TOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "int8",
+            "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
+                      "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} hbm_gbs"},
+            "shapes": shapes}
+    if not args.no_cpu_baseline:
+        ref = reference_gemm_points(list(GEMM_SHAPES.values()), GEMM_T)
+        if "unavailable" in ref:
+            line["cpu_baseline"] = ref
+        else:
+            for sh in shapes:
+                n, k, t = sh["key"]
+                if (n, k, t) in ref["points"]:
+                    sh["cpu_us"], sh["cpu_tops"] = (round(v, 2) for v in ref["points"][(n, k, t)][:2])
+            _, tops_, isa = ref["points"].get(head["key"], (None, None, None))
+            line["cpu_baseline"] = {"value": None if tops_ is None else round(tops_, 2), "unit": "TOPS",
+                                    "cores": ref["cores"], "kind": "reference",
+                                    "sample": f"{ref['command']} ({isa}): median of 3 k_gemm_q8 "
+                                              "calls per shape; value is up T=2048, per-shape figures in shapes"}
+    for sh in shapes:
+        del sh["key"]
+    print(json.dumps(line), flush=True)
 
 
 # ---- config 4: the GEMV -> tensor-core GEMM crossover sweep -------------------------------------------------------
@@ -510,25 +627,6 @@ def run_gemm(args):
 SWEEP_PROJECTIONS = {"wq": (4096, 4096, "rows"), "wk/wv": (1024, 4096, "rows"), "wo": (4096, 4096, "cols"),
                      "w1/w3": (14336, 4096, "rows"), "w2": (4096, 14336, "cols"), "cls": (128256, 4096, "rows")}
 SWEEP_T = (1, 2, 4, 8, 16, 64, 256, 1024, 4096)
-
-
-def timed_graph(torch, launch, warmup, launches):
-    """Mean microseconds of `launch(i)`: warm-up calls, then `launches` calls captured in one graph with a pair of CUDA
-    events around each, replayed once."""
-    for i in range(warmup):
-        launch(i)
-    evs = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-           for _ in range(launches)]
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for i in range(launches):
-            evs[i][0].record()
-            launch(warmup + i)
-            evs[i][1].record()
-    graph.replay()
-    torch.cuda.synchronize()
-    del graph
-    return float(np.mean([a.elapsed_time(b) for a, b in evs])) * 1e3
 
 
 def run_sweep(args):
