@@ -437,10 +437,11 @@ static float *upload_f32(const float *src, size_t count) {
 static int read_header(const unsigned char *h, size_t bytes, Config *p, int *gs) {
   memset(p, 0, sizeof(*p));
   config_defaults(p);
-  uint32_t magic;
+  uint32_t magic = 0;
   int version, shared = 0;
-  memcpy(&magic, h, 4);
-  if (bytes < 256 || magic != Q8_MAGIC)
+  if (bytes >= 256)
+    memcpy(&magic, h, 4);
+  if (magic != Q8_MAGIC)
     return efail("unsupported INT8 checkpoint: expected ak42 version 2 or 3");
   memcpy(&version, h + 4, 4);
   if (version == 3) {
