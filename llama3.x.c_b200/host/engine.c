@@ -8,6 +8,7 @@
  * residual += (p0 + p1 + ...), which at two ranks is the reference's residual[i] += p0[i] + p1[i]
  * (src/workers.c:455-458). */
 #define _POSIX_C_SOURCE 200809L
+#include <errno.h>
 #include <fcntl.h>
 #include <math.h>
 #include <stdarg.h>
@@ -174,6 +175,9 @@ static int validate_config(const Config *p, int gs) {
   if (!isfinite(p->rope_factor) || !isfinite(p->rope_low) || !isfinite(p->rope_high) || p->rope_factor < 1 ||
       p->rope_low <= 0 || p->rope_high <= p->rope_low || p->rope_original <= 0)
     return efail("invalid RoPE scaling metadata");
+  if (p->format == 3 && (p->bos_id < 0 || p->bos_id >= p->vocab_size || p->eos_id < 0 || p->eos_id >= p->vocab_size ||
+                         p->eot_id < -1 || p->eot_id >= p->vocab_size || p->eom_id < -1 || p->eom_id >= p->vocab_size))
+    return efail("invalid special token metadata");
   if (gs <= 0 || gs > 131071 || p->dim % gs || p->hidden_dim % gs)
     return efail("unsupported INT8 group size %d: must divide dim and hidden_dim and fit int32 accumulation", gs);
   return 0;
@@ -434,7 +438,8 @@ static float *upload_f32(const float *src, size_t count) {
   return d;
 }
 
-static int read_header(const unsigned char *h, size_t bytes, Config *p, int *gs) {
+/* checkpoint_map's header rules for the INT8 executable (src/runtime.c:214-275). */
+static int read_header(const char *path, const unsigned char *h, size_t bytes, Config *p, int *gs) {
   memset(p, 0, sizeof(*p));
   config_defaults(p);
   uint32_t magic = 0;
@@ -447,6 +452,8 @@ static int read_header(const unsigned char *h, size_t bytes, Config *p, int *gs)
   if (version == 3) {
     int precision;
     memcpy(&precision, h + 36, 4);
+    if (precision < 0 || precision > 1)
+      return efail("unsupported checkpoint precision %d", precision);
     if (precision != 1)
       return efail("checkpoint precision requires run executable");
     memcpy(p, h + 8, 28);
@@ -480,7 +487,7 @@ static int read_header(const unsigned char *h, size_t bytes, Config *p, int *gs)
   }
   p->format = version;
   if (shared < 0 || shared > 1)
-    return efail("invalid classifier flag");
+    return efail("invalid classifier flag in '%s'", path);
   p->shared = shared;
   if (version != 3) {
     p->max_seq_len = p->seq_len;
@@ -489,16 +496,51 @@ static int read_header(const unsigned char *h, size_t bytes, Config *p, int *gs)
   return validate_config(p, *gs);
 }
 
-static size_t q8_bytes(size_t count, int gs) { return count + count / (size_t)gs * sizeof(float); }
+/* Size arithmetic of a checkpoint the header describes, failing on overflow as checked_mul / checked_add do
+ * (src/runtime.c:70-78): a header whose sizes wrap around must not pass the truncation check. *of records the first
+ * overflow (which has failed) and makes the rest return 0. */
+static size_t mul_checked(size_t a, size_t b, int *of) {
+  if (*of)
+    return 0;
+  if (a && b > SIZE_MAX / a) {
+    *of = 1;
+    efail("size multiplication overflow: %zu * %zu", a, b);
+    return 0;
+  }
+  return a * b;
+}
 
+static size_t add_checked(size_t a, size_t b, int *of) {
+  if (*of)
+    return 0;
+  if (b > SIZE_MAX - a) {
+    *of = 1;
+    efail("size addition overflow: %zu + %zu", a, b);
+    return 0;
+  }
+  return a + b;
+}
+
+static size_t q8_bytes(size_t count, int gs, int *of) {
+  return add_checked(count, mul_checked(count / (size_t)gs, sizeof(float), of), of);
+}
+
+/* Bytes of a Q8 checkpoint (src/runtime.c:276-290); 0 after an overflow, which has already failed. */
 static size_t checkpoint_bytes(const Config *p, int gs) {
-  size_t d = p->dim, h = p->hidden_dim, l = p->n_layers, kv = (size_t)p->head_dim * p->n_kv_heads;
-  size_t v = p->vocab_size;
-  size_t n = 256 + (2 * l + 1) * d * sizeof(float) + q8_bytes(v * d, gs);
-  n += l * (2 * q8_bytes(d * d, gs) + 2 * q8_bytes(d * kv, gs) + 3 * q8_bytes(d * h, gs));
+  int of = 0;
+  size_t d = p->dim, h = p->hidden_dim, l = p->n_layers, v = p->vocab_size;
+  size_t kv = mul_checked((size_t)p->head_dim, (size_t)p->n_kv_heads, &of);
+  size_t norms = mul_checked(add_checked(mul_checked(2, l, &of), 1, &of), d, &of);
+  size_t embedding = q8_bytes(mul_checked(v, d, &of), gs, &of);
+  size_t n = add_checked(256, mul_checked(norms, sizeof(float), &of), &of);
+  n = add_checked(n, embedding, &of);
+  size_t layer = mul_checked(2, q8_bytes(mul_checked(d, d, &of), gs, &of), &of);
+  layer = add_checked(layer, mul_checked(2, q8_bytes(mul_checked(d, kv, &of), gs, &of), &of), &of);
+  layer = add_checked(layer, mul_checked(3, q8_bytes(mul_checked(d, h, &of), gs, &of), &of), &of);
+  n = add_checked(n, mul_checked(l, layer, &of), &of);
   if (!p->shared)
-    n += q8_bytes(v * d, gs);
-  return n;
+    n = add_checked(n, embedding, &of);
+  return of ? 0 : n;
 }
 
 static int load_weights(Engine *e, const unsigned char *base, size_t bytes) {
@@ -566,7 +608,7 @@ void engine_load_context(Model *model, const char *path, int context) {
   memset(model, 0, sizeof(*model));
   int fd = open(path, O_RDONLY);
   if (fd < 0) {
-    efail("cannot open checkpoint '%s'", path);
+    efail("cannot open checkpoint '%s': %s", path, strerror(errno));
     return;
   }
   struct stat st;
@@ -584,14 +626,23 @@ void engine_load_context(Model *model, const char *path, int context) {
   }
   Config p;
   int gs = 0;
-  if (read_header(base, bytes, &p, &gs)) {
+  if (read_header(path, base, bytes, &p, &gs)) {
     munmap(base, bytes);
     return;
   }
   size_t needed = checkpoint_bytes(&p, gs);
-  if (needed > bytes || (p.format == 3 && needed != bytes)) {
+  if (!needed) {
+    munmap(base, bytes);
+    return;
+  }
+  if (needed > bytes) {
     munmap(base, bytes);
     efail("truncated checkpoint '%s': need %zu bytes, found %zu", path, needed, bytes);
+    return;
+  }
+  if (p.format == 3 && needed != bytes) {
+    munmap(base, bytes);
+    efail("version 3 checkpoint has unexpected trailing bytes");
     return;
   }
   if (context < 0 || context > p.seq_len) {

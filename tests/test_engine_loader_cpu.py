@@ -1,0 +1,106 @@
+"""CPU tests of the engine's checkpoint loader (engine_load_context): every header and file that the reference's
+checkpoint_map and validate_config reject (src/runtime.c:148-168, 179-290) is rejected with the reference's message,
+before the engine touches a GPU. The library runs under KC_FAIL_RETURN, so the message is kept and the process lives.
+No test here reaches a valid load: that would allocate device memory."""
+import ctypes
+import os
+import struct
+
+import pytest
+
+from conftest import load_engine
+
+MAGIC = 0x616B3432
+SMALL = dict(dim=64, hidden=128, layers=1, heads=2, kv=1, vocab=32, seq=16)
+
+
+def v2_header(dim, hidden, layers, heads, kv, vocab, seq, shared=0, gs=64):
+    h = struct.pack("<Ii7iBi", MAGIC, 2, dim, hidden, layers, heads, kv, vocab, seq, shared, gs)
+    return h + bytes(256 - len(h))
+
+
+def v3_header(dim, hidden, layers, heads, kv, vocab, seq, shared=0, gs=64, precision=1, eos=1, name=b"tiny",
+              reserved=0):
+    h = bytearray(256)
+    struct.pack_into("<Ii7iiii", h, 0, MAGIC, 3, dim, hidden, layers, heads, kv, vocab, seq, precision, shared, gs)
+    struct.pack_into("<ffifffiiiiiii", h, 48, 1e-5, 500000.0, 0, 1.0, 1.0, 4.0, 8192, seq, dim // heads, 0, eos,
+                     -1, -1)
+    h[100:100 + len(name)] = name
+    h[255] = reserved
+    return bytes(h)
+
+
+def q8_bytes(n, gs=64):
+    return n + n // gs * 4
+
+
+def file_bytes(dim, hidden, layers, heads, kv, vocab, seq, shared=0, gs=64):
+    kvd = dim // heads * kv
+    n = 256 + (2 * layers + 1) * dim * 4 + q8_bytes(vocab * dim, gs)
+    n += layers * (2 * q8_bytes(dim * dim, gs) + 2 * q8_bytes(dim * kvd, gs) + 3 * q8_bytes(dim * hidden, gs))
+    return n + (0 if shared else q8_bytes(vocab * dim, gs))
+
+
+@pytest.fixture(scope="module")
+def load():
+    eng = load_engine()
+    lib = eng.load_library()  # binds the engine and selects KC_FAIL_RETURN
+
+    def run(path, context=0):
+        model = eng.Model()
+        lib.engine_load_context(ctypes.byref(model), os.fsencode(str(path)), context)
+        with pytest.raises(eng._kc().KernelError) as err:
+            eng._check()
+        assert not model.implementation
+        return str(err.value)
+
+    return run
+
+
+def write(tmp_path, data, name="model.bin"):
+    p = tmp_path / name
+    p.write_bytes(data)
+    return p
+
+
+def test_missing_and_short_files(load, tmp_path):
+    assert load(tmp_path / "absent.bin").startswith(f"cannot open checkpoint '{tmp_path / 'absent.bin'}': ")
+    assert "invalid/truncated checkpoint" in load(write(tmp_path, bytes(100)))
+    assert "expected a regular file" in load(tmp_path)  # a directory
+
+
+@pytest.mark.parametrize("header,message", [
+    (bytes(256), "unsupported INT8 checkpoint: expected ak42 version 2 or 3"),
+    (struct.pack("<Ii", MAGIC, 4) + bytes(248), "unsupported checkpoint version 4 for this executable"),
+    (v3_header(**SMALL, precision=0), "checkpoint precision requires run executable"),
+    (v3_header(**SMALL, precision=7), "unsupported checkpoint precision 7"),
+    (v2_header(**SMALL, shared=2), "invalid classifier flag in '"),
+    (v2_header(**{**SMALL, "dim": 0}), "invalid checkpoint dimensions: all seven dimensions must be positive"),
+    (v2_header(**{**SMALL, "heads": 3}), "unsupported attention dimensions"),
+    (v2_header(**{**SMALL, "heads": 4, "kv": 3}), "unsupported attention dimensions"),
+    (v2_header(**SMALL, gs=48), "unsupported INT8 group size 48"),
+    (v3_header(**SMALL, eos=SMALL["vocab"]), "invalid special token metadata"),
+    (v3_header(**SMALL, name=b"x" * 128), "unterminated model name"),
+    (v3_header(**SMALL, reserved=1), "unsupported nonzero reserved checkpoint metadata"),
+])
+def test_headers_the_reference_rejects(load, tmp_path, header, message):
+    assert message in load(write(tmp_path, header + bytes(4096)))
+
+
+def test_sizes_that_overflow_are_rejected_not_wrapped(load, tmp_path):
+    # Valid divisibility, but the layer tensors' byte count exceeds 2^64: the reference's checked_mul fails.
+    huge = dict(dim=1 << 30, hidden=1 << 30, layers=1 << 30, heads=1 << 20, kv=1 << 20, vocab=1 << 30, seq=1)
+    assert "size multiplication overflow" in load(write(tmp_path, v2_header(**huge)))
+
+
+def test_truncated_and_trailing_bytes(load, tmp_path):
+    need = file_bytes(**SMALL)
+    msg = load(write(tmp_path, v2_header(**SMALL) + bytes(need - 256 - 1)))
+    assert f"need {need} bytes, found {need - 1}" in msg and msg.startswith("truncated checkpoint '")
+    assert load(write(tmp_path, v3_header(**SMALL) + bytes(need - 256 + 4))) == \
+        "version 3 checkpoint has unexpected trailing bytes"
+
+
+def test_context_beyond_the_checkpoint(load, tmp_path):
+    path = write(tmp_path, v2_header(**SMALL) + bytes(file_bytes(**SMALL) - 256))
+    assert load(path, context=SMALL["seq"] + 1) == "requested context exceeds checkpoint context"
