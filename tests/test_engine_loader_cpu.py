@@ -104,3 +104,25 @@ def test_truncated_and_trailing_bytes(load, tmp_path):
 def test_context_beyond_the_checkpoint(load, tmp_path):
     path = write(tmp_path, v2_header(**SMALL) + bytes(file_bytes(**SMALL) - 256))
     assert load(path, context=SMALL["seq"] + 1) == "requested context exceeds checkpoint context"
+
+
+def test_random_models_are_validated_like_checkpoints(load):
+    # engine_init_random applies the same configuration rules before it allocates anything.
+    eng = load_engine()
+    lib = eng.load_library()
+
+    def init(gs=64, context=0, **kw):
+        cfg = eng.Config()
+        for k, v in dict(dim=64, hidden_dim=128, n_layers=1, n_heads=2, n_kv_heads=1, vocab_size=32, seq_len=16,
+                         **kw).items():
+            setattr(cfg, k, v)
+        model = eng.Model()
+        lib.engine_init_random(ctypes.byref(model), ctypes.byref(cfg), gs, 1, context)
+        with pytest.raises(eng._kc().KernelError) as err:
+            eng._check()
+        assert not model.implementation
+        return str(err.value)
+
+    assert "unsupported INT8 group size 48" in init(gs=48)
+    assert "unsupported attention dimensions" in init(n_heads=3)
+    assert init(context=17) == "requested context exceeds the model's context"
