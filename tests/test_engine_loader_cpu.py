@@ -113,8 +113,8 @@ def test_random_models_are_validated_like_checkpoints(load):
 
     def init(gs=64, context=0, **kw):
         cfg = eng.Config()
-        for k, v in dict(dim=64, hidden_dim=128, n_layers=1, n_heads=2, n_kv_heads=1, vocab_size=32, seq_len=16,
-                         **kw).items():
+        for k, v in {**dict(dim=64, hidden_dim=128, n_layers=1, n_heads=2, n_kv_heads=1, vocab_size=32, seq_len=16),
+                     **kw}.items():
             setattr(cfg, k, v)
         model = eng.Model()
         lib.engine_init_random(ctypes.byref(model), ctypes.byref(cfg), gs, 1, context)
