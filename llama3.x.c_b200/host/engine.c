@@ -10,6 +10,7 @@
 #define _POSIX_C_SOURCE 200809L
 #include <errno.h>
 #include <fcntl.h>
+#include <limits.h>
 #include <math.h>
 #include <stdarg.h>
 #include <stdint.h>
@@ -63,6 +64,7 @@ typedef struct {
   void *stream, *comm;
   void *peer; /* peer-memory all-reduce of the decode residual (kd_peer_*), or NULL for NCCL */
   int w8a32;  /* LLAMA_Q8_ACTIVATIONS=fp32: fp32 activations against the int8 weights, one row per forward */
+  long batch_env; /* rows per engine_forward_batch the environment asks for, before the context cap */
   int fused;  /* the decode step's fused GEMV modes fit these shapes (fused_shapes) */
   int reduce_fused; /* with peer: Wo and W2 reduce inside their GEMV (kd_peer_matmul_q8_add, reduce_shapes) */
   float *xb;  /* W8A32: the normalized row the projections read */
@@ -220,23 +222,46 @@ static int plan(Engine *e) {
   return 0;
 }
 
-static int prefill_batch_from_env(int context) {
-  const char *b = getenv("LLAMA_PREFILL_BATCH");
-  long count = DEFAULT_PREFILL_BATCH;
-  if (b && *b) {
-    char *end;
-    if (strspn(b, "0123456789") != strlen(b) || (count = strtol(b, &end, 10)) < 1 || count > 1L << 30)
-      return efail("LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX");
-  }
-  return count < context ? (int)count : context;
-}
+/* The environment the reference's Q8 engine reads before it maps a checkpoint, with its rules and messages:
+ * LLAMA_PRECISION (prefill_precision(1), src/prefill.c:9-22), LLAMA_Q8_ACTIVATIONS (src/engine.c:131-135) and
+ * prefill_configure's LLAMA_PREFILL_GEMM, LLAMA_PREFILL_BATCH and LLAMA_PREFILL_LOGITS (src/prefill.c:24-50).
+ * The GPU's batched GEMM gives the per-row kernel's bits, so LLAMA_PREFILL_GEMM=off only makes the default batch one
+ * row. W8A32 always runs one row per forward (src/engine.c:97-104), whatever the batch asked for. */
+typedef struct {
+  int w8a32;
+  long batch;
+} Knobs;
 
-/* LLAMA_Q8_ACTIVATIONS as the reference reads it (src/engine.c:132-135): int8 (the default, W8A8) or fp32 (W8A32). */
-static int activations_from_env(void) {
+static int read_knobs(Knobs *k) {
+  const char *precision = getenv("LLAMA_PRECISION");
+  if (precision && *precision && strcmp(precision, "fp32") && strcmp(precision, "bf16"))
+    return efail("LLAMA_PRECISION must be fp32 or bf16");
+  if (precision && !strcmp(precision, "bf16"))
+    return efail("LLAMA_PRECISION=bf16 applies to FP32 checkpoints (run); Q8_0 checkpoints keep their int8 semantics "
+                 "(runq)");
   const char *a = getenv("LLAMA_Q8_ACTIVATIONS");
   if (a && *a && strcmp(a, "int8") && strcmp(a, "fp32"))
     return efail("LLAMA_Q8_ACTIVATIONS must be int8 or fp32");
-  return a && !strcmp(a, "fp32");
+  k->w8a32 = a && !strcmp(a, "fp32");
+  const char *gemm = getenv("LLAMA_PREFILL_GEMM");
+  if (gemm && *gemm && strcmp(gemm, "auto") && strcmp(gemm, "on") && strcmp(gemm, "off"))
+    return efail("LLAMA_PREFILL_GEMM must be auto, on or off");
+  k->batch = k->w8a32 || (gemm && !strcmp(gemm, "off")) ? 1 : DEFAULT_PREFILL_BATCH;
+  const char *b = getenv("LLAMA_PREFILL_BATCH");
+  if (b && *b) {
+    if (strspn(b, "0123456789") != strlen(b))
+      return efail("LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX");
+    errno = 0;
+    char *end;
+    const long count = strtol(b, &end, 10);
+    if (errno || *end || count < 1 || count > INT_MAX)
+      return efail("LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX");
+    k->batch = count;
+  }
+  const char *logits = getenv("LLAMA_PREFILL_LOGITS");
+  if (logits && *logits && strcmp(logits, "last") && strcmp(logits, "all"))
+    return efail("LLAMA_PREFILL_LOGITS must be last or all");
+  return 0;
 }
 
 /* The decode step's fused kernels (RMSNorm and quantize inside the GEMV, the output quantizer) run on the TMA GEMV,
@@ -262,7 +287,7 @@ static int reduce_shapes(const Engine *e) {
 static int max_batch_for(Engine *e) {
   e->fused = fused_shapes(e); /* plan() has set the shard shapes */
   e->reduce_fused = reduce_shapes(e);
-  return e->w8a32 ? 1 : prefill_batch_from_env(e->context);
+  return e->w8a32 ? 1 : e->batch_env < e->context ? (int)e->batch_env : e->context;
 }
 
 /* Device buffers sized for the context and the batch. */
@@ -606,6 +631,9 @@ void engine_load(Model *model, const char *path) { engine_load_context(model, pa
 void engine_load_context(Model *model, const char *path, int context) {
   kc_clear_error();
   memset(model, 0, sizeof(*model));
+  Knobs knobs;
+  if (read_knobs(&knobs))
+    return;
   int fd = open(path, O_RDONLY);
   if (fd < 0) {
     efail("cannot open checkpoint '%s': %s", path, strerror(errno));
@@ -660,8 +688,10 @@ void engine_load_context(Model *model, const char *path, int context) {
   e->context = context ? context : (p.seq_len < DEFAULT_CONTEXT_CAP ? p.seq_len : DEFAULT_CONTEXT_CAP);
   e->c.seq_len = e->context;
   model->file_bytes = bytes;
-  if ((e->w8a32 = activations_from_env()) < 0 || plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) ||
-      allocate_state(e) || load_weights(e, base, bytes)) {
+  e->w8a32 = knobs.w8a32;
+  e->batch_env = knobs.batch;
+  if (plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) || allocate_state(e) ||
+      load_weights(e, base, bytes)) {
     munmap(base, bytes);
     engine_free(model);
     return;
@@ -673,6 +703,9 @@ void engine_load_context(Model *model, const char *path, int context) {
 void engine_init_random(Model *model, const Config *config, int group_size, unsigned long long seed, int context) {
   kc_clear_error();
   memset(model, 0, sizeof(*model));
+  Knobs knobs;
+  if (read_knobs(&knobs))
+    return;
   Config p;
   memset(&p, 0, sizeof(p));
   memcpy(&p, config, 7 * sizeof(int));
@@ -694,8 +727,9 @@ void engine_init_random(Model *model, const Config *config, int group_size, unsi
   e->gs = group_size;
   e->context = context ? context : p.seq_len;
   e->c.seq_len = e->context;
-  if ((e->w8a32 = activations_from_env()) < 0 || plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) ||
-      allocate_state(e)) {
+  e->w8a32 = knobs.w8a32;
+  e->batch_env = knobs.batch;
+  if (plan(e) || (e->max_batch = max_batch_for(e)) < 0 || connect(e) || allocate_state(e)) {
     engine_free(model);
     return;
   }

@@ -126,3 +126,31 @@ def test_random_models_are_validated_like_checkpoints(load):
     assert "unsupported INT8 group size 48" in init(gs=48)
     assert "unsupported attention dimensions" in init(n_heads=3)
     assert init(context=17) == "requested context exceeds the model's context"
+
+
+@pytest.mark.parametrize("name,value,message", [
+    ("LLAMA_PRECISION", "fp16", "LLAMA_PRECISION must be fp32 or bf16"),
+    ("LLAMA_PRECISION", "bf16", "LLAMA_PRECISION=bf16 applies to FP32 checkpoints (run)"),
+    ("LLAMA_Q8_ACTIVATIONS", "int4", "LLAMA_Q8_ACTIVATIONS must be int8 or fp32"),
+    ("LLAMA_PREFILL_GEMM", "maybe", "LLAMA_PREFILL_GEMM must be auto, on or off"),
+    ("LLAMA_PREFILL_BATCH", "0", "LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX"),
+    ("LLAMA_PREFILL_BATCH", "-4", "LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX"),
+    ("LLAMA_PREFILL_BATCH", " 8", "LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX"),
+    ("LLAMA_PREFILL_BATCH", "2147483648", "LLAMA_PREFILL_BATCH must be a positive integer <= INT_MAX"),
+    ("LLAMA_PREFILL_LOGITS", "first", "LLAMA_PREFILL_LOGITS must be last or all"),
+])
+def test_environment_the_reference_rejects(load, tmp_path, monkeypatch, name, value, message):
+    # prefill_precision / prefill_configure (src/prefill.c:9-50) and src/engine.c:131-135: checked before the file.
+    monkeypatch.setenv(name, value)
+    assert message in load(tmp_path / "absent.bin")
+
+
+@pytest.mark.parametrize("name,value", [
+    ("LLAMA_PRECISION", "fp32"), ("LLAMA_Q8_ACTIVATIONS", "fp32"), ("LLAMA_Q8_ACTIVATIONS", "int8"),
+    ("LLAMA_PREFILL_GEMM", "off"), ("LLAMA_PREFILL_GEMM", "auto"), ("LLAMA_PREFILL_BATCH", "2147483647"),
+    ("LLAMA_PREFILL_LOGITS", "all"), ("LLAMA_PREFILL_LOGITS", ""),
+])
+def test_environment_the_reference_accepts(load, tmp_path, monkeypatch, name, value):
+    # Accepted settings get as far as opening the checkpoint.
+    monkeypatch.setenv(name, value)
+    assert load(tmp_path / "absent.bin").startswith("cannot open checkpoint")
