@@ -177,6 +177,10 @@ static void gemv(const char *name, const KcGemvSeg *segs, int nseg, const K8Inpu
       kc_fail("%s: negative row count", name);
       return;
     }
+    if (segs[i].d > 0 && !segs[i].out) {
+      kc_fail("%s: missing output", name);
+      return;
+    }
     if (!weight_ok(name, K8Weight{segs[i].wq, segs[i].ws}) ||
         (kind == KC_SWIGLU && !weight_ok(name, K8Weight{segs[i].w3q, segs[i].w3s})))
       return;
@@ -365,8 +369,8 @@ static int kc_kind_of(GemmKind k) {
 
 static bool gemm_args_ok(const char *name, const int8_t *xq, const float *xs, int m, int k, int gs,
                          const GemmQ8Segment *segments, int count) {
-  if (count < 1 || count > GEMM_MAX_SEGMENTS)
-    return kc_fail("GEMM needs 1..%d segments, got %d", GEMM_MAX_SEGMENTS, count);
+  if (!segments || count < 1 || count > GEMM_MAX_SEGMENTS)
+    return kc_fail("GEMM needs 1..%d segments, got %d", GEMM_MAX_SEGMENTS, segments ? count : 0);
   if (gs <= 0 || k % gs)
     return kc_fail("Q8 GEMM: K=%d is not a multiple of the group size %d", k, gs);
   for (int s = 0; s < count; s++) {
@@ -379,7 +383,16 @@ static bool gemm_args_ok(const char *name, const int8_t *xq, const float *xs, in
   }
   if (m < 0 || k < 0)
     return kc_fail("%s: negative shape", name);
-  (void)xq, (void)xs;
+  // The kernels read every pointer they are given: a missing one is an error here, never an address on the GPU.
+  if (m > 0 && k > 0) {
+    if (!xq || !xs)
+      return kc_fail("%s: missing activations", name);
+    for (int s = 0; s < count; s++) {
+      const GemmQ8Segment &g = segments[s];
+      if (g.n > 0 && (!g.c || !g.w.q || !g.w.s || (g.kind == GEMM_SWIGLU && !g.w3.s)))
+        return kc_fail("%s: segment %d is missing its output, weight values or scales", name, s);
+    }
+  }
   return true;
 }
 
@@ -484,6 +497,9 @@ static bool gemm_run(Q8GemmBackend backend, const int8_t *xq, const float *xs, i
 }
 
 void k_gemm_q8(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments, int count) {
+  // The arguments are checked before the backend is picked: pick() copies the segments into a fixed array.
+  if (!gemm_args_ok("k_gemm_q8", xq, xs, m, k, gs, segments, count))
+    return;
   gemm_run(pick(xq, m, k, gs, segments, count), xq, xs, m, k, gs, segments, count);
 }
 
