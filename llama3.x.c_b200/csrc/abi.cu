@@ -258,8 +258,8 @@ void k_matmul_q8_ld_worker(float *out, const K8Input *x, const K8Weight *w, size
 
 // Segments of one kind as KcGemvSeg; false (and fail()) otherwise.
 static bool gemv_segments(const char *name, const GemmQ8Segment *segments, int count, KcGemvSeg *segs, int *kind) {
-  if (count < 1 || count > GEMM_MAX_SEGMENTS)
-    return kc_fail("%s: needs 1..%d segments, got %d", name, GEMM_MAX_SEGMENTS, count);
+  if (!segments || count < 1 || count > GEMM_MAX_SEGMENTS)
+    return kc_fail("%s: needs 1..%d segments, got %d", name, GEMM_MAX_SEGMENTS, segments ? count : 0);
   *kind = -1;
   for (int i = 0; i < count; i++) {
     const GemmQ8Segment &g = segments[i];
@@ -268,6 +268,8 @@ static bool gemv_segments(const char *name, const GemmQ8Segment *segments, int c
     if (k < 0 || (*kind >= 0 && k != *kind) || (k == KC_SWIGLU && (count != 1 || !g.w3.q || !g.w3.s)) || g.n < 0 ||
         !weight_ok(name, g.w))
       return kc_fail("%s: segments need one kind (a SwiGLU pair alone), weights and non-negative rows", name);
+    if (g.n > 0 && !g.c)
+      return kc_fail("%s: segment %d is missing its output", name, i);
     *kind = k;
     segs[i] = KcGemvSeg{g.c, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
   }

@@ -119,3 +119,23 @@ def test_support_kernel_shapes(lib):
     assert rejected(L) == "k_rmsnorm_rows: invalid shape rows=-1 size=64"
     L.k_rmsnorm_rows(A, A, A, 1, 0, 1e-5)
     assert rejected(L) == "k_rmsnorm_rows: invalid shape rows=1 size=0"
+
+
+def test_fused_and_tail_gemv_arguments(lib):
+    kc, L = lib
+    L.k_matmul_q8_fused(A, A, 1e-5, 128, 128, 64, segs(kc, seg(kc), seg(kc, c=None)), 2, None)
+    assert rejected(L) == "k_matmul_q8_fused: segment 1 is missing its output"
+    L.k_matmul_q8_fused(A, A, 1e-5, 128, 128, 64, None, 1, None)
+    assert rejected(L) == "k_matmul_q8_fused: needs 1..3 segments, got 0"
+    L.k_matmul_q8_fused(A, A, 1e-5, 128, 128, 64, segs(kc, seg(kc), seg(kc, kind=kc.GEMM_ADD)), 2, None)
+    assert "segments need one kind" in rejected(L)
+    L.k_matmul_q8_fused(None, A, 1e-5, 128, 128, 64, segs(kc, seg(kc)), 1, None)
+    assert rejected(L) == "k_matmul_q8_fused: missing activations"
+    L.k_matmul_q8_tail(w8a8(kc), 128, 128, 64, segs(kc, seg(kc)), 1, None)
+    assert rejected(L) == "k_matmul_q8_tail: missing tail"
+    tail = kc.KernelTail(kind=kc.K_TAIL_QUANTIZE_OUTPUT)  # without q and s
+    L.k_matmul_q8_tail(w8a8(kc), 128, 128, 64, segs(kc, seg(kc, n=128)), 1, ctypes.byref(tail))
+    assert "the output quantizer needs one STORE or SWIGLU segment" in rejected(L)
+    tail = kc.KernelTail(kind=9)
+    L.k_matmul_q8_tail(w8a8(kc), 128, 128, 64, segs(kc, seg(kc)), 1, ctypes.byref(tail))
+    assert rejected(L) == "k_matmul_q8_tail: invalid tail kind 9"
