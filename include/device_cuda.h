@@ -68,8 +68,8 @@ void kd_peer_free(void *peer);
  * (project_residual / project_reduce_fn, src/tp.c:232-244 and 316-335: a K_PARTIAL share whose rows are flagged to the
  * exchange as they finish, exchange_rows_done / exchange_reduce_add_flags in src/workers.c:476-521, then added into
  * the residual): x[r] += sum over ranks, in rank order, of row r of this rank's slice (wq [d][ld] int8, ws [d][ld / gs]) times its activations (xq [n], xs [n / gs]),
- * each rank's product in the AMX order. Bitwise equal to k_matmul_q8_ld(..., K_PARTIAL) followed by
- * kd_peer_allreduce_add. d <= max_floats of kd_peer_init; gs a power of two in 16..1024 dividing n and ld, with
+ * each rank's product in the reference's AVX-512 GEMV order. Bitwise equal to k_matmul_q8_ld(..., K_PARTIAL)
+ * followed by kd_peer_allreduce_add. d <= max_floats of kd_peer_init; gs 64, 128, ... 1024 dividing n and ld, with
  * (ld / gs) a multiple of 4 and 16-byte aligned activations and scale rows, else rejected (-1). Every rank makes the
  * same calls in the same order, on the same number of SMs. */
 int kd_peer_matmul_q8_add(void *peer, float *x, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,

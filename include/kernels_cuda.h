@@ -13,8 +13,9 @@
  *
  * Weight layout is the checkpoint's: values row-major [rows][ld] int8 (ld a multiple of gs), scales [rows][ld / gs]
  * fp32. Weight values, weight scales and activations passed to the GEMV/GEMM must be 16-byte aligned, and ld / gs a
- * multiple of 4 (cudaMalloc'd buffers with the reference's shapes satisfy this). The supported group sizes are the
- * powers of two 16..256 (the checkpoints use 64); other group sizes take a slower general kernel.
+ * multiple of 4 (cudaMalloc'd buffers with the reference's shapes satisfy this). The fast kernels take group sizes
+ * 64, 128, 256 (the checkpoints use 64); other group sizes take a slower general kernel in the reference's portable
+ * order.
  * W8A32 (K8Input.q == NULL, fp32 activations in f) runs on every k_matmul_q8* entry point, bitwise the reference's
  * AVX-512 kernel (dots_q8f_body, src/gemv.c:141-180) when gs % 16 == 0 and its portable loop otherwise. */
 #ifndef LLAMA3X_KERNELS_CUDA_H
@@ -61,8 +62,9 @@ typedef enum {
   Q8_GEMM_PORTABLE,
   Q8_GEMM_AVX512,
   Q8_GEMM_AMX,
-  Q8_GEMM_GPU_DP4A = 16,   /* the row kernel (decode GEMV), one launch per activation row */
-  Q8_GEMM_GPU_TCGEN05 = 17 /* tcgen05 int8 MMA with TMEM accumulators, fed by TMA */
+  Q8_GEMM_GPU_DP4A = 16,   /* the row kernel (decode GEMV, the reference's AVX-512 / portable order), one launch per
+                              activation row */
+  Q8_GEMM_GPU_TCGEN05 = 17 /* tcgen05 int8 MMA with TMEM accumulators, fed by TMA (the AMX-INT8 order) */
 } Q8GemmBackend;
 
 /* ---- set-up (include/kernels.h:16-31) ---------------------------------------------------------------------------- */
@@ -98,6 +100,8 @@ void k_quantize(int8_t *q, float *s, const float *x, int n, int gs);
 void k_quantize_rows(int8_t *q, float *s, const float *x, size_t ldx, int m, int n, int gs);
 
 /* ---- decode GEMV (include/kernels.h:111-122) --------------------------------------------------------------------- */
+/* Bitwise the reference's k_matmul_q8 on an AVX-512 host (q8_dots, src/gemv.c:401-438): dots_q8_body's 16-lane order
+ * for gs % 64 == 0, the portable loop otherwise; W8A32 (x->q NULL) in dots_q8f_body's order or the portable loop. */
 void k_matmul_q8(float *out, const K8Input *x, K8Weight w, int n, int d, int gs);
 void k_matmul_q8_add(float *out, const K8Input *x, K8Weight w, int n, int d, int gs);
 void k_matmul_q8_qkv(float *q, float *k, float *v, const K8Input *x, K8Weight wq, K8Weight wk, K8Weight wv, int n,
@@ -126,7 +130,7 @@ void k_matmul_q8_ld_worker(float *out, const K8Input *x, const K8Weight *w, size
  * quantized in gs-groups (k_quantize's rule) by every CTA into its own shared memory, while the first weight stages
  * stream in. Bitwise the pair k_rmsnorm_q8_rows (or k_quantize) + k_matmul_q8*, in one launch. The 1-3 segments share
  * one kind: GEMM_STORE, GEMM_ADD, GEMM_PARTIAL (rows `n` of c from w) or GEMM_SWIGLU (one segment, w and w3); weight
- * rows have stride ld. gs 16..256, a power of two. */
+ * rows have stride ld. gs 64, 128 or 256. */
 typedef struct KernelTail KernelTail;
 /* `tail` (may be NULL) as for k_matmul_q8_tail below. */
 void k_matmul_q8_fused(const float *x, const float *weight, float epsilon, size_t ld, int n, int gs,
@@ -184,9 +188,12 @@ typedef struct {
 void pack_s8_vnni_many(const PackS8 *jobs, int count);
 
 /* ---- batched prefill GEMM (include/gemm.h:130-135) --------------------------------------------------------------- */
-/* From 8 activation rows on, shapes the tensor-core kernel takes (gs 64, k % 256 == 0, 16-byte aligned operands, a
- * SwiGLU pair as the only segment) run on it; fewer rows and other shapes run one decode GEMV per row. Both give the
- * same bits. The tensor-core path stages the transposed activation scales in one buffer per device that the library
+/* Shapes the tensor-core kernel takes (gs 64, k % 256 == 0, 16-byte aligned operands, a SwiGLU pair as the only
+ * segment) run on it at every row count, in the reference's AMX-INT8 order (amx_q8_chunk, src/gemm.c:554-610), so a
+ * row's result never depends on its batch; other shapes run one decode GEMV per row, in the order of the reference's
+ * AVX-512 GEMM rung for gs % 64 == 0 (bitwise its GEMV, src/gemm.c:862-899) and of its portable rung otherwise.
+ * k_gemm_q8_pick reports the rung for the segments (src/gemm.c:991-1004); it cannot see k or the activations, so a
+ * k % 256 != 0 or an unaligned activation pointer still sends k_gemm_q8 to the row rung. The tensor-core path stages the transposed activation scales in one buffer per device that the library
  * grows with cudaMalloc when a call needs more (k_gemm_q8_noalloc uses a fixed array instead). Every call on a device
  * shares that buffer, so calls on one device must not overlap on the GPU: issue them from one stream, as the
  * reference's team_run is not reentrant (include/workers.h:26). */

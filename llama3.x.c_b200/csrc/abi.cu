@@ -7,6 +7,9 @@
 #include <string.h>
 
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "../../include/kernels_cuda.h"
 #include "common.cuh"
@@ -65,6 +68,22 @@ int kc_device_sms() {
 }
 
 bool kc_pdl_enabled() { return pdl_on; }
+
+cudaError_t kc_allow_smem(const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void *, int>> done;  // (kernel, device) pairs already raised to their limit
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev}))
+    return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    done.insert({kernel, dev});
+  return e;
+}
 
 cudaStream_t kc_stream() { return tl_stream; }
 
@@ -441,25 +460,41 @@ static float *gemm_scratch(size_t floats) {
   return buf[dev];
 }
 
-// Activation rows from which the tensor-core GEMM beats one GEMV launch per row (the reference's k_gemm_q8_pick
-// threshold analogue). Measured on B200 over every 8B projection shard at 1/2/4/8-way splits: the crossover is 8 for
-// most shards, 4 for the widest (W1/W3, the classifier) and 16 for W2 unsplit. Both rungs give bitwise-equal
-// outputs, so the threshold affects only speed.
-static const int kTcMinRows = 8;
+// The rung k_gemm_q8 takes: the tensor-core GEMM (the reference's AMX-INT8 order, amx_q8_chunk src/gemm.c:554-610)
+// for every batch it can describe, whatever the row count, so a row's result never depends on the size of its batch,
+// as on the reference's AMX backend; otherwise one decode-GEMV launch per activation row, in the order of the
+// reference's AVX-512 rung (q8_micro_body src/gemm.c:862-899, bitwise its GEMV) for gs % 64 == 0 and of its portable
+// rung otherwise. The tensor-core GEMM needs gs 64, K % 256 == 0, 16-byte aligned operands and a SwiGLU pair as the
+// only segment.
+static bool tc_segments_ok(int gs, const KcGemmSeg *segs, int count) {
+  if (gs != 64)
+    return false;
+  for (int s = 0; s < count; s++) {
+    if (segs[s].kind == KC_SWIGLU && count != 1)
+      return false;
+    if (((uintptr_t)segs[s].wq & 15) || ((uintptr_t)segs[s].ws & 15))
+      return false;
+    if (segs[s].kind == KC_SWIGLU && (((uintptr_t)segs[s].w3q & 15) || ((uintptr_t)segs[s].w3s & 15)))
+      return false;
+  }
+  return true;
+}
 
+// What k_gemm_q8 runs for these segments (src/gemm.c:991-1004 reports the same for the CPU backends). The pick sees
+// neither K nor the activations: k_gemm_q8 also needs K % 256 == 0 and 16-byte aligned activation rows for the
+// tensor-core rung, and takes the row rung when they are not.
 Q8GemmBackend k_gemm_q8_pick(int gs, const GemmQ8Segment *segments, int count) {
-  (void)gs, (void)segments, (void)count;
-  return Q8_GEMM_GPU_TCGEN05;
+  if (count < 1 || count > GEMM_MAX_SEGMENTS || !segments)
+    return Q8_GEMM_GPU_DP4A;
+  KcGemmSeg segs[GEMM_MAX_SEGMENTS];
+  to_kc_segs(segments, count, segs);
+  return tc_segments_ok(gs, segs, count) ? Q8_GEMM_GPU_TCGEN05 : Q8_GEMM_GPU_DP4A;
 }
 
 static Q8GemmBackend pick(const int8_t *xq, int m, int k, int gs, const GemmQ8Segment *segments, int count) {
   KcGemmSeg segs[GEMM_MAX_SEGMENTS];
   to_kc_segs(segments, count, segs);
-  bool swiglu_ok = true;
-  for (int s = 0; s < count; s++)
-    if (segs[s].kind == KC_SWIGLU && count != 1)
-      swiglu_ok = false;
-  if (m >= kTcMinRows && swiglu_ok && kc_gemm_tc_supported(segs, count, xq, m, k, gs))
+  if (tc_segments_ok(gs, segs, count) && kc_gemm_tc_supported(segs, count, xq, m, k, gs))
     return Q8_GEMM_GPU_TCGEN05;
   return Q8_GEMM_GPU_DP4A;
 }

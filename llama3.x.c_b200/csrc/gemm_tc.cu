@@ -439,14 +439,9 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
       !kc_tmap_2d(&mp.xs, xsT, 4, ldt, groups, (uint64_t)ldt * 4, kTN, 2, false))
     return -1;
   const size_t smem = kSmemBytes;
-  static bool attr_set[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_q8_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(gemm_q8_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set[dev] = true;
-  }
+  if (kc_allow_smem(reinterpret_cast<const void *>(gemm_q8_tc_kernel<false>), (int)smem) != cudaSuccess ||
+      kc_allow_smem(reinterpret_cast<const void *>(gemm_q8_tc_kernel<true>), (int)smem) != cudaSuccess)
+    return -2;
   const int sms = kc_device_sms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles < sms ? tiles : sms);

@@ -2,22 +2,28 @@
 // epilogues of the reference's GEMV drivers (src/gemv.c:441-528: STORE / ADD / PARTIAL over 1-3 segments, SWIGLU on
 // a w1/w3 pair).
 //
-// Arithmetic: every group dot is the exact int32 sum of gs int8 products (dp4a), and each output row accumulates
-//   acc = fmaf((float)dot_g * xs[g], ws[r][g], acc)      for g = 0, 1, ..., ascending, from acc = 0
-// which is the AMX-INT8 backend's rescale (amx_q8_chunk, src/gemm.c:604-608). The result is therefore bitwise the
-// reference's AMX path and the tensor-core prefill GEMM of this library, and agrees with the reference's scalar and
-// AVX-512 GEMVs within the reference's own Q8 budget (tests/kernels.c:138-170).
+// Arithmetic: the reference's AVX-512 W8A8 kernel, dots_q8_body (src/gemv.c:109-139), which its k_matmul_q8 runs for
+// gs % 64 == 0 on every AVX-512 host. A row is 16 vector lanes; lane L (0..15) owns bytes 4L..4L+3 of every 64-byte
+// piece of the row. Per group g its int32 sum is exact (vpdpbusd with |x| and sign(x)·w is the signed dot, since no
+// int8 value is -128), and it is rescaled into the lane's own fp32 accumulator:
+//   acc[L] = fmaf((float)dot_L(g) * xs[g], ws[r][g], acc[L])      for g = 0, 1, ..., ascending, from acc = 0
+// The row's result is the 16 accumulators reduced in _mm512_reduce_add_ps's tree (lanes 8 apart, then 4, 2, 1). The
+// output is therefore bitwise the reference's decode GEMV.
 //
-// Data movement: the weight bytes are HBM-bound. Each CTA owns a contiguous range of output rows (the static split of
-// q8_team_static, src/gemv.c:483-490), walks it in sub-tiles of 32 physical weight rows that never straddle a
-// segment, and streams each sub-tile through shared memory in 1 KiB K-chunks with TMA tensor copies: one 3-D box
-// [8 K-blocks x 32 rows x 128 B] (128-byte swizzled; two 16-row halves from w1 and w3 for SwiGLU) for the weights and
-// one box of the chunk's weight scales, completing on one mbarrier, several stages deep (TMA issue costs tens of
-// cycles per instruction, so a stage is one or two instructions, not one per row or per 128 B). Inside a stage, lane r of every
-// dot warp owns weight row r and warp w takes groups w, w+8, ... of the chunk, so the int32 dots need no shuffles and,
-// thanks to the swizzle, 8 consecutive lanes read 8 distinct bank quads. A ninth warp runs the ordered fp32 chain for
-// all 32 rows (one lane per row) from a double-buffered transposed buffer, writes the outputs and refills the freed
-// stage. Dot warps and the chain warp hand the buffers over with named barriers; no CTA-wide barrier sits in the loop.
+// Work split: 8 threads per weight row, thread j holding the accumulators of lanes 2j and 2j+1 (one dp4a each per
+// 64-byte piece; the int32 lane sum is turned into its exact float by adding 1.5·2^23 inside the dp4a and
+// subtracting it in fp32, cheaper than a conversion instruction). So every thread carries its own two ordered chains
+// through the whole row and no partial result crosses a warp: the 16-lane tree at the end of the row is three
+// shuffles within 8 lanes.
+//
+// Data movement: the weight bytes are HBM-bound. Each CTA owns a contiguous range of output rows in whole octets (8
+// rows), walks it in sub-tiles of 32 physical weight rows that never straddle a segment, and streams each sub-tile
+// through shared memory in 1 KiB K-chunks with TMA tensor copies: per octet of rows one 3-D box [8 K-blocks x 8 rows x
+// 128 B] (128-byte swizzled; only the octets the sub-tile covers are read, so no row is read by two CTAs), plus one
+// box of the chunk's weight scales, completing on the stage's full barrier, several stages deep. A producer warp
+// refills a stage once the 8 compute warps have arrived on its empty barrier; nothing else synchronises the loop.
+// Bank conflicts: the 8 threads of a row read 64 contiguous bytes (4 swizzled 16-byte pieces), and the two rows of a
+// half-warp are 4 apart within their 8-row swizzle atom, so they hit the other 4 pieces.
 //
 // Launch overlap: the kernel lets its dependent start at once (griddepcontrol.launch_dependents) and issues its first
 // weight stage before waiting on the kernel it depends on (griddepcontrol.wait), so under programmatic dependent
@@ -32,25 +38,20 @@
 
 namespace {
 
-constexpr int kDotWarps = 8;
-constexpr int kThreads = (kDotWarps + 1) * 32;  // 8 dot warps + 1 chain/producer warp
-constexpr int kTileRows = 32;                   // physical weight rows per sub-tile (one per lane)
-#ifndef KC_GEMV_CHUNK
-#define KC_GEMV_CHUNK 1024
-#endif
-constexpr int kChunk = KC_GEMV_CHUNK;           // K bytes per stage
-constexpr int kBoxCols = 128;                   // bytes per 128B-swizzled box row
-constexpr int kBoxes = kChunk / kBoxCols;
+constexpr int kComputeWarps = 8;
+constexpr int kThreads = (kComputeWarps + 1) * 32;  // 8 compute warps + 1 TMA producer warp
+constexpr int kTileRows = 32;                       // physical weight rows per sub-tile (4 per compute warp)
+constexpr int kOctRows = 8;                         // weight rows per TMA box: one 1024-byte swizzle atom per K-block
+constexpr int kChunk = 1024;                        // K bytes per stage
+constexpr int kBoxCols = 128;                       // bytes per 128B-swizzled box row
+constexpr int kBoxes = kChunk / kBoxCols;           // K-blocks per chunk
+constexpr int kOctBytes = kOctRows * kChunk;        // one octet of rows over a chunk
 constexpr int kWeightStage = kTileRows * kChunk;
-constexpr int kFastGroups = kChunk / 64;            // groups of a full chunk at gs 64
-constexpr int kWarpGroups = kFastGroups / kDotWarps;  // ... of them per dot warp
-// Named barriers (0 is __syncthreads): T_FULL + b / T_EMPTY + b for the two chain buffers b.
-#ifndef KC_GEMV_TBUF
-#define KC_GEMV_TBUF 2
-#endif
-constexpr int kTBuf = KC_GEMV_TBUF;  // chain buffers: how many stages the dot warps may run ahead of the chain warp
-constexpr int kBarTFull = 1, kBarTEmpty = 1 + kTBuf;
-static_assert(kTBuf >= 2 && kTBuf <= 4, "chain buffers");
+constexpr int kMaxDepth = 8;
+constexpr int kCtrlBytes = 512;  // full and empty barriers, flags, 65 floats of prologue scratch
+// 1.5 * 2^23: an int32 v with |v| < 2^22 added to these bits reads as the float 12582912 + v exactly.
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;
 
 struct GemvSegDev {
   float *out;
@@ -138,98 +139,83 @@ __device__ __forceinline__ Sub subtile(const Plan &p, int k) {
   return r;
 }
 
-__device__ __forceinline__ bool lane_active(bool swiglu, int lane, int cnt) {
-  return swiglu ? (lane & 15) < cnt : lane < cnt;
-}
 
-// Named barriers with immediate ids: a register id makes ptxas reserve all 16 of the CTA's barriers, and the SM's
-// barrier pool then holds one CTA of this kernel at a time.
-template <int ID>
-__device__ __forceinline__ void bar_sync_id() {
-  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(kThreads) : "memory");
-}
-template <int ID>
-__device__ __forceinline__ void bar_arrive_id() {
-  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "n"(kThreads) : "memory");
-}
-// Barrier BASE + idx (idx < kTBuf), with the id an immediate in every branch.
-template <int BASE>
-__device__ __forceinline__ void bar_sync_named(int idx) {
-  switch (idx) {
-    case 0: bar_sync_id<BASE>(); break;
-    case 1: bar_sync_id<BASE + 1>(); break;
-    case 2: if (kTBuf > 2) bar_sync_id<BASE + (kTBuf > 2 ? 2 : 0)>(); break;
-    default: if (kTBuf > 3) bar_sync_id<BASE + (kTBuf > 3 ? 3 : 0)>(); break;
-  }
-}
-template <int BASE>
-__device__ __forceinline__ void bar_arrive_named(int idx) {
-  switch (idx) {
-    case 0: bar_arrive_id<BASE>(); break;
-    case 1: bar_arrive_id<BASE + 1>(); break;
-    case 2: if (kTBuf > 2) bar_arrive_id<BASE + (kTBuf > 2 ? 2 : 0)>(); break;
-    default: if (kTBuf > 3) bar_arrive_id<BASE + (kTBuf > 3 ? 3 : 0)>(); break;
-  }
-}
-
-// Stage layout: the weights of one 32-row sub-tile (two 16-row halves, w1 then w3, for SwiGLU) as 8 K-blocks of
-// [half rows][128 B] per half, 128B-swizzled; then the weight scales [32 rows][gpc floats].
-// Issued by the chain warp. With k-block maps lane 0 (and lane 1 for w3) moves a whole half in one instruction;
-// otherwise lanes b < 8 (and 16 + b) move one [rows x 128 B] box each. Lanes 30/31 load the scale box(es). Every box
-// is copied whole (rows past the sub-tile are the next rows of the segment, or the tensor map's zero fill past the
-// matrix), so the transaction count is fixed per stage.
+// Stage layout: four octet slots of [8 K-blocks][8 rows][128 B] (128B-swizzled), octet o holding physical rows
+// 8o..8o+7 of the sub-tile (for SwiGLU: octets 0-1 are w1's 16 rows, 2-3 w3's), then the weight scales [32 rows][gpc
+// floats] (w1's 16 rows, then w3's). Issued by the producer warp. Only the octets the sub-tile's rows reach are copied
+// (the scale box is always whole: rows past the matrix are zero-filled), so the transaction count is computed per
+// stage. With k-block maps lanes 0-3 move one octet each in a single instruction; otherwise lane 8o + b moves K-block
+// b of octet o as a [128 B x 8 rows] box. Every box is copied whole: rows and columns past the matrix are the tensor
+// map's zero fill.
 __device__ __forceinline__ void issue_stage(const GemvMaps &m, int gpc, int kblock, const Sub &t, int chunk, bool swiglu,
                                             int lane, uint8_t *buf, uint64_t *bar) {
+  const int noct = (t.cnt + kOctRows - 1) / kOctRows;  // octets per half (SwiGLU) or per sub-tile
+  const int srows = swiglu ? kTileRows / 2 : kTileRows;
   if (lane == 0)
-    mbar_arrive_expect_tx(bar, (unsigned)(kWeightStage + kTileRows * gpc * 4));
+    mbar_arrive_expect_tx(bar, (unsigned)((swiglu ? 2 * noct : noct) * kOctBytes + kTileRows * gpc * 4));
   __syncwarp();
-  const int half = swiglu ? kTileRows / 2 : kTileRows;
-  const int kb_stride = half * kBoxCols;
-  const CUtensorMap *w = swiglu ? &m.wmap[0] : &m.wmap[0] + t.seg;
-  const CUtensorMap *sm = swiglu ? &m.smap[0] : &m.smap[0] + t.seg;
-  if (kblock) {
-    if (lane == 0)
-      tma_load_3d(buf, w, 0, t.row0, chunk * kBoxes, bar);
-    if (swiglu && lane == 1)
-      tma_load_3d(buf + half * kChunk, &m.w3map, 0, t.row0, chunk * kBoxes, bar);
-  } else {
-    const int x0 = chunk * kChunk;
-    if (lane < kBoxes)
-      tma_load_2d(buf + lane * kb_stride, w, x0 + lane * kBoxCols, t.row0, bar);
-    else if (swiglu && lane >= 16 && lane < 16 + kBoxes)
-      tma_load_2d(buf + half * kChunk + (lane - 16) * kb_stride, &m.w3map, x0 + (lane - 16) * kBoxCols, t.row0, bar);
+  const int o = kblock ? lane : lane >> 3;  // the octet slot this lane serves
+  const bool w3 = swiglu && o >= 2;
+  const int orow = swiglu ? (o & 1) : o;  // octet index within its half
+  if (o < 4 && orow < noct) {
+    const CUtensorMap *w = w3 ? &m.w3map : swiglu ? &m.wmap[0] : &m.wmap[0] + t.seg;
+    const int row = t.row0 + orow * kOctRows;
+    if (kblock)
+      tma_load_3d(buf + o * kOctBytes, w, 0, row, chunk * kBoxes, bar);
+    else
+      tma_load_2d(buf + o * kOctBytes + (lane & 7) * (kOctRows * kBoxCols), w, chunk * kChunk + (lane & 7) * kBoxCols,
+                  row, bar);
   }
   if (lane == 31)
-    tma_load_2d(buf + kWeightStage, sm, chunk * gpc, t.row0, bar);
+    tma_load_2d(buf + kWeightStage, swiglu ? &m.smap[0] : &m.smap[0] + t.seg, chunk * gpc, t.row0, bar);
   if (swiglu && lane == 30)
-    tma_load_2d(buf + kWeightStage + half * gpc * 4, &m.s3map, chunk * gpc, t.row0, bar);
+    tma_load_2d(buf + kWeightStage + srows * gpc * 4, &m.s3map, chunk * gpc, t.row0, bar);
 }
 
-// Byte offset inside a stage of the 16-byte piece `k16` (0 .. 63 along K) of physical row r (0 .. 31): its half,
-// its K-block k16 / 8, its row within the half, then the 128B swizzle (piece index XOR row within the 8-row atom).
-template <int HALF>
-__device__ __forceinline__ int piece_offset(int r, int k16) {
-  return (r >= HALF ? HALF * kChunk : 0) + (k16 >> 3) * (HALF * kBoxCols) + (r & (HALF - 1)) * kBoxCols +
-         (((k16 & 7) ^ (r & 7)) << 4);
+__device__ __forceinline__ uint2 lds64(const void *p) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+  return v;
 }
 
-// Exact int32 dot of group g of physical row r with the activations (4 independent dp4a chains for gs 64).
-template <int GS, int HALF>
-__device__ __forceinline__ int group_dot(const uint8_t *buf, const int8_t *xrow, int r, int g, int gs) {
-  if (GS == 64) {
-    int4 w[4], x[4];
+// Byte offset, from the start of a row inside its octet slot, of the 8 bytes at K offset `kb8 * 8` of the chunk for
+// a row at position `r7` of its octet: K-block, then the 16-byte piece XOR the row (the 128B swizzle), then the half
+// of the piece.
+__device__ __forceinline__ int row_offset(int r7, int kb8) {
+  return (kb8 >> 4) * (kOctRows * kBoxCols) + ((((kb8 >> 1) & 7) ^ r7) << 4) + ((kb8 & 1) << 3);
+}
+
+// One gs-group of a chunk for this thread's two lanes: the exact int32 sums of lanes 2j and 2j+1 (one dp4a each per
+// 64-byte piece, started from the magic bits), their exact floats, times xs, fused into the accumulators with ws.
+template <int GS>
+__device__ __forceinline__ void group_step(const uint8_t *rowbuf, int r7, const int8_t *xrow, int g, int gs, int j,
+                                           float xs, float ws, float &a0, float &a1) {
+  const int gsz = GS ? GS : gs;
+  int d0 = kMagicBits, d1 = kMagicBits;
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-      w[q] = lds128(buf + piece_offset<HALF>(r, g * 4 + q));
-      x[q] = lds128(xrow + g * 64 + q * 16);
-    }
-    int d0 = dot16(w[0], x[0], 0), d1 = dot16(w[1], x[1], 0), d2 = dot16(w[2], x[2], 0), d3 = dot16(w[3], x[3], 0);
-    return (d0 + d1) + (d2 + d3);
+  for (int c = 0; c < gsz; c += 64) {
+    const int kb8 = (g * gsz + c) / 8 + j;  // 8-byte unit of the chunk
+    const uint2 w = lds64(rowbuf + row_offset(r7, kb8));
+    const uint2 x = lds64(xrow + kb8 * 8);
+    d0 = __dp4a((int)w.x, (int)x.x, d0);
+    d1 = __dp4a((int)w.y, (int)x.y, d1);
   }
-  int dot = 0;
-  for (int q = 0; q < gs / 16; q++)
-    dot = dot16(lds128(buf + piece_offset<HALF>(r, g * (gs / 16) + q)), lds128(xrow + g * gs + q * 16), dot);
-  return dot;
+  const float f0 = __fsub_rn(__int_as_float(d0), kMagic), f1 = __fsub_rn(__int_as_float(d1), kMagic);
+  a0 = __fmaf_rn(__fmul_rn(f0, xs), ws, a0);
+  a1 = __fmaf_rn(__fmul_rn(f1, xs), ws, a1);
+}
+
+// _mm512_reduce_add_ps over the 16 lane accumulators of a row, held by 8 consecutive threads (two each): lanes 8
+// apart, 4 apart, 2 apart, then the last pair. Float addition is commutative, so which thread adds is free; the pairs
+// are the tree's. The result is valid in the row's thread j = 0.
+__device__ __forceinline__ float row_reduce(float a0, float a1) {
+  a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 4, 8));
+  a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 4, 8));
+  a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 2, 8));
+  a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 2, 8));
+  a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 1, 8));
+  a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 1, 8));
+  return __fadd_rn(a0, a1);
 }
 
 // Copies n floats from global to shared memory with all the CTA's threads, each keeping kStageBatch 16-byte loads in
@@ -520,10 +506,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   const bool swiglu = a.kind == KC_SWIGLU;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, c = blockIdx.x;
-  const int u0 = a.units * c / G, u1 = a.units * (c + 1) / G;  // units * grid < 2^31 (checked on the host)
+  // Whole octets of units per CTA (units < 2^31 / 1024, checked on the host).
+  const int noct = (a.units + kOctRows - 1) / kOctRows;
+  const int u0 = min(a.units, kOctRows * (int)((long long)noct * c / G));
+  const int u1 = min(a.units, kOctRows * (int)((long long)noct * (c + 1) / G));
   if (u1 <= u0) {
-    if (a.tail.kind && a.tail.kind != KC_TAIL_QUANTIZE_OUTPUT)
-      finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem));
+    if (a.tail.kind && a.tail.kind != KC_TAIL_QUANTIZE_OUTPUT)  // the flag lives past the tail's scratch
+      finish_tail(a, reinterpret_cast<float *>(smem), reinterpret_cast<int *>(smem + a.depth * a.stage_bytes));
     if (RED) {  // no rows, but the call still counts
       pdl_wait();
       if (tid == 0)
@@ -538,19 +527,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   const int gpc = kChunk / gs;
   float *const out0 = a.seg[0].out, *const out1 = a.seg[1].out, *const out2 = a.seg[2].out;
 
-  // Shared memory: the stages (1024-byte aligned for the swizzle), then barriers, flags, chain buffers, activations.
+  // Shared memory: the stages (1024-byte aligned for the swizzle), the control block, then the activations.
   uint8_t *stages = smem;
-  uint8_t *tail = smem + depth * stage_bytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(tail);
-  volatile int *abort_flag = reinterpret_cast<int *>(tail + 8 * 8);
-  volatile int *issued = reinterpret_cast<int *>(tail + 8 * 8 + 4);
-  float *T = reinterpret_cast<float *>(tail + 128);
-  float *XS = T + kTBuf * gpc * kTileRows;
+  uint8_t *ctrl = smem + depth * stage_bytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(ctrl);
+  uint64_t *empty = full + kMaxDepth;
+  volatile int *abort_flag = reinterpret_cast<int *>(ctrl + 16 * kMaxDepth);
+  volatile int *issued = abort_flag + 1;
+  int *tail_flag = const_cast<int *>(abort_flag) + 2;
+  float *scratch = reinterpret_cast<float *>(ctrl + 16 * kMaxDepth + 16);
+  float *XS = reinterpret_cast<float *>(ctrl + kCtrlBytes);
   int8_t *XQ = reinterpret_cast<int8_t *>(XS + ((n / gs + 3) & ~3));
 
   if (tid == 0) {
-    for (int i = 0; i < depth; i++)
-      mbar_init(&bars[i], 1);
+    for (int i = 0; i < depth; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kComputeWarps);
+    }
     *abort_flag = 0;
     *issued = min(depth, S);
     fence_mbar_init();
@@ -559,8 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   // Weights do not depend on the previous kernel: the first stage streams in before waiting for it. The others are
   // issued once the activation loads are on their way, so those few kilobytes do not queue behind the whole
   // prefetch on the way into this SM.
-  if (warp == kDotWarps && S > 0)
-    issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &bars[0]);
+  if (warp == kComputeWarps && S > 0)
+    issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &full[0]);
   pdl_wait();
   // The counter was written by the previous reducing call, complete once pdl_wait returns.
   const unsigned seq = RED ? a.peer.epoch[c] + 1u : 0u;
@@ -571,126 +564,91 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
     for (int i = tid; i < n / gs; i += kThreads)
       XS[i] = __ldg(a.xs + i);
   } else {
-    prepare_activation(a, XQ, XS, reinterpret_cast<float *>(XQ + ((n + 15) & ~15)), T, gs);
+    prepare_activation(a, XQ, XS, reinterpret_cast<float *>(XQ + ((n + 15) & ~15)), scratch, gs);
   }
-  if (warp == kDotWarps)
+  if (warp == kComputeWarps)
     for (int i = 1; i < depth && i < S; i++)
       issue_stage(m, gpc, a.kblock, subtile(plan, i / nchunks), i % nchunks, swiglu, lane, stages + i * stage_bytes,
-                  &bars[i]);
+                  &full[i]);
   __syncthreads();
 
-  if (warp < kDotWarps) {
-    // ---- dot warps: exact int32 group dots of 32 rows, scaled by the activation scale, into T[stage & 1] ----
+  if (warp < kComputeWarps) {
+    // ---- compute warps: warp w holds rows b, b+4, b+16, b+20 of each sub-tile (b = 8(w/4) + w%4), 8 threads each;
+    // for SwiGLU rows 16.. are w3's, so a unit's w1 and w3 rows sit 16 lanes apart in one warp.
+    const int rho = lane >> 3, j = lane & 7;
+    const int pr = (warp >> 2) * 8 + (warp & 3) + (rho & 1) * 4 + (rho >> 1) * 16;
+    const int r7 = pr & 7;
+    const int unit_in_tile = swiglu ? (pr & 15) : pr;
+    float a0 = 0.0f, a1 = 0.0f;
     int slot = 0, chunk = 0, sub = 0;
     unsigned phase = 0;
     for (int i = 0; i < S; i++) {
-      const Sub t = subtile(plan, sub);
-      if (!*abort_flag && !mbar_wait_bounded(&bars[slot], phase))
+      if (!*abort_flag && !mbar_wait_bounded(&full[slot], phase))
         *abort_flag = 1;
-      if (i >= kTBuf)
-        bar_sync_named<kBarTEmpty>(i % kTBuf);
       const uint8_t *buf = stages + slot * stage_bytes;
-      float *Tb = T + (i % kTBuf) * gpc * kTileRows;
+      const uint8_t *rowbuf = buf + (pr >> 3) * kOctBytes + r7 * kBoxCols;
+      const float *wsr = reinterpret_cast<const float *>(buf + kWeightStage) + pr * gpc;
+      const int8_t *xrow = XQ + chunk * kChunk;
+      const float *xsc = XS + chunk * gpc;
       const int groups = min(gpc, (n - chunk * kChunk) / gs);
-      if (lane_active(swiglu, lane, t.cnt)) {
-        const int8_t *xrow = XQ + chunk * kChunk;
-        const float *xsc = XS + chunk * gpc;
-        if (GS == 64 && groups == kFastGroups) {
-          // All of this warp's groups at once: 4 independent dp4a chains per group in flight.
-          int d[kWarpGroups];
+      if (GS == 64 && groups == kChunk / 64) {
 #pragma unroll
-          for (int j = 0; j < kWarpGroups; j++)
-            d[j] = swiglu ? group_dot<GS, 16>(buf, xrow, lane, warp + j * kDotWarps, gs)
-                          : group_dot<GS, 32>(buf, xrow, lane, warp + j * kDotWarps, gs);
-#pragma unroll
-          for (int j = 0; j < kWarpGroups; j++)
-            Tb[(warp + j * kDotWarps) * kTileRows + lane] =
-                __fmul_rn(__int2float_rn(d[j]), xsc[warp + j * kDotWarps]);
-        } else {
-          for (int g = warp; g < groups; g += kDotWarps) {
-            const int d = swiglu ? group_dot<GS, 16>(buf, xrow, lane, g, gs) : group_dot<GS, 32>(buf, xrow, lane, g, gs);
-            Tb[g * kTileRows + lane] = __fmul_rn(__int2float_rn(d), xsc[g]);
+        for (int h = 0; h < kChunk / 64; h += 4) {
+          const float4 w4 = *reinterpret_cast<const float4 *>(wsr + h);
+          const float4 x4 = *reinterpret_cast<const float4 *>(xsc + h);
+          group_step<GS>(rowbuf, r7, xrow, h + 0, gs, j, x4.x, w4.x, a0, a1);
+          group_step<GS>(rowbuf, r7, xrow, h + 1, gs, j, x4.y, w4.y, a0, a1);
+          group_step<GS>(rowbuf, r7, xrow, h + 2, gs, j, x4.z, w4.z, a0, a1);
+          group_step<GS>(rowbuf, r7, xrow, h + 3, gs, j, x4.w, w4.w, a0, a1);
+        }
+      } else {
+        for (int g = 0; g < groups; g++)
+          group_step<GS>(rowbuf, r7, xrow, g, gs, j, xsc[g], wsr[g], a0, a1);
+      }
+      // This warp's last read of the stage: release it to the producer.
+      __syncwarp();
+      if (lane == 0)
+        mbar_arrive(&empty[slot]);
+      if (chunk == nchunks - 1) {
+        const Sub t = subtile(plan, sub);
+        const float r = row_reduce(a0, a1);
+        const float gate = __shfl_down_sync(0xffffffffu, r, 16);
+        float *out = (t.seg == 0 ? out0 : t.seg == 1 ? out1 : out2) + t.row0;
+        if (j == 0 && unit_in_tile < t.cnt) {
+          if (swiglu) {
+            if (rho < 2)
+              out[unit_in_tile] = silu_gate_dev(r, gate);
+          } else if (a.kind == KC_ADD) {
+            out[unit_in_tile] = __fadd_rn(out[unit_in_tile], r);
+          } else if (RED) {
+            push_row(a.peer, par, seq, t.row0 + unit_in_tile, r);
+          } else {
+            out[unit_in_tile] = r;
           }
         }
+        a0 = 0.0f, a1 = 0.0f;
       }
-      bar_arrive_named<kBarTFull>(i % kTBuf);
       if (++slot == depth)
         slot = 0, phase ^= 1u;
       if (++chunk == nchunks)
         chunk = 0, sub++;
     }
   } else {
-    // ---- chain warp: the ordered fp32 accumulation (one lane per row), the epilogue, and the TMA producer ----
-    float acc = 0.0f;
-    int slot = 0, chunk = 0, sub = 0;
-    int nchunk = depth % nchunks, nsub = depth / nchunks;  // chunk and sub-tile of stage i + depth
-    for (int i = 0; i < S; i++) {
-      const Sub t = subtile(plan, sub);
-      bar_sync_named<kBarTFull>(i % kTBuf);
-      const float *Tb = T + (i % kTBuf) * gpc * kTileRows;
-      const float *wsr = reinterpret_cast<const float *>(stages + slot * stage_bytes + kWeightStage) + lane * gpc;
-      const int groups = min(gpc, (n - chunk * kChunk) / gs);
-      if (GS == 64 && groups == kFastGroups && lane_active(swiglu, lane, t.cnt)) {
-        // 16 groups at a time: their scaled dots and weight scales loaded first, then the 16 dependent FMAs.
-#pragma unroll
-        for (int h = 0; h < kFastGroups; h += 16) {
-          float tv[16], wv[16];
-#pragma unroll
-          for (int g = 0; g < 16; g += 4) {
-            float4 w4 = *reinterpret_cast<const float4 *>(wsr + h + g);
-            wv[g] = w4.x, wv[g + 1] = w4.y, wv[g + 2] = w4.z, wv[g + 3] = w4.w;
-          }
-#pragma unroll
-          for (int g = 0; g < 16; g++)
-            tv[g] = Tb[(h + g) * kTileRows + lane];
-#pragma unroll
-          for (int g = 0; g < 16; g++)
-            acc = __fmaf_rn(tv[g], wv[g], acc);
-        }
-      } else if (lane_active(swiglu, lane, t.cnt)) {
-        for (int g = 0; g < groups; g += 4) {
-          float4 w4 = *reinterpret_cast<const float4 *>(wsr + g);
-          acc = __fmaf_rn(Tb[g * kTileRows + lane], w4.x, acc);
-          if (g + 1 < groups)
-            acc = __fmaf_rn(Tb[(g + 1) * kTileRows + lane], w4.y, acc);
-          if (g + 2 < groups)
-            acc = __fmaf_rn(Tb[(g + 2) * kTileRows + lane], w4.z, acc);
-          if (g + 3 < groups)
-            acc = __fmaf_rn(Tb[(g + 3) * kTileRows + lane], w4.w, acc);
-        }
+    // ---- producer warp: refills stage slot i % depth with stage i once every compute warp has released stage
+    // i - depth.
+    int nchunk = depth % nchunks, nsub = depth / nchunks;  // chunk and sub-tile of stage i
+    for (int i = depth; i < S; i++) {
+      const int slot = i % depth;
+      if (*abort_flag || !mbar_wait_bounded(&empty[slot], (unsigned)(i / depth - 1) & 1u)) {
+        *abort_flag = 1;
+        break;
       }
-      if (chunk == nchunks - 1) {
-        float gate = __shfl_down_sync(0xffffffffu, acc, 16);
-        float *out = (t.seg == 0 ? out0 : t.seg == 1 ? out1 : out2) + t.row0;
-        if (swiglu) {
-          if (lane < t.cnt)
-            out[lane] = silu_gate_dev(acc, gate);
-        } else if (lane < t.cnt) {
-          if (a.kind == KC_ADD)
-            out[lane] = __fadd_rn(out[lane], acc);
-          else if (RED)
-            push_row(a.peer, par, seq, t.row0 + lane, acc);
-          else
-            out[lane] = acc;
-        }
-        acc = 0.0f;
-      }
-      // Stage i is fully consumed (dot warps passed T_FULL after their last read of its weights, and the chain has
-      // read its scales): refill the slot with stage i + depth.
-      if (i + depth < S && !*abort_flag) {
-        issue_stage(m, gpc, a.kblock, subtile(plan, nsub), nchunk, swiglu, lane, stages + slot * stage_bytes,
-                    &bars[slot]);
-        if (lane == 0)
-          *issued = i + depth + 1;
-      }
+      issue_stage(m, gpc, a.kblock, subtile(plan, nsub), nchunk, swiglu, lane, stages + slot * stage_bytes,
+                  &full[slot]);
+      if (lane == 0)
+        *issued = i + 1;
       if (++nchunk == nchunks)
         nchunk = 0, nsub++;
-      if (i + kTBuf < S)
-        bar_arrive_named<kBarTEmpty>(i % kTBuf);
-      if (++slot == depth)
-        slot = 0;
-      if (++chunk == nchunks)
-        chunk = 0, sub++;
     }
   }
   // After an abort, let every copy still in flight land (bounded waits) before the shared memory goes away: for each
@@ -698,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   __syncthreads();
   if (*abort_flag && tid == 0)
     for (int j = max(0, *issued - depth); j < *issued; j++)
-      mbar_wait_bounded(&bars[j % depth], (unsigned)(j / depth) & 1u);
+      mbar_wait_bounded(&full[j % depth], (unsigned)(j / depth) & 1u);
   if (RED) {
     reduce_rows(a.peer, out0, u0, u1, par, seq);
     __syncthreads();
@@ -710,13 +668,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
     quantize_output_groups(a.tail, out0, u0, u1, gs, reinterpret_cast<int *>(stages));
   } else if (a.tail.kind) {
     __syncthreads();
-    finish_tail(a, reinterpret_cast<float *>(stages), const_cast<int *>(abort_flag) + 2);
+    finish_tail(a, reinterpret_cast<float *>(stages), tail_flag);
   }
 }
 
-// The general rung, for shapes the TMA kernel cannot describe (group sizes below 16 or not a power of two, scale rows
-// that are not 16-byte multiples, unaligned pointers): one warp per output row, the group dot reduced exactly across
-// the warp, lane 0 applying the same ordered rescale. Slow but bitwise identical to the fast kernel.
+
+// The general rung, for shapes the TMA kernel does not take (group sizes that are not a power-of-two multiple of 64,
+// scale rows that are not 16-byte multiples, unaligned pointers): one warp per output row, in the order the
+// reference's k_matmul_q8 uses for the group size (q8_dots, src/gemv.c:401-438):
+//  - gs % 64 == 0: the AVX-512 lane order of dots_q8_body, lanes 0-15 of the warp being the 16 vector lanes (bitwise
+//    the TMA kernel);
+//  - otherwise its portable loop: the exact int32 group dot (reduced across the warp), then, by lane 0,
+//    val = val + ((float)dot * ws[g]) * xs[g], no fused multiply-add.
 __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, GemvSegDev s1, GemvSegDev s2,
                                                                const int8_t *wq0, const int8_t *wq1, const int8_t *wq2,
                                                                const float *ws0, const float *ws1, const float *ws2,
@@ -735,19 +698,35 @@ __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, Gem
   const int row = unit - seg.unit0;
   const int8_t *wq = (s == 0 ? wq0 : s == 1 ? wq1 : wq2) + row * ld;
   const float *ws = (s == 0 ? ws0 : s == 1 ? ws1 : ws2) + row * (ld / gs);
+  const bool avx = gs % 64 == 0;
   float acc[2] = {0.0f, 0.0f};
   for (int pass = 0; pass < (kind == KC_SWIGLU ? 2 : 1); pass++) {
     const int8_t *w = pass ? w3q + row * ld : wq;
     const float *sc = pass ? w3s + row * (ld / gs) : ws;
+    float a = 0.0f;
     for (int g = 0; g < n / gs; g++) {
       int dot = 0;
-      for (int k = lane; k < gs; k += 32)
-        dot += (int)xq[g * gs + k] * (int)w[g * gs + k];
+      if (avx) {
+        if (lane < 16)
+          for (int c = 0; c < gs; c += 64)
+            for (int k = 0; k < 4; k++)
+              dot += (int)xq[g * gs + c + 4 * lane + k] * (int)w[g * gs + c + 4 * lane + k];
+        a = __fmaf_rn(__fmul_rn(__int2float_rn(dot), xs[g]), sc[g], a);
+      } else {
+        for (int k = lane; k < gs; k += 32)
+          dot += (int)xq[g * gs + k] * (int)w[g * gs + k];
 #pragma unroll
-      for (int o = 16; o; o >>= 1)
-        dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      acc[pass] = __fmaf_rn(__fmul_rn(__int2float_rn(dot), xs[g]), sc[g], acc[pass]);
+        for (int o = 16; o; o >>= 1)
+          dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        a = __fadd_rn(a, __fmul_rn(__fmul_rn(__int2float_rn(dot), sc[g]), xs[g]));
+      }
     }
+    if (avx) {  // _mm512_reduce_add_ps: lanes 8 apart, 4, 2, 1
+#pragma unroll
+      for (int o = 8; o; o >>= 1)
+        a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, o, 16));
+    }
+    acc[pass] = a;
   }
   if (lane == 0) {
     float *out = seg.out + row;
@@ -762,17 +741,19 @@ __global__ void __launch_bounds__(256) gemv_q8_generic_kernel(GemvSegDev s0, Gem
 
 // act_floats: fp32 staging of the fused activation modes (n, or 2n with the norm weights).
 size_t smem_bytes(int n, int gs, int stage_bytes, int depth, int act_floats) {
-  return (size_t)depth * stage_bytes + 128 + (size_t)kTBuf * (kChunk / gs) * kTileRows * 4 + (size_t)((n / gs + 3) & ~3) * 4 +
-         (size_t)((n + 15) & ~15) + (size_t)act_floats * 4 + 1024;
+  return (size_t)depth * stage_bytes + kCtrlBytes + (size_t)((n / gs + 3) & ~3) * 4 + (size_t)((n + 15) & ~15) +
+         (size_t)act_floats * 4 + 1024;
 }
 
+// The weight map moves octets of rows ([8 K-blocks x 8 rows x 128 B] boxes, or [128 B x 8 rows] without k-block
+// maps); the scale map moves [gpc floats x scale_rows] boxes.
 bool encode_weight(CUtensorMap *wmap, CUtensorMap *smap, const int8_t *wq, const float *ws, int rows, int n,
-                   long long ld, int gs, int box_rows, bool kblock) {
+                   long long ld, int gs, int scale_rows, bool kblock) {
   const int gpc = kChunk / gs;
-  bool ok = kblock ? kc_tmap_kblocks(wmap, wq, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxes, box_rows)
-                   : kc_tmap_2d(wmap, wq, 1, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxCols, box_rows, true);
+  bool ok = kblock ? kc_tmap_kblocks(wmap, wq, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxes, kOctRows)
+                   : kc_tmap_2d(wmap, wq, 1, (uint64_t)n, (uint64_t)rows, (uint64_t)ld, kBoxCols, kOctRows, true);
   return ok &&
-         kc_tmap_2d(smap, ws, 4, (uint64_t)(n / gs), (uint64_t)rows, (uint64_t)(ld / gs) * 4, gpc, box_rows, false);
+         kc_tmap_2d(smap, ws, 4, (uint64_t)(n / gs), (uint64_t)rows, (uint64_t)(ld / gs) * 4, gpc, scale_rows, false);
 }
 
 }  // namespace
@@ -931,7 +912,8 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   GemvArgs A;
   memset(&M, 0, sizeof(M));
   memset(&A, 0, sizeof(A));
-  if (gs < 16 || gs > kChunk || (gs & (gs - 1)) || n % gs || ld % gs || ld < n || ((ld / gs) * 4) % 16 ||
+  // The lane order is the reference's for gs % 64 == 0; other group sizes take the general rung's portable order.
+  if (gs < 64 || gs > kChunk || (gs & (gs - 1)) || n % gs || ld % gs || ld < n || ((ld / gs) * 4) % 16 ||
       ((uintptr_t)xq & 15) || (act && gs > 256))
     return -1;
   int act_floats = 0;
@@ -949,7 +931,7 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     A.peer = *peer;
   }
   const bool swiglu = kind == KC_SWIGLU;
-  const int box_rows = swiglu ? kTileRows / 2 : kTileRows;
+  const int scale_rows = swiglu ? kTileRows / 2 : kTileRows;
   int units = 0;
   for (int s = 0; s < nseg; s++) {
     A.seg[s].out = segs[s].out;
@@ -966,9 +948,9 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     for (int s = 0; s < nseg && ok; s++) {
       if (segs[s].d == 0)
         continue;
-      ok = encode_weight(&M.wmap[s], &M.smap[s], segs[s].wq, segs[s].ws, segs[s].d, n, ld, gs, box_rows, kblock) &&
+      ok = encode_weight(&M.wmap[s], &M.smap[s], segs[s].wq, segs[s].ws, segs[s].d, n, ld, gs, scale_rows, kblock) &&
            (!swiglu ||
-            encode_weight(&M.w3map, &M.s3map, segs[s].w3q, segs[s].w3s, segs[s].d, n, ld, gs, box_rows, kblock));
+            encode_weight(&M.w3map, &M.s3map, segs[s].w3q, segs[s].w3s, segs[s].d, n, ld, gs, scale_rows, kblock));
     }
     if (ok)
       break;
@@ -994,8 +976,9 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
 #define KC_GEMV_SMEM_BUDGET (200 * 1024)
 #endif
 #ifndef KC_GEMV_MAX_DEPTH
-#define KC_GEMV_MAX_DEPTH 4
+#define KC_GEMV_MAX_DEPTH 5
 #endif
+  static_assert(KC_GEMV_MAX_DEPTH <= kMaxDepth, "pipeline depth");
   // The fused modes may use the rest of the 227 KB for their fp32 staging rather than give up pipeline depth.
   size_t budget = act ? 226 * 1024 : KC_GEMV_SMEM_BUDGET;
   if (smem_bytes(n, gs, A.stage_bytes, 2, act_floats) > budget)
@@ -1024,21 +1007,17 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
     A.tail = *tail;
   }
   const int sms = kc_device_sms();
-  int grid = units < sms ? units : sms;
+  const int octets = (units + kOctRows - 1) / kOctRows;  // the CTAs split the units in whole octets
+  int grid = octets < sms ? octets : sms;
   if (grid_limit > 0 && grid > grid_limit)
     grid = grid_limit;
   if (kind == KC_REDUCE_ADD)  // one grid size for every call: each CTA's counter counts every call
     grid = sms < kPeerGemvMaxCtas ? sms : kPeerGemvMaxCtas;
-  static bool attr_set[64][4];
-  int dev = 0;
-  cudaGetDevice(&dev);
   const int variant = (gs == 64 ? 0 : 1) + (kind == KC_REDUCE_ADD ? 2 : 0);
   void (*const kernels[4])(const GemvMaps, const GemvArgs) = {gemv_q8_kernel<64, false>, gemv_q8_kernel<0, false>,
                                                               gemv_q8_kernel<64, true>, gemv_q8_kernel<0, true>};
-  if (dev < 64 && !attr_set[dev][variant]) {
-    cudaFuncSetAttribute(kernels[variant], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_set[dev][variant] = true;
-  }
+  if (kc_allow_smem(reinterpret_cast<const void *>(kernels[variant]), 227 * 1024) != cudaSuccess)
+    return -2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -1052,3 +1031,4 @@ static int launch_tma(const KcGemvSeg *segs, int nseg, const int8_t *xq, const f
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[variant], M, A);
   return e == cudaSuccess ? 0 : -2;
 }
+

@@ -41,6 +41,9 @@ bool kc_fail(const char *format, ...);
 void kc_count_launch();
 // Programmatic dependent launch of the kernels that support it (kernels_set_pdl; on by default).
 bool kc_pdl_enabled();
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device, once per (kernel, device); safe to
+// call from several host threads at once.
+cudaError_t kc_allow_smem(const void *kernel, int bytes);
 
 // Launches `kernel` on `stream` with programmatic dependent launch allowed (kernels_set_pdl): it may be scheduled
 // while the previous kernel in the stream drains, so every kernel launched this way starts with griddepcontrol.wait

@@ -56,6 +56,8 @@ def lib():
         L.orc_gemm_amx_order.argtypes = [_f32p, ctypes.c_int, _i8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i8p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int]
         L.orc_silu_gate.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.orc_gemv_ref_order.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_silu_gate.restype = ctypes.c_float
         L.orc_rmsnorm_scalar.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_float]
         L.orc_rmsnorm_avx512_order.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_float]
@@ -114,6 +116,27 @@ def gemv_f32(x, wq, ws, gs):
     f = lib().orc_gemv_f32_avx512_order if gs % 16 == 0 else lib().orc_gemv_f32_scalar
     f(_p(out, _f32p), _p(x, _f32p), _p(wq, _i8p), _p(ws, _f32p), ld, x.shape[-1], d, gs)
     return out
+
+
+def gemv(xq, xs, wq, ws, gs, kind=STORE, out=None, w3q=None, w3s=None, n=None):
+    """The reference's decode GEMV (k_matmul_q8 on an AVX-512 host, src/gemv.c:401-528) for one activation row and d
+    weight rows (row stride wq.shape[1]; n inputs, default all): dots_q8_body's 16-lane order for gs % 64 == 0, the
+    portable loop otherwise, with the STORE / ADD / PARTIAL / SWIGLU epilogues."""
+    xq = np.ascontiguousarray(np.ravel(xq), np.int8)
+    xs = np.ascontiguousarray(np.ravel(xs), np.float32)
+    wq = np.ascontiguousarray(wq, np.int8)
+    ws = np.ascontiguousarray(ws, np.float32)
+    d, ld = wq.shape
+    n = xq.shape[0] if n is None else n
+    y = np.zeros(d, np.float32) if out is None else np.array(out, np.float32, copy=True).reshape(d)
+    a3 = b3 = None
+    if kind == SWIGLU:
+        w3q = np.ascontiguousarray(w3q, np.int8)
+        w3s = np.ascontiguousarray(w3s, np.float32)
+        a3, b3 = _p(w3q, _i8p), _p(w3s, _f32p)
+    lib().orc_gemv_ref_order(_p(y, _f32p), _p(xq, _i8p), _p(xs, _f32p), _p(wq, _i8p), _p(ws, _f32p), a3, b3, ld, n, d,
+                             gs, kind)
+    return y
 
 
 def gemm(xq, xs, wq, ws, gs, kind=STORE, c=None, w3q=None, w3s=None):

@@ -134,6 +134,54 @@ static float reduce16(const float *a) {
   return t2[0] + t2[1];
 }
 
+static float avx512_q8_dot(const int8_t *x, const float *xs, const int8_t *w, const float *ws, int k, int gs) {
+  /* dots_q8_body (src/gemv.c:109-139), one row: 16 lanes; per group lane l's int32 sum of bytes 4l..4l+3 of every
+   * 64-byte piece (vpdpbusd of |x| and sign(x)*w: the exact signed dot, no int8 value being -128), then
+   * acc[l] = fma((float)dot * xs[g], ws[g], acc[l]); the row is the 16 lanes reduced as _mm512_reduce_add_ps. */
+  float acc[16];
+  memset(acc, 0, sizeof(acc));
+  for (int g = 0; g < k / gs; g++) {
+    for (int l = 0; l < 16; l++) {
+      int32_t d = 0;
+      for (int c = 0; c < gs; c += 64)
+        for (int b = 0; b < 4; b++) {
+          size_t off = (size_t)g * gs + c + 4 * l + b;
+          d += (int32_t)x[off] * (int32_t)w[off];
+        }
+      float t = (float)d * xs[g];
+      acc[l] = fmaf(t, ws[g], acc[l]);
+    }
+  }
+  return reduce16(acc);
+}
+
+static float portable_q8_dot(const int8_t *x, const float *xs, const int8_t *w, const float *ws, int k, int gs) {
+  /* q8_dots' portable loop (src/gemv.c:426-436): val += ((float)ival) * ws * xs per group, ascending */
+  float val = 0.0f;
+  for (int j = 0; j <= k - gs; j += gs)
+    val += ((float)group_dot(x + j, w + j, gs)) * ws[j / gs] * xs[j / gs];
+  return val;
+}
+
+void orc_gemv_ref_order(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                        const int8_t *w3q, const float *w3s, size_t ld, int n, int d, int gs, int kind) {
+  /* k_matmul_q8 on an AVX-512 host (q8_dots, src/gemv.c:401-416): the AVX-512 body for gs % 64 == 0, else the
+   * portable loop; epilogues of q8_range (src/gemv.c:441-480): STORE / PARTIAL write, ADD accumulates, SWIGLU writes
+   * silu_gate(dot(w1), dot(w3)). */
+  size_t scale_ld = ld / (size_t)gs;
+  float (*dot)(const int8_t *, const float *, const int8_t *, const float *, int, int) =
+      gs % 64 == 0 ? avx512_q8_dot : portable_q8_dot;
+  for (int r = 0; r < d; r++) {
+    float sum = dot(xq, xs, wq + (size_t)r * ld, ws + (size_t)r * scale_ld, n, gs);
+    if (kind == ORC_ADD)
+      out[r] += sum;
+    else if (kind == ORC_SWIGLU)
+      out[r] = orc_silu_gate(sum, dot(xq, xs, w3q + (size_t)r * ld, w3s + (size_t)r * scale_ld, n, gs));
+    else
+      out[r] = sum;
+  }
+}
+
 void orc_gemv_f32_avx512_order(float *out, const float *x, const int8_t *wq, const float *ws, size_t ld, int n, int d,
                                int gs) {
   /* W8A32 (fp32 activations), dots_q8f_body (src/gemv.c:141-180), the reference's path when gs % 16 == 0: per row 16

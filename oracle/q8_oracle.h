@@ -33,6 +33,13 @@ void orc_group_dots(int32_t *dots, const int8_t *xq, int m, int k, int gs, const
 void orc_gemv_scalar(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, size_t ld,
                      int n, int d, int gs);
 
+/* The reference's decode GEMV, k_matmul_q8 on an AVX-512 host (q8_dots, src/gemv.c:401-438): dots_q8_body's 16-lane
+ * order for gs % 64 == 0 (per lane an exact int32 sum of bytes 4l..4l+3 of each 64-byte piece, an FMA chain over the
+ * groups, then _mm512_reduce_add_ps), the portable loop otherwise; one activation row, d weight rows, with the
+ * STORE / ADD / PARTIAL / SWIGLU epilogues (w3q / w3s for SWIGLU). */
+void orc_gemv_ref_order(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                        const int8_t *w3q, const float *w3s, size_t ld, int n, int d, int gs, int kind);
+
 /* The AMX-INT8 order (amx_q8_chunk, src/gemm.c:554-610): acc = fmaf((float)dot * xs, ws, acc) per group, ascending,
  * from acc = 0. C[m][n] for one segment; `kind` applies the epilogue of q8_gemm_chunks (src/gemm.c:963-989):
  * STORE / PARTIAL write, ADD accumulates, SWIGLU writes silu_gate(acc(w), acc(w3)). */

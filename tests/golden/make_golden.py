@@ -12,6 +12,7 @@ Cases (all small; numpy PCG64 seeds below):
                   (k_gemm_q8_amx_dots_test)
   rms_*           k_rmsnorm on the AVX-512 ISA (src/kernels_simd.c:136-161) and the scalar one (src/kernels.c:8-21)
   gemvf_*         k_matmul_q8 on fp32 activations (W8A32), AVX-512 ISA for gs % 16 == 0, else scalar
+  gemv512_*       k_matmul_q8 on the AVX-512 ISA (dots_q8_body, src/gemv.c:109-139), the reference's decode GEMV
   vnni_*          pack_s8_vnni of a 37 x 200 slice (row stride 256)
 """
 import sys
@@ -84,6 +85,13 @@ def main():
     packed = np.zeros(L.s8_vnni_bytes(37, 200), np.int8)
     L.pack_s8_vnni(O._p(packed, O._i8p), O._p(w, O._i8p), 37, 200, 256)
     out.update(vnni_w=w, vnni_packed=packed)
+    # The reference's decode GEMV on an AVX-512 host (generated last, so the arrays above keep their values).
+    for d, n, gs in [(37, 1024, 64), (16, 4096, 64), (9, 512, 128), (5, 768, 256), (8, 14336, 64)]:
+        wq, ws = O.seeded_q8_matrix(d, n, gs, seed=7 * d + n)
+        xq, xs = O.quantize((rng.standard_normal(n) * rng.uniform(0.1, 5)).astype(np.float32), gs)
+        key = f"gemv512_{d}_{n}_{gs}"
+        out.update({key + "_wq": wq, key + "_ws": ws, key + "_xq": xq, key + "_xs": xs,
+                    key + "_y": O.ref_gemv(xq, xs, wq, ws, gs, O.KERNELS_AVX512)})
     path = Path(__file__).with_name("q8_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({path.stat().st_size} bytes, {len(out)} arrays)")

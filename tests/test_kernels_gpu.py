@@ -1,8 +1,10 @@
 """GPU parity tests of the sm_100a kernels through the C-ABI, against the oracle (and the reference's golden vectors).
 
-Bar (written per test): bit-exact for int8 values, scales, int32 group dots and the fp32 GEMV/GEMM outputs, which
-follow the reference's AMX-INT8 rescale order; within the reference's own budget (2e-5 * sum|w.x| + 1e-6,
-tests/kernels.c:138-170) against its scalar GEMV; SwiGLU within 2 ulp (expf) of the oracle.
+Bar (written per test): bit-exact for int8 values, scales, int32 group dots and the fp32 GEMV/GEMM outputs. The decode
+GEMV follows the reference's k_matmul_q8 on an AVX-512 host (dots_q8_body's 16-lane order for gs % 64 == 0, the
+portable loop otherwise); the tensor-core GEMM follows its AMX-INT8 rescale order. Both stay within the reference's own
+budget (2e-5 * sum|w.x| + 1e-6, tests/kernels.c:138-170) of the exact product; SwiGLU within 2 ulp (expf) of the
+oracle.
 """
 from pathlib import Path
 
@@ -113,17 +115,20 @@ def test_gemv_store_bitwise(kc, oracle, d, n, gs):
     wq, ws, xq, xs = make_case(oracle, d, n, gs, d + n)
     y = kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs)
     kc.status()
-    ref = oracle.gemm(xq, xs, wq, ws, gs)[0]
+    ref = oracle.gemv(xq, xs, wq, ws, gs)
     assert (bits(host(y)) == bits(ref)).all()
 
 
-def test_gemv_golden_amx_and_scalar(kc, oracle):
-    key = "amx_1_40_512"
-    if key + "_c" in GOLDEN:
-        y = kc.gemv(dev(GOLDEN[key + "_xq"][0]), dev(GOLDEN[key + "_xs"][0]), dev(GOLDEN[key + "_wq"]),
-                    dev(GOLDEN[key + "_ws"]), 64)
+def test_gemv_golden_reference(kc, oracle):
+    """The reference's own decode GEMV outputs (k_matmul_q8 on its AVX-512 ISA, golden gemv512_*), bitwise; and its
+    scalar-ISA outputs (golden gemv_*) within its Q8 budget."""
+    keys = sorted({k[:-2] for k in GOLDEN.files if k.startswith("gemv512_") and k.endswith("_y")})
+    assert keys
+    for k in keys:
+        gs = int(k.split("_")[-1])
+        y = kc.gemv(dev(GOLDEN[k + "_xq"]), dev(GOLDEN[k + "_xs"]), dev(GOLDEN[k + "_wq"]), dev(GOLDEN[k + "_ws"]), gs)
         kc.status()
-        assert (bits(host(y)) == bits(GOLDEN[key + "_c"][0])).all()
+        assert (bits(host(y)) == bits(GOLDEN[k + "_y"])).all(), k
     for d, n in [(37, 1024), (16, 4096)]:
         k = f"gemv_{d}_{n}"
         wq, ws, xq, xs = (GOLDEN[k + s] for s in ("_wq", "_ws", "_xq", "_xs"))
@@ -145,9 +150,9 @@ def test_gemv_add_and_partial(kc, oracle, d, n, gs):
     kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs, kind=kc.K_ADD, out=out)
     part = kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), gs, kind=kc.K_PARTIAL)
     kc.status()
-    ref = oracle.gemm(xq, xs, wq, ws, gs, kind=oracle.ADD, c=base[None])[0]
+    ref = oracle.gemv(xq, xs, wq, ws, gs, kind=oracle.ADD, out=base)
     assert (bits(host(out)) == bits(ref)).all()
-    assert (bits(host(part)) == bits(oracle.gemm(xq, xs, wq, ws, gs)[0])).all()
+    assert (bits(host(part)) == bits(oracle.gemv(xq, xs, wq, ws, gs))).all()
 
 
 def test_gemv_column_slice_with_row_stride(kc, oracle):
@@ -162,7 +167,7 @@ def test_gemv_column_slice_with_row_stride(kc, oracle):
     out = torch.zeros(d, device="cuda")
     kc.k_matmul_q8_ld(out, dev(xq2), dev(xs2), wt[:, col0:], st[:, col0 // gs:], ld, n, d, gs, kc.K_PARTIAL)
     kc.status()
-    assert (bits(host(out)) == bits(oracle.gemm(xq2, xs2, wslice, sslice, gs)[0])).all()
+    assert (bits(host(out)) == bits(oracle.gemv(xq2, xs2, wslice, sslice, gs))).all()
 
 
 @pytest.mark.parametrize("n,dq,dkv", [(2048, 2048, 512), (1024, 100, 37), (4096, 4096, 1024)])
@@ -174,7 +179,7 @@ def test_gemv_qkv_three_segments(kc, oracle, n, dq, dkv):
     kc.k_matmul_q8_qkv(*outs, dev(xq), dev(xs), *[(dev(a), dev(b)) for a, b in mats], n, dq, dkv, gs)
     kc.status()
     for o, (wq, ws) in zip(outs, mats):
-        assert (bits(host(o)) == bits(oracle.gemm(xq, xs, wq, ws, gs)[0])).all()
+        assert (bits(host(o)) == bits(oracle.gemv(xq, xs, wq, ws, gs))).all()
 
 
 @pytest.mark.parametrize("d,n", [(40, 1024), (8192, 2048), (14336, 4096)])
@@ -184,7 +189,7 @@ def test_gemv_swiglu(kc, oracle, d, n):
     w3q, w3s = oracle.seeded_q8_matrix(d, n, gs, 32)
     out = kc.gemv(dev(xq), dev(xs), dev(w1q), dev(w1s), gs, kind=kc.K_SWIGLU, w3=(dev(w3q), dev(w3s)))
     kc.status()
-    ref = oracle.gemm(xq, xs, w1q, w1s, gs, kind=oracle.SWIGLU, w3q=w3q, w3s=w3s)[0]
+    ref = oracle.gemv(xq, xs, w1q, w1s, gs, kind=oracle.SWIGLU, w3q=w3q, w3s=w3s)
     assert ulp_diff(host(out), ref).max() <= 2
 
 
@@ -275,7 +280,7 @@ def test_gemv_config0_full_size_properties(kc, oracle):
     y = host(kc.gemv(dev(xq), dev(xs), dev(wq), dev(ws), 64))
     y2 = host(kc.gemv(dev(xq), dev(xs * 2), dev(wq), dev(ws), 64))
     kc.status()
-    assert (bits(y) == bits(oracle.gemm(xq, xs, wq, ws, 64)[0])).all()
+    assert (bits(y) == bits(oracle.gemv(xq, xs, wq, ws, 64))).all()
     assert (bits(y2) == bits(y * 2)).all()
 
 
@@ -292,8 +297,12 @@ def test_gemm_golden_amx(kc, m, d, k):
     assert (bits(host(c)) == bits(GOLDEN[key + "_c"])).all()
 
 
-def test_gemm_segments_and_kinds(kc, oracle):
-    m, k, gs = 5, 1024, 64
+@pytest.mark.parametrize("m", [5, 1])
+def test_gemm_segments_and_kinds(kc, oracle, m):
+    """An ADD segment beside a SwiGLU pair: the tensor-core kernel takes a SwiGLU pair only as its sole segment, so
+    k_gemm_q8_pick reports the row rung and k_gemm_q8 runs it, every row in the reference's GEMV order. The ADD segment
+    alone goes to the tensor cores at any row count, in the AMX order."""
+    k, gs = 1024, 64
     rng = np.random.default_rng(3)
     xq, xs = oracle.quantize(rng.standard_normal((m, k)).astype(np.float32), gs)
     wa = oracle.seeded_q8_matrix(64, k, gs, 40)
@@ -303,11 +312,19 @@ def test_gemm_segments_and_kinds(kc, oracle):
     ca, cb = dev(base), torch.zeros((m, 48), device="cuda")
     segs = [kc.segment(ca, (dev(wa[0]), dev(wa[1])), kc.GEMM_ADD),
             kc.segment(cb, (dev(wb[0]), dev(wb[1])), kc.GEMM_SWIGLU, w3=(dev(w3[0]), dev(w3[1])))]
+    assert kc.k_gemm_q8_pick(gs, segs) == kc.Q8_GEMM_GPU_DP4A
     kc.k_gemm_q8(dev(xq), dev(xs), m, k, gs, segs)
     kc.status()
+    for r in range(m):
+        assert (bits(host(ca)[r]) == bits(oracle.gemv(xq[r], xs[r], *wa, gs, kind=oracle.ADD, out=base[r]))).all()
+        ref = oracle.gemv(xq[r], xs[r], *wb, gs, kind=oracle.SWIGLU, w3q=w3[0], w3s=w3[1])
+        assert ulp_diff(host(cb)[r], ref).max() <= 2
+    ca = dev(base)
+    alone = [kc.segment(ca, (dev(wa[0]), dev(wa[1])), kc.GEMM_ADD)]
+    assert kc.k_gemm_q8_pick(gs, alone) == kc.Q8_GEMM_GPU_TCGEN05
+    kc.k_gemm_q8(dev(xq), dev(xs), m, k, gs, alone)
+    kc.status()
     assert (bits(host(ca)) == bits(oracle.gemm(xq, xs, *wa, gs, kind=oracle.ADD, c=base))).all()
-    ref = oracle.gemm(xq, xs, *wb, gs, kind=oracle.SWIGLU, w3q=w3[0], w3s=w3[1])
-    assert ulp_diff(host(cb), ref).max() <= 2
 
 
 # ---- RMSNorm, fused quantize, RoPE ----------------------------------------------------------------------------------
@@ -417,8 +434,9 @@ def test_gemm_tc_add_swiglu_and_segments(kc, oracle):
 
 
 def test_gemm_tc_config1_full_size(kc, oracle):
-    # Config 1 up-projection at T=128 (14336 x 4096): bitwise the oracle on a sample of 96 weight rows, and bitwise the
-    # decode GEMV (a different kernel, same arithmetic) for 3 token rows -- size-independent checks.
+    # Config 1 up-projection at T=128 (14336 x 4096): bitwise the oracle on a sample of 96 weight rows; the decode GEMV
+    # of 3 token rows (the reference's AVX-512 order) against the oracle on the same rows, and within the reference's
+    # Q8 budget of the GEMM's AMX-order rows.
     T, N, K, gs = 128, 14336, 4096, 64
     g = torch.Generator(device="cuda").manual_seed(0)
     wq, ws = kc.quantize(torch.randn((N, K), generator=g, device="cuda") * 0.02, gs)
@@ -430,9 +448,12 @@ def test_gemm_tc_config1_full_size(kc, oracle):
     ref = oracle.gemm(host(xq), host(xs), hw, host(ws)[rows], gs)
     assert (bits(host(c)[:, rows]) == bits(ref)).all()
     for t in (0, 77, 127):
-        y = kc.gemv(xq[t], xs[t], wq, ws, gs)
+        y = host(kc.gemv(xq[t], xs[t], wq, ws, gs))
         kc.status()
-        assert (bits(host(y)) == bits(host(c)[t])).all()
+        assert (bits(y[rows]) == bits(oracle.gemv(host(xq)[t], host(xs)[t], hw, host(ws)[rows], gs))).all()
+        mag = oracle.group_dots(np.abs(host(xq)[t]).astype(np.int8), np.abs(hw).astype(np.int8), gs)[:, 0, :]
+        budget = 2e-5 * (mag * host(ws)[rows].T * host(xs)[t][:, None]).sum(0) + 1e-6
+        assert np.all(np.abs(y[rows] - host(c)[t, rows]) <= 2 * budget)
 
 
 def test_k_gemm_q8_picks_tensor_cores_for_batches(kc, oracle):
@@ -468,7 +489,7 @@ def test_fused_norm_qkv_bitwise(kc, oracle, n):
     rq, rs = oracle.quantize(oracle.rmsnorm(x, w, 1e-5), gs)
     for f, a, (wq, ws) in zip(fused, apart, mats):
         assert (bits(host(f)) == bits(host(a))).all()
-        assert (bits(host(f)) == bits(oracle.gemm(rq, rs, wq, ws, gs)[0])).all()
+        assert (bits(host(f)) == bits(oracle.gemv(rq, rs, wq, ws, gs))).all()
 
 
 def test_fused_norm_swiglu_and_quantize_add_bitwise(kc, oracle):
@@ -496,7 +517,7 @@ def test_fused_norm_swiglu_and_quantize_add_bitwise(kc, oracle):
     kc.status()
     assert (bits(host(res_f)) == bits(host(res_a))).all()
     rq, rs = oracle.quantize(host(hb), gs)
-    assert (bits(host(res_f)) == bits(oracle.gemm(rq, rs, *w2, gs, kind=oracle.ADD, c=base[None])[0])).all()
+    assert (bits(host(res_f)) == bits(oracle.gemv(rq, rs, *w2, gs, kind=oracle.ADD, out=base))).all()
 
 
 def test_fused_partial_on_a_column_slice(kc, oracle):
@@ -513,8 +534,8 @@ def test_fused_partial_on_a_column_slice(kc, oracle):
     kc.k_matmul_q8_fused(dev(x), None, 0.0, full, n, gs, [seg])
     kc.status()
     rq, rs = oracle.quantize(x, gs)
-    ref = oracle.gemm(rq, rs, np.ascontiguousarray(wq[:, c0:c0 + n]), np.ascontiguousarray(ws[:, c0 // gs:(c0 + n) // gs]),
-                      gs)[0]
+    ref = oracle.gemv(rq, rs, np.ascontiguousarray(wq[:, c0:c0 + n]), np.ascontiguousarray(ws[:, c0 // gs:(c0 + n) // gs]),
+                      gs)
     assert (bits(host(out)) == bits(ref)).all()
 
 

@@ -43,6 +43,21 @@ def test_gemv_scalar_golden(oracle, d, n):
     assert (bits(y) == bits(GOLDEN[k + "_y"])).all()
 
 
+GEMV512_CASES = [(37, 1024, 64), (16, 4096, 64), (9, 512, 128), (5, 768, 256), (8, 14336, 64)]
+
+
+@pytest.mark.parametrize("d,n,gs", GEMV512_CASES)
+def test_gemv_reference_order_golden(oracle, d, n, gs):
+    """The decode GEMV the GPU reproduces: the reference's k_matmul_q8 on its AVX-512 ISA (dots_q8_body's 16 lanes and
+    _mm512_reduce_add_ps), bitwise; ADD adds that product to the output in one rounding."""
+    k = f"gemv512_{d}_{n}_{gs}"
+    xq, xs, wq, ws = (GOLDEN[k + t] for t in ("_xq", "_xs", "_wq", "_ws"))
+    y = oracle.gemv(xq, xs, wq, ws, gs)
+    assert (bits(y) == bits(GOLDEN[k + "_y"])).all()
+    base = np.linspace(-1, 1, d).astype(np.float32)
+    assert (bits(oracle.gemv(xq, xs, wq, ws, gs, kind=oracle.ADD, out=base)) == bits(base + GOLDEN[k + "_y"])).all()
+
+
 AMX_CASES = [(1, 40, 512), (7, 48, 1024), (33, 32, 256)]
 
 
@@ -77,8 +92,8 @@ def test_rmsnorm_golden(oracle, n):
 
 
 def test_gemv_orders_agree_within_reference_budget(oracle):
-    # tests/kernels.c:138-170: |y - exact| <= 2e-5 * sum|w.x| + 1e-6 for every Q8 kernel; the AMX order (what the GPU
-    # computes) and the scalar order are two such kernels.
+    # tests/kernels.c:138-170: |y - exact| <= 2e-5 * sum|w.x| + 1e-6 for every Q8 kernel; the scalar order, the AMX
+    # order (the GPU's GEMM) and the AVX-512 order (the GPU's GEMV) are three such kernels.
     rng = np.random.default_rng(5)
     wq, ws = oracle.seeded_q8_matrix(64, 4096, 64, seed=3)
     xq, xs = oracle.quantize(rng.standard_normal(4096).astype(np.float32), 64)
@@ -90,6 +105,7 @@ def test_gemv_orders_agree_within_reference_budget(oracle):
     mag = (sa * ws.T.astype(np.float64) * xs[:, None]).sum(0)
     assert np.all(np.abs(a - exact) <= 2e-5 * mag + 1e-6)
     assert np.all(np.abs(b - exact) <= 2e-5 * mag + 1e-6)
+    assert np.all(np.abs(oracle.gemv(xq, xs, wq, ws, 64) - exact) <= 2e-5 * mag + 1e-6)
 
 
 needs_ref = pytest.mark.skipif(not Path(__file__).resolve().parents[1].joinpath("oracle/_ref/libllama_ref.so").exists(),
@@ -108,6 +124,12 @@ def test_oracle_matches_compiled_reference(oracle, seed):
     wq, ws = oracle.seeded_q8_matrix(24, 2048, 64, seed=seed)
     xq, xs = oracle.quantize(rng.standard_normal(2048).astype(np.float32), 64)
     assert (bits(oracle.gemv_scalar(xq, xs, wq, ws, 64)) == bits(oracle.ref_gemv(xq, xs, wq, ws, 64))).all()
+    for gs in (64, 128, 32):  # the AVX-512 body for gs % 64 == 0, the portable loop below
+        wq3, ws3 = oracle.seeded_q8_matrix(19, 1024, gs, seed=seed + gs)
+        xq3, xs3 = oracle.quantize(rng.standard_normal(1024).astype(np.float32), gs)
+        ref = oracle.ref_gemv(xq3, xs3, wq3, ws3, gs, oracle.KERNELS_AVX512)
+        oracle.ref_select(oracle.KERNELS_SCALAR)
+        assert (bits(oracle.gemv(xq3, xs3, wq3, ws3, gs)) == bits(ref)).all()
     if oracle.ref_amx_unavailable() is None:
         xq2, xs2 = oracle.quantize(rng.standard_normal((5, 2048)).astype(np.float32), 64)
         assert (bits(oracle.gemm(xq2, xs2, wq, ws, 64)) == bits(oracle.ref_gemm_amx(xq2, xs2, wq, ws, 64))).all()

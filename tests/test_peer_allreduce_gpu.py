@@ -105,13 +105,13 @@ def gemv_inputs(oracle, call, rank, d, n, gs=64):
 
 
 def gemv_expected(oracle, world, call, d, n):
-    """x0 + (((p_0 + p_1) + ...) in float32, p_r = rank r's product in the AMX order; call 2 adds the standalone
+    """x0 + (((p_0 + p_1) + ...) in float32, p_r = rank r's product in the reference's GEMV order; call 2 adds the standalone
     all-reduce of the result (every rank contributes its x, which all ranks hold equal)."""
     x0 = gemv_inputs(oracle, call, 0, d, n)[0]
     s = None
     for r in range(world):
         _, xq, xs, wq, ws = gemv_inputs(oracle, call, r, d, n)
-        part = oracle.gemm(xq, xs, wq, ws, 64)[0]
+        part = oracle.gemv(xq, xs, wq, ws, 64)
         s = part if s is None else (s + part).astype(np.float32)
     want = (x0 + s).astype(np.float32)
     if call == 2:
@@ -160,7 +160,7 @@ def _gemv_rank(rank, world, nccl_id, out):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_reducing_gemv_bitwise(world, oracle):
     """Rank r holds column slice r of the weights and of the activations; after each call every rank's x equals
-    x0 + (((p_0 + p_1) + p_2) + ...) with p_r rank r's product in the AMX order (the oracle GEMM), bit for bit."""
+    x0 + (((p_0 + p_1) + p_2) + ...) with p_r rank r's product in the reference's GEMV order (the oracle), bit for bit."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from conftest import load_engine
