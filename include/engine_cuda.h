@@ -31,6 +31,15 @@ typedef struct {
 
 typedef enum { LOGITS_NONE, LOGITS_LAST, LOGITS_ALL } LogitsWanted;
 
+/* include/runtime.h:76-85 */
+typedef struct {
+  size_t reserved_bytes, active_bytes, resident_bytes;
+  int node;
+  int verified;
+  int full;
+  size_t pages_queried, pages_wrong_node, pages_missing;
+} KvStats;
+
 typedef struct {
   Config config;
   void *implementation;
@@ -51,9 +60,17 @@ void engine_load_context(Model *model, const char *path, int context);
 float *engine_forward(Model *model, int token, int position);
 float *engine_forward_batch(Model *model, const int *tokens, int count, int pos0, LogitsWanted want);
 int engine_max_batch(const Model *model);
+/* KV cache accounting (include/runtime.h:111-113): reserved and active bytes of the K and V caches of all ranks for
+ * positions [0, position). The caches are device memory allocated whole at load: resident equals reserved, node is -1
+ * and nothing is verified, as there is no host page placement to query. */
+void engine_kv_stats(Model *model, int position, int verify, KvStats *out);
 void engine_free(Model *model);
 const char *engine_precision(void);
 int engine_group_size(void);
+/* One position's RoPE table (include/kernels.h:67, src/kernels_simd.c:194-201): 2 * head_dim floats, cosines
+ * duplicated per pair, then (-sin, +sin) per pair, with rope_frequency's Llama 3.1 scaling (src/kernels.c:49-60). A
+ * host function: it lives in the engine library because it takes the engine's Config. */
+void k_rope_table(const Config *p, int position, float *table);
 
 /* ---- GPU additions (no counterpart in the reference) ------------------------------------------------------------- */
 /* Tensor parallelism, set before loading: this process is `rank` of `world` (1, 2, 4 or 8) on CUDA device `device`,

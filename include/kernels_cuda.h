@@ -221,10 +221,13 @@ void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t l
  * (k_attention_free releases only what it allocated). One row runs the split-K decode kernel, a batch the flash-style
  * prefill kernel; both agree with the reference's attention within fp32 rounding, and with each other (a batched row
  * against the same position alone) to the same degree, not bitwise. `att` is the reference's host scratch and is
- * ignored. */
+ * ignored. AttentionWork has the reference's layout (include/kernels.h:127-132), so a caller compiled against the
+ * reference's header passes a struct this library reads field for field: partial (device memory), max_chunks (the
+ * 64-position splits of the longest context it serves), n_heads and head_dim (checked against each call), workers
+ * (always 1: one GPU does the work of the reference's team), external and capacity (floats in partial). */
 typedef struct {
   float *partial;
-  int max_chunks, n_heads, n_kv_heads, head_dim, seq_len, rows;
+  int max_chunks, n_heads, head_dim, workers;
   int external;
   size_t capacity;
 } AttentionWork;

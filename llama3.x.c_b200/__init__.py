@@ -53,10 +53,10 @@ K_TAIL_NONE, K_TAIL_QUANTIZE, K_TAIL_NORM_QUANTIZE, K_TAIL_ROPE_KV_STORE, K_TAIL
 
 
 class AttentionWork(ctypes.Structure):
-    """include/kernels_cuda.h: split-K partials in device memory."""
-    _fields_ = [("partial", ctypes.c_void_p), ("max_chunks", ctypes.c_int),
-                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
-                ("seq_len", ctypes.c_int), ("rows", ctypes.c_int), ("external", ctypes.c_int),
+    """include/kernels_cuda.h: split-K partials in device memory, in the reference's layout
+    (include/kernels.h:127-132)."""
+    _fields_ = [("partial", ctypes.c_void_p), ("max_chunks", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("workers", ctypes.c_int), ("external", ctypes.c_int),
                 ("capacity", ctypes.c_size_t)]
 
 

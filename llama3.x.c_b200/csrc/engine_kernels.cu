@@ -768,7 +768,7 @@ bool attention_shape_ok(const char *name, const AttentionWork *w, int n_heads, i
   if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || hd <= 0 || seq <= 0 ||
       (!attention_fast_shape(n_heads, n_kv, hd) && (size_t)seq * sizeof(float) > kGenericMaxSmem))
     return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d / context %d", name, n_heads, n_kv, hd, seq);
-  if (n_heads != w->n_heads || n_kv != w->n_kv_heads || hd != w->head_dim || seq != w->seq_len)
+  if (n_heads != w->n_heads || hd != w->head_dim || max_splits_for(seq) > w->max_chunks)
     return kc_fail("%s: shape differs from the one the work was initialized for", name);
   return true;
 }
@@ -960,10 +960,8 @@ void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int
   work->partial = reinterpret_cast<float *>(base);
   work->max_chunks = max_splits_for(seq_len);
   work->n_heads = n_heads;
-  work->n_kv_heads = n_kv_heads;
   work->head_dim = head_dim;
-  work->seq_len = seq_len;
-  work->rows = rows;
+  work->workers = 1;
   work->external = external;
   work->capacity = partial / sizeof(float);
 }

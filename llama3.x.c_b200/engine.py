@@ -40,6 +40,14 @@ class EngineStats(ctypes.Structure):
                 ("decode_tokens", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong)]
 
 
+class KvStats(ctypes.Structure):
+    """include/engine_cuda.h (the reference's KvStats, include/runtime.h:76-85)"""
+    _fields_ = [("reserved_bytes", ctypes.c_size_t), ("active_bytes", ctypes.c_size_t),
+                ("resident_bytes", ctypes.c_size_t), ("node", ctypes.c_int), ("verified", ctypes.c_int),
+                ("full", ctypes.c_int), ("pages_queried", ctypes.c_size_t), ("pages_wrong_node", ctypes.c_size_t),
+                ("pages_missing", ctypes.c_size_t)]
+
+
 LOGITS_NONE, LOGITS_LAST, LOGITS_ALL = 0, 1, 2
 COMM_ID_BYTES = 128
 
@@ -53,6 +61,8 @@ ENGINE_SIGNATURES = {
     "engine_forward": (_c.POINTER(_c.c_float), [_MP, _c.c_int, _c.c_int]),
     "engine_forward_batch": (_c.POINTER(_c.c_float), [_MP, _IP, _c.c_int, _c.c_int, _c.c_int]),
     "engine_max_batch": (_c.c_int, [_MP]),
+    "engine_kv_stats": (None, [_MP, _c.c_int, _c.c_int, _c.POINTER(KvStats)]),
+    "k_rope_table": (None, [_c.POINTER(Config), _c.c_int, _c.POINTER(_c.c_float)]),
     "engine_free": (None, [_MP]),
     "engine_precision": (_c.c_char_p, []),
     "engine_group_size": (_c.c_int, []),
@@ -250,6 +260,13 @@ class Engine:
     def stats_reset(self):
         self.lib.engine_stats_reset(self._m)
 
+    def kv_stats(self, position, verify=0):
+        """engine_kv_stats: the K/V cache accounting of the reference's report (include/runtime.h:111-113)."""
+        st = KvStats()
+        self.lib.engine_kv_stats(self._m, position, verify, ctypes.byref(st))
+        _check()
+        return {f: getattr(st, f) for f, _ in KvStats._fields_}
+
     def save(self, path):
         if self.lib.engine_save(self._m, os.fsencode(str(path))) != 0:
             _check()
@@ -264,6 +281,14 @@ class Engine:
 
     def __exit__(self, *exc):
         self.close()
+
+
+def rope_table(config, position):
+    """k_rope_table (include/kernels.h:67) for `config` (a Config) at `position`: 2 * head_dim floats."""
+    import numpy as np
+    out = np.zeros(2 * config.head_dim, np.float32)
+    load_library().k_rope_table(ctypes.byref(config), position, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
 
 
 def share_comm_id(rank, world):

@@ -141,21 +141,26 @@ static float rope_freq(const Config *p, int j) {
   return f;
 }
 
-/* Rows [0, positions) of [2 * head_dim]: cosines duplicated per pair, then (-sin, +sin) per pair. */
+/* k_rope_table (include/kernels.h:67, src/kernels_simd.c:194-201): one position's row of [2 * head_dim] floats,
+ * cosines duplicated per pair, then (-sin, +sin) per pair. */
+void k_rope_table(const Config *p, int position, float *table) {
+  int hd = p->head_dim;
+  for (int j = 0; j < hd; j += 2) {
+    float angle = position * rope_freq(p, j), c = cosf(angle), s = sinf(angle);
+    table[j] = table[j + 1] = c;
+    table[hd + j] = -s;
+    table[hd + j + 1] = s;
+  }
+}
+
+/* Rows [0, positions) of k_rope_table, the device copy's source. */
 static float *rope_table_host(const Config *p, int positions) {
   int hd = p->head_dim;
   float *t = malloc((size_t)positions * 2 * hd * sizeof(float));
   if (!t)
     return NULL;
-  for (int pos = 0; pos < positions; pos++) {
-    float *row = t + (size_t)pos * 2 * hd;
-    for (int j = 0; j < hd; j += 2) {
-      float angle = pos * rope_freq(p, j), c = cosf(angle), s = sinf(angle);
-      row[j] = row[j + 1] = c;
-      row[hd + j] = -s;
-      row[hd + j + 1] = s;
-    }
-  }
+  for (int pos = 0; pos < positions; pos++)
+    k_rope_table(p, pos, t + (size_t)pos * 2 * hd);
   return t;
 }
 
@@ -1211,6 +1216,30 @@ void engine_stats(Model *model, EngineStats *out) {
     return;
   *out = e->stats;
   out->kernel_launches = (long long)(kc_launch_count() - e->launches_base) - e->captured + e->replayed;
+}
+
+/* engine_kv_stats (include/runtime.h:111-113, tp_kv_stats src/tp.c:1147-1160): the K and V caches of every rank, as
+ * the reference counts both sockets' caches. They are device memory allocated whole at load, so reserved and resident
+ * are the same bytes; there is no host page placement to query (node -1, not verified), whatever `verify` asks. */
+void engine_kv_stats(Model *model, int position, int verify, KvStats *out) {
+  (void)verify;
+  Engine *e = model ? model->implementation : NULL;
+  if (!out)
+    return;
+  memset(out, 0, sizeof(*out));
+  out->node = -1;
+  if (!e) {
+    efail("engine_kv_stats: no model loaded");
+    return;
+  }
+  if (position < 0 || position > e->context) {
+    efail("engine_kv_stats: position %d outside the context of %d", position, e->context);
+    return;
+  }
+  size_t per_position = 2 * (size_t)e->c.n_layers * (size_t)e->kvl * sizeof(float) * (size_t)e->S;
+  out->reserved_bytes = per_position * (size_t)e->context;
+  out->active_bytes = per_position * (size_t)position;
+  out->resident_bytes = out->reserved_bytes;
 }
 
 void engine_stats_reset(Model *model) {

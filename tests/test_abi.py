@@ -75,6 +75,39 @@ def test_c_header_layout_matches(tmp_path):
         ["216", "88", "216", "272"]
 
 
+def test_kv_stats_layout():
+    """KvStats keeps the reference's x86-64 layout (include/runtime.h:76-85): three size_t, three ints, three size_t."""
+    from conftest import load_engine
+    eng = load_engine()
+    assert eng.KvStats.node.offset == 24 and eng.KvStats.pages_queried.offset == 40 and ctypes.sizeof(eng.KvStats) == 64
+
+
+def test_attention_work_layout():
+    """AttentionWork keeps the reference's x86-64 layout (include/kernels.h:127-132)."""
+    mod = load_package()
+    W = mod.AttentionWork
+    assert [f for f, _ in W._fields_] == ["partial", "max_chunks", "n_heads", "head_dim", "workers", "external",
+                                          "capacity"]
+    assert W.workers.offset == 20 and W.capacity.offset == 32 and ctypes.sizeof(W) == 40
+
+
+def test_rope_table_matches_the_oracle():
+    """k_rope_table (a host function of the engine library, include/kernels.h:67) equals the oracle's restatement
+    of the reference's table (src/kernels_simd.c:194-201, rope_frequency src/kernels.c:49-60) bitwise, with and
+    without the Llama 3.1 scaling."""
+    import numpy as np
+    from conftest import load_engine
+    from oracle import oracle as O
+    eng = load_engine()
+    for rope_type, factor in ((0, 1.0), (1, 8.0)):
+        c = eng.Config(head_dim=128, rope_theta=500000.0, rope_type=rope_type, rope_factor=factor, rope_low=1.0,
+                       rope_high=4.0, rope_original=8192)
+        for pos in (0, 1, 77, 8191):
+            got = eng.rope_table(c, pos)
+            want = O.rope_table(pos, 128, 500000.0, rope_type, factor, 1.0, 4.0, 8192)
+            assert (got.view(np.int32) == want.view(np.int32)).all(), (rope_type, pos)
+
+
 def test_name_is_null_before_init():
     mod = load_package()
     assert mod.load().kernels_name() is None

@@ -209,3 +209,38 @@ def test_reference_probe_driver_runs_the_gpu_engine(files, name):
     logits = np.frombuffer(raw, np.float32).reshape(stable, -1)
     for i in range(stable):
         assert close(logits[i], GOLDEN[f"{name}_logits"][i]), f"position {i}"
+
+
+def test_kv_stats_counts_the_caches(eng, files):
+    """engine_kv_stats (include/runtime.h:111-113): reserved = both caches over the context, active = the positions
+    asked for, resident = reserved (device memory allocated at load), no node placement to verify."""
+    c = models.MODELS["small"]
+    kv = c["dim"] // c["n_heads"] * c["n_kv_heads"]
+    with eng.Engine.load(str(files["small"]), context=128) as m:
+        st = m.kv_stats(100, verify=1)
+    per = 2 * c["n_layers"] * kv * 4
+    assert st["reserved_bytes"] == per * 128 and st["active_bytes"] == per * 100
+    assert st["resident_bytes"] == st["reserved_bytes"] and st["node"] == -1 and st["verified"] == 0
+
+
+def test_runq_cli_links_and_generates(tmp_path):
+    """The reference's own CLI (src/app.c, the runq executable) linked unchanged against libllama3x_engine.so
+    (oracle/_ref/runq-gpu, oracle/Makefile) runs the reference test suite's command on its fixture (tests/
+    test_runtime.py:38-40: greedy, seed 123, prompt "A") and generates the token ids the reference's own runq generated
+    (tests/golden/runq_golden.npz, recorded through LLAMA_TOKENS_OUT)."""
+    import json
+    import os
+    import subprocess
+    exe = HERE.parent / "oracle" / "_ref" / "runq-gpu"
+    if not exe.exists():
+        pytest.skip("oracle/_ref/runq-gpu was not built (make -C oracle where the reference sources exist)")
+    g = np.load(HERE / "golden" / "runq_golden.npz")
+    model, tok, out = tmp_path / "int8.bin", tmp_path / "tokenizer.bin", tmp_path / "tokens.json"
+    model.write_bytes(np.load(HERE / "golden" / "ref_fixture.npz")["int8_bin"].tobytes())
+    tok.write_bytes(g["tokenizer_bin"].tobytes())
+    r = subprocess.run([str(exe), str(model), "-z", str(tok), *[str(f) for f in g["flags"]]], capture_output=True,
+                       text=True, timeout=120, env={**os.environ, "LLAMA_TOKENS_OUT": str(out)})
+    assert r.returncode == 0, r.stderr[-2000:]
+    ids = json.loads(out.read_text())
+    assert ids["prompt"] == g["prompt"].tolist()
+    assert ids["generated"] == g["generated"].tolist()
