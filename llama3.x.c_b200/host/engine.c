@@ -1010,17 +1010,17 @@ float *engine_forward(Model *model, int token, int position) {
 }
 
 /* Classifier over `rows` rows of the final residual starting at row r0, into dst (device, [rows][vl]). */
+/* The batch's classifier, per row as the reference's forward_batch does it (src/tp.c:608-621): the final RMSNorm and
+ * quantize of each row, then the decode GEMV (k_matmul_q8), so a row's logits are the ones a decode step at that
+ * position would give from the same hidden state. */
 static void classify_rows(Engine *e, int r0, int rows, float *dst) {
   const Config *p = &e->c;
   int dim = p->dim, gs = e->gs;
   k_rmsnorm_q8_rows(e->xq, e->xs, NULL, e->x + (size_t)r0 * dim, dim, e->rms_final, rows, dim, p->norm_eps, gs);
-  if (rows == 1) {
-    K8Input in = {e->xq, e->xs, NULL};
-    k_matmul_q8(dst, &in, k8(e->cls), dim, e->vl, gs);
-    return;
+  for (int r = 0; r < rows; r++) {
+    K8Input in = {e->xq + (size_t)r * dim, e->xs + (size_t)r * (dim / gs), NULL};
+    k_matmul_q8(dst + (size_t)r * e->vl, &in, k8(e->cls), dim, e->vl, gs);
   }
-  GemmQ8Segment seg = {dst, e->vl, k8(e->cls), {NULL, NULL}, NULL, NULL, e->vl, GEMM_STORE};
-  k_gemm_q8(e->xq, e->xs, rows, dim, gs, &seg, 1);
 }
 
 static void prefill_layers(Engine *e, int m, int pos0) {
@@ -1118,7 +1118,7 @@ float *engine_forward_batch(Model *model, const int *tokens, int count, int pos0
       if (!e->batch_logits_host || !e->batch_logits_dev)
         return NULL;
     }
-    /* Per row as the reference (src/tp.c:608-621); rows are classified as one GEMM, bitwise the per-row GEMV. */
+    /* Per row as the reference (src/tp.c:608-621). */
     if (e->w8a32)  /* the one row's local logits, from the decode step */
       kd_copy(e->batch_logits_dev, e->logits_dev, (size_t)e->vl * sizeof(float));
     else

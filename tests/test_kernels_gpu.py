@@ -629,8 +629,16 @@ def test_output_quantizer_after_fused_swiglu_bitwise(kc, oracle, hidden):
 
 
 def test_output_quantizer_store_segment_bitwise(kc, oracle):
-    """K_TAIL_QUANTIZE_OUTPUT on a STORE GEMV with int8 input, group size 32, rows that do not split evenly."""
-    gs, n, d = 32, 2048, 4096 + 5 * 32
+    """K_TAIL_QUANTIZE_OUTPUT on a STORE GEMV with int8 input, group size 128, rows that do not split evenly; a group
+    size the lane-order kernel does not take (32: the reference's portable order) is refused, not run elsewhere."""
+    gs, n, d = 128, 2048, 4096 + 5 * 128
+    with pytest.raises(kc.KernelError, match="shape not supported"):
+        z = torch.zeros(64, device="cuda")
+        kc.k_matmul_q8_tail(torch.zeros(256, dtype=torch.int8, device="cuda"), torch.zeros(8, device="cuda"), 256, 256,
+                            32, [kc.segment(z, (torch.zeros((64, 256), dtype=torch.int8, device="cuda"),
+                                                torch.zeros((64, 8), device="cuda")))],
+                            _tail(kc, kc.K_TAIL_QUANTIZE_OUTPUT, q=torch.empty(64, dtype=torch.int8, device="cuda"),
+                                  s=torch.empty(2, device="cuda")))
     rng = np.random.default_rng(23)
     wq, ws = oracle.seeded_q8_matrix(d, n, gs, 23)
     xq, xs = kc.quantize(dev(rng.standard_normal(n).astype(np.float32)), gs)
