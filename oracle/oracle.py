@@ -56,6 +56,14 @@ def lib():
         L.orc_gemm_amx_order.argtypes = [_f32p, ctypes.c_int, _i8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          _i8p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int]
         L.orc_silu_gate.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.orc_exp512.argtypes = [ctypes.c_float]
+        L.orc_exp512.restype = ctypes.c_float
+        L.orc_attention_chunks.argtypes = [ctypes.c_int] * 4
+        L.orc_attention_chunks.restype = ctypes.c_int
+        L.orc_attention_decode.argtypes = [_f32p] * 4 + [ctypes.c_int] * 7
+        L.orc_attention_decode.restype = ctypes.c_int
+        L.orc_attention_tiled.argtypes = [_f32p] * 4 + [ctypes.c_int] * 8
+        L.orc_attention_tiled.restype = ctypes.c_int
         L.orc_gemv_ref_order.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, _i8p, _f32p, ctypes.c_size_t, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_silu_gate.restype = ctypes.c_float
@@ -365,6 +373,60 @@ def ref_attention(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, seq_
     L.k_attention_layout(_p(out, _f32p), _p(q, _f32p), _p(kc, _f32p), _p(vc, _f32p), _p(att, _f32p),
                          ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len, position, head_dim,
                          seq_len * head_dim)
+    L.k_attention_free(ctypes.byref(work))
+    ref_select(KERNELS_SCALAR)
+    return out
+
+
+def attention_limit(n_kv_heads, seq_len, workers=1):
+    """attention_max_chunks (src/attention.c:527-530): the work's chunk limit for a team of `workers`."""
+    return max((workers + n_kv_heads - 1) // n_kv_heads, (seq_len + 255) // 256)
+
+
+def attention_decode(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, seq_len, position, workers=1):
+    """The reference's split decode attention (orc_attention_decode) on the head-major cache [n_kv][seq][hd]."""
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(key_cache, np.float32)
+    vc = np.ascontiguousarray(value_cache, np.float32)
+    out = np.zeros(n_heads * head_dim, np.float32)
+    rc = lib().orc_attention_decode(_p(out, _f32p), _p(q, _f32p), _p(kc, _f32p), _p(vc, _f32p), n_heads, n_kv_heads,
+                                    head_dim, seq_len, position, workers,
+                                    attention_limit(n_kv_heads, seq_len, workers))
+    assert rc == 0
+    return out
+
+
+def attention_tiled(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, seq_len, pos0, m, workers=1):
+    """The reference's default batched attention (orc_attention_tiled) for m > 1 rows at positions pos0.."""
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(key_cache, np.float32)
+    vc = np.ascontiguousarray(value_cache, np.float32)
+    out = np.zeros((m, n_heads * head_dim), np.float32)
+    rc = lib().orc_attention_tiled(_p(out, _f32p), _p(q, _f32p), _p(kc, _f32p), _p(vc, _f32p), n_heads, n_kv_heads,
+                                   head_dim, seq_len, pos0, m, workers, attention_limit(n_kv_heads, seq_len, workers))
+    assert rc == 0
+    return out
+
+
+def ref_attention_batch(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, seq_len, pos0, m,
+                        isa=KERNELS_AVX512):
+    """The reference's batched attention (k_attention_batch_kv on its default head-major layout, src/attention.c:
+    1444-1453), serial (no team), its default variant (tiled)."""
+    L = ref()
+    L.k_attention_init_rows.argtypes = [ctypes.POINTER(RefAttentionWork)] + [ctypes.c_int] * 5 + [_f32p]
+    L.k_attention_free.argtypes = [ctypes.POINTER(RefAttentionWork)]
+    L.k_attention_batch_kv.argtypes = [_f32p] * 5 + [ctypes.POINTER(RefAttentionWork)] + [ctypes.c_int] * 6
+    if not ref_select(isa):
+        raise RuntimeError("instruction set unavailable")
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(key_cache, np.float32)
+    vc = np.ascontiguousarray(value_cache, np.float32)
+    out = np.zeros((m, n_heads * head_dim), np.float32)
+    att = np.zeros(n_heads * seq_len, np.float32)
+    work = RefAttentionWork()
+    L.k_attention_init_rows(ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len, m, None)
+    L.k_attention_batch_kv(_p(out, _f32p), _p(q, _f32p), _p(kc, _f32p), _p(vc, _f32p), _p(att, _f32p),
+                           ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len, pos0, m)
     L.k_attention_free(ctypes.byref(work))
     ref_select(KERNELS_SCALAR)
     return out

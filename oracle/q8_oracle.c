@@ -5,6 +5,7 @@
  * reference's C source says it does. */
 #include "q8_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -329,4 +330,203 @@ void orc_random_q8(int8_t *q, float *s, size_t row0, size_t rows, size_t cols, i
     orc_quantize(q + r * cols, s + r * (cols / gs), row, (int)cols, gs);
   }
   free(row);
+}
+
+/* ---- attention (src/attention.c), head-major K/V cache [n_kv][seq][hd] ------------------------------------------ */
+
+float orc_exp512(float x) {
+  /* exp512 (src/kernels_internal.h:62-76), one lane: clamp to [-87.33654, 88.72283], n = round-to-nearest-even of
+   * x * log2(e), r = x - n * ln2 in two fused steps (ln2 split as 0.693359375 - 2.12194440e-4), a degree-6 Horner
+   * polynomial in fused steps, y * r^2 + (r + 1), times 2^n. */
+  x = fminf(fmaxf(x, -87.33654f), 88.72283f);
+  float n = nearbyintf(x * 1.44269504088896341f);
+  float r = fmaf(-n, 0.693359375f, x);
+  r = fmaf(-n, -2.12194440e-4f, r);
+  float y = 1.9875691500e-4f;
+  y = fmaf(y, r, 1.3981999507e-3f);
+  y = fmaf(y, r, 8.3334519073e-3f);
+  y = fmaf(y, r, 4.1665795894e-2f);
+  y = fmaf(y, r, 1.6666665459e-1f);
+  y = fmaf(y, r, 5.0000001201e-1f);
+  y = fmaf(y, r * r, r + 1.0f);
+  return ldexpf(y, (int)n);
+}
+
+int orc_attention_chunks(int positions, int n_kv_heads, int limit, int workers) {
+  /* attention_chunks (src/attention.c:516-526) */
+  int chunks = (workers + n_kv_heads - 1) / n_kv_heads;
+  int longest = (positions + 31) / 32, shortest = (positions + 255) / 256;
+  if (chunks > longest)
+    chunks = longest;
+  if (chunks < shortest)
+    chunks = shortest;
+  if (chunks > limit)
+    chunks = limit;
+  return chunks < 1 ? 1 : chunks;
+}
+
+static void merge_partials(const float *base, size_t slot, int chunks, int hd, float *o) {
+  /* merge_chunks (src/attention.c:664-682); partials with sum 0 and max -FLT_MAX are skipped */
+  float max_val = base[hd];
+  for (int c = 1; c < chunks; c++)
+    if (base[c * slot + hd] > max_val)
+      max_val = base[c * slot + hd];
+  float sum = 0.0f;
+  memset(o, 0, (size_t)hd * sizeof(float));
+  for (int c = 0; c < chunks; c++) {
+    const float *chunk = base + c * slot;
+    if (chunk[hd + 1] == 0.0f && chunk[hd] == -FLT_MAX)
+      continue;
+    float weight = expf(chunk[hd] - max_val);
+    sum += weight * chunk[hd + 1];
+    for (int i = 0; i < hd; i++)
+      o[i] += weight * chunk[i];
+  }
+  for (int i = 0; i < hd; i++)
+    o[i] /= sum;
+}
+
+static void split_chunk(const float *q, const float *K, const float *V, int hd, int t0, int t1, float *a, float *o) {
+  /* attention_chunk_avx512 (src/attention.c:40-105), one head over positions [t0, t1) of its KV head's rows: 16-lane
+   * FMA scores over the head's 16-float vectors, _mm512_reduce_add_ps, / sqrtf(hd); the max; exp512 of score - max;
+   * lane l of the exp-sum takes positions t0 + 16 i + l; P.V as one FMA chain per output element over the positions. */
+  int vectors = (hd + 15) / 16;
+  float divisor = sqrtf((float)hd);
+  for (int t = t0; t < t1; t++) {
+    float lanes[16];
+    memset(lanes, 0, sizeof(lanes));
+    for (int v = 0; v < vectors; v++)
+      for (int l = 0; l < 16 && 16 * v + l < hd; l++)
+        lanes[l] = fmaf(q[16 * v + l], K[(size_t)t * hd + 16 * v + l], lanes[l]);
+    a[t - t0] = reduce16(lanes) / divisor;
+  }
+  float max_val = -FLT_MAX;
+  for (int t = t0; t < t1; t++)
+    if (a[t - t0] > max_val)
+      max_val = a[t - t0];
+  float vsum[16];
+  memset(vsum, 0, sizeof(vsum));
+  for (int t = t0; t < t1; t++) {
+    float e = orc_exp512(a[t - t0] - max_val);
+    a[t - t0] = e;
+    vsum[(t - t0) % 16] += e;
+  }
+  for (int d = 0; d < hd; d++) {
+    float acc = 0.0f;
+    for (int t = t0; t < t1; t++)
+      acc = fmaf(a[t - t0], V[(size_t)t * hd + d], acc);
+    o[d] = acc;
+  }
+  o[hd] = max_val;
+  o[hd + 1] = reduce16(vsum);
+}
+
+int orc_attention_decode(float *out, const float *q, const float *kc, const float *vc, int n_heads, int n_kv_heads,
+                         int hd, int seq, int position, int workers, int limit) {
+  /* attention_decode_split (src/attention.c:760-810) with its team's chunk plan: chunks of attention_chunks, chunk c
+   * covering [P c / chunks, P (c + 1) / chunks) of the P = position + 1 positions, merged per head. */
+  int positions = position + 1, kv_mul = n_heads / n_kv_heads;
+  int chunks = orc_attention_chunks(positions, n_kv_heads, limit, workers);
+  size_t slot = (size_t)hd + 2;
+  float *part = malloc((size_t)chunks * slot * sizeof(float)), *a = malloc((size_t)positions * sizeof(float));
+  if (!part || !a) {
+    free(part), free(a);
+    return -1;
+  }
+  for (int h = 0; h < n_heads; h++) {
+    int g = h / kv_mul;
+    const float *K = kc + (size_t)g * seq * hd, *V = vc + (size_t)g * seq * hd;
+    for (int c = 0; c < chunks; c++) {
+      int t0 = (int)((long long)positions * c / chunks), t1 = (int)((long long)positions * (c + 1) / chunks);
+      split_chunk(q + (size_t)h * hd, K, V, hd, t0, t1, a, part + c * slot);
+    }
+    merge_partials(part, slot, chunks, hd, out + (size_t)h * hd);
+  }
+  free(part), free(a);
+  return 0;
+}
+
+static void tiled_chunk(const float *q, const float *K, const float *V, int hd, int t0, int t1, int visible,
+                        float *o) {
+  /* attention_tiled_avx512 (src/attention.c:245-334), one query vector over chunk [t0, t1) of which it sees positions
+   * below `visible`: q scaled by 1 / sqrtf(hd) once; per tile of 32 positions from t0, scores as one FMA chain over the
+   * head's elements in order; when the tile's maximum exceeds the running one, the sum and the accumulator are scaled
+   * by exp512(old - new); probabilities exp512(score - max); the tile's sum is lanes j and 16 + j added, then
+   * _mm512_reduce_add_ps, added to the running sum; P.V as one FMA chain per element over the tile's positions. */
+  float scale = 1.0f / sqrtf((float)hd);
+  float qs[256], acc[256], m = -FLT_MAX, l = 0.0f;
+  for (int d = 0; d < hd; d++)
+    qs[d] = q[d] * scale, acc[d] = 0.0f;
+  int end = t1 < visible ? t1 : visible;
+  if (end <= t0) {
+    memset(o, 0, (size_t)hd * sizeof(float));
+    o[hd] = -FLT_MAX;
+    o[hd + 1] = 0.0f;
+    return;
+  }
+  for (int t = t0; t < end; t += 32) {
+    int n = end - t < 32 ? end - t : 32;
+    float s[32], e[32];
+    for (int j = 0; j < n; j++) {
+      float a = 0.0f;
+      for (int d = 0; d < hd; d++)
+        a = fmaf(qs[d], K[(size_t)(t + j) * hd + d], a);
+      s[j] = a;
+    }
+    float tile_max = -FLT_MAX;
+    for (int j = 0; j < n; j++)
+      if (s[j] > tile_max)
+        tile_max = s[j];
+    if (tile_max > m) {
+      float alpha = orc_exp512(m - tile_max);
+      l *= alpha;
+      for (int d = 0; d < hd; d++)
+        acc[d] *= alpha;
+      m = tile_max;
+    }
+    float lanes[16];
+    for (int j = 0; j < 32; j++)
+      e[j] = j < n ? orc_exp512(s[j] - m) : 0.0f;
+    for (int j = 0; j < 16; j++)
+      lanes[j] = e[j] + e[16 + j];
+    l += reduce16(lanes);
+    for (int j = 0; j < n; j++)
+      for (int d = 0; d < hd; d++)
+        acc[d] = fmaf(e[j], V[(size_t)(t + j) * hd + d], acc[d]);
+  }
+  for (int d = 0; d < hd; d++)
+    o[d] = acc[d];
+  o[hd] = m;
+  o[hd + 1] = l;
+}
+
+int orc_attention_tiled(float *out, const float *q, const float *kc, const float *vc, int n_heads, int n_kv_heads,
+                        int hd, int seq, int pos0, int m, int workers, int limit) {
+  /* attention_tiled_driver (src/attention.c:1175-1229) for m > 1 rows at positions pos0.. (row r sees pos0 + r + 1
+   * positions): rows in blocks of 16 / (query heads per KV head); tiled_plan (src/attention.c:1078-1085) gives each
+   * block's chunk length (a multiple of 32) and count from attention_chunks at its last row; every row of the block
+   * uses that plan, its chunks merged per head. out and q: m rows of n_heads * hd. */
+  int kv_mul = n_heads / n_kv_heads, rblock = 16 / kv_mul < 1 ? 1 : 16 / kv_mul;
+  size_t slot = (size_t)hd + 2;
+  int max_chunks = orc_attention_chunks(pos0 + m, n_kv_heads, limit, workers);
+  float *part = malloc((size_t)(max_chunks + 1) * slot * sizeof(float));
+  if (!part || hd > 256)
+    return free(part), -1;
+  for (int r = 0; r < m; r++) {
+    int block = r / rblock, block_end = (block + 1) * rblock < m ? (block + 1) * rblock : m;
+    int positions = pos0 + block_end;
+    int wanted = orc_attention_chunks(positions, n_kv_heads, limit, workers);
+    int len = ((positions + wanted - 1) / wanted + 31) / 32 * 32, chunks = (positions + len - 1) / len;
+    for (int h = 0; h < n_heads; h++) {
+      int g = h / kv_mul;
+      const float *K = kc + (size_t)g * seq * hd, *V = vc + (size_t)g * seq * hd;
+      for (int c = 0; c < chunks; c++) {
+        int t0 = c * len, t1 = (c + 1) * len < positions ? (c + 1) * len : positions;
+        tiled_chunk(q + ((size_t)r * n_heads + h) * hd, K, V, hd, t0, t1, pos0 + r + 1, part + c * slot);
+      }
+      merge_partials(part, slot, chunks, hd, out + ((size_t)r * n_heads + h) * hd);
+    }
+  }
+  free(part);
+  return 0;
 }

@@ -65,6 +65,18 @@ void orc_rope_table(float *table, int position, int head_dim, float theta, int r
                     float high, int original);
 void orc_rope_apply(float *q, float *k, const float *table, int n_heads, int n_kv_heads, int head_dim);
 
+/* The reference's attention on the head-major cache [n_kv_heads][seq][hd] (its default LLAMA_KV_LAYOUT=head), with
+ * its team's chunk plan (`workers`, attention_chunks src/attention.c:516-526; `limit` = the work's max_chunks):
+ * orc_attention_decode is the split decode (src/attention.c:40-105, 664-682, 760-810) for one row at `position`;
+ * orc_attention_tiled the default batched variant (src/attention.c:245-334, 1078-1229) for m > 1 rows from pos0.
+ * orc_exp512 is exp512 (src/kernels_internal.h:62-76) on one lane. Return -1 on allocation failure. */
+float orc_exp512(float x);
+int orc_attention_chunks(int positions, int n_kv_heads, int limit, int workers);
+int orc_attention_decode(float *out, const float *q, const float *kc, const float *vc, int n_heads, int n_kv_heads,
+                         int hd, int seq, int position, int workers, int limit);
+int orc_attention_tiled(float *out, const float *q, const float *kc, const float *vc, int n_heads, int n_kv_heads,
+                        int hd, int seq, int pos0, int m, int workers, int limit);
+
 #ifdef __cplusplus
 }
 #endif
