@@ -1,0 +1,881 @@
+// GQA attention over the fp32 head-major K/V cache [kv_head][position][head_dim], in the reference's own arithmetic
+// (LucianCrainic/llama3.x.c, src/attention.c), so that it is bitwise the reference's AVX-512 attention:
+//  - one row (decode, and a batch of one): the split variant (attention_decode_split, src/attention.c:760-810). The
+//    P = position + 1 positions are cut into `chunks` of the team plan (attention_chunks, :516-526), chunk c covering
+//    [P c / chunks, P (c + 1) / chunks). Per query head and chunk (attention_chunk_avx512, :40-105): each score is 16
+//    lane FMA chains over the head's 16-float vectors, reduced in _mm512_reduce_add_ps's tree, divided by
+//    sqrtf(head_dim); the chunk's maximum; exp512 of score - max (the reference's Cephes-style exponential,
+//    src/kernels_internal.h:62-76); the exp-sum in 16 lanes (lane l takes positions t0 + 16 i + l) and the same tree;
+//    P.V as one FMA chain per output element over the chunk's positions;
+//  - a batch of rows: the tiled variant (attention_tiled_avx512 and its driver, :245-334, :1078-1229). Rows form
+//    blocks of 16 / (query heads per KV head); a block's chunk length (a multiple of 32) and count come from the plan at
+//    its last row. Per query vector and chunk: q scaled once by 1 / sqrtf(head_dim); per 32-position tile the scores as
+//    one FMA chain over the head's elements, the tile maximum, and when it exceeds the running one the sum and the
+//    accumulator scaled by exp512(old - new); probabilities exp512(score - max); the tile sum as lanes j + 16 + j, then
+//    the tree, added to the running sum; P.V as one FMA chain per element over the tile's positions;
+//  - both: the chunks merged per head (merge_chunks, :664-682): the maximum over the chunks, then in chunk order
+//    sum += w l and o += w acc with w = expf(m - max) (computed in double and rounded once, which equals glibc's
+//    expf except where the exact value lies within a hair of a rounding midpoint), then o / sum.
+// The team plan is the reference's with a team of one (AttentionWork.workers = 1): one chunk per 256 positions, what
+// the reference's engine uses whenever its team is no larger than the (local) KV heads.
+//
+// Kernels: a split CTA per (KV head, chunk) for a row; a tiled CTA per (KV head, group of row blocks) streaming the
+// 32-position K/V tiles of the group's causal range (bulk copies, double-buffered) with 64 query vectors on register
+// tiles; a merge CTA per (query head, row) that also quantizes the head's outputs for the Wo product. Shapes outside
+// the fast kernels (head_dim not 32, 64 or 128, query heads per KV head not dividing 16) run slow one-thread-per-query
+// restatements of the same arithmetic.
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/kernels_cuda.h"
+#include "common.cuh"
+#include "kernels_cuda_internal.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kTile = 32;        // positions per tile of the batched variant (its TILED_POS)
+constexpr int kSplitMax = 256;   // positions of a split chunk at most (attention_chunks' shortest bound)
+constexpr int kQV = 64;          // query vectors of a batched CTA
+constexpr int kMaxHd = 256;      // the reference's AVX-512 attention takes head_dim <= 256
+constexpr int kMaxNq = 16;       // query heads per KV head (TILED_MAX_Q)
+
+// ---- the reference's arithmetic, one lane ---------------------------------------------------------------------------
+
+// exp512 (src/kernels_internal.h:62-76) on one lane: the clamp, n = round-to-nearest-even of x * log2(e), the two-step
+// reduction by ln 2, the degree-6 Horner polynomial, y * r^2 + (r + 1), then y * 2^n (the result of scalef, one
+// rounding: 2^n is exact for n in [-126, 127]; n = 128 goes through y * 2 first, also exact).
+__device__ __forceinline__ float exp512_dev(float x) {
+  x = fminf(fmaxf(x, -87.33654f), 88.72283f);
+  const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = __fmaf_rn(-n, 0.693359375f, x);
+  r = __fmaf_rn(-n, -2.12194440e-4f, r);
+  float y = 1.9875691500e-4f;
+  y = __fmaf_rn(y, r, 1.3981999507e-3f);
+  y = __fmaf_rn(y, r, 8.3334519073e-3f);
+  y = __fmaf_rn(y, r, 4.1665795894e-2f);
+  y = __fmaf_rn(y, r, 1.6666665459e-1f);
+  y = __fmaf_rn(y, r, 5.0000001201e-1f);
+  y = __fmaf_rn(y, __fmul_rn(r, r), __fadd_rn(r, 1.0f));
+  const int ni = (int)n;
+  if (ni <= 127)
+    return __fmul_rn(y, __int_as_float((ni + 127) << 23));
+  return __fmul_rn(__fmul_rn(y, 2.0f), __int_as_float((ni - 1 + 127) << 23));
+}
+
+// expf of the merge (glibc's, correctly rounded but for values within a hair of a rounding midpoint).
+__device__ __forceinline__ float expf_ref(float x) { return (float)exp((double)x); }
+
+// _mm512_reduce_add_ps over 16 values in registers: halves 8 apart, then 4, then pairs (0, 2) and (1, 3), then the two.
+__device__ __forceinline__ float tree16(const float *a) {
+  float t8[8], t4[4];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+    t8[i] = __fadd_rn(a[8 + i], a[i]);
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    t4[i] = __fadd_rn(t8[4 + i], t8[i]);
+  return __fadd_rn(__fadd_rn(t4[0], t4[2]), __fadd_rn(t4[1], t4[3]));
+}
+
+// The same tree over a value held by each of 16 consecutive lanes (lane 0 of the 16 gets the result).
+__device__ __forceinline__ float tree16_lanes(float v) {
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8, 16));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 16));
+  return __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 16));
+}
+
+// attention_chunks (src/attention.c:516-526).
+__host__ __device__ inline int plan_chunks(int positions, int n_kv, int limit, int workers) {
+  int chunks = (workers + n_kv - 1) / n_kv;
+  const int longest = (positions + 31) / 32, shortest = (positions + 255) / 256;
+  if (chunks > longest)
+    chunks = longest;
+  if (chunks < shortest)
+    chunks = shortest;
+  if (chunks > limit)
+    chunks = limit;
+  return chunks < 1 ? 1 : chunks;
+}
+
+// tiled_plan (src/attention.c:1078-1085): chunk length and count of the block of row `row` (rows counted from the
+// batch's first row at pos0, m rows in the batch, `rblock` rows a block).
+struct TilePlan {
+  int len, chunks;
+};
+__host__ __device__ inline TilePlan tile_plan(int row, int rblock, int m, int pos0, int n_kv, int limit, int workers) {
+  const int block = row / rblock, end = (block + 1) * rblock < m ? (block + 1) * rblock : m;
+  const int positions = pos0 + end, wanted = plan_chunks(positions, n_kv, limit, workers);
+  TilePlan p;
+  p.len = ((positions + wanted - 1) / wanted + kTile - 1) / kTile * kTile;
+  p.chunks = (positions + p.len - 1) / p.len;
+  return p;
+}
+
+__host__ __device__ inline int tile_rblock(int nq) { return 16 / nq < 1 ? 1 : 16 / nq; }
+
+// ---- the partials and their merge ----------------------------------------------------------------------------------
+// Partial of (row r of the wave, query head h, chunk c): part[((r * n_heads + h) * cstride + c) * (hd + 2)]:
+// the hd accumulator values, then the maximum, then the exp-sum.
+
+// Merges row r's chunks for query head h (blockIdx.x) and writes the head's outputs; with oq, also quantizes them in
+// gs-groups (k_quantize's rule) when gs divides head_dim. One thread per output element; every thread walks the
+// chunks in order, so all compute the same maximum and sum.
+// tiled: the row's plan is its block's (tile_plan), chunks past its visible positions hold nothing and are skipped;
+// otherwise (split) the row is the wave's only row and every one of the plan_chunks chunks holds a partial.
+__global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out_ld, int8_t *oq, float *os,
+                                                        const float *part, const int *pos_dev, int pos0, int row0,
+                                                        int m, int tiled, int n_heads, int n_kv, int hd, int seq,
+                                                        int limit, int workers, int cstride, int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[kMaxHd / 32];
+  __shared__ float vals[kMaxHd];
+  const int h = blockIdx.x, rr = blockIdx.y, r = row0 + rr, d = threadIdx.x;
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int vis = base + r + 1;  // positions the row sees
+  if (base < 0 || vis > seq) {
+    if (h == 0 && rr == 0 && d == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+    return;
+  }
+  int chunks, live;
+  if (tiled) {
+    const TilePlan p = tile_plan(r, tile_rblock(n_heads / n_kv), m, base, n_kv, limit, workers);
+    chunks = p.chunks;
+    live = (vis + p.len - 1) / p.len < chunks ? (vis + p.len - 1) / p.len : chunks;
+  } else {
+    chunks = plan_chunks(vis, n_kv, limit, workers);
+    live = chunks;
+  }
+  const int slot = hd + 2;
+  const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
+  float mx = __ldcg(pb + hd);
+  for (int c = 1; c < live; c++)
+    mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + hd));
+  float sum = 0.0f, o = 0.0f;
+  for (int c = 0; c < live; c++) {
+    const float *pc = pb + (long long)c * slot;
+    const float w = expf_ref(__fsub_rn(__ldcg(pc + hd), mx));
+    sum = __fadd_rn(sum, __fmul_rn(w, __ldcg(pc + hd + 1)));
+    if (d < hd)
+      o = __fadd_rn(o, __fmul_rn(w, __ldcg(pc + d)));
+  }
+  (void)chunks;
+  const float v = __fdiv_rn(o, sum);
+  float *dst = out + (long long)r * out_ld + (long long)h * hd;
+  if (d < hd)
+    dst[d] = v;
+  if (!oq || gs <= 0 || hd % gs)
+    return;
+  // Quantize the head's outputs group by group: the group maximum of |v| (order-free), scale = max / 127.
+  const int warp = d >> 5, lane = d & 31;
+  vals[d] = v;
+  const int bad = d < hd && !isfinite(v);
+  float a = d < hd ? fabsf(v) : 0.0f;
+  if (__syncthreads_or(bad)) {
+    if (d == 0)
+      kc_raise(KC_ERR_NONFINITE);
+    return;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1)
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+  if (lane == 0)
+    red[warp] = a;
+  __syncthreads();
+  if (d < hd) {
+    const int g0 = (d / gs) * gs, w0 = g0 >> 5, w1 = (g0 + gs - 1) >> 5;
+    float gmax = 0.0f;
+    if (gs >= 32) {
+      for (int w = w0; w <= w1; w++)
+        gmax = fmaxf(gmax, red[w]);
+    } else {
+      for (int i = g0; i < g0 + gs; i++)
+        gmax = fmaxf(gmax, fabsf(vals[i]));
+    }
+    const float scl = __fdiv_rn(gmax, 127.0f);
+    const long long e = (long long)r * out_ld + (long long)h * hd + d;
+    oq[e] = (int8_t)quantize_value(v, scl);
+    if (d == g0)
+      os[e / gs] = scl;
+  }
+}
+
+// ---- slow restatements for the shapes the fast kernels do not take --------------------------------------------------
+
+// One thread per (query head, chunk) of one row: attention_chunk_avx512 (src/attention.c:40-105) for head_dim <= 256.
+__global__ void split_generic_kernel(const float *q, const float *kc, const float *vc, const int *pos_dev, int pos0,
+                                     int n_heads, int n_kv, int hd, int seq, int limit, int workers, int cstride,
+                                     float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int h = blockIdx.x, c = threadIdx.x;
+  const int P = (pos_dev ? *pos_dev : pos0) + 1;
+  if (P < 1 || P > seq)
+    return;  // the merge kernel reports it
+  const int chunks = plan_chunks(P, n_kv, limit, workers);
+  if (c >= chunks)
+    return;
+  const int t0 = (int)((long long)P * c / chunks), t1 = (int)((long long)P * (c + 1) / chunks);
+  const int g = h / (n_heads / n_kv), vectors = (hd + 15) / 16;
+  const float *qh = q + (long long)h * hd, *K = kc + (long long)g * seq * hd, *V = vc + (long long)g * seq * hd;
+  float *o = part + ((long long)h * cstride + c) * (hd + 2);
+  const float divisor = __fsqrt_rn((float)hd);
+  // Pass 1: the maximum score. Pass 2: exp-sum lanes. Pass 3: P.V per element (scores recomputed each pass).
+  auto score = [&](int t) {
+    float lanes[16];
+    for (int l = 0; l < 16; l++)
+      lanes[l] = 0.0f;
+    for (int v = 0; v < vectors; v++)
+      for (int l = 0; l < 16 && 16 * v + l < hd; l++)
+        lanes[l] = __fmaf_rn(qh[16 * v + l], K[(long long)t * hd + 16 * v + l], lanes[l]);
+    return __fdiv_rn(tree16(lanes), divisor);
+  };
+  float mx = -FLT_MAX;
+  for (int t = t0; t < t1; t++)
+    mx = fmaxf(mx, score(t));
+  float vsum[16];
+  for (int l = 0; l < 16; l++)
+    vsum[l] = 0.0f;
+  for (int t = t0; t < t1; t++)
+    vsum[(t - t0) & 15] = __fadd_rn(vsum[(t - t0) & 15], exp512_dev(__fsub_rn(score(t), mx)));
+  for (int d = 0; d < hd; d++)
+    o[d] = 0.0f;
+  for (int t = t0; t < t1; t++) {
+    const float e = exp512_dev(__fsub_rn(score(t), mx));
+    for (int d = 0; d < hd; d++)
+      o[d] = __fmaf_rn(e, V[(long long)t * hd + d], o[d]);
+  }
+  o[hd] = mx;
+  o[hd + 1] = tree16(vsum);
+}
+
+// One thread per (query head, row, chunk) of a batch: attention_tiled_avx512 (src/attention.c:245-334) for one query
+// vector, head_dim <= 256. The accumulator lives in the partial itself.
+__global__ void tiled_generic_kernel(const float *q, long long q_ld, const float *kc, const float *vc, int pos0,
+                                     int row0, int rows, int m, int n_heads, int n_kv, int hd, int seq, int limit,
+                                     int workers, int cstride, float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int h = blockIdx.x, rr = blockIdx.y, c = threadIdx.x, r = row0 + rr;
+  if (rr >= rows)
+    return;
+  const int nq = n_heads / n_kv, g = h / nq, vis = pos0 + r + 1;
+  const TilePlan p = tile_plan(r, tile_rblock(nq), m, pos0, n_kv, limit, workers);
+  const int t0 = c * p.len, t1 = min((c + 1) * p.len, vis);
+  if (c >= p.chunks || t1 <= t0)
+    return;  // nothing visible: the merge skips the chunk
+  const float *qh = q + (long long)r * q_ld + (long long)h * hd, *K = kc + (long long)g * seq * hd,
+              *V = vc + (long long)g * seq * hd;
+  float *o = part + (((long long)rr * n_heads + h) * cstride + c) * (hd + 2);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  float m_run = -FLT_MAX, l = 0.0f;
+  for (int d = 0; d < hd; d++)
+    o[d] = 0.0f;
+  for (int t = t0; t < t1; t += kTile) {
+    const int n = min(kTile, t1 - t);
+    float s[kTile], e[kTile];
+    for (int j = 0; j < n; j++) {
+      float a = 0.0f;
+      for (int d = 0; d < hd; d++)
+        a = __fmaf_rn(__fmul_rn(qh[d], scale), K[(long long)(t + j) * hd + d], a);
+      s[j] = a;
+    }
+    float tmax = -FLT_MAX;
+    for (int j = 0; j < n; j++)
+      tmax = fmaxf(tmax, s[j]);
+    if (tmax > m_run) {
+      const float alpha = exp512_dev(__fsub_rn(m_run, tmax));
+      l = __fmul_rn(l, alpha);
+      for (int d = 0; d < hd; d++)
+        o[d] = __fmul_rn(o[d], alpha);
+      m_run = tmax;
+    }
+    for (int j = 0; j < kTile; j++)
+      e[j] = j < n ? exp512_dev(__fsub_rn(s[j], m_run)) : 0.0f;
+    float lanes[16];
+    for (int j = 0; j < 16; j++)
+      lanes[j] = __fadd_rn(e[j], e[16 + j]);
+    l = __fadd_rn(l, tree16(lanes));
+    for (int j = 0; j < n; j++)
+      for (int d = 0; d < hd; d++)
+        o[d] = __fmaf_rn(e[j], V[(long long)(t + j) * hd + d], o[d]);
+  }
+  o[hd] = m_run;
+  o[hd + 1] = l;
+}
+
+// ---- the split variant for one row (decode) -----------------------------------------------------------------------
+// CTA (KV head g, chunk c) of the row at position pos: its nq query heads over the chunk's positions (at most 256).
+// Shared memory: A holds the chunk's K rows, then (once the scores are done) V rows 128..; B holds V rows 0..127; the
+// group's queries; the scores, overwritten by their exponentials; per head the maximum and the exp-sum.
+__host__ __device__ constexpr size_t split_smem_bytes(int hd) {
+  return ((size_t)kSplitMax * hd + (size_t)(kSplitMax / 2) * hd + (size_t)kMaxNq * hd + (size_t)kMaxNq * kSplitMax +
+          2 * kMaxNq) * sizeof(float) + 2 * sizeof(uint64_t);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads) split_kernel(const float *q, const float *kc, const float *vc,
+                                                         const int *pos_dev, int pos0, int n_kv, int nq, int seq,
+                                                         int limit, int workers, int cstride, float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float sm[];
+  float *A = sm, *B = A + kSplitMax * HD, *Q = B + (kSplitMax / 2) * HD, *S = Q + kMaxNq * HD;
+  float *hmax = S + kMaxNq * kSplitMax, *hsum = hmax + kMaxNq;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(hsum + kMaxNq);
+  const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = (pos_dev ? *pos_dev : pos0) + 1;
+  if (P < 1 || P > seq)
+    return;  // the merge kernel reports it
+  const int chunks = plan_chunks(P, n_kv, limit, workers);
+  if (c >= chunks)
+    return;
+  const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;
+  const int nb = n < kSplitMax / 2 ? n : kSplitMax / 2;  // V rows in B
+  const float *Kg = kc + ((long long)g * seq + t0) * HD, *Vg = vc + ((long long)g * seq + t0) * HD;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar[0], (unsigned)(n + nb) * HD * sizeof(float));
+    bulk_g2s(A, Kg, (unsigned)n * HD * sizeof(float), &bar[0]);
+    bulk_g2s(B, Vg, (unsigned)nb * HD * sizeof(float), &bar[0]);
+  }
+  for (int i = tid; i < nq * HD; i += kThreads)
+    Q[i] = q[(long long)g * nq * HD + i];
+  __syncthreads();
+  if (!__syncthreads_and(mbar_wait_bounded(&bar[0], 0))) {
+    if (tid == 0)
+      mbar_wait_bounded(&bar[0], 0);  // let the copies in flight land (bounded) before the CTA leaves
+    return;
+  }
+  // Scores: a half-warp per (head, position), lane L owning lanes L of the head's 16-float vectors.
+  {
+    const int hw = tid >> 4, L = tid & 15, h = hw % nq, step = kThreads / 16 / nq;
+    float qr[HD / 16];
+#pragma unroll
+    for (int v = 0; v < HD / 16; v++)
+      qr[v] = Q[h * HD + 16 * v + L];
+    const float divisor = __fsqrt_rn((float)HD);
+    const int iters = (n + step - 1) / step;
+    for (int it = 0; it < iters; it++) {
+      const int t = it * step + hw / nq, tc = t < n ? t : 0;
+      float s = 0.0f;
+#pragma unroll
+      for (int v = 0; v < HD / 16; v++)
+        s = __fmaf_rn(qr[v], A[tc * HD + 16 * v + L], s);
+      s = tree16_lanes(s);
+      if (L == 0 && t < n)
+        S[h * kSplitMax + t] = __fdiv_rn(s, divisor);
+    }
+  }
+  __syncthreads();
+  // K is consumed: V rows nb.. go into A while the softmax runs.
+  if (tid == 0 && n > nb) {
+    mbar_arrive_expect_tx(&bar[1], (unsigned)(n - nb) * HD * sizeof(float));
+    bulk_g2s(A, Vg + (long long)nb * HD, (unsigned)(n - nb) * HD * sizeof(float), &bar[1]);
+  }
+  // Per head (a warp each): the maximum, exp512 in place, the exp-sum in 16 lanes then the tree.
+  for (int h = warp; h < nq; h += kThreads / 32) {
+    float *sh = S + h * kSplitMax;
+    float mx = -FLT_MAX;
+    for (int t = lane; t < n; t += 32)
+      mx = fmaxf(mx, sh[t]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float vs = 0.0f;
+    if (lane < 16)
+      for (int t = lane; t < n; t += 16) {
+        const float e = exp512_dev(__fsub_rn(sh[t], mx));
+        sh[t] = e;
+        vs = __fadd_rn(vs, e);
+      }
+    vs = tree16_lanes(vs);
+    if (lane == 0)
+      hmax[h] = mx, hsum[h] = vs;
+  }
+  __syncthreads();
+  // P.V: a chain per (head, element) over the positions in order, V rows 0..nb-1 from B, then nb.. from A.
+  constexpr int kChains = kMaxNq * HD / kThreads;
+  float acc[kChains];
+#pragma unroll
+  for (int k = 0; k < kChains; k++)
+    acc[k] = 0.0f;
+  for (int t = 0; t < nb; t++) {
+#pragma unroll
+    for (int k = 0; k < kChains; k++) {
+      const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
+      if (h < nq)
+        acc[k] = __fmaf_rn(S[h * kSplitMax + t], B[t * HD + d], acc[k]);
+    }
+  }
+  bool ok = true;
+  if (n > nb) {
+    ok = __syncthreads_and(mbar_wait_bounded(&bar[1], 0));
+    for (int t = nb; t < n && ok; t++) {
+#pragma unroll
+      for (int k = 0; k < kChains; k++) {
+        const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
+        if (h < nq)
+          acc[k] = __fmaf_rn(S[h * kSplitMax + t], A[(t - nb) * HD + d], acc[k]);
+      }
+    }
+  }
+  if (!ok) {
+    if (tid == 0)
+      mbar_wait_bounded(&bar[1], 0);
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kChains; k++) {
+    const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
+    if (h < nq)
+      part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + d] = acc[k];
+  }
+  if (tid < nq) {
+    float *o = part + ((long long)(g * nq + tid) * cstride + c) * (HD + 2);
+    o[HD] = hmax[tid];
+    o[HD + 1] = hsum[tid];
+  }
+}
+
+// ---- the tiled variant for a batch of rows (prefill) ---------------------------------------------------------------
+// CTA (KV head g, group of R rows = whole or part blocks): its query vectors v = (row - first row) * nq + head, at
+// most 64, over the 32-position tiles of the group's causal range. Per tile: K and V rows by bulk copy (two buffers,
+// the next tile's copy in flight), K transposed for the score tiles, scores (2 queries x 4 positions a thread, chains
+// over the head's elements in order), the online softmax per query (a warp per 8 queries, a lane per position), then
+// P.V (4 queries x hd/16 elements a thread, chains over the tile's positions in order). A query whose chunk (its
+// block's plan) changes at a tile writes the finished chunk's partial first and starts again from zero.
+__host__ __device__ constexpr size_t tiled_smem_bytes(int hd) {
+  return ((size_t)4 * kTile * hd + (size_t)hd * kTile + (size_t)hd * kQV + (size_t)kQV * (kTile + 1) +
+          (size_t)kTile * kQV + 4 * kQV) * sizeof(float) + 2 * sizeof(uint64_t);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long long q_ld, const float *kc,
+                                                         const float *vc, const int *pos_dev, int pos0, int row0,
+                                                         int rows, int m, int R, int n_kv, int nq, int seq, int limit,
+                                                         int workers, int cstride, float *part) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float sm[];
+  float *Kb = sm, *Vb = Kb + 2 * kTile * HD, *kt = Vb + 2 * kTile * HD, *qs = kt + HD * kTile;
+  float *S = qs + HD * kQV, *P = S + kQV * (kTile + 1);
+  float *ms = P + kTile * kQV, *ls = ms + kQV, *al = ls + kQV;
+  int *cur = reinterpret_cast<int *>(al + kQV);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(cur + kQV);
+  constexpr int DB = HD / 16;
+  const int g = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int rl0 = blockIdx.y * R, nr = min(R, rows - rl0);  // rows of this CTA, from wave row rl0
+  if (nr <= 0 || base < 0 || base + row0 + rl0 + nr > seq)
+    return;  // the merge kernel reports bad positions
+  const int qv = nr * nq, rblock = tile_rblock(nq), n_heads = n_kv * nq;
+  const int vis_max = base + row0 + rl0 + nr, ntiles = (vis_max + kTile - 1) / kTile;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  // Queries, scaled, transposed: qs[d][v].
+  for (int i = tid; i < kQV * HD; i += kThreads) {
+    const int v = i / HD, d = i - v * HD;
+    float x = 0.0f;
+    if (v < qv)
+      x = __fmul_rn(q[(long long)(row0 + rl0 + v / nq) * q_ld + (long long)(g * nq + v % nq) * HD + d], scale);
+    qs[d * kQV + v] = x;
+  }
+  if (tid < kQV)
+    ms[tid] = -FLT_MAX, ls[tid] = 0.0f, al[tid] = 1.0f, cur[tid] = -1;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const float *Kg = kc + (long long)g * seq * HD, *Vg = vc + (long long)g * seq * HD;
+  auto issue = [&](int k) {
+    const int t = k * kTile, cnt = min(kTile, vis_max - t);
+    const unsigned bytes = (unsigned)cnt * HD * sizeof(float);
+    mbar_arrive_expect_tx(&bar[k & 1], 2 * bytes);
+    bulk_g2s(Kb + (k & 1) * kTile * HD, Kg + (long long)t * HD, bytes, &bar[k & 1]);
+    bulk_g2s(Vb + (k & 1) * kTile * HD, Vg + (long long)t * HD, bytes, &bar[k & 1]);
+  };
+  if (tid == 0)
+    issue(0);
+  // This thread's P.V tile: queries 4 qq.., elements DB dg..; its queries' plans.
+  const int qq = tid >> 4, dg = tid & 15;
+  float acc[4][DB];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int d = 0; d < DB; d++)
+      acc[i][d] = 0.0f;
+  auto out_of = [&](int v, int chunk) {  // partial of query v, chunk `chunk`
+    return part + (((long long)(rl0 + v / nq) * n_heads + g * nq + v % nq) * cstride + chunk) * (HD + 2);
+  };
+  int failed = -1;  // the tile whose copy did not complete in time
+  for (int k = 0; k < ntiles; k++) {
+    const int t = k * kTile, cnt = min(kTile, vis_max - t), b = k & 1;
+    if (!__syncthreads_and(mbar_wait_bounded(&bar[b], (k >> 1) & 1))) {
+      failed = k;
+      break;
+    }
+    if (tid == 0 && k + 1 < ntiles)
+      issue(k + 1);  // its buffer's last readers finished before the barrier above
+    // K transposed: kt[d][p], zero past the tile's rows.
+    for (int i = tid; i < kTile * HD; i += kThreads) {
+      const int p = i / HD, d = i - p * HD;
+      kt[d * kTile + p] = p < cnt ? Kb[b * kTile * HD + i] : 0.0f;
+    }
+    __syncthreads();
+    // Scores: queries 2 qp, 2 qp + 1 and positions 4 pq.. of this thread, chains over d in order.
+    {
+      const int qp = tid >> 3, pq = tid & 7;
+      float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll 8
+      for (int d = 0; d < HD; d++) {
+        const float2 qv2 = *reinterpret_cast<const float2 *>(qs + d * kQV + 2 * qp);
+        const float4 kv4 = *reinterpret_cast<const float4 *>(kt + d * kTile + 4 * pq);
+        s[0][0] = __fmaf_rn(qv2.x, kv4.x, s[0][0]);
+        s[0][1] = __fmaf_rn(qv2.x, kv4.y, s[0][1]);
+        s[0][2] = __fmaf_rn(qv2.x, kv4.z, s[0][2]);
+        s[0][3] = __fmaf_rn(qv2.x, kv4.w, s[0][3]);
+        s[1][0] = __fmaf_rn(qv2.y, kv4.x, s[1][0]);
+        s[1][1] = __fmaf_rn(qv2.y, kv4.y, s[1][1]);
+        s[1][2] = __fmaf_rn(qv2.y, kv4.z, s[1][2]);
+        s[1][3] = __fmaf_rn(qv2.y, kv4.w, s[1][3]);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          S[(2 * qp + i) * (kTile + 1) + 4 * pq + j] = s[i][j];
+    }
+    __syncthreads();
+    // Online softmax: a warp per 8 queries, lane = position. A query whose chunk changes writes its finished (max,
+    // sum) first and starts again; al[v] carries the accumulator's factor (1 when the maximum did not move) and
+    // cur[v] the chunk the accumulator belongs to, flush[] the chunk to write out first (or -1).
+    for (int i = 0; i < 8; i++) {
+      const int v = warp * 8 + i;
+      const int r = row0 + rl0 + v / nq, vis = base + r + 1;
+      const int nv = v < qv ? max(0, min(kTile, vis - t)) : 0;
+      float e = 0.0f, alpha = 1.0f;
+      if (nv > 0) {
+        const TilePlan p = tile_plan(r, rblock, m, base, n_kv, limit, workers);
+        const int ck = t / p.len;
+        float mrun = ms[v], lrun = ls[v];
+        if (ck != cur[v]) {
+          if (cur[v] >= 0 && lane == 0) {
+            float *o = out_of(v, cur[v]);
+            o[HD] = mrun;
+            o[HD + 1] = lrun;
+          }
+          mrun = -FLT_MAX, lrun = 0.0f;
+        }
+        const float s = lane < nv ? S[v * (kTile + 1) + lane] : -FLT_MAX;
+        float tmax = s;
+#pragma unroll
+        for (int off = 16; off; off >>= 1)
+          tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+        if (tmax > mrun) {
+          alpha = exp512_dev(__fsub_rn(mrun, tmax));
+          lrun = __fmul_rn(lrun, alpha);
+          mrun = tmax;
+        }
+        e = lane < nv ? exp512_dev(__fsub_rn(s, mrun)) : 0.0f;
+        const float pair = __fadd_rn(e, __shfl_down_sync(0xffffffffu, e, 16));
+        const float tsum = tree16_lanes(pair);
+        lrun = __fadd_rn(lrun, tsum);
+        __syncwarp();
+        if (lane == 0) {
+          ms[v] = mrun, ls[v] = lrun;
+          // The P.V threads read the old cur[v] (the chunk to write out) and the new one through al and fl.
+          S[v * (kTile + 1) + kTile] = __int_as_float(ck != cur[v] ? cur[v] : -2);  // flush marker
+          cur[v] = ck;
+        }
+      } else if (lane == 0) {
+        S[v * (kTile + 1) + kTile] = __int_as_float(-2);
+      }
+      P[lane * kQV + v] = e;
+      if (lane == 0)
+        al[v] = alpha;
+    }
+    __syncthreads();
+    // P.V.
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int v = 4 * qq + i;
+      const int fl = __float_as_int(S[v * (kTile + 1) + kTile]);
+      if (fl >= 0) {  // the query's previous chunk is finished: write it out, start from zero
+        float *o = out_of(v, fl);
+#pragma unroll
+        for (int d = 0; d < DB; d++) {
+          o[dg * DB + d] = acc[i][d];
+          acc[i][d] = 0.0f;
+        }
+      } else if (fl == -1) {  // the query's first chunk starts here
+#pragma unroll
+        for (int d = 0; d < DB; d++)
+          acc[i][d] = 0.0f;
+      }
+      const float a = al[v];
+#pragma unroll
+      for (int d = 0; d < DB; d++)
+        acc[i][d] = __fmul_rn(acc[i][d], a);
+    }
+    const float *Vt = Vb + b * kTile * HD;
+    for (int p = 0; p < cnt; p++) {
+      const float4 pv = *reinterpret_cast<const float4 *>(P + p * kQV + 4 * qq);
+      float vv[DB];
+#pragma unroll
+      for (int d = 0; d < DB; d += 4) {
+        const float4 x = *reinterpret_cast<const float4 *>(Vt + p * HD + dg * DB + d);
+        vv[d] = x.x, vv[d + 1] = x.y, vv[d + 2] = x.z, vv[d + 3] = x.w;
+      }
+      const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int d = 0; d < DB; d++)
+          acc[i][d] = __fmaf_rn(pr[i], vv[d], acc[i][d]);
+    }
+    __syncthreads();  // the buffers of this tile are refilled two tiles on
+  }
+  if (failed >= 0) {  // that tile's copy is the only one in flight: let it land (bounded) before leaving
+    if (tid == 0)
+      mbar_wait_bounded(&bar[failed & 1], (failed >> 1) & 1);
+    return;
+  }
+  // The last chunk of every query.
+  if (tid < qv && cur[tid] >= 0) {
+    float *o = out_of(tid, cur[tid]);
+    o[HD] = ms[tid];
+    o[HD + 1] = ls[tid];
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int v = 4 * qq + i;
+    if (v < qv && cur[v] >= 0) {
+      float *o = out_of(v, cur[v]);
+#pragma unroll
+      for (int d = 0; d < DB; d++)
+        o[dg * DB + d] = acc[i][d];
+    }
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------------------------------------
+
+bool launched(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    kc_count_launch();
+    return true;
+  }
+  return kc_fail("%s: CUDA launch failed: %s", what, cudaGetErrorString(e));
+}
+
+int limit_for(int seq) { return (seq + kSplitMax - 1) / kSplitMax; }  // attention_max_chunks with a team of one
+
+bool fast_shape(int n_heads, int n_kv, int hd) {
+  const int nq = n_heads / n_kv;
+  return (hd == 32 || hd == 64 || hd == 128) && nq <= kMaxNq && kMaxNq % nq == 0;
+}
+
+// Shared-memory limits of the fast kernels, raised once per device.
+bool smem_ready(int hd) {
+  const void *split = hd == 128  ? reinterpret_cast<const void *>(split_kernel<128>)
+                      : hd == 64 ? reinterpret_cast<const void *>(split_kernel<64>)
+                                 : reinterpret_cast<const void *>(split_kernel<32>);
+  const void *tiled = hd == 128  ? reinterpret_cast<const void *>(tiled_kernel<128>)
+                      : hd == 64 ? reinterpret_cast<const void *>(tiled_kernel<64>)
+                                 : reinterpret_cast<const void *>(tiled_kernel<32>);
+  return kc_allow_smem(split, (int)split_smem_bytes(hd)) == cudaSuccess &&
+         kc_allow_smem(tiled, (int)tiled_smem_bytes(hd)) == cudaSuccess;
+}
+
+// Rows of the tiled variant's CTA: whole blocks of 16 / nq rows, 64 query vectors at most.
+int tiled_rows_per_cta(int nq) {
+  const int rb = tile_rblock(nq), blocks = kQV / (rb * nq);
+  return (blocks < 1 ? 1 : blocks) * rb;
+}
+
+// One row (decode) or a batch of rows of attention into out (row stride out_ld), optionally quantized into oq/os.
+bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, float *os, const float *q,
+                    long long q_ld, const float *kc, const float *vc, AttentionWork *w, int n_heads, int n_kv, int hd,
+                    int seq, const int *pos_dev, int pos0, int rows, int gs) {
+  if (!w || !w->partial)
+    return kc_fail("%s: attention work is not initialized", name);
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || hd <= 0 || hd > kMaxHd || seq <= 0 || rows < 0 ||
+      n_heads / n_kv > 1024)
+    return kc_fail("%s: unsupported heads %d / KV heads %d / head_dim %d / context %d", name, n_heads, n_kv, hd, seq);
+  if (n_heads != w->n_heads || hd != w->head_dim || limit_for(seq) > w->max_chunks)
+    return kc_fail("%s: shape differs from the one the work was initialized for", name);
+  if (oq && (gs <= 0 || (n_heads / n_kv * hd) % gs || out_ld % gs))
+    return kc_fail("%s: group size %d does not divide a KV head's outputs", name, gs);
+  if (!pos_dev && (pos0 < 0 || pos0 + rows > seq))
+    return kc_fail("%s: positions %d..%d outside the context of %d", name, pos0, pos0 + rows - 1, seq);
+  if (rows == 0)
+    return true;
+  const int nq = n_heads / n_kv, limit = w->max_chunks, workers = w->workers > 0 ? w->workers : 1;
+  const bool fast = fast_shape(n_heads, n_kv, hd);
+  if (fast && !smem_ready(hd))
+    return kc_fail("%s: cannot reserve shared memory for the attention kernels", name);
+  const bool fused_q = oq && hd % gs == 0;  // the merge quantizes whole groups inside a head
+  const int slot = hd + 2, merge_threads = (hd + 31) / 32 * 32;
+  cudaStream_t st = kc_stream();
+  if (rows == 1) {
+    if ((size_t)n_heads * limit * slot > w->capacity)
+      return kc_fail("%s: attention work too small", name);
+    if (!fast) {
+      kc_launch_pdl(split_generic_kernel, dim3(n_heads), dim3(limit), 0, st, q, kc, vc, pos_dev, pos0, n_heads, n_kv,
+                    hd, seq, limit, workers, limit, w->partial);
+    } else {
+      void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *) =
+          hd == 128 ? split_kernel<128> : hd == 64 ? split_kernel<64> : split_kernel<32>;
+      kc_launch_pdl(k, dim3(n_kv, limit), dim3(kThreads), split_smem_bytes(hd), st, q, kc, vc, pos_dev, pos0, n_kv,
+                    nq, seq, limit, workers, limit, w->partial);
+    }
+    if (!launched(name))
+      return false;
+    kc_launch_pdl(merge_kernel, dim3(n_heads, 1), dim3(merge_threads), 0, st, out, out_ld,
+                  fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
+                  pos_dev, pos0, 0, 1, 0, n_heads, n_kv, hd, seq, limit, workers, limit, gs);
+    if (!launched(name))
+      return false;
+  } else {
+    // Waves of rows whose partials fit the work; the chunk stride is the most chunks a row of the wave can have.
+    const int R = tiled_rows_per_cta(nq), rblock = tile_rblock(nq);
+    for (int row0 = 0; row0 < rows;) {
+      int wave = rows - row0, cstride = limit;
+      for (;;) {
+        if (!pos_dev) {
+          cstride = 1;
+          for (int r = row0; r < row0 + wave; r += rblock) {
+            const int c = tile_plan(r, rblock, rows, pos0, n_kv, limit, workers).chunks;
+            cstride = c > cstride ? c : cstride;
+          }
+          const int c = tile_plan(row0 + wave - 1, rblock, rows, pos0, n_kv, limit, workers).chunks;
+          cstride = c > cstride ? c : cstride;
+        }
+        const size_t fit = w->capacity / ((size_t)n_heads * cstride * slot);
+        if (fit >= (size_t)wave)
+          break;
+        if (fit < 1)
+          return kc_fail("%s: attention work too small", name);
+        wave = (int)fit;
+      }
+      if (!fast) {
+        if (pos_dev)
+          return kc_fail("%s: a batch at device positions needs head_dim 32, 64 or 128", name);
+        kc_launch_pdl(tiled_generic_kernel, dim3(n_heads, wave), dim3(cstride), 0, st, q, q_ld, kc, vc, pos0, row0,
+                      wave, rows, n_heads, n_kv, hd, seq, limit, workers, cstride, w->partial);
+      } else {
+        void (*k)(const float *, long long, const float *, const float *, const int *, int, int, int, int, int, int,
+                  int, int, int, int, int, float *) =
+            hd == 128 ? tiled_kernel<128> : hd == 64 ? tiled_kernel<64> : tiled_kernel<32>;
+        kc_launch_pdl(k, dim3(n_kv, (wave + R - 1) / R), dim3(kThreads), tiled_smem_bytes(hd), st, q, q_ld, kc, vc,
+                      pos_dev, pos0, row0, wave, rows, R, n_kv, nq, seq, limit, workers, cstride, w->partial);
+      }
+      if (!launched(name))
+        return false;
+      kc_launch_pdl(merge_kernel, dim3(n_heads, wave), dim3(merge_threads), 0, st, out, out_ld,
+                    fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
+                    pos_dev, pos0, row0, rows, 1, n_heads, n_kv, hd, seq, limit, workers, cstride, gs);
+      if (!launched(name))
+        return false;
+      row0 += wave;
+    }
+  }
+  if (oq && !fused_q) {
+    if (kc_launch_quantize_rows(oq, os, out, out_ld, rows, n_heads * hd, gs, st) != 0)
+      return kc_fail("%s: CUDA launch failed: %s", name, cudaGetErrorString(cudaGetLastError()));
+    kc_count_launch();
+  }
+  return true;
+}
+
+// Rows of partials the work holds: the rows asked for, capped by a 512 MiB budget (longer batches run in waves),
+// never less than one.
+int work_rows(int n_heads, int head_dim, int seq_len, int rows) {
+  const size_t per_row = (size_t)n_heads * limit_for(seq_len) * (head_dim + 2) * sizeof(float);
+  const size_t fit = ((size_t)512 << 20) / per_row;
+  return (int)(fit < 1 ? 1 : fit < (size_t)rows ? fit : (size_t)rows);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t k_attention_bytes_rows(int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows) {
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || seq_len <= 0 || rows <= 0)
+    return 0;
+  return (size_t)work_rows(n_heads, head_dim, seq_len, rows) * n_heads * limit_for(seq_len) * (head_dim + 2) *
+         sizeof(float);
+}
+
+void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows,
+                           void *memory) {
+  const size_t bytes = k_attention_bytes_rows(n_heads, n_kv_heads, head_dim, seq_len, rows);
+  memset(work, 0, sizeof(*work));
+  if (!bytes) {
+    kc_fail("k_attention_init_rows: invalid shape");
+    return;
+  }
+  char *base = static_cast<char *>(memory);
+  int external = 1;
+  if (!base) {
+    if (cudaMalloc(&base, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      kc_fail("k_attention_init_rows: cannot allocate %zu bytes of attention work", bytes);
+      return;
+    }
+    external = 0;
+  }
+  work->partial = reinterpret_cast<float *>(base);
+  work->max_chunks = limit_for(seq_len);
+  work->n_heads = n_heads;
+  work->head_dim = head_dim;
+  work->workers = 1;
+  work->external = external;
+  work->capacity = bytes / sizeof(float);
+}
+
+void k_attention_free(AttentionWork *work) {
+  if (work->partial && !work->external)
+    cudaFree(work->partial);
+  memset(work, 0, sizeof(*work));
+}
+
+void k_attention_kv(float *out, const float *q, const float *key_cache, const float *value_cache, float *att,
+                    AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int position) {
+  (void)att;
+  const long long ld = (long long)n_heads * head_dim;
+  attention_rows("k_attention_kv", out, ld, nullptr, nullptr, q, ld, key_cache, value_cache, work, n_heads,
+                 n_kv_heads, head_dim, seq_len, nullptr, position, 1, 0);
+}
+
+void k_attention_batch_kv(float *out, const float *q, const float *key_cache, const float *value_cache, float *att,
+                          AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int pos0,
+                          int m) {
+  (void)att;
+  const long long ld = (long long)n_heads * head_dim;
+  attention_rows("k_attention_batch_kv", out, ld, nullptr, nullptr, q, ld, key_cache, value_cache, work, n_heads,
+                 n_kv_heads, head_dim, seq_len, nullptr, pos0, m, 0);
+}
+
+void k_attention_q8_rows(float *out, int8_t *oq, float *os, const float *q, const float *key_cache,
+                         const float *value_cache, AttentionWork *work, int n_heads, int n_kv_heads, int head_dim,
+                         int seq_len, const int *position, int pos0, int rows, int gs) {
+  const long long ld = (long long)n_heads * head_dim;
+  attention_rows("k_attention_q8_rows", out, ld, oq, os, q, ld, key_cache, value_cache, work, n_heads, n_kv_heads,
+                 head_dim, seq_len, position, pos0, rows, gs);
+}
+
+}  // extern "C"

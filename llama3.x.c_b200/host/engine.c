@@ -328,7 +328,8 @@ static int allocate_state(Engine *e) {
     e->ev[i] = kd_event_create();
   if (failed())
     return -1;
-  k_attention_init_rows(&e->attn, e->hl, e->kl, e->hd, e->context, 1, NULL); /* decode's split partials */
+  /* The chunk partials of one row (decode) or of a batch's rows (prefill, in waves when they exceed the work). */
+  k_attention_init_rows(&e->attn, e->hl, e->kl, e->hd, e->context, e->max_batch, NULL);
   float *table = rope_table_host(p, e->context);
   if (!table)
     return efail("cannot allocate the RoPE table");
