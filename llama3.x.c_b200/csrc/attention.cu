@@ -14,8 +14,7 @@
 //    accumulator scaled by exp512(old - new); probabilities exp512(score - max); the tile sum as lanes j + 16 + j, then
 //    the tree, added to the running sum; P.V as one FMA chain per element over the tile's positions;
 //  - both: the chunks merged per head (merge_chunks, :664-682): the maximum over the chunks, then in chunk order
-//    sum += w l and o += w acc with w = expf(m - max) (computed in double and rounded once, which equals glibc's
-//    expf except where the exact value lies within a hair of a rounding midpoint), then o / sum.
+//    sum += w l and o += w acc with w = expf(m - max) (the C library's expf, expf_libc), then o / sum.
 // The team plan is the reference's with a team of one (AttentionWork.workers = 1): one chunk per 256 positions, what
 // the reference's engine uses whenever its team is no larger than the (local) KV heads.
 //
@@ -65,8 +64,6 @@ __device__ __forceinline__ float exp512_dev(float x) {
   return __fmul_rn(__fmul_rn(y, 2.0f), __int_as_float((ni - 1 + 127) << 23));
 }
 
-// expf of the merge (glibc's, correctly rounded but for values within a hair of a rounding midpoint).
-__device__ __forceinline__ float expf_ref(float x) { return (float)exp((double)x); }
 
 // _mm512_reduce_add_ps over 16 values in registers: halves 8 apart, then 4, then pairs (0, 2) and (1, 3), then the two.
 __device__ __forceinline__ float tree16(const float *a) {
@@ -159,7 +156,7 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
   float sum = 0.0f, o = 0.0f;
   for (int c = 0; c < live; c++) {
     const float *pc = pb + (long long)c * slot;
-    const float w = expf_ref(__fsub_rn(__ldcg(pc + hd), mx));
+    const float w = expf_libc(__fsub_rn(__ldcg(pc + hd), mx));
     sum = __fadd_rn(sum, __fmul_rn(w, __ldcg(pc + hd + 1)));
     if (d < hd)
       o = __fadd_rn(o, __fmul_rn(w, __ldcg(pc + d)));
