@@ -88,6 +88,11 @@ void engine_init_random(Model *model, const Config *config, int group_size, unsi
  * device memory, so no host round trip per token). Stops after an EOS/EOT/EOM token or at the end of the context, as
  * the probe does. Writes the tokens to `out` and returns how many, or -1. */
 int engine_generate(Model *model, const int *prompt, int count, int steps, int *out);
+/* Writes a seeded random-init model of `config`'s architecture (the seven dimensions and `shared`) as a version 2
+ * Q8_0 checkpoint both engines load: N(0, 0.02) weights from a counter-based generator (SplitMix64 finalizer,
+ * Box-Muller) quantized in group_size groups by k_quantize's rule, RMSNorm weights 1, on every online core. The
+ * benchmark's models: the same bytes for the GPU engine and the reference's. Returns 0, or -1 with the fail() policy. */
+int engine_write_random(const char *path, const Config *config, int group_size, unsigned long long seed);
 /* Writes the model (this rank's copy; world 1 only) as a version 2 Q8_0 checkpoint the reference loads. */
 int engine_save(Model *model, const char *path);
 /* The engine's CUDA stream (cudaStream_t), for timing with events on it. */

@@ -26,7 +26,7 @@ ENGINE_LIB = HERE / "libllama3x_engine.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr"]
-CFLAGS = ["-std=c11", "-O2", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
+CFLAGS = ["-std=c11", "-O2", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter", "-pthread"]
 
 
 def nvcc():
@@ -82,7 +82,7 @@ def build(force=False, verbose=False):
         gcc = shutil.which("gcc") or "cc"
         tmp = ENGINE_LIB.with_suffix(".so.tmp")
         _run([gcc, *CFLAGS, "-shared", *map(str, host), "-o", str(tmp), f"-L{HERE}", "-lllama3x_cuda",
-              "-Wl,-rpath,$ORIGIN", "-lm"], verbose)
+              "-Wl,-rpath,$ORIGIN", "-lm", "-pthread"], verbose)
         os.replace(tmp, ENGINE_LIB)
     return LIB
 

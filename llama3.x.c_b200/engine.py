@@ -70,6 +70,7 @@ ENGINE_SIGNATURES = {
     "engine_init_random": (None, [_MP, _c.POINTER(Config), _c.c_int, _c.c_ulonglong, _c.c_int]),
     "engine_generate": (_c.c_int, [_MP, _IP, _c.c_int, _c.c_int, _IP]),
     "engine_save": (_c.c_int, [_MP, _c.c_char_p]),
+    "engine_write_random": (_c.c_int, [_c.c_char_p, _c.POINTER(Config), _c.c_int, _c.c_ulonglong]),
     "engine_stream": (_c.c_void_p, [_MP]),
     "engine_stats": (None, [_MP, _c.POINTER(EngineStats)]),
     "engine_stats_reset": (None, [_MP]),
@@ -281,6 +282,17 @@ class Engine:
 
     def __exit__(self, *exc):
         self.close()
+
+
+def write_random(path, dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len, shared=False,
+                 group_size=64, seed=1):
+    """engine_write_random: the seeded random-init checkpoint of this architecture at `path` (returns the path)."""
+    c = Config(dim=dim, hidden_dim=hidden_dim, n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv_heads,
+               vocab_size=vocab_size, seq_len=seq_len, shared=int(shared))
+    if load_library().engine_write_random(os.fsencode(str(path)), ctypes.byref(c), group_size, seed) != 0:
+        _check()
+        raise _kc().KernelError("engine_write_random failed")
+    return path
 
 
 def rope_table(config, position):

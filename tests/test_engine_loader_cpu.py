@@ -5,6 +5,7 @@ No test here reaches a valid load: that would allocate device memory."""
 import ctypes
 import os
 import struct
+from pathlib import Path
 
 import pytest
 
@@ -154,3 +155,16 @@ def test_environment_the_reference_accepts(load, tmp_path, monkeypatch, name, va
     # Accepted settings get as far as opening the checkpoint.
     monkeypatch.setenv(name, value)
     assert load(tmp_path / "absent.bin").startswith("cannot open checkpoint")
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_write_random_equals_the_oracle_checkpoint(tmp_path, shared):
+    """engine_write_random (the product's benchmark checkpoint writer) writes byte for byte the checkpoint of the
+    oracle's generator (oracle/model_file.py), so the GPU engine and the reference load the same model."""
+    from conftest import load_engine
+    from oracle import model_file
+    eng = load_engine()
+    cfg = dict(dim=256, hidden_dim=384, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=300, seq_len=64, shared=shared)
+    a = eng.write_random(tmp_path / "gpu.bin", **cfg, seed=1)
+    b = model_file.write_random_checkpoint(tmp_path / "oracle.bin", **cfg, seed=1)
+    assert Path(a).read_bytes() == Path(b).read_bytes()
