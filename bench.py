@@ -24,8 +24,13 @@ list of every kernel the request launches.
 The weights (8.5 GB at 8B) exceed L2 many times over, so every decode step streams them from HBM.
 
 --impl reference times the reference's own CPU engine (oracle/_ref/libllama_ref_engine.so, built from its sources:
-engine_forward_batch + engine_forward) on all host cores, on the same architecture written as a seeded checkpoint,
-each step a bounded sample (a 128-token prefill and 8 decode tokens). Under torchrun only rank 0 runs it. For the
+engine_forward_batch + engine_forward) on all host cores on the GPU arm's workload: the same checkpoint bytes (the
+engine library's engine_write_random, seed 1), the same prompt, the prompt prefilled once, then each step a bounded
+sample of the greedy decode (8 tokens) at the same positions. Under torchrun only rank 0 runs it.
+
+The 8b / 1b lines carry a `parity` block: the timed request's first 64 greedy tokens and the prompt's last logits
+against the reference's own run of the same workload (tests/golden/bench_golden.npz), and whether every rank holds the
+same logits. For the
 gemv, ffn and gemm workloads it runs the reference's own microbenchmark instead (oracle/_ref/gemm-bench, built from
 tests/gemm_bench.c) on the same shapes; those workloads' own lines carry the same figures as cpu_baseline.
 """
@@ -52,7 +57,7 @@ ARCH = {
                shared=True),
 }
 REQUEST = {"8b": (2048, 256), "1b": (128, 256)}  # prompt tokens, generated tokens
-REF_SAMPLE = (128, 8)  # the reference's bounded per-step sample: prompt tokens, decode tokens
+REF_DECODE = 8  # greedy tokens per timed step of the reference's engine (a bounded sample of the 256)
 
 
 def load_package():
@@ -167,6 +172,41 @@ def prompt_tokens(n, vocab, seed=3):
     return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
 
 
+# ---- the benchmark model: one seeded checkpoint for the GPU engine and the reference's engine --------------------
+
+CKPT_SEED = 1
+GOLDEN = ROOT / "tests" / "golden" / "bench_golden.npz"  # the reference's own tokens and logits on these workloads
+
+
+def checkpoint_bytes(a, gs=64):
+    d, h, L, V = a["dim"], a["hidden_dim"], a["n_layers"], a["vocab_size"]
+    kv = d // a["n_heads"] * a["n_kv_heads"]
+
+    def q8(n):
+        return n + n // gs * 4
+
+    return 256 + (2 * L + 1) * d * 4 + q8(V * d) * (1 if a["shared"] else 2) + \
+        L * (2 * q8(d * d) + 2 * q8(d * kv) + 3 * q8(d * h))
+
+
+def checkpoint_dir():
+    shm = Path("/dev/shm")
+    if shm.exists() and os.statvfs(shm).f_bavail * os.statvfs(shm).f_frsize > 24 * 2**30:
+        return shm
+    return Path("/tmp")
+
+
+def bench_checkpoint(arch, rank=0, world=1):
+    """engine_write_random's seeded checkpoint of the architecture (seed 1): written once by rank 0 (kept when a file of
+    the right size is already there: the reference's arm writes the same bytes), then read by every rank."""
+    a = ARCH[arch]
+    path = checkpoint_dir() / f"llama3x_bench_{arch}.bin"
+    if rank == 0 and not (path.exists() and path.stat().st_size == checkpoint_bytes(a)):
+        load_engine().write_random(path, **a, seed=CKPT_SEED)
+    barrier(world)
+    return path
+
+
 # ---- the dominant kernel: the decode GEMV, timed alone ------------------------------------------------------------
 
 def gemv_roofline(kc, torch, rows, cols, gs=64, launches=60, swiglu=True):
@@ -218,10 +258,13 @@ def gemv_roofline(kc, torch, rows, cols, gs=64, launches=60, swiglu=True):
 
 # ---- the reference's CPU path: its engine, and its kernels alone ---------------------------------------------------
 
-def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
-    """The reference's Q8 engine (engine_forward_batch for the prompt, engine_forward per decode token, greedy) on all
-    host cores. Returns the dict of a cpu_baseline entry plus prefill tok/s."""
-    from oracle import model_file
+def reference_engine_sample(arch, steps, warmup, decode_per_step=REF_DECODE):
+    """The reference's Q8 engine (oracle/_ref/libllama_ref_engine.so: engine_forward_batch over the prompt in its own
+    microbatches, then engine_forward per greedy token) on all host cores, on the GPU arm's workload: the same
+    checkpoint bytes (engine_write_random, seed 1), the same prompt, decoding at the same positions. The prompt is
+    prefilled once (timed: prefill tok/s); each step then decodes `decode_per_step` tokens continuing the greedy stream
+    from position len(prompt) on; the first `warmup` steps are not timed. Returns the dict of a cpu_baseline entry plus
+    prefill tok/s."""
     from oracle import oracle as O
     lib_path = O.HERE / "_ref" / "libllama_ref_engine.so"
     if not lib_path.exists():
@@ -230,12 +273,10 @@ def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
     cores = os.cpu_count() or 1
     os.environ.setdefault("LLAMA_THREADS", str(cores))
     a = ARCH[arch]
-    shm = Path("/dev/shm")
-    base = shm if shm.exists() and os.statvfs(shm).f_bavail * os.statvfs(shm).f_frsize > 24 * 2**30 else Path("/tmp")
     t0 = time.perf_counter()
-    path = model_file.write_random_checkpoint(base / f"llama3x_bench_{arch}.bin", **a, seed=1)
+    path = bench_checkpoint(arch)
     gen_s = time.perf_counter() - t0
-    eng = load_engine()  # only for the layout-compatible Model struct (include/runtime.h); no GPU code is called
+    eng = load_engine()  # the layout-compatible Model struct (include/runtime.h) and the checkpoint writer
     L = ctypes.CDLL(str(lib_path))
     MP = ctypes.POINTER(eng.Model)
     L.engine_load_context.argtypes = [MP, ctypes.c_char_p, ctypes.c_int]
@@ -243,35 +284,44 @@ def reference_engine_sample(arch, steps, warmup, prompt_len, decode_len):
     L.engine_forward.restype = ctypes.POINTER(ctypes.c_float)
     L.engine_forward_batch.argtypes = [MP, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int]
     L.engine_forward_batch.restype = ctypes.POINTER(ctypes.c_float)
+    L.engine_max_batch.argtypes = [MP]
     L.engine_free.argtypes = [MP]
+    P, D = REQUEST[arch]
+    total = (warmup + steps) * decode_per_step
     model = eng.Model()
     t0 = time.perf_counter()
-    L.engine_load_context(ctypes.byref(model), os.fsencode(str(path)), prompt_len + decode_len)
+    L.engine_load_context(ctypes.byref(model), os.fsencode(str(path)), P + total)
     load_s = time.perf_counter() - t0
     V = a["vocab_size"]
-    prompt = prompt_tokens(prompt_len, V)
-    arr = (ctypes.c_int * prompt_len)(*prompt.tolist())
-    pre, dec = [], []
-    for i in range(warmup + steps):
+    prompt = prompt_tokens(P, V)
+    mb = L.engine_max_batch(ctypes.byref(model))
+    t0 = time.perf_counter()
+    i = 0
+    while i < P:
+        n = min(mb, P - i)
+        logits = L.engine_forward_batch(ctypes.byref(model), (ctypes.c_int * n)(*prompt[i:i + n].tolist()), n, i,
+                                        eng.LOGITS_LAST if i + n == P else eng.LOGITS_NONE)
+        i += n
+    prefill_s = time.perf_counter() - t0
+    tok = int(np.argmax(np.ctypeslib.as_array(logits, (V,))))
+    pos, dec = P, []
+    for s in range(warmup + steps):
         t0 = time.perf_counter()
-        logits = L.engine_forward_batch(ctypes.byref(model), arr, prompt_len, 0, eng.LOGITS_LAST)
-        t1 = time.perf_counter()
-        tok = int(np.argmax(np.ctypeslib.as_array(logits, (V,))))
-        for j in range(decode_len):
-            logits = L.engine_forward(ctypes.byref(model), tok, prompt_len + j)
+        for _ in range(decode_per_step):
+            logits = L.engine_forward(ctypes.byref(model), tok, pos)
             tok = int(np.argmax(np.ctypeslib.as_array(logits, (V,))))
-        t2 = time.perf_counter()
-        if i >= warmup:
-            pre.append(t1 - t0)
-            dec.append(t2 - t1)
+            pos += 1
+        if s >= warmup:
+            dec.append(time.perf_counter() - t0)
     L.engine_free(ctypes.byref(model))
-    decode = decode_len * len(dec) / sum(dec)
-    prefill = prompt_len * len(pre) / sum(pre)
+    decode = decode_per_step * len(dec) / sum(dec)
     return {"value": round(decode, 3), "unit": "tok/s", "cores": int(os.environ["LLAMA_THREADS"]), "kind": "reference",
-            "prefill_tok_s": round(prefill, 2),
-            "sample": f"reference engine (engine_forward_batch + engine_forward, LLAMA_KERNELS=auto) on the {arch} "
-                      f"architecture: {steps} x ({prompt_len}-token prefill + {decode_len} greedy decode tokens); "
-                      f"checkpoint written in {gen_s:.0f} s, loaded in {load_s:.0f} s"}
+            "prefill_tok_s": round(P / prefill_s, 2),
+            "sample": f"reference engine (engine_forward_batch in microbatches of {mb}, then engine_forward; "
+                      f"LLAMA_KERNELS=auto) on the {arch} architecture, the GPU arm's checkpoint and prompt: the "
+                      f"{P}-token prefill once, then {steps} timed steps of {decode_per_step} greedy tokens at "
+                      f"positions {P + warmup * decode_per_step}..{P + total - 1} after {warmup} untimed; checkpoint "
+                      f"ready in {gen_s:.0f} s, loaded in {load_s:.0f} s"}
 
 
 def reference_kernel_bench(bench_args, reps, kernels="auto"):
@@ -338,6 +388,47 @@ def run_profile_request(args):
     print(json.dumps({"profile_request": args.workload, "prompt": P, "tokens": tokens}), flush=True)
 
 
+def parity_block(eng, m, arch, world, rank, prompt, tokens):
+    """The GPU engine against the reference's own run of this workload (tests/golden/bench_golden.npz, made by the
+    reference's engine on the same checkpoint bytes and prompt: tests/golden/make_bench_golden.py): the first 64 greedy
+    tokens of the timed request, the first step's logits (the prompt's last row) bit for bit, and whether every rank
+    holds the same logits. On 2 GPUs the reference's two-socket run (its own tensor-parallel split) is the comparison;
+    it splits over at most two sockets, so 4 and 8 GPUs compare with its one-socket run."""
+    import hashlib
+    logits = m.forward_batch(prompt, 0, eng.LOGITS_LAST)
+    digest = hashlib.sha256(np.ascontiguousarray(logits, np.float32).tobytes()).hexdigest()
+    same = True
+    if world > 1:
+        import torch.distributed as dist
+        digests = [None] * world
+        dist.all_gather_object(digests, digest)
+        same = all(d == digests[0] for d in digests)
+    key = f"{arch}_s2" if world == 2 else f"{arch}_s1"
+    block = {"reduction": m.reduction(), "ranks_logits_identical": same}
+    if not GOLDEN.exists():
+        block["unavailable"] = "tests/golden/bench_golden.npz is missing"
+        return block
+    g = np.load(GOLDEN)
+    if key + "_tokens" not in g.files:
+        block["unavailable"] = f"no reference run {key} in tests/golden/bench_golden.npz"
+        return block
+    ref, margins, maxes, first = (g[key + t] for t in ("_tokens", "_margins", "_maxes", "_first"))
+    n = len(ref)
+    ours = [int(t) for t in tokens[:n]]
+    div = next((i for i, (x, y) in enumerate(zip(ours, ref.tolist())) if x != y), None)
+    if div is None and len(ours) < n:
+        div = len(ours)
+    block.update({
+        "reference": f"{key}: the reference's engine, {g[key + '_env']}" +
+                     ("" if world in (1, 2) else " (its one-socket run: it splits over at most two sockets)"),
+        "tokens_compared": n, "tokens_equal": div is None, "first_divergence_step": div,
+        "ref_margin_at_divergence": None if div is None or div >= n else round(float(margins[div] / maxes[div]), 6),
+        "first_logits_bitwise": bool((np.asarray(logits, np.float32).view(np.int32) == first.view(np.int32)).all()),
+        "first_logits_max_rel_diff": float(np.abs(logits - first).max() / np.abs(first).max()),
+    })
+    return block
+
+
 def run_engine(args):
     import torch
     world, rank, local = dist_setup()
@@ -348,7 +439,10 @@ def run_engine(args):
     P, D = REQUEST[args.workload]
     nccl_id = eng.share_comm_id(rank, world) if world > 1 else None
     t0 = time.perf_counter()
-    m = eng.Engine.random(**a, seed=1, context=a["seq_len"], tp=(rank, world, local, nccl_id) if world > 1 else None)
+    path = bench_checkpoint(args.workload, rank, world)
+    ckpt_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    m = eng.Engine.load(str(path), context=a["seq_len"], tp=(rank, world, local, nccl_id) if world > 1 else None)
     init_s = time.perf_counter() - t0
     prompt = prompt_tokens(P, a["vocab_size"])
     for _ in range(args.warmup):
@@ -368,6 +462,8 @@ def run_engine(args):
     wall = max_over_ranks(world, wall)
     decode = st["decode_tokens"] / (decode_ms / 1e3)
     prefill = st["prefill_tokens"] / (prefill_ms / 1e3)
+
+    parity = parity_block(eng, m, args.workload, world, rank, prompt, tokens)
 
     # End to end through the reference-facing API with host buffers: engine_forward per token (the token and position
     # go host -> device, the vocabulary's logits come back to the host), host argmax, as probe-int8 generate does.
@@ -399,17 +495,15 @@ def run_engine(args):
         "metric": METRIC, "value": round(decode, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round((prefill_ms + decode_ms) / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)",
-        "data": "synthetic: seeded random-init Q8_0 weights N(0,0.02), uniform-random prompt ids",
-        "config": {"workload": f"config {3 if args.workload == '8b' else 2}: {args.workload.upper()} architecture, "
-                               f"{P}-token prefill + {D} greedy tokens per step",
-                   "model": f"llama-{args.workload}-arch", **{k: a[k] for k in ("dim", "hidden_dim", "n_layers",
-                                                                                "n_heads", "n_kv_heads", "vocab_size")},
-                   "context": a["seq_len"], "global_batch": 1, "seq_len": P + D,
-                   "parallelism": f"tp{world}", "l2": f"weights {weights / 1e9:.2f} GB per GPU >> L2"},
+        "data": "synthetic: seeded random-init Q8_0 checkpoint (engine_write_random, N(0,0.02)), uniform-random "
+                "prompt ids; the same bytes the reference's arm loads",
+        "config": engine_config(args.workload, P, D, world),
         "prefill_tok_s": round(prefill, 1), "decode_tok_s": round(decode, 2),
         "decode_ms_per_token": round(decode_ms / max(1, st["decode_tokens"]), 4),
         "decode_weight_gbs": round(weights / (decode_ms / max(1, st["decode_tokens"]) / 1e3) / 1e9, 1),
-        "wall_s": round(wall, 3), "init_s": round(init_s, 2), "tokens_last_step": len(tokens),
+        "wall_s": round(wall, 3), "init_s": round(init_s, 2), "checkpoint_s": round(ckpt_s, 2),
+        "tokens_last_step": len(tokens),
+        "parity": parity,
         "e2e": {"value": round(E / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4 * a["vocab_size"],
                 "path": "engine_forward per token (host token in, host logits out, host argmax)"},
@@ -421,13 +515,23 @@ def run_engine(args):
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = reference_engine_sample(args.workload, steps=1, warmup=1, prompt_len=REF_SAMPLE[0],
-                                                       decode_len=REF_SAMPLE[1])
+        line["cpu_baseline"] = reference_engine_sample(args.workload, steps=2, warmup=1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def engine_config(arch, P, D, world):
+    """The workload's `config` entry, shared by both arms."""
+    a = ARCH[arch]
+    return {"workload": f"config {3 if arch == '8b' else 2}: {arch.upper()} architecture, {P}-token prefill + {D} "
+                        "greedy tokens per request",
+            "model": f"llama-{arch}-arch", **{k: a[k] for k in ("dim", "hidden_dim", "n_layers", "n_heads",
+                                                                 "n_kv_heads", "vocab_size")},
+            "context": a["seq_len"], "global_batch": 1, "seq_len": P + D,
+            "parallelism": f"tp{world}" if world else "cpu", "l2": "weights >> L2: every decode step streams them"}
 
 
 def weight_bytes(a, world, gs=64):
@@ -482,19 +586,16 @@ def run_reference(args):
         run_reference_kernels(args)
         return
     wl = args.workload if args.workload in ARCH else "8b"
-    r = reference_engine_sample(wl, steps=args.steps, warmup=args.warmup, prompt_len=REF_SAMPLE[0],
-                                decode_len=REF_SAMPLE[1])
+    r = reference_engine_sample(wl, steps=args.steps, warmup=args.warmup)
     if "unavailable" in r:
         print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}), flush=True)
         return
-    a = ARCH[wl]
+    P, D = REQUEST[wl]
     line = {"metric": METRIC, "impl": "reference", "value": r["value"], "unit": "tok/s", "n_gpus": 0,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": f"config {3 if wl == '8b' else 2}: {wl.upper()} architecture on the host cores, "
-                                   f"bounded sample per step", "model": f"llama-{wl}-arch",
-                       **{k: a[k] for k in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size")},
-                       "global_batch": 1, "parallelism": "cpu"},
+            "vs_baseline": None, "dtype": "int8 (W8A8, fp32 accumulate)",
+            "data": "synthetic: the GPU arm's seeded checkpoint (engine_write_random) and prompt",
+            "config": engine_config(wl, P, D, 0),
             "prefill_tok_s": r["prefill_tok_s"], "decode_tok_s": r["value"],
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

@@ -95,6 +95,9 @@ int engine_generate(Model *model, const int *prompt, int count, int steps, int *
 int engine_write_random(const char *path, const Config *config, int group_size, unsigned long long seed);
 /* Writes the model (this rank's copy; world 1 only) as a version 2 Q8_0 checkpoint the reference loads. */
 int engine_save(Model *model, const char *path);
+/* The decode step's Wo/W2 reduction, agreed by every rank: "none" (one GPU), "peer_gemv" (inside the GEMV over NVLink
+ * peer memory), "peer_kernel" (a separate peer all-reduce kernel) or "nccl" (ncclAllReduce + add). */
+const char *engine_reduction(Model *model);
 /* The engine's CUDA stream (cudaStream_t), for timing with events on it. */
 void *engine_stream(Model *model);
 /* What engine_generate did since the model was set up or engine_stats_reset: device time of its prefill (the prompt

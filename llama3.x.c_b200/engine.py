@@ -72,6 +72,7 @@ ENGINE_SIGNATURES = {
     "engine_save": (_c.c_int, [_MP, _c.c_char_p]),
     "engine_write_random": (_c.c_int, [_c.c_char_p, _c.POINTER(Config), _c.c_int, _c.c_ulonglong]),
     "engine_stream": (_c.c_void_p, [_MP]),
+    "engine_reduction": (_c.c_char_p, [_MP]),
     "engine_stats": (None, [_MP, _c.POINTER(EngineStats)]),
     "engine_stats_reset": (None, [_MP]),
 }
@@ -260,6 +261,10 @@ class Engine:
 
     def stats_reset(self):
         self.lib.engine_stats_reset(self._m)
+
+    def reduction(self):
+        """engine_reduction: how the decode step joins the Wo/W2 shards (none, peer_gemv, peer_kernel or nccl)."""
+        return self.lib.engine_reduction(self._m).decode()
 
     def kv_stats(self, position, verify=0):
         """engine_kv_stats: the K/V cache accounting of the reference's report (include/runtime.h:111-113)."""

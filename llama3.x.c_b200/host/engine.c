@@ -1252,6 +1252,16 @@ void engine_stats_reset(Model *model) {
   e->captured = e->replayed = 0;
 }
 
+/* The reduction that joins the Wo and W2 shards in a decode step, the same on every rank (agree_on_peer): "none" on
+ * one GPU, "peer_gemv" when it runs inside the GEMV (kd_peer_matmul_q8_add), "peer_kernel" for the separate peer
+ * all-reduce kernel, "nccl" for ncclAllReduce + add. The batched prefill always reduces with ncclAllReduce + add. */
+const char *engine_reduction(Model *model) {
+  Engine *e = model ? model->implementation : NULL;
+  if (!e || e->S == 1)
+    return "none";
+  return e->peer ? (e->reduce_fused ? "peer_gemv" : "peer_kernel") : "nccl";
+}
+
 void *engine_stream(Model *model) {
   Engine *e = model->implementation;
   return e ? e->stream : NULL;

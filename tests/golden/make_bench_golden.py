@@ -52,7 +52,7 @@ L.engine_forward_batch.argtypes = [MP, ctypes.POINTER(ctypes.c_int), ctypes.c_in
 L.engine_forward_batch.restype = ctypes.POINTER(ctypes.c_float)
 L.engine_max_batch.argtypes = [MP]
 model = eng.Model()
-L.engine_load_context(ctypes.byref(model), os.fsencode(path), P + %d)
+L.engine_load_context(ctypes.byref(model), os.fsencode(path), P + __STEPS__)
 V = a["vocab_size"]
 prompt = bench.prompt_tokens(P, V)
 mb = L.engine_max_batch(ctypes.byref(model))
@@ -63,17 +63,17 @@ while i < P:
                                 1 if i + n == P else 0)
     i += n
 toks, margins, maxes, first = [], [], [], None
-for s in range(%d):
+for s in range(__STEPS__):
     x = np.ctypeslib.as_array(lg, (V,)).copy()
     if first is None:
         first = x
     o = np.argsort(x)[::-1][:2]
     toks.append(int(o[0])); margins.append(float(x[o[0]] - x[o[1]])); maxes.append(float(np.abs(x).max()))
-    if s + 1 < %d:
+    if s + 1 < __STEPS__:
         lg = L.engine_forward(ctypes.byref(model), int(o[0]), P + s)
 np.savez(out, tokens=np.array(toks, np.int32), margins=np.array(margins, np.float32),
          maxes=np.array(maxes, np.float32), first=first, max_batch=np.int32(mb))
-''' % (STEPS, STEPS, STEPS)
+'''.replace("__STEPS__", str(STEPS))
 
 
 def main():
