@@ -307,81 +307,99 @@ __global__ void tiled_generic_kernel(const float *q, long long q_ld, const float
 }
 
 // ---- the split variant for one row (decode) -----------------------------------------------------------------------
-// CTA (KV head g, chunk c) of the row at position pos: its nq query heads over the chunk's positions (at most 256).
-// Shared memory: A holds the chunk's K rows, then (once the scores are done) V rows 128..; B holds V rows 0..127; the
-// group's queries; the scores, overwritten by their exponentials; per head the maximum and the exp-sum.
+// A cluster of kSplitCtas CTAs per (KV head g, chunk c) of the row at position pos: CTA k of the cluster loads K rows
+// [k n / 4, (k + 1) n / 4) of the chunk's n <= 256 positions (one bulk copy) and computes their scores for the group's
+// nq heads (a half-warp per score: lane L's FMA chain over the head's 16-float vectors, then the 16-lane tree), which
+// it stores into every CTA of the cluster (distributed shared memory); after a cluster barrier each CTA holds all
+// the chunk's scores, takes the maximum, exp512 and the 16-lane exp-sum per head (the same in every CTA), and runs the
+// P.V chains of its quarter of the head's elements over V[chunk rows][its quarter] (cp.async copies). So each K and
+// V element is read once, and the CTAs of a layer fill the GPU.
+constexpr int kSplitCtas = 4;
+constexpr int kSplitThreads = 128;
+
 __host__ __device__ constexpr size_t split_smem_bytes(int hd) {
-  return ((size_t)kSplitMax * hd + (size_t)(kSplitMax / 2) * hd + (size_t)kMaxNq * hd + (size_t)kMaxNq * kSplitMax +
-          2 * kMaxNq) * sizeof(float) + 2 * sizeof(uint64_t);
+  return ((size_t)(kSplitMax / kSplitCtas) * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)kMaxNq * hd +
+          (size_t)kMaxNq * kSplitMax + 2 * kMaxNq) * sizeof(float) + sizeof(uint64_t);
+}
+
+__device__ __forceinline__ void st_cluster_f32(float *local, unsigned rank, float v) {
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads) split_kernel(const float *q, const float *kc, const float *vc,
-                                                         const int *pos_dev, int pos0, int n_kv, int nq, int seq,
-                                                         int limit, int workers, int cstride, float *part) {
+__global__ void __launch_bounds__(kSplitThreads) split_kernel(const float *q, const float *kc, const float *vc,
+                                                              const int *pos_dev, int pos0, int n_kv, int nq, int seq,
+                                                              int limit, int workers, int cstride, float *part) {
   pdl_wait();
   pdl_launch_dependents();
+  constexpr int QD = HD / kSplitCtas;  // elements of the head this CTA's P.V covers
   extern __shared__ __align__(16) float sm[];
-  float *A = sm, *B = A + kSplitMax * HD, *Q = B + (kSplitMax / 2) * HD, *S = Q + kMaxNq * HD;
+  float *Kq = sm, *Vq = Kq + (kSplitMax / kSplitCtas) * HD, *Q = Vq + kSplitMax * QD, *S = Q + kMaxNq * HD;
   float *hmax = S + kMaxNq * kSplitMax, *hsum = hmax + kMaxNq;
   uint64_t *bar = reinterpret_cast<uint64_t *>(hsum + kMaxNq);
-  const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x, c = blockIdx.y, k = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int P = (pos_dev ? *pos_dev : pos0) + 1;
   if (P < 1 || P > seq)
-    return;  // the merge kernel reports it
+    return;  // every CTA of the cluster leaves here together; the merge kernel reports it
   const int chunks = plan_chunks(P, n_kv, limit, workers);
   if (c >= chunks)
-    return;
-  const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;
-  const int nb = n < kSplitMax / 2 ? n : kSplitMax / 2;  // V rows in B
+    return;  // likewise together
+  const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;  // n <= 256
+  const int k0 = n * k / kSplitCtas, kn = n * (k + 1) / kSplitCtas - k0;  // this CTA's K rows
   const float *Kg = kc + ((long long)g * seq + t0) * HD, *Vg = vc + ((long long)g * seq + t0) * HD;
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    mbar_init(bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bar[0], (unsigned)(n + nb) * HD * sizeof(float));
-    bulk_g2s(A, Kg, (unsigned)n * HD * sizeof(float), &bar[0]);
-    bulk_g2s(B, Vg, (unsigned)nb * HD * sizeof(float), &bar[0]);
+  if (tid == 0 && kn > 0) {
+    mbar_arrive_expect_tx(bar, (unsigned)kn * HD * sizeof(float));
+    bulk_g2s(Kq, Kg + (long long)k0 * HD, (unsigned)kn * HD * sizeof(float), bar);
   }
-  for (int i = tid; i < nq * HD; i += kThreads)
+  // V[chunk rows][k QD .. (k + 1) QD): QD / 4 16-byte pieces a row.
+  for (int i = tid; i < n * (QD / 4); i += kSplitThreads) {
+    const int t = i / (QD / 4), p4 = i - t * (QD / 4);
+    cp_async16(Vq + t * QD + 4 * p4, Vg + (long long)t * HD + k * QD + 4 * p4);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int i = tid; i < nq * HD; i += kSplitThreads)
     Q[i] = q[(long long)g * nq * HD + i];
-  __syncthreads();
-  if (!__syncthreads_and(mbar_wait_bounded(&bar[0], 0))) {
-    if (tid == 0)
-      mbar_wait_bounded(&bar[0], 0);  // let the copies in flight land (bounded) before the CTA leaves
-    return;
-  }
-  // Scores: a half-warp per (head, position), lane L owning lanes L of the head's 16-float vectors.
-  {
-    const int hw = tid >> 4, L = tid & 15, h = hw % nq, step = kThreads / 16 / nq;
-    float qr[HD / 16];
-#pragma unroll
-    for (int v = 0; v < HD / 16; v++)
-      qr[v] = Q[h * HD + 16 * v + L];
+  const bool ok = kn == 0 || __syncthreads_and(mbar_wait_bounded(bar, 0));
+  if (ok) {
+    // Scores of this CTA's positions, stored into every CTA of the cluster.
+    const int hw = tid >> 4, L = tid & 15, halves = kSplitThreads / 16;
     const float divisor = __fsqrt_rn((float)HD);
-    const int iters = (n + step - 1) / step;
+    const int pairs = nq * kn, iters = (pairs + halves - 1) / halves;
     for (int it = 0; it < iters; it++) {
-      const int t = it * step + hw / nq, tc = t < n ? t : 0;
-      float s = 0.0f;
+      const int pr = it * halves + hw, prc = pr < pairs ? pr : 0, h = prc / kn, t = prc - h * kn;
+      float sc = 0.0f;
 #pragma unroll
       for (int v = 0; v < HD / 16; v++)
-        s = __fmaf_rn(qr[v], A[tc * HD + 16 * v + L], s);
-      s = tree16_lanes(s);
-      if (L == 0 && t < n)
-        S[h * kSplitMax + t] = __fdiv_rn(s, divisor);
+        sc = __fmaf_rn(Q[h * HD + 16 * v + L], Kq[t * HD + 16 * v + L], sc);
+      sc = __shfl_sync(0xffffffffu, tree16_lanes(sc), 0, 16);  // the tree's result, to lanes 1.. of the half-warp
+      if (L < kSplitCtas && pr < pairs)  // lane L stores the score into CTA L of the cluster
+        st_cluster_f32(S + h * kSplitMax + k0 + t, (unsigned)L, __fdiv_rn(sc, divisor));
     }
+  } else if (tid == 0) {
+    mbar_wait_bounded(bar, 0);  // let the copy in flight land (bounded) before leaving
   }
-  __syncthreads();
-  // K is consumed: V rows nb.. go into A while the softmax runs.
-  if (tid == 0 && n > nb) {
-    mbar_arrive_expect_tx(&bar[1], (unsigned)(n - nb) * HD * sizeof(float));
-    bulk_g2s(A, Vg + (long long)nb * HD, (unsigned)(n - nb) * HD * sizeof(float), &bar[1]);
+  cluster_sync_all();  // every CTA of the cluster arrives, whatever happened above
+  if (!ok) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    return;
   }
   // Per head (a warp each): the maximum, exp512 in place, the exp-sum in 16 lanes then the tree.
-  for (int h = warp; h < nq; h += kThreads / 32) {
+  for (int h = warp; h < nq; h += kSplitThreads / 32) {
     float *sh = S + h * kSplitMax;
     float mx = -FLT_MAX;
     for (int t = lane; t < n; t += 32)
@@ -400,45 +418,28 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const float *q, const f
     if (lane == 0)
       hmax[h] = mx, hsum[h] = vs;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  // P.V: a chain per (head, element) over the positions in order, V rows 0..nb-1 from B, then nb.. from A.
-  constexpr int kChains = kMaxNq * HD / kThreads;
-  float acc[kChains];
+  // P.V: a chain per (head, element of this CTA's quarter) over the chunk's positions in order.
+  for (int i = tid; i < nq * QD; i += kSplitThreads) {
+    const int h = i / QD, d = i - h * QD;
+    const float *e = S + h * kSplitMax;
+    float acc = 0.0f;
+    int t = 0;
+    for (; t + 8 <= n; t += 8) {
+      float ev[8], vv[8];
 #pragma unroll
-  for (int k = 0; k < kChains; k++)
-    acc[k] = 0.0f;
-  for (int t = 0; t < nb; t++) {
+      for (int u = 0; u < 8; u++)
+        ev[u] = e[t + u], vv[u] = Vq[(t + u) * QD + d];
 #pragma unroll
-    for (int k = 0; k < kChains; k++) {
-      const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
-      if (h < nq)
-        acc[k] = __fmaf_rn(S[h * kSplitMax + t], B[t * HD + d], acc[k]);
+      for (int u = 0; u < 8; u++)
+        acc = __fmaf_rn(ev[u], vv[u], acc);
     }
+    for (; t < n; t++)
+      acc = __fmaf_rn(e[t], Vq[t * QD + d], acc);
+    part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + k * QD + d] = acc;
   }
-  bool ok = true;
-  if (n > nb) {
-    ok = __syncthreads_and(mbar_wait_bounded(&bar[1], 0));
-    for (int t = nb; t < n && ok; t++) {
-#pragma unroll
-      for (int k = 0; k < kChains; k++) {
-        const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
-        if (h < nq)
-          acc[k] = __fmaf_rn(S[h * kSplitMax + t], A[(t - nb) * HD + d], acc[k]);
-      }
-    }
-  }
-  if (!ok) {
-    if (tid == 0)
-      mbar_wait_bounded(&bar[1], 0);
-    return;
-  }
-#pragma unroll
-  for (int k = 0; k < kChains; k++) {
-    const int i = tid + k * kThreads, h = i / HD, d = i - h * HD;
-    if (h < nq)
-      part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + d] = acc[k];
-  }
-  if (tid < nq) {
+  if (k == 0 && tid < nq) {
     float *o = part + ((long long)(g * nq + tid) * cstride + c) * (HD + 2);
     o[HD] = hmax[tid];
     o[HD + 1] = hsum[tid];
@@ -448,13 +449,16 @@ __global__ void __launch_bounds__(kThreads) split_kernel(const float *q, const f
 // ---- the tiled variant for a batch of rows (prefill) ---------------------------------------------------------------
 // CTA (KV head g, group of R rows = whole or part blocks): its query vectors v = (row - first row) * nq + head, at
 // most 64, over the 32-position tiles of the group's causal range. Per tile: K and V rows by bulk copy (two buffers,
-// the next tile's copy in flight), K transposed for the score tiles, scores (2 queries x 4 positions a thread, chains
-// over the head's elements in order), the online softmax per query (a warp per 8 queries, a lane per position), then
-// P.V (4 queries x hd/16 elements a thread, chains over the tile's positions in order). A query whose chunk (its
-// block's plan) changes at a tile writes the finished chunk's partial first and starts again from zero.
+// the next tile's copy in flight), K transposed for the score tiles; then each thread takes 2 queries x 4 positions:
+// their scores (chains over the head's elements in order) and, with the 8 threads that share the queries (8
+// consecutive lanes, 32 positions), the online softmax of the tile: the tile maximum by shuffles, the rescale of the
+// running sum, exp512, and the tile sum in the reference's order (positions j and 16 + j, then the 16-lane tree) by
+// shuffles across the 8 lanes. Every lane of a group keeps the queries' running maximum, sum and chunk. Then P.V
+// (4 queries x hd/16 elements a thread, chains over the tile's positions in order). A query whose chunk (its block's
+// plan) changes at a tile writes the finished chunk's partial first and starts again from zero.
 __host__ __device__ constexpr size_t tiled_smem_bytes(int hd) {
-  return ((size_t)4 * kTile * hd + (size_t)hd * kTile + (size_t)hd * kQV + (size_t)kQV * (kTile + 1) +
-          (size_t)kTile * kQV + 4 * kQV) * sizeof(float) + 2 * sizeof(uint64_t);
+  return ((size_t)4 * kTile * hd + (size_t)hd * kTile + (size_t)hd * kQV + (size_t)kTile * kQV + 2 * kQV) *
+             sizeof(float) + 2 * sizeof(uint64_t);
 }
 
 template <int HD>
@@ -466,12 +470,11 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
   pdl_launch_dependents();
   extern __shared__ __align__(16) float sm[];
   float *Kb = sm, *Vb = Kb + 2 * kTile * HD, *kt = Vb + 2 * kTile * HD, *qs = kt + HD * kTile;
-  float *S = qs + HD * kQV, *P = S + kQV * (kTile + 1);
-  float *ms = P + kTile * kQV, *ls = ms + kQV, *al = ls + kQV;
-  int *cur = reinterpret_cast<int *>(al + kQV);
-  uint64_t *bar = reinterpret_cast<uint64_t *>(cur + kQV);
+  float *P = qs + HD * kQV, *al = P + kTile * kQV;
+  int *fl = reinterpret_cast<int *>(al + kQV);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(fl + kQV);
   constexpr int DB = HD / 16;
-  const int g = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x, tid = threadIdx.x;
   const int base = pos_dev ? *pos_dev : pos0;
   const int rl0 = blockIdx.y * R, nr = min(R, rows - rl0);  // rows of this CTA, from wave row rl0
   if (nr <= 0 || base < 0 || base + row0 + rl0 + nr > seq)
@@ -487,8 +490,6 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
       x = __fmul_rn(q[(long long)(row0 + rl0 + v / nq) * q_ld + (long long)(g * nq + v % nq) * HD + d], scale);
     qs[d * kQV + v] = x;
   }
-  if (tid < kQV)
-    ms[tid] = -FLT_MAX, ls[tid] = 0.0f, al[tid] = 1.0f, cur[tid] = -1;
   if (tid == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
@@ -505,7 +506,20 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
   };
   if (tid == 0)
     issue(0);
-  // This thread's P.V tile: queries 4 qq.., elements DB dg..; its queries' plans.
+  auto out_of = [&](int v, int chunk) {  // partial of query v, chunk `chunk`
+    return part + (((long long)(rl0 + v / nq) * n_heads + g * nq + v % nq) * cstride + chunk) * (HD + 2);
+  };
+  // Score / softmax role: queries 2 qp + i (i = 0, 1), positions 4 pq + j (j = 0..3) of each tile.
+  const int qp = tid >> 3, pq = tid & 7;
+  int vis[2], len[2], cur[2] = {-1, -1};
+  float mrun[2] = {-FLT_MAX, -FLT_MAX}, lrun[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int v = 2 * qp + i, r = row0 + rl0 + v / nq;
+    vis[i] = v < qv ? base + r + 1 : 0;
+    len[i] = tile_plan(r, rblock, m, base, n_kv, limit, workers).len;
+  }
+  // P.V role: queries 4 qq.., elements DB dg...
   const int qq = tid >> 4, dg = tid & 15;
   float acc[4][DB];
 #pragma unroll
@@ -513,9 +527,6 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
 #pragma unroll
     for (int d = 0; d < DB; d++)
       acc[i][d] = 0.0f;
-  auto out_of = [&](int v, int chunk) {  // partial of query v, chunk `chunk`
-    return part + (((long long)(rl0 + v / nq) * n_heads + g * nq + v % nq) * cstride + chunk) * (HD + 2);
-  };
   int failed = -1;  // the tile whose copy did not complete in time
   for (int k = 0; k < ntiles; k++) {
     const int t = k * kTile, cnt = min(kTile, vis_max - t), b = k & 1;
@@ -525,98 +536,94 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
     }
     if (tid == 0 && k + 1 < ntiles)
       issue(k + 1);  // its buffer's last readers finished before the barrier above
-    // K transposed: kt[d][p], zero past the tile's rows.
     for (int i = tid; i < kTile * HD; i += kThreads) {
       const int p = i / HD, d = i - p * HD;
       kt[d * kTile + p] = p < cnt ? Kb[b * kTile * HD + i] : 0.0f;
     }
     __syncthreads();
-    // Scores: queries 2 qp, 2 qp + 1 and positions 4 pq.. of this thread, chains over d in order.
-    {
-      const int qp = tid >> 3, pq = tid & 7;
-      float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
 #pragma unroll 8
-      for (int d = 0; d < HD; d++) {
-        const float2 qv2 = *reinterpret_cast<const float2 *>(qs + d * kQV + 2 * qp);
-        const float4 kv4 = *reinterpret_cast<const float4 *>(kt + d * kTile + 4 * pq);
-        s[0][0] = __fmaf_rn(qv2.x, kv4.x, s[0][0]);
-        s[0][1] = __fmaf_rn(qv2.x, kv4.y, s[0][1]);
-        s[0][2] = __fmaf_rn(qv2.x, kv4.z, s[0][2]);
-        s[0][3] = __fmaf_rn(qv2.x, kv4.w, s[0][3]);
-        s[1][0] = __fmaf_rn(qv2.y, kv4.x, s[1][0]);
-        s[1][1] = __fmaf_rn(qv2.y, kv4.y, s[1][1]);
-        s[1][2] = __fmaf_rn(qv2.y, kv4.z, s[1][2]);
-        s[1][3] = __fmaf_rn(qv2.y, kv4.w, s[1][3]);
-      }
-#pragma unroll
-      for (int i = 0; i < 2; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          S[(2 * qp + i) * (kTile + 1) + 4 * pq + j] = s[i][j];
+    for (int d = 0; d < HD; d++) {
+      const float2 qv2 = *reinterpret_cast<const float2 *>(qs + d * kQV + 2 * qp);
+      const float4 kv4 = *reinterpret_cast<const float4 *>(kt + d * kTile + 4 * pq);
+      s[0][0] = __fmaf_rn(qv2.x, kv4.x, s[0][0]);
+      s[0][1] = __fmaf_rn(qv2.x, kv4.y, s[0][1]);
+      s[0][2] = __fmaf_rn(qv2.x, kv4.z, s[0][2]);
+      s[0][3] = __fmaf_rn(qv2.x, kv4.w, s[0][3]);
+      s[1][0] = __fmaf_rn(qv2.y, kv4.x, s[1][0]);
+      s[1][1] = __fmaf_rn(qv2.y, kv4.y, s[1][1]);
+      s[1][2] = __fmaf_rn(qv2.y, kv4.z, s[1][2]);
+      s[1][3] = __fmaf_rn(qv2.y, kv4.w, s[1][3]);
     }
-    __syncthreads();
-    // Online softmax: a warp per 8 queries, lane = position. A query whose chunk changes writes its finished (max,
-    // sum) first and starts again; al[v] carries the accumulator's factor (1 when the maximum did not move) and
-    // cur[v] the chunk the accumulator belongs to, flush[] the chunk to write out first (or -1).
-    for (int i = 0; i < 8; i++) {
-      const int v = warp * 8 + i;
-      const int r = row0 + rl0 + v / nq, vis = base + r + 1;
-      const int nv = v < qv ? max(0, min(kTile, vis - t)) : 0;
-      float e = 0.0f, alpha = 1.0f;
-      if (nv > 0) {
-        const TilePlan p = tile_plan(r, rblock, m, base, n_kv, limit, workers);
-        const int ck = t / p.len;
-        float mrun = ms[v], lrun = ls[v];
-        if (ck != cur[v]) {
-          if (cur[v] >= 0 && lane == 0) {
-            float *o = out_of(v, cur[v]);
-            o[HD] = mrun;
-            o[HD + 1] = lrun;
+    // Online softmax. The 4 groups of a warp may differ in whether they see the tile, so every shuffle runs in every
+    // lane; the state only moves where the group sees positions.
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int v = 2 * qp + i, nv = max(0, min(kTile, vis[i] - t));
+      const bool live = nv > 0;  // the same in all 8 lanes of the group
+      float alpha = 1.0f;
+      int marker = -2;  // for the P.V threads: -2 nothing, -1 first chunk, else the chunk to write out first
+      if (live) {
+        const int ck = t / len[i];
+        if (ck != cur[i]) {
+          if (cur[i] >= 0 && pq == 0) {
+            float *o = out_of(v, cur[i]);
+            o[HD] = mrun[i];
+            o[HD + 1] = lrun[i];
           }
-          mrun = -FLT_MAX, lrun = 0.0f;
+          marker = cur[i];
+          cur[i] = ck;
+          mrun[i] = -FLT_MAX, lrun[i] = 0.0f;
         }
-        const float s = lane < nv ? S[v * (kTile + 1) + lane] : -FLT_MAX;
-        float tmax = s;
-#pragma unroll
-        for (int off = 16; off; off >>= 1)
-          tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-        if (tmax > mrun) {
-          alpha = exp512_dev(__fsub_rn(mrun, tmax));
-          lrun = __fmul_rn(lrun, alpha);
-          mrun = tmax;
-        }
-        e = lane < nv ? exp512_dev(__fsub_rn(s, mrun)) : 0.0f;
-        const float pair = __fadd_rn(e, __shfl_down_sync(0xffffffffu, e, 16));
-        const float tsum = tree16_lanes(pair);
-        lrun = __fadd_rn(lrun, tsum);
-        __syncwarp();
-        if (lane == 0) {
-          ms[v] = mrun, ls[v] = lrun;
-          // The P.V threads read the old cur[v] (the chunk to write out) and the new one through al and fl.
-          S[v * (kTile + 1) + kTile] = __int_as_float(ck != cur[v] ? cur[v] : -2);  // flush marker
-          cur[v] = ck;
-        }
-      } else if (lane == 0) {
-        S[v * (kTile + 1) + kTile] = __int_as_float(-2);
       }
-      P[lane * kQV + v] = e;
-      if (lane == 0)
-        al[v] = alpha;
+      float tmax = -FLT_MAX;
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        if (4 * pq + j < nv)
+          tmax = fmaxf(tmax, s[i][j]);
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+      if (live && tmax > mrun[i]) {
+        alpha = exp512_dev(__fsub_rn(mrun[i], tmax));
+        lrun[i] = __fmul_rn(lrun[i], alpha);
+        mrun[i] = tmax;
+      }
+      float e[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        e[j] = 4 * pq + j < nv ? exp512_dev(__fsub_rn(s[i][j], mrun[i])) : 0.0f;
+      // Tile sum: pair[p] = e[p] + e[16 + p] (p < 16: lanes pq < 4 hold p, pq + 4 hold 16 + p), t8[p] =
+      // pair[8 + p] + pair[p] (p < 8: lanes pq and pq + 2), t4[p] = t8[4 + p] + t8[p] (lanes 0 and 1), then
+      // (t4[0] + t4[2]) + (t4[1] + t4[3]) in lane 0 of the group.
+      float a[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        a[j] = __fadd_rn(e[j], __shfl_xor_sync(0xffffffffu, e[j], 4));
+        a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], 2));
+        a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], 1));
+      }
+      const float tsum = __shfl_sync(0xffffffffu, __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3])), 0, 8);
+      if (live)
+        lrun[i] = __fadd_rn(lrun[i], tsum);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        P[(4 * pq + j) * kQV + v] = e[j];
+      if (pq == 0)
+        al[v] = alpha, fl[v] = marker;
     }
     __syncthreads();
-    // P.V.
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int v = 4 * qq + i;
-      const int fl = __float_as_int(S[v * (kTile + 1) + kTile]);
-      if (fl >= 0) {  // the query's previous chunk is finished: write it out, start from zero
-        float *o = out_of(v, fl);
+      const int v = 4 * qq + i, f = fl[v];
+      if (f >= 0) {  // the query's previous chunk is finished: write it out, start from zero
+        float *o = out_of(v, f);
 #pragma unroll
         for (int d = 0; d < DB; d++) {
           o[dg * DB + d] = acc[i][d];
           acc[i][d] = 0.0f;
         }
-      } else if (fl == -1) {  // the query's first chunk starts here
+      } else if (f == -1) {  // the query's first chunk starts here
 #pragma unroll
         for (int d = 0; d < DB; d++)
           acc[i][d] = 0.0f;
@@ -627,6 +634,7 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
         acc[i][d] = __fmul_rn(acc[i][d], a);
     }
     const float *Vt = Vb + b * kTile * HD;
+#pragma unroll 4
     for (int p = 0; p < cnt; p++) {
       const float4 pv = *reinterpret_cast<const float4 *>(P + p * kQV + 4 * qq);
       float vv[DB];
@@ -650,16 +658,24 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
     return;
   }
   // The last chunk of every query.
-  if (tid < qv && cur[tid] >= 0) {
-    float *o = out_of(tid, cur[tid]);
-    o[HD] = ms[tid];
-    o[HD + 1] = ls[tid];
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    if (pq == 0 && cur[i] >= 0) {
+      float *o = out_of(2 * qp + i, cur[i]);
+      o[HD] = mrun[i];
+      o[HD + 1] = lrun[i];
+    }
+  __syncthreads();  // fl: the P.V threads read the final chunk of their queries from the score threads' state below
+  if (pq == 0) {
+    fl[2 * qp] = cur[0];
+    fl[2 * qp + 1] = cur[1];
   }
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const int v = 4 * qq + i;
-    if (v < qv && cur[v] >= 0) {
-      float *o = out_of(v, cur[v]);
+    if (v < qv && fl[v] >= 0) {
+      float *o = out_of(v, fl[v]);
 #pragma unroll
       for (int d = 0; d < DB; d++)
         o[dg * DB + d] = acc[i][d];
@@ -736,8 +752,19 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
     } else {
       void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *) =
           hd == 128 ? split_kernel<128> : hd == 64 ? split_kernel<64> : split_kernel<32>;
-      kc_launch_pdl(k, dim3(n_kv, limit), dim3(kThreads), split_smem_bytes(hd), st, q, kc, vc, pos_dev, pos0, n_kv,
-                    nq, seq, limit, workers, limit, w->partial);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(n_kv, limit, kSplitCtas);
+      cfg.blockDim = dim3(kSplitThreads);
+      cfg.dynamicSmemBytes = split_smem_bytes(hd);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
+      attr[1].id = cudaLaunchAttributeClusterDimension;
+      attr[1].val.clusterDim.x = 1, attr[1].val.clusterDim.y = 1, attr[1].val.clusterDim.z = kSplitCtas;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      cudaLaunchKernelEx(&cfg, k, q, kc, vc, pos_dev, pos0, n_kv, nq, seq, limit, workers, limit, w->partial);
     }
     if (!launched(name))
       return false;
