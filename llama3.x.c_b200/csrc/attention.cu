@@ -40,6 +40,7 @@ constexpr int kSplitMax = 256;   // positions of a split chunk at most (attentio
 constexpr int kQV = 64;          // query vectors of a batched CTA
 constexpr int kMaxHd = 256;      // the reference's AVX-512 attention takes head_dim <= 256
 constexpr int kMaxNq = 16;       // query heads per KV head (TILED_MAX_Q)
+constexpr int kMergeChunks = 16; // chunk partials a merge CTA stages at a time
 
 // ---- the reference's arithmetic, one lane ---------------------------------------------------------------------------
 
@@ -131,6 +132,8 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
   pdl_launch_dependents();
   __shared__ float red[kMaxHd / 32];
   __shared__ float vals[kMaxHd];
+  __shared__ float stage[kMergeChunks * (kMaxHd + 2)];
+  __shared__ float wts[kMergeChunks];
   const int h = blockIdx.x, rr = blockIdx.y, r = row0 + rr, d = threadIdx.x;
   const int base = pos_dev ? *pos_dev : pos0;
   const int vis = base + r + 1;  // positions the row sees
@@ -148,18 +151,39 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
     chunks = plan_chunks(vis, n_kv, limit, workers);
     live = chunks;
   }
-  const int slot = hd + 2;
+  const int slot = hd + 2, nt = blockDim.x;
   const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
-  float mx = __ldcg(pb + hd);
-  for (int c = 1; c < live; c++)
+  // The maximum over the chunks (order-free), every chunk's maximum loaded at once.
+  float mx = -FLT_MAX;
+  for (int c = d; c < live; c += nt)
     mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + hd));
+#pragma unroll
+  for (int off = 16; off; off >>= 1)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((d & 31) == 0)
+    red[d >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < nt / 32; w++)
+    mx = fmaxf(mx, red[w]);
+  // Then the chunks in order, kMergeChunks at a time staged in shared memory by one round of parallel loads; each
+  // chunk's weight is taken once, and every thread adds the sums in chunk order.
   float sum = 0.0f, o = 0.0f;
-  for (int c = 0; c < live; c++) {
-    const float *pc = pb + (long long)c * slot;
-    const float w = expf_libc(__fsub_rn(__ldcg(pc + hd), mx));
-    sum = __fadd_rn(sum, __fmul_rn(w, __ldcg(pc + hd + 1)));
-    if (d < hd)
-      o = __fadd_rn(o, __fmul_rn(w, __ldcg(pc + d)));
+  for (int c0 = 0; c0 < live; c0 += kMergeChunks) {
+    const int nc = min(kMergeChunks, live - c0);
+    __syncthreads();  // the previous block's reads are done (and red's, above)
+    for (int i = d; i < nc * slot; i += nt)
+      stage[i] = __ldcg(pb + (long long)c0 * slot + i);
+    __syncthreads();
+    if (d < nc)
+      wts[d] = expf_libc(__fsub_rn(stage[d * slot + hd], mx));
+    __syncthreads();
+    for (int c = 0; c < nc; c++) {
+      const float w = wts[c];
+      sum = __fadd_rn(sum, __fmul_rn(w, stage[c * slot + hd + 1]));
+      if (d < hd)
+        o = __fadd_rn(o, __fmul_rn(w, stage[c * slot + d]));
+    }
   }
   (void)chunks;
   const float v = __fdiv_rn(o, sum);
