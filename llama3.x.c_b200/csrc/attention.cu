@@ -333,23 +333,36 @@ __global__ void tiled_generic_kernel(const float *q, long long q_ld, const float
 // ---- the split variant for one row (decode) -----------------------------------------------------------------------
 // A cluster of kSplitCtas CTAs per (KV head g, chunk c) of the row at position pos: CTA k of the cluster loads K rows
 // [k n / 4, (k + 1) n / 4) of the chunk's n <= 256 positions (one bulk copy) and computes their scores for the group's
-// nq heads (a half-warp per score: lane L's FMA chain over the head's 16-float vectors, then the 16-lane tree), which
-// it stores into every CTA of the cluster (distributed shared memory); after a cluster barrier each CTA holds all
-// the chunk's scores, takes the maximum, exp512 and the 16-lane exp-sum per head (the same in every CTA), and runs the
-// P.V chains of its quarter of the head's elements over V[chunk rows][its quarter] (cp.async copies). So each K and
-// V element is read once, and the CTAs of a layer fill the GPU.
+// nq heads, which it stores into every CTA of the cluster (distributed shared memory); after a cluster barrier each
+// CTA holds all the chunk's scores, takes the maximum, exp512 and the 16-lane exp-sum per head (the same in every
+// CTA), and runs the P.V chains of its quarter of the head's elements over V[chunk rows][its quarter] (cp.async
+// copies). So each K and V element is read once. A cluster walks chunks y, y + gridDim.y, ... (about one wave of
+// clusters). With `tickets`, the CTA that finishes a KV head's last chunk also merges the group's partials (the
+// arithmetic of merge_kernel) and writes its outputs, so no second launch waits on the partials.
 constexpr int kSplitCtas = 4;
-constexpr int kSplitThreads = 128;
+constexpr int kSplitThreads = 256;
+constexpr int kSplitTickets = 256;  // KV heads the fused merge serves (a ticket word each, past the partials)
 
-__host__ __device__ constexpr size_t split_smem_bytes(int hd) {
-  return ((size_t)(kSplitMax / kSplitCtas) * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)kMaxNq * hd +
-          (size_t)kMaxNq * kSplitMax + 2 * kMaxNq) * sizeof(float) + sizeof(uint64_t);
+// Floats before the mbarrier: K quarter [kSplitMax / 4][hd], V quarter [kSplitMax][hd / 4], Q [nq][hd],
+// scores [nq][kSplitMax], the per-head maximum and exp-sum.
+__host__ __device__ constexpr size_t split_smem_floats(int hd, int nq) {
+  return (size_t)(kSplitMax / kSplitCtas) * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)nq * hd +
+         (size_t)nq * kSplitMax + 2 * kMaxNq;
+}
+__host__ __device__ constexpr size_t split_smem_bytes(int hd, int nq) {
+  return split_smem_floats(hd, nq) * sizeof(float) + sizeof(uint64_t);
 }
 
 __device__ __forceinline__ void st_cluster_f32(float *local, unsigned rank, float v) {
   unsigned remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u32(unsigned *local, unsigned rank, unsigned v) {
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -360,114 +373,284 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
+// One butterfly step of the 16-lane tree over W positions at once: the lane keeps the half of its positions whose
+// bit `off` matches its own and adds its partner's copy of them (a + b is b + a, so both lanes of a pair agree with
+// the tree's operand order).
+template <int W>
+__device__ __forceinline__ void tree_step(const float *in, float *outv, int L, int off) {
+  const bool hi = L & off;
+#pragma unroll
+  for (int i = 0; i < W / 2; i++) {
+    const float send = hi ? in[i] : in[W / 2 + i], keep = hi ? in[W / 2 + i] : in[i];
+    outv[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+  }
+}
+
+// Group g's merge by the CTA that finished its last chunk: merge_kernel's arithmetic (the maximum over the chunks, then
+// in chunk order sum += w l and o += w acc with w = expf(m_c - max), then o / sum, then the optional quantization),
+// for the nq heads at once, chunk partials staged in shared memory a block at a time.
 template <int HD>
-__global__ void __launch_bounds__(kSplitThreads) split_kernel(const float *q, const float *kc, const float *vc,
+__device__ void merge_group(float *sm, int sm_floats, const float *part, int g, int nq, int chunks, int cstride,
+                            float *out, int8_t *oq, float *os, int gs) {
+  constexpr int slot = HD + 2, nt = kSplitThreads, kOut = (kMaxNq * HD + nt - 1) / nt;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, outs = nq * HD;
+  float *mxs = sm, *vals = mxs + kMaxNq, *scl = vals + nq * HD, *wts = scl + nq * HD;
+  // At least 8 chunks a block for every shape fast_shape admits (the K and V quarters alone hold 128 hd floats).
+  const int cb = (sm_floats - (kMaxNq + 2 * nq * HD)) / (nq * (slot + 1));
+  float *stage = wts + nq * cb;
+  const float *pg = part + (long long)g * nq * cstride * slot;
+  for (int hh = warp; hh < nq; hh += nt / 32) {
+    float mx = -FLT_MAX;
+    for (int c = lane; c < chunks; c += 32)
+      mx = fmaxf(mx, __ldcg(pg + ((long long)hh * cstride + c) * slot + HD));
+#pragma unroll
+    for (int off = 16; off; off >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0)
+      mxs[hh] = mx;
+  }
+  float sum[kOut], acc[kOut];
+#pragma unroll
+  for (int u = 0; u < kOut; u++)
+    sum[u] = 0.0f, acc[u] = 0.0f;
+  for (int c0 = 0; c0 < chunks; c0 += cb) {
+    const int nc = chunks - c0 < cb ? chunks - c0 : cb;
+    __syncthreads();  // the maxima are in; the previous block's reads are done
+    for (int i = tid; i < nq * nc * slot; i += nt) {
+      const int hh = i / (nc * slot), rem = i - hh * nc * slot;
+      stage[i] = __ldcg(pg + ((long long)hh * cstride + c0) * slot + rem);
+    }
+    __syncthreads();
+    for (int i = tid; i < nq * nc; i += nt) {
+      const int hh = i / nc;
+      wts[i] = expf_libc(__fsub_rn(stage[i * slot + HD], mxs[hh]));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kOut; u++) {
+      const int o = tid + u * nt;
+      if (o < outs) {
+        const int hh = o / HD, d = o - hh * HD;
+        const float *sp = stage + hh * nc * slot, *wp = wts + hh * nc;
+        for (int c = 0; c < nc; c++) {
+          const float w = wp[c];
+          sum[u] = __fadd_rn(sum[u], __fmul_rn(w, sp[c * slot + HD + 1]));
+          acc[u] = __fadd_rn(acc[u], __fmul_rn(w, sp[c * slot + d]));
+        }
+      }
+    }
+  }
+  float *dst = out + (long long)g * outs;
+  int bad = 0;
+#pragma unroll
+  for (int u = 0; u < kOut; u++) {
+    const int o = tid + u * nt;
+    if (o < outs) {
+      const float v = __fdiv_rn(acc[u], sum[u]);
+      dst[o] = v;
+      vals[o] = v;
+      bad |= !isfinite(v);
+    }
+  }
+  if (!oq || gs <= 0 || HD % gs)
+    return;
+  if (__syncthreads_or(bad)) {
+    if (tid == 0)
+      kc_raise(KC_ERR_NONFINITE);
+    return;
+  }
+  // Group maxima of |v| (order-free), a warp per group; scale = max / 127.
+  for (int grp = warp; grp < outs / gs; grp += nt / 32) {
+    float a = 0.0f;
+    for (int i = lane; i < gs; i += 32)
+      a = fmaxf(a, fabsf(vals[grp * gs + i]));
+#pragma unroll
+    for (int off = 16; off; off >>= 1)
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+    if (lane == 0)
+      scl[grp] = __fdiv_rn(a, 127.0f);
+  }
+  __syncthreads();
+  const long long e0 = (long long)g * outs;
+  for (int o = tid; o < outs; o += nt) {
+    const float sc = scl[o / gs];
+    oq[e0 + o] = (int8_t)quantize_value(vals[o], sc);
+    if (o % gs == 0)
+      os[(e0 + o) / gs] = sc;
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q, const float *kc, const float *vc,
                                                               const int *pos_dev, int pos0, int n_kv, int nq, int seq,
-                                                              int limit, int workers, int cstride, float *part) {
+                                                              int limit, int workers, int cstride, float *part,
+                                                              unsigned *tickets, float *out, int8_t *oq, float *os,
+                                                              int gs) {
   pdl_wait();
   pdl_launch_dependents();
   constexpr int QD = HD / kSplitCtas;  // elements of the head this CTA's P.V covers
   extern __shared__ __align__(16) float sm[];
-  float *Kq = sm, *Vq = Kq + (kSplitMax / kSplitCtas) * HD, *Q = Vq + kSplitMax * QD, *S = Q + kMaxNq * HD;
-  float *hmax = S + kMaxNq * kSplitMax, *hsum = hmax + kMaxNq;
-  uint64_t *bar = reinterpret_cast<uint64_t *>(hsum + kMaxNq);
-  const int g = blockIdx.x, c = blockIdx.y, k = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sm_floats = (int)split_smem_floats(HD, nq);
+  float *Kq = sm, *Vq = Kq + (kSplitMax / kSplitCtas) * HD, *Q = Vq + kSplitMax * QD, *S = Q + nq * HD;
+  float *hmax = S + nq * kSplitMax, *hsum = hmax + kMaxNq;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + sm_floats);
+  __shared__ unsigned fails[kSplitCtas];
+  __shared__ int last;
+  static_assert(kSplitCtas == 4, "the failure vote reads four slots");
+  const int g = blockIdx.x, k = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int P = (pos_dev ? *pos_dev : pos0) + 1;
-  if (P < 1 || P > seq)
-    return;  // every CTA of the cluster leaves here together; the merge kernel reports it
+  if (P < 1 || P > seq) {  // every CTA of the cluster leaves here together
+    if (tickets && g == 0 && blockIdx.y == 0 && k == 0 && tid == 0)
+      kc_raise(KC_ERR_BAD_ARGS);  // (without tickets the merge kernel reports it)
+    return;
+  }
   const int chunks = plan_chunks(P, n_kv, limit, workers);
-  if (c >= chunks)
+  if ((int)blockIdx.y >= chunks)
     return;  // likewise together
-  const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;  // n <= 256
-  const int k0 = n * k / kSplitCtas, kn = n * (k + 1) / kSplitCtas - k0;  // this CTA's K rows
-  const float *Kg = kc + ((long long)g * seq + t0) * HD, *Vg = vc + ((long long)g * seq + t0) * HD;
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  if (tid == 0 && kn > 0) {
-    mbar_arrive_expect_tx(bar, (unsigned)kn * HD * sizeof(float));
-    bulk_g2s(Kq, Kg + (long long)k0 * HD, (unsigned)kn * HD * sizeof(float), bar);
-  }
-  // V[chunk rows][k QD .. (k + 1) QD): QD / 4 16-byte pieces a row.
-  for (int i = tid; i < n * (QD / 4); i += kSplitThreads) {
-    const int t = i / (QD / 4), p4 = i - t * (QD / 4);
-    cp_async16(Vq + t * QD + 4 * p4, Vg + (long long)t * HD + k * QD + 4 * p4);
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
   for (int i = tid; i < nq * HD; i += kSplitThreads)
     Q[i] = q[(long long)g * nq * HD + i];
-  const bool ok = kn == 0 || __syncthreads_and(mbar_wait_bounded(bar, 0));
-  if (ok) {
-    // Scores of this CTA's positions, stored into every CTA of the cluster.
-    const int hw = tid >> 4, L = tid & 15, halves = kSplitThreads / 16;
-    const float divisor = __fsqrt_rn((float)HD);
-    const int pairs = nq * kn, iters = (pairs + halves - 1) / halves;
-    for (int it = 0; it < iters; it++) {
-      const int pr = it * halves + hw, prc = pr < pairs ? pr : 0, h = prc / kn, t = prc - h * kn;
-      float sc = 0.0f;
-#pragma unroll
-      for (int v = 0; v < HD / 16; v++)
-        sc = __fmaf_rn(Q[h * HD + 16 * v + L], Kq[t * HD + 16 * v + L], sc);
-      sc = __shfl_sync(0xffffffffu, tree16_lanes(sc), 0, 16);  // the tree's result, to lanes 1.. of the half-warp
-      if (L < kSplitCtas && pr < pairs)  // lane L stores the score into CTA L of the cluster
-        st_cluster_f32(S + h * kSplitMax + k0 + t, (unsigned)L, __fdiv_rn(sc, divisor));
-    }
-  } else if (tid == 0) {
-    mbar_wait_bounded(bar, 0);  // let the copy in flight land (bounded) before leaving
-  }
-  cluster_sync_all();  // every CTA of the cluster arrives, whatever happened above
-  if (!ok) {
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    return;
-  }
-  // Per head (a warp each): the maximum, exp512 in place, the exp-sum in 16 lanes then the tree.
-  for (int h = warp; h < nq; h += kSplitThreads / 32) {
-    float *sh = S + h * kSplitMax;
-    float mx = -FLT_MAX;
-    for (int t = lane; t < n; t += 32)
-      mx = fmaxf(mx, sh[t]);
-#pragma unroll
-    for (int off = 16; off; off >>= 1)
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float vs = 0.0f;
-    if (lane < 16)
-      for (int t = lane; t < n; t += 16) {
-        const float e = exp512_dev(__fsub_rn(sh[t], mx));
-        sh[t] = e;
-        vs = __fadd_rn(vs, e);
-      }
-    vs = tree16_lanes(vs);
-    if (lane == 0)
-      hmax[h] = mx, hsum[h] = vs;
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  // P.V: a chain per (head, element of this CTA's quarter) over the chunk's positions in order.
-  for (int i = tid; i < nq * QD; i += kSplitThreads) {
-    const int h = i / QD, d = i - h * QD;
-    const float *e = S + h * kSplitMax;
-    float acc = 0.0f;
-    int t = 0;
-    for (; t + 8 <= n; t += 8) {
-      float ev[8], vv[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        ev[u] = e[t + u], vv[u] = Vq[(t + u) * QD + d];
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        acc = __fmaf_rn(ev[u], vv[u], acc);
+  // The cluster walks chunks blockIdx.y, blockIdx.y + gridDim.y, ...; every CTA of it takes the same steps.
+  unsigned phase = 0;
+  for (int c = blockIdx.y; c < chunks; c += gridDim.y) {
+    const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;  // <= 256
+    const int k0 = n * k / kSplitCtas, kn = n * (k + 1) / kSplitCtas - k0;  // this CTA's K rows
+    const float *Kg = kc + ((long long)g * seq + t0) * HD, *Vg = vc + ((long long)g * seq + t0) * HD;
+    if (tid == 0 && kn > 0) {
+      mbar_arrive_expect_tx(bar, (unsigned)kn * HD * sizeof(float));
+      bulk_g2s(Kq, Kg + (long long)k0 * HD, (unsigned)kn * HD * sizeof(float), bar);
     }
-    for (; t < n; t++)
-      acc = __fmaf_rn(e[t], Vq[t * QD + d], acc);
-    part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + k * QD + d] = acc;
+    // V[chunk rows][k QD .. (k + 1) QD): QD / 4 16-byte pieces a row.
+    for (int i = tid; i < n * (QD / 4); i += kSplitThreads) {
+      const int t = i / (QD / 4), p4 = i - t * (QD / 4);
+      cp_async16(Vq + t * QD + 4 * p4, Vg + (long long)t * HD + k * QD + 4 * p4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    bool ok = true;
+    if (kn > 0) {
+      ok = __syncthreads_and(mbar_wait_bounded(bar, phase));
+      phase ^= 1u;
+    }
+    if (ok) {
+      // Scores: a warp per (16 positions, 2 heads), a half-warp per head, lane L the reference's lane L (its FMA
+      // chain over elements 16 v + L); the 16-lane tree of all 16 positions runs as one butterfly, after which lane
+      // L holds position L's score.
+      const int hw = lane >> 4, L = lane & 15, groups = (kn + 15) >> 4, pairs = (nq + 1) >> 1;
+      const float divisor = __fsqrt_rn((float)HD);
+      for (int task = warp; task < groups * pairs; task += kSplitThreads / 32) {
+        const int grp = task % groups, h = (task / groups) * 2 + hw, hc = h < nq ? h : nq - 1;
+        float qv[HD / 16];
+#pragma unroll
+        for (int v = 0; v < HD / 16; v++)
+          qv[v] = Q[hc * HD + 16 * v + L];
+        int row[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          row[j] = (grp * 16 + j < kn ? grp * 16 + j : kn - 1) * HD + L;
+        float a16[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          a16[j] = 0.0f;
+#pragma unroll
+        for (int v = 0; v < HD / 16; v++)
+#pragma unroll
+          for (int j = 0; j < 16; j++)
+            a16[j] = __fmaf_rn(qv[v], Kq[row[j] + 16 * v], a16[j]);
+        float t8[8], t4[4], t2[2], t1[1];
+        tree_step<16>(a16, t8, L, 8);
+        tree_step<8>(t8, t4, L, 4);
+        tree_step<4>(t4, t2, L, 2);
+        tree_step<2>(t2, t1, L, 1);
+        const int t = grp * 16 + L;
+        if (h < nq && t < kn) {
+          const float sc = __fdiv_rn(t1[0], divisor);
+#pragma unroll
+          for (int r = 0; r < kSplitCtas; r++)
+            st_cluster_f32(S + h * kSplitMax + k0 + t, (unsigned)r, sc);
+        }
+      }
+    } else if (tid == 0) {
+      mbar_wait_bounded(bar, phase ^ 1u);  // let the copy in flight land (bounded) before leaving
+    }
+    // Each CTA's verdict (uniform within it) into slot k of every CTA, so that all of them see one failure.
+    if (tid < kSplitCtas)
+      st_cluster_u32(fails + k, (unsigned)tid, ok ? 0u : 1u);
+    cluster_sync_all();  // every CTA of the cluster arrives, whatever happened above
+    if (fails[0] | fails[1] | fails[2] | fails[3]) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      break;  // the whole cluster stops in the same iteration (the error is raised)
+    }
+    // Per head (a warp each): the maximum, exp512 in place, the exp-sum in 16 lanes then the tree.
+    for (int h = warp; h < nq; h += kSplitThreads / 32) {
+      float *sh = S + h * kSplitMax;
+      float mx = -FLT_MAX;
+      for (int t = lane; t < n; t += 32)
+        mx = fmaxf(mx, sh[t]);
+#pragma unroll
+      for (int off = 16; off; off >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      for (int t = lane; t < n; t += 32)
+        sh[t] = exp512_dev(__fsub_rn(sh[t], mx));
+      __syncwarp();
+      float vs = 0.0f;
+      if (lane < 16)
+        for (int t = lane; t < n; t += 16)
+          vs = __fadd_rn(vs, sh[t]);
+      vs = tree16_lanes(vs);
+      if (lane == 0)
+        hmax[h] = mx, hsum[h] = vs;
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // P.V: a chain per (head, element of this CTA's quarter) over the chunk's positions in order.
+    for (int i = tid; i < nq * QD; i += kSplitThreads) {
+      const int h = i / QD, d = i - h * QD;
+      const float *e = S + h * kSplitMax;
+      float acc = 0.0f;
+      int t = 0;
+      for (; t + 8 <= n; t += 8) {
+        float ev[8], vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          ev[u] = e[t + u], vv[u] = Vq[(t + u) * QD + d];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          acc = __fmaf_rn(ev[u], vv[u], acc);
+      }
+      for (; t < n; t++)
+        acc = __fmaf_rn(e[t], Vq[t * QD + d], acc);
+      part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + k * QD + d] = acc;
+    }
+    if (k == 0 && tid < nq) {
+      float *o = part + ((long long)(g * nq + tid) * cstride + c) * (HD + 2);
+      o[HD] = hmax[tid];
+      o[HD + 1] = hsum[tid];
+    }
+    // The scores, K and V buffers are refilled by the cluster's next chunk: every CTA is done with them first.
+    cluster_sync_all();
   }
-  if (k == 0 && tid < nq) {
-    float *o = part + ((long long)(g * nq + tid) * cstride + c) * (HD + 2);
-    o[HD] = hmax[tid];
-    o[HD + 1] = hsum[tid];
+  if (!tickets)
+    return;
+  // Every CTA that took chunks counts them (after a failure too, so the count stays whole); the one that completes
+  // the KV head's 4 x chunks merges it and resets the ticket for the next call.
+  const unsigned mine = (unsigned)((chunks - 1 - (int)blockIdx.y) / (int)gridDim.y + 1);
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned before = atomicAdd(tickets + g, mine);
+    last = before + mine == (unsigned)(kSplitCtas * chunks);
+    if (last) {
+      tickets[g] = 0u;
+      __threadfence();
+    }
   }
+  __syncthreads();
+  if (last)
+    merge_group<HD>(sm, sm_floats, part, g, nq, chunks, cstride, out, oq, os, gs);
 }
 
 // ---- the tiled variant for a batch of rows (prefill) ---------------------------------------------------------------
@@ -733,7 +916,7 @@ bool smem_ready(int hd) {
   const void *tiled = hd == 128  ? reinterpret_cast<const void *>(tiled_kernel<128>)
                       : hd == 64 ? reinterpret_cast<const void *>(tiled_kernel<64>)
                                  : reinterpret_cast<const void *>(tiled_kernel<32>);
-  return kc_allow_smem(split, (int)split_smem_bytes(hd)) == cudaSuccess &&
+  return kc_allow_smem(split, (int)split_smem_bytes(hd, kMaxNq)) == cudaSuccess &&
          kc_allow_smem(tiled, (int)tiled_smem_bytes(hd)) == cudaSuccess;
 }
 
@@ -742,6 +925,21 @@ int tiled_rows_per_cta(int nq) {
   const int rb = tile_rblock(nq), blocks = kQV / (rb * nq);
   return (blocks < 1 ? 1 : blocks) * rb;
 }
+
+// Rows of partials the work holds: the rows asked for, capped by a 512 MiB budget (longer batches run in waves),
+// never less than one.
+int work_rows(int n_heads, int head_dim, int seq_len, int rows) {
+  const size_t per_row = (size_t)n_heads * limit_for(seq_len) * (head_dim + 2) * sizeof(float);
+  const size_t fit = ((size_t)512 << 20) / per_row;
+  return (int)(fit < 1 ? 1 : fit < (size_t)rows ? fit : (size_t)rows);
+}
+
+size_t partial_bytes(int n_heads, int head_dim, int seq_len, int rows) {
+  return (size_t)work_rows(n_heads, head_dim, seq_len, rows) * n_heads * limit_for(seq_len) * (head_dim + 2) *
+         sizeof(float);
+}
+
+unsigned *work_tickets(AttentionWork *w) { return reinterpret_cast<unsigned *>(w->partial + w->capacity); }
 
 // One row (decode) or a batch of rows of attention into out (row stride out_ld), optionally quantized into oq/os.
 bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, float *os, const float *q,
@@ -768,34 +966,50 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
   const int slot = hd + 2, merge_threads = (hd + 31) / 32 * 32;
   cudaStream_t st = kc_stream();
   if (rows == 1) {
+    bool merged = false;  // the split kernel merged the partials itself
     if ((size_t)n_heads * limit * slot > w->capacity)
       return kc_fail("%s: attention work too small", name);
     if (!fast) {
       kc_launch_pdl(split_generic_kernel, dim3(n_heads), dim3(limit), 0, st, q, kc, vc, pos_dev, pos0, n_heads, n_kv,
                     hd, seq, limit, workers, limit, w->partial);
     } else {
-      void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *) =
+      void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *,
+                unsigned *, float *, int8_t *, float *, int) =
           hd == 128 ? split_kernel<128> : hd == 64 ? split_kernel<64> : split_kernel<32>;
       cudaLaunchConfig_t cfg = {};
+      // About one wave of clusters (as many as fit at once): each walks the chunks y, y + gridDim.y, ... of the row.
+      int clusters = 0;
       cfg.gridDim = dim3(n_kv, limit, kSplitCtas);
       cfg.blockDim = dim3(kSplitThreads);
-      cfg.dynamicSmemBytes = split_smem_bytes(hd);
+      cfg.dynamicSmemBytes = split_smem_bytes(hd, nq);
       cfg.stream = st;
       cudaLaunchAttribute attr[2];
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
-      attr[1].id = cudaLaunchAttributeClusterDimension;
-      attr[1].val.clusterDim.x = 1, attr[1].val.clusterDim.y = 1, attr[1].val.clusterDim.z = kSplitCtas;
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = kSplitCtas;
       cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        clusters = kc_device_sms() / kSplitCtas;
+      }
+      const int per_kv = clusters / n_kv;
+      cfg.gridDim.y = per_kv < 1 ? 1 : per_kv < limit ? per_kv : limit;
+      unsigned *tickets = n_kv <= kSplitTickets ? work_tickets(w) : nullptr;
+      if (tickets)
+        merged = true;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
       cfg.numAttrs = 2;
-      cudaLaunchKernelEx(&cfg, k, q, kc, vc, pos_dev, pos0, n_kv, nq, seq, limit, workers, limit, w->partial);
+      cudaLaunchKernelEx(&cfg, k, q, kc, vc, pos_dev, pos0, n_kv, nq, seq, limit, workers, limit, w->partial, tickets,
+                         out, fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, gs);
     }
     if (!launched(name))
       return false;
-    kc_launch_pdl(merge_kernel, dim3(n_heads, 1), dim3(merge_threads), 0, st, out, out_ld,
+    if (!merged)
+      kc_launch_pdl(merge_kernel, dim3(n_heads, 1), dim3(merge_threads), 0, st, out, out_ld,
                   fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
-                  pos_dev, pos0, 0, 1, 0, n_heads, n_kv, hd, seq, limit, workers, limit, gs);
-    if (!launched(name))
+                    pos_dev, pos0, 0, 1, 0, n_heads, n_kv, hd, seq, limit, workers, limit, gs);
+    if (!merged && !launched(name))
       return false;
   } else {
     // Waves of rows whose partials fit the work; the chunk stride is the most chunks a row of the wave can have.
@@ -849,14 +1063,7 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
   return true;
 }
 
-// Rows of partials the work holds: the rows asked for, capped by a 512 MiB budget (longer batches run in waves),
-// never less than one.
-int work_rows(int n_heads, int head_dim, int seq_len, int rows) {
-  const size_t per_row = (size_t)n_heads * limit_for(seq_len) * (head_dim + 2) * sizeof(float);
-  const size_t fit = ((size_t)512 << 20) / per_row;
-  return (int)(fit < 1 ? 1 : fit < (size_t)rows ? fit : (size_t)rows);
-}
-
+// The merge tickets past the partials (kSplitTickets words, zeroed by k_attention_init_rows).
 }  // namespace
 
 extern "C" {
@@ -864,8 +1071,7 @@ extern "C" {
 size_t k_attention_bytes_rows(int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows) {
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || seq_len <= 0 || rows <= 0)
     return 0;
-  return (size_t)work_rows(n_heads, head_dim, seq_len, rows) * n_heads * limit_for(seq_len) * (head_dim + 2) *
-         sizeof(float);
+  return partial_bytes(n_heads, head_dim, seq_len, rows) + kSplitTickets * sizeof(unsigned);
 }
 
 void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int head_dim, int seq_len, int rows,
@@ -892,7 +1098,14 @@ void k_attention_init_rows(AttentionWork *work, int n_heads, int n_kv_heads, int
   work->head_dim = head_dim;
   work->workers = 1;
   work->external = external;
-  work->capacity = bytes / sizeof(float);
+  work->capacity = partial_bytes(n_heads, head_dim, seq_len, rows) / sizeof(float);
+  if (cudaMemsetAsync(work_tickets(work), 0, kSplitTickets * sizeof(unsigned), kc_stream()) != cudaSuccess) {
+    cudaGetLastError();
+    if (!external)
+      cudaFree(base);
+    memset(work, 0, sizeof(*work));
+    kc_fail("k_attention_init_rows: cannot clear the merge tickets");
+  }
 }
 
 void k_attention_free(AttentionWork *work) {
