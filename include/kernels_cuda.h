@@ -216,15 +216,19 @@ void k_rmsnorm_q8_rows(int8_t *q, float *s, float *out, const float *x, size_t l
 /* ---- K/V cache and attention (include/kernels.h:126-179) --------------------------------------------------------- */
 /* The cache is the reference's head-major layout (LLAMA_KV_LAYOUT=head, its default): one layer's K or V cache is
  * [n_kv_heads][seq_len][head_dim] fp32. AttentionWork holds the split-K partials in device memory (the reference keeps
- * them in host memory); head_dim 32, 64 or 128, at most 8 query heads per KV head. `memory` passed to
- * k_attention_init_rows is device memory of k_attention_bytes_rows bytes, or NULL to let the call allocate it
- * (k_attention_free releases only what it allocated). One row runs the split-K decode kernel, a batch the flash-style
- * prefill kernel; both agree with the reference's attention within fp32 rounding, and with each other (a batched row
- * against the same position alone) to the same degree, not bitwise. `att` is the reference's host scratch and is
- * ignored. AttentionWork has the reference's layout (include/kernels.h:127-132), so a caller compiled against the
- * reference's header passes a struct this library reads field for field: partial (device memory), max_chunks (the
- * 64-position splits of the longest context it serves), n_heads and head_dim (checked against each call), workers
- * (always 1: one GPU does the work of the reference's team), external and capacity (floats in partial). */
+ * them in host memory); head_dim 32, 64 or 128 with at most 16 query heads per KV head take the fast kernels, other
+ * shapes up to head_dim 256 a slower restatement of the same arithmetic. `memory` passed to k_attention_init_rows is
+ * device memory of k_attention_bytes_rows bytes (the partials, then 1 KiB of merge tickets that the call zeroes on
+ * the library's stream), or NULL to let the call allocate it (k_attention_free releases only what it allocated).
+ * One row runs the split decode kernel, which is bitwise the reference's AVX-512 decode attention
+ * (attention_chunk_avx512 + merge_chunks, src/attention.c) with the chunk plan of a team of one (256-position
+ * chunks); a batch runs the tiled kernel, bitwise its batched attention (attention_tiled_avx512, src/attention.c:233-344,
+ * planned as at src/attention.c:1078-1085).
+ * `att` is the reference's host scratch and is ignored. AttentionWork has the reference's layout
+ * (include/kernels.h:127-132), so a caller compiled against the reference's header passes a struct this library
+ * reads field for field: partial (device memory), max_chunks (the 256-position splits of the longest context it
+ * serves), n_heads and head_dim (checked against each call), workers (always 1: one GPU does the work of the
+ * reference's team), external and capacity (floats of partials in partial). */
 typedef struct {
   float *partial;
   int max_chunks, n_heads, head_dim, workers;
@@ -284,8 +288,9 @@ int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, c
 /* Same arguments and results as k_gemm_q8, but the tensor-core path stages its transposed activation scales in a
  * fixed array compiled into the library (K_GEMM_Q8_NOALLOC_MAX_SCALES floats, 4 MiB, one per device) instead of a
  * buffer it allocates: (k / gs) * round_up(m, 4) must not exceed that, or the call is rejected. The first call on a
- * device looks the array's address up (cudaGetSymbolAddress, with that device current), so make it once during setup,
- * before any stream capture.
+ * device looks the array's address up (cudaGetSymbolAddress, with that device current, under a lock), so make it once
+ * during setup, before any stream capture. The address is kept for the life of the process: after cudaDeviceReset
+ * the module loads again elsewhere, so do not call this entry point on a device that was reset.
  * Nothing needs to start at zero: every call rewrites the whole part of the array it reads. Calls on one device share
  * the array, so two calls in flight at once (different streams or threads) race; issue them on one stream.
  * Returns 0 on success, -1 when the arguments are rejected (kc_last_error says why, under KC_FAIL_RETURN). */

@@ -54,17 +54,18 @@ static bool launched(int rc, const char *what) {
 }
 
 int kc_device_sms() {
-  static int sms[64];
+  static std::atomic<int> sms[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64)
     return 148;
-  if (!sms[dev]) {
-    int v = 0;
+  int v = sms[dev].load(std::memory_order_relaxed);
+  if (!v) {  // a race only repeats the same query
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    sms[dev] = v > 0 ? v : 148;
+    v = v > 0 ? v : 148;
+    sms[dev].store(v, std::memory_order_relaxed);
   }
-  return sms[dev];
+  return v;
 }
 
 bool kc_pdl_enabled() { return pdl_on; }
@@ -187,28 +188,23 @@ static bool weight_ok(const char *name, K8Weight w) {
   return true;
 }
 
-static void gemv(const char *name, const KcGemvSeg *segs, int nseg, const K8Input *x, size_t ld, int n, int gs,
+// Checks and launches one GEMV; false (the reason recorded) when it did neither.
+static bool gemv(const char *name, const KcGemvSeg *segs, int nseg, const K8Input *x, size_t ld, int n, int gs,
                  int kind) {
   if (!gemv_shape_ok(name, x, ld, n, gs))
-    return;
+    return false;
   for (int i = 0; i < nseg; i++) {
-    if (segs[i].d < 0) {
-      kc_fail("%s: negative row count", name);
-      return;
-    }
-    if (segs[i].d > 0 && !segs[i].out) {
-      kc_fail("%s: missing output", name);
-      return;
-    }
+    if (segs[i].d < 0)
+      return kc_fail("%s: negative row count", name);
+    if (segs[i].d > 0 && !segs[i].out)
+      return kc_fail("%s: missing output", name);
     if (!weight_ok(name, K8Weight{segs[i].wq, segs[i].ws}) ||
         (kind == KC_SWIGLU && !weight_ok(name, K8Weight{segs[i].w3q, segs[i].w3s})))
-      return;
+      return false;
   }
-  if (!x->q) {  // W8A32
-    launched(kc_launch_gemv_w8a32(segs, nseg, x->f, n, (long long)ld, gs, kind, tl_stream), name);
-    return;
-  }
-  launched(kc_launch_gemv(segs, nseg, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
+  if (!x->q)  // W8A32
+    return launched(kc_launch_gemv_w8a32(segs, nseg, x->f, n, (long long)ld, gs, kind, tl_stream), name);
+  return launched(kc_launch_gemv(segs, nseg, x->q, x->s, n, (long long)ld, gs, kind, tl_stream, 0), name);
 }
 
 void k_matmul_q8(float *out, const K8Input *x, K8Weight w, int n, int d, int gs) {
@@ -417,7 +413,7 @@ static bool gemm_args_ok(const char *name, const int8_t *xq, const float *xs, in
   return true;
 }
 
-static void gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
+static bool gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int gs, const GemmQ8Segment *segments,
                            int count) {
   // One row-kernel launch per activation row and segment.
   int groups = k / gs;
@@ -426,9 +422,11 @@ static void gemm_rows_dp4a(const int8_t *xq, const float *xs, int m, int k, int 
       const GemmQ8Segment &g = segments[s];
       KcGemvSeg seg = {g.c + (size_t)r * g.ldc, g.w.q, g.w.s, g.w3.q, g.w3.s, g.n};
       K8Input in = {xq + (size_t)r * k, xs + (size_t)r * groups, nullptr};
-      gemv("k_gemm_q8", &seg, 1, &in, (size_t)k, k, gs, kc_kind_of(g.kind));
+      if (!gemv("k_gemm_q8", &seg, 1, &in, (size_t)k, k, gs, kc_kind_of(g.kind)))
+        return false;
     }
   }
+  return true;
 }
 
 static int to_kc_segs(const GemmQ8Segment *segments, int count, KcGemmSeg *out) {
@@ -442,12 +440,14 @@ static int to_kc_segs(const GemmQ8Segment *segments, int count, KcGemmSeg *out) 
 // Scratch for the transposed activation scales of k_gemm_q8, one buffer per device, grown on demand (the only
 // allocation the GEMM entry points make; the engine passes its own transposed scales instead).
 static float *gemm_scratch(size_t floats) {
+  static std::mutex mu;
   static float *buf[64];
   static size_t cap[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64)
     return nullptr;
+  std::lock_guard<std::mutex> hold(mu);
   if (cap[dev] < floats) {
     if (buf[dev])
       cudaFree(buf[dev]);
@@ -567,13 +567,19 @@ int k_gemm_q8_dots_test(int32_t *dots, const int8_t *xq, int m, int k, int gs, c
 // library's device image (4 MiB per device); every call overwrites the [K/64][round_up(m, 4)] prefix it reads.
 static __device__ __align__(256) float noalloc_scales[K_GEMM_Q8_NOALLOC_MAX_SCALES];
 
+// The array's address on the current device, looked up once per device under a lock (two host threads making their
+// first call at once both see one lookup). The cache assumes the device's context lives as long as the process: after
+// cudaDeviceReset the module is loaded again at another address, so a process that resets a device must not call this
+// entry point afterwards.
 static float *noalloc_scales_address() {
+  static std::mutex mu;
   static float *addr[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     kc_fail("k_gemm_q8_noalloc: no current CUDA device");
     return nullptr;
   }
+  std::lock_guard<std::mutex> hold(mu);
   if (!addr[dev]) {
     void *p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scales);
@@ -593,11 +599,8 @@ int k_gemm_q8_noalloc(const int8_t *xq, const float *xs, int m, int k, int gs, c
   if (m == 0 || k == 0)
     return 0;
   const Q8GemmBackend backend = pick(xq, m, k, gs, segments, count);
-  if (backend == Q8_GEMM_GPU_DP4A) {  // one GEMV launch per row: no scratch at all
-    kc_clear_error();
-    gemm_rows_dp4a(xq, xs, m, k, gs, segments, count);
-    return kc_last_error()[0] ? -1 : 0;
-  }
+  if (backend == Q8_GEMM_GPU_DP4A)  // one GEMV launch per row: no scratch at all
+    return gemm_rows_dp4a(xq, xs, m, k, gs, segments, count) ? 0 : -1;
   const size_t need = kc_gemm_xst_floats(m, k / gs);
   if (need > (size_t)K_GEMM_Q8_NOALLOC_MAX_SCALES) {
     kc_fail("k_gemm_q8_noalloc: m=%d k=%d needs %zu scale floats, above the fixed %d", m, k, need,

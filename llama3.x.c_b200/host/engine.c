@@ -552,7 +552,16 @@ static size_t add_checked(size_t a, size_t b, int *of) {
   return a + b;
 }
 
+/* tensor_bytes (src/runtime.c:170-177): scales follow the bytes unpadded, so a count that is not a multiple of gs and
+ * of 4 would leave them unaligned; the reference refuses such a file with this message. */
 static size_t q8_bytes(size_t count, int gs, int *of) {
+  if (*of)
+    return 0;
+  if (count % (size_t)gs || count % sizeof(float)) {
+    *of = 1;
+    efail("unsupported INT8 tensor alignment/group size: %zu elements", count);
+    return 0;
+  }
   return add_checked(count, mul_checked(count / (size_t)gs, sizeof(float), of), of);
 }
 

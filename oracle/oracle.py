@@ -27,10 +27,21 @@ def _p(a, t):
     return a.ctypes.data_as(t)
 
 
+def reference_checkout():
+    """The reference's sources: $LLAMA3X_REFERENCE, else a checkout named `reference` beside this repository; None
+    when neither holds src/gemv.c."""
+    import os
+    for cand in (os.environ.get("LLAMA3X_REFERENCE"), HERE.parent.parent / "reference"):
+        if cand and (Path(cand) / "src" / "gemv.c").exists():
+            return Path(cand)
+    return None
+
+
 def build():
-    """Compile liboracle.so (and the reference under _ref/ when its sources exist) with oracle/Makefile."""
+    """Compile liboracle.so (and the reference under _ref/ when its sources are found) with oracle/Makefile."""
     import subprocess
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    ref = reference_checkout()
+    subprocess.run(["make", "-s", "-C", str(HERE)] + ([f"REF={ref}"] if ref else []), check=True)
 
 
 _lib = None

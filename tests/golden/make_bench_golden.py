@@ -2,7 +2,7 @@
 its sources by oracle/Makefile: src/engine.c + src/runq.c + its kernels) on the benchmark workloads, for the parity
 checks of bench.py and tests/test_bench_parity_gpu.py.
 
-    make -C oracle && python tests/golden/make_bench_golden.py
+    make -C oracle REF=REFERENCE_CHECKOUT && python tests/golden/make_bench_golden.py
 
 Workloads (BASELINE configs 3 and 2): the seeded random-init Q8_0 checkpoints (seed 1) of the 8B and 1B
 architectures written by oracle/model_file.py (the GPU side writes the same bytes with engine_write_random), the
@@ -78,7 +78,7 @@ np.savez(out, tokens=np.array(toks, np.int32), margins=np.array(margins, np.floa
 
 def main():
     if not (ROOT / "oracle" / "_ref" / "libllama_ref_engine.so").exists():
-        raise SystemExit("oracle/_ref/libllama_ref_engine.so is missing: run `make -C oracle` where the reference exists")
+        raise SystemExit("oracle/_ref/libllama_ref_engine.so is missing: run `make -C oracle REF=<reference checkout>`")
     out = {}
     for name, (arch, env) in RUNS.items():
         tmp = Path("/tmp") / f"llama3x_golden_{name}.npz"

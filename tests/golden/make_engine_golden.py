@@ -1,7 +1,7 @@
 """Generates tests/golden/engine_golden.npz: the REFERENCE's own end-to-end outputs (oracle/_ref/probe-int8, its
 tests/probe.c driver built from its sources by oracle/Makefile) on the seeded checkpoints of models.py.
 
-    make -C oracle && python tests/golden/make_engine_golden.py
+    make -C oracle REF=REFERENCE_CHECKOUT && python tests/golden/make_engine_golden.py
 
 Per model (prompt = models.prompt(name, P)):
   <name>_prompt     the prompt token ids
@@ -70,7 +70,7 @@ def w8a32(out, name, path, p, V):
 
 def main():
     if not models.O.PROBE_INT8.exists():
-        raise SystemExit("oracle/_ref/probe-int8 is missing: run `make -C oracle` where the reference exists")
+        raise SystemExit("oracle/_ref/probe-int8 is missing: run `make -C oracle REF=<reference checkout>`")
     out = {}
     with tempfile.TemporaryDirectory() as tmp:
         for name, n in PROMPTS.items():

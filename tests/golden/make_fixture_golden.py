@@ -9,7 +9,7 @@
 The reference is imported from its checkout at generation time (it is not vendored). Where oracle/_ref/probe-int8
 exists, the reference compiled here is run on the fixture first and must reproduce those 48 values.
 
-    python tests/golden/make_fixture_golden.py [REFERENCE_CHECKOUT]
+    python tests/golden/make_fixture_golden.py REFERENCE_CHECKOUT
 """
 import importlib.util
 import json
@@ -26,7 +26,9 @@ ROOT = HERE.parents[1]
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_fixture_golden.py REFERENCE_CHECKOUT")
+    ref = Path(sys.argv[1])
     spec = importlib.util.spec_from_file_location("reference_fixtures", ref / "tests" / "fixtures.py")
     fixtures = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(fixtures)

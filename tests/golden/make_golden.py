@@ -1,7 +1,7 @@
 """Generates tests/golden/q8_golden.npz from the REFERENCE ITSELF (oracle/_ref/libllama_ref.so, compiled from
 LucianCrainic/llama3.x.c's own sources by oracle/Makefile), on seeded inputs.
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF=REFERENCE_CHECKOUT && python tests/golden/make_golden.py
 
 Cases (all small; numpy PCG64 seeds below):
   quant_ties      k_quantize on the reference test suite's tie values at scale 1 (tests/kernels.c:111-116: 127, 2.5,
@@ -27,7 +27,7 @@ from oracle import oracle as O  # noqa: E402
 
 def main():
     if not O.ref_available():
-        raise SystemExit("oracle/_ref/libllama_ref.so is missing: run `make -C oracle` where the reference exists")
+        raise SystemExit("oracle/_ref/libllama_ref.so is missing: run `make -C oracle REF=<reference checkout>`")
     rng = np.random.default_rng(20261201)
     out = {}
     ties = np.zeros(64, np.float32)

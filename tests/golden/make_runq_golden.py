@@ -8,7 +8,7 @@ with LLAMA_TOKENS_OUT recording the prompt ids and the generated ids. Stored: th
 and the two id lists; the checkpoint is the one tests/golden/ref_fixture.npz already holds (checked here). tests/test_engine_gpu.py runs the same command with oracle/_ref/runq-gpu (the
 same CLI linked against the GPU engine) and compares.
 
-    make -C oracle && python tests/golden/make_runq_golden.py REFERENCE_CHECKOUT
+    make -C oracle REF=REFERENCE_CHECKOUT && python tests/golden/make_runq_golden.py REFERENCE_CHECKOUT
 """
 import importlib.util
 import json
@@ -34,7 +34,7 @@ def main():
     spec.loader.exec_module(fixtures)
     runq = ROOT / "oracle" / "_ref" / "runq"
     if not runq.exists():
-        raise SystemExit("oracle/_ref/runq is missing: run `make -C oracle` where the reference exists")
+        raise SystemExit("oracle/_ref/runq is missing: run `make -C oracle REF=<reference checkout>`")
     with tempfile.TemporaryDirectory() as tmp:
         root = fixtures.create(Path(tmp) / "shared")
         out = Path(tmp) / "tokens.json"

@@ -83,6 +83,10 @@ def test_missing_and_short_files(load, tmp_path):
     (v3_header(**SMALL, eos=SMALL["vocab"]), "invalid special token metadata"),
     (v3_header(**SMALL, name=b"x" * 128), "unterminated model name"),
     (v3_header(**SMALL, reserved=1), "unsupported nonzero reserved checkpoint metadata"),
+    # tensor_bytes (src/runtime.c:170-177): gs 2 divides dim 6 and hidden 4, but the 3 x 6 embedding has 18 elements,
+    # not a multiple of 4, so its scales would start unaligned.
+    (v2_header(dim=6, hidden=4, layers=1, heads=1, kv=1, vocab=3, seq=4, gs=2),
+     "unsupported INT8 tensor alignment/group size: 18 elements"),
 ])
 def test_headers_the_reference_rejects(load, tmp_path, header, message):
     assert message in load(write(tmp_path, header + bytes(4096)))
