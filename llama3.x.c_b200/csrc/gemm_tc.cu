@@ -16,13 +16,14 @@
 //               [2 groups x 128 tokens] into a ring of 8 the epilogue releases.
 //   warp 1      MMA issuer: allocates 512 TMEM columns (four 128 x 128 int32 buffers), issues two MMAs per group into
 //               the next buffer the epilogue has released, commits the buffer to the epilogue and the stage to the ring.
-//   warps 2-9   epilogue (warp % 4 = TMEM lane quadrant = 32 weight rows, (warp - 2) / 4 = 64-token half): per
-//               group it reads its 32 x 64 int32 dots in 16-column chunks (each read in flight while the previous
-//               chunk is promoted with packed f32x2 instructions) and releases the buffer once the last chunk is in
-//               registers. Four buffers let the MMA run up to three groups ahead of the promotion. Column chunks
-//               past the last token are not promoted (they are never stored).
+//   warps 2-17  epilogue (warp % 4 = TMEM lane quadrant = 32 weight rows, (warp - 2) / 4 = 32-token column
+//               quarter): per group one read of its 32 x 32 int32 dots as packed column pairs, the buffer released as
+//               soon as they are in registers, then the promotion with packed f32x2 instructions; four epilogue warps
+//               per SM sub-partition cover one another's TMEM read latency. Four buffers let the MMA run up to three
+//               groups ahead of the promotion. 16-column chunks past the last token are not promoted (they are never
+//               stored). Weight scales are read four groups at a time, the next four a step ahead.
 // Group promotion: the group's first MMA overwrites its TMEM buffer (no clearing), the epilogue converts each exact
-// int32 dot to float (exact: |dot| <= 64*127^2 < 2^24) and applies mul, fma as packed pairs.
+// int32 dot to float (exact: |dot| <= 64*128^2 < 2^24) and applies mul, fma as packed pairs.
 //
 // Every mbarrier wait is bounded (a timeout raises KC_ERR_TIMEOUT, sets a CTA abort flag that turns the remaining
 // waits into no-ops, and the CTA still releases its TMEM).
@@ -46,8 +47,8 @@ constexpr int kStageB = kTN * 128;            // activations: 128 tokens x 128 B
 constexpr int kStageBytes = kStageA + kStageB;
 constexpr int kStageX = 2 * kTN * 4;          // activation scales of one stage: 2 groups x 128 tokens
 constexpr int kEpiWarp0 = 2;                  // warps 0 (TMA) and 1 (MMA) come first
-constexpr int kEpiCols = 64;                  // token columns per epilogue thread
-constexpr int kEpiWarps = 4 * (kTN / kEpiCols);  // 4 lane quadrants x column halves
+constexpr int kEpiCols = 32;                  // token columns per epilogue thread
+constexpr int kEpiWarps = 4 * (kTN / kEpiCols);  // 4 lane quadrants x 4 column quarters
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kTmemBufs = 4;                  // 128-column int32 accumulators in flight
 constexpr int kTmemCols = kTmemBufs * 128;
@@ -103,21 +104,33 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity, vo
   return false;
 }
 
-// Promotes 16 token columns of one group: acc[p] = fma(((float)dot) * xs, ws, acc[p]) for 8 column pairs. The int32
-// dots convert exactly (|dot| <= 64 * 127^2 < 2^24).
-__device__ __forceinline__ void promote16(uint64_t *acc, const uint32_t (&r)[16], const float *xs, uint64_t ws2) {
-  const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+// A packed pair of exact int32 group dots as the packed pair of floats, each half converted exactly
+// (|dot| <= 64 * 128^2 = 2^20 < 2^24).
+__device__ __forceinline__ uint64_t dots_to_f2(uint64_t v) {
+  uint64_t r;
+  asm("{\n\t.reg .b32 lo, hi;\n\t.reg .f32 flo, fhi;\n\t"
+      "mov.b64 {lo, hi}, %1;\n\t"
+      "cvt.rn.f32.s32 flo, lo;\n\tcvt.rn.f32.s32 fhi, hi;\n\t"
+      "mov.b64 %0, {flo, fhi};\n\t}"
+      : "=l"(r)
+      : "l"(v));
+  return r;
+}
+
+// Promotes 16 token columns of one group, held as 8 packed pairs: acc[p] = fma(((float)dot) * xs, ws, acc[p]) (the
+// reference's rounding sequence: one rounded product, then one fused multiply-add). xs: the 16 activation scales.
+__device__ __forceinline__ void promote16(uint64_t *acc, const uint64_t *r, const float *xs, uint64_t ws2) {
+  const ulonglong2 *xs2 = reinterpret_cast<const ulonglong2 *>(xs);
 #pragma unroll
   for (int p4 = 0; p4 < 4; p4++) {
-    const float4 x = xs4[p4];
-    const uint64_t f0 = f2_pack(__int2float_rn((int)r[4 * p4]), __int2float_rn((int)r[4 * p4 + 1]));
-    const uint64_t f1 = f2_pack(__int2float_rn((int)r[4 * p4 + 2]), __int2float_rn((int)r[4 * p4 + 3]));
-    acc[2 * p4] = f2_fma(f2_mul(f0, f2_pack(x.x, x.y)), ws2, acc[2 * p4]);
-    acc[2 * p4 + 1] = f2_fma(f2_mul(f1, f2_pack(x.z, x.w)), ws2, acc[2 * p4 + 1]);
+    const ulonglong2 x = xs2[p4];
+    acc[2 * p4] = f2_fma(f2_mul(dots_to_f2(r[2 * p4]), x.x), ws2, acc[2 * p4]);
+    acc[2 * p4 + 1] = f2_fma(f2_mul(dots_to_f2(r[2 * p4 + 1]), x.y), ws2, acc[2 * p4 + 1]);
   }
 }
 
-template <bool DOTS>  // DOTS: the test hook's variant, which stores the raw int32 group dots instead of promoting
+// DOTS: the test hook's variant, which stores the raw int32 group dots instead of promoting.
+template <bool DOTS>
 __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_constant__ GemmMaps mp, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // The 128-byte swizzle is a function of the address bits, so the operand stages start on a 1024-byte boundary.
@@ -229,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
     }
   } else if (warp >= kEpiWarp0) {
     // ---- epilogue: promotion of every group, in order ----
-    const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;  // lane quadrant, 64-token column half
+    const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;  // lane quadrant, 32-token column quarter
     const int row = 32 * q + lane;  // TMEM lane = row of the weight tile
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + kEpiCols * h;
     int st = 0, gidx = 0;
@@ -252,65 +265,50 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_q8_tc_kernel(const __grid_co
 #pragma unroll
       for (int i = 0; i < kEpiCols / 2; i++)
         acc[i] = 0;
-      // TMEM reads are software-pipelined against the promotion in 16-column chunks: the next chunk is in flight
-      // while the current one is promoted. rA holds chunk 0 of the current group on entry to each group.
-      uint32_t rA[16], rB[16];
-      bool ok = wait_or_abort(&tfull[gidx % kTmemBufs], (gidx / kTmemBufs) & 1, abort_flag);
-      tc_fence_after();
-      tmem_ld16(tq + (gidx % kTmemBufs) * kTN, rA);
-      tmem_wait_ld();
+      // Per group: one read of the warp's 32 columns, the buffer released as soon as they are in registers, then the
+      // promotion (the other epilogue warps of the sub-partition cover the read's latency). Weight scales come four
+      // groups at a time, the next four loaded a step ahead.
+      const float4 *ws4 = reinterpret_cast<const float4 *>(wsr);
+      float4 wq4 = __ldg(ws4), wn4 = groups > 4 ? __ldg(ws4 + 1) : wq4;
       for (int j = 0; j < spt; j++, st++) {
         const int xslot = st % kXsStages;
         wait_or_abort(&xfull[xslot], (st / kXsStages) & 1, abort_flag);
         const float *xsT = xsring + xslot * (kStageX / 4);
-        for (int gg = 0; gg < 2 && 2 * j + gg < groups; gg++, gidx++) {
+        if (j > 0 && (j & 1) == 0) {  // groups 2j, 2j + 1 start a new four
+          wq4 = wn4;
+          if (2 * j + 4 < groups)
+            wn4 = __ldg(ws4 + (j >> 1) + 1);
+        }
+#pragma unroll
+        for (int gg = 0; gg < 2; gg++, gidx++) {
           const int g = 2 * j + gg, b = gidx % kTmemBufs;
-          const bool last = g + 1 == groups;
-          const float wv = __ldg(wsr + g);
+          const bool ok = wait_or_abort(&tfull[b], (gidx / kTmemBufs) & 1, abort_flag);
+          tc_fence_after();
+          uint64_t r[16];
+          tmem_ld32_pairs(tq + b * kTN, r);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            mbar_arrive(&tempty[b]);
+          if (!ok)
+            continue;
+          if (DOTS) {
+            if (row_ok && tl.s == 0 && !tl.swiglu)
+#pragma unroll
+              for (int i = 0; i < 32; i++)
+                if (tl.m0 + kEpiCols * h + i < a.M)
+                  a.dots[((size_t)g * a.M + tl.m0 + kEpiCols * h + i) * seg_n + n] =
+                      (int32_t)(uint32_t)(r[i >> 1] >> (32 * (i & 1)));
+            continue;
+          }
+          const float wv = (j & 1) ? (gg ? wq4.w : wq4.z) : (gg ? wq4.y : wq4.x);
           const uint64_t ws2 = f2_pack(wv, wv);
           const float *xs = xsT + gg * kTN + kEpiCols * h;
-          const uint32_t tb = tq + b * kTN;
-          const bool promote = ok && !DOTS;
-          const bool dump = DOTS && ok && row_ok && tl.s == 0 && !tl.swiglu;
-#pragma unroll
-          for (int c = 0; c < 4; c += 2) {
-            tmem_ld16(tb + 16 * (c + 1), rB);
-            if (promote && 16 * c < live)
-              promote16(acc + 8 * c, rA, xs + 16 * c, ws2);
-            if (dump)
-#pragma unroll
-              for (int i = 0; i < 16; i++)
-                if (tl.m0 + kEpiCols * h + 16 * c + i < a.M)
-                  a.dots[((size_t)g * a.M + tl.m0 + kEpiCols * h + 16 * c + i) * seg_n + n] =
-                      (int32_t)rA[i];
-            tmem_wait_ld();
-            const bool ok_cur = ok;
-            if (c == 0) {
-              tmem_ld16(tb + 32, rA);
-            } else {
-              // All 64 columns are in registers: release the buffer.
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0)
-                mbar_arrive(&tempty[b]);
-              if (!last) {  // chunk 0 of the next group
-                const int bn = (gidx + 1) % kTmemBufs;
-                ok = wait_or_abort(&tfull[bn], ((gidx + 1) / kTmemBufs) & 1, abort_flag);
-                tc_fence_after();
-                tmem_ld16(tq + bn * kTN, rA);
-              }
-            }
-            if (ok_cur && !DOTS && 16 * (c + 1) < live)
-              promote16(acc + 8 * (c + 1), rB, xs + 16 * (c + 1), ws2);
-            if (dump)
-#pragma unroll
-              for (int i = 0; i < 16; i++)
-                if (tl.m0 + kEpiCols * h + 16 * (c + 1) + i < a.M)
-                  a.dots[((size_t)g * a.M + tl.m0 + kEpiCols * h + 16 * (c + 1) + i) * seg_n + n] =
-                      (int32_t)rB[i];
-            if (c == 0 || !last)
-              tmem_wait_ld();
-          }
+          if (live > 0)
+            promote16(acc, r, xs, ws2);
+          if (live > 16)
+            promote16(acc + 8, r + 8, xs + 16, ws2);
         }
         __syncwarp();
         if (lane == 0)
@@ -439,8 +437,8 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
       !kc_tmap_2d(&mp.xs, xsT, 4, ldt, groups, (uint64_t)ldt * 4, kTN, 2, false))
     return -1;
   const size_t smem = kSmemBytes;
-  if (kc_allow_smem(reinterpret_cast<const void *>(gemm_q8_tc_kernel<false>), (int)smem) != cudaSuccess ||
-      kc_allow_smem(reinterpret_cast<const void *>(gemm_q8_tc_kernel<true>), (int)smem) != cudaSuccess)
+  auto kern = dots ? gemm_q8_tc_kernel<true> : gemm_q8_tc_kernel<false>;
+  if (kc_allow_smem(reinterpret_cast<const void *>(kern), (int)smem) != cudaSuccess)
     return -2;
   const int sms = kc_device_sms();
   cudaLaunchConfig_t cfg = {};
@@ -453,11 +451,10 @@ int kc_launch_gemm_tc(const KcGemmSeg *segs, int nseg, const int8_t *xq, const f
   attr[0].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = dots ? cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<true>, mp, a)
-                             : cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<false>, mp, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp, a);
   if (e != cudaSuccess) {
     cudaFuncAttributes fa;
-    cudaFuncGetAttributes(&fa, gemm_q8_tc_kernel<false>);
+    cudaFuncGetAttributes(&fa, kern);
     fprintf(stderr, "gemm_q8_tc_kernel launch: %s (regs %d, threads %d, max threads %d, smem %zu + static %zu)\n",
             cudaGetErrorString(e), fa.numRegs, kThreads, fa.maxThreadsPerBlock, smem, fa.sharedSizeBytes);
     return -2;

@@ -88,6 +88,36 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// 32 lanes (this warp's quadrant) x 32 consecutive 32-bit columns, as 16 packed pairs of neighbouring columns (the
+// operand form of the f32x2 instructions: no register moves between the load and packed arithmetic).
+__device__ __forceinline__ void tmem_ld32_pairs(uint32_t taddr, uint64_t (&r)[16]) {
+  asm volatile(
+      "{\n\t.reg .b32 a0, a1, a2, a3, a4, a5, a6, a7, a8, a9, a10, a11, a12, a13, a14, a15;\n\t"
+      ".reg .b32 a16, a17, a18, a19, a20, a21, a22, a23, a24, a25, a26, a27, a28, a29, a30, a31;\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {a0, a1, a2, a3, a4, a5, a6, a7, a8, a9, a10, a11, a12, a13, a14, a15,"
+      " a16, a17, a18, a19, a20, a21, a22, a23, a24, a25, a26, a27, a28, a29, a30, a31}, [%16];\n\t"
+      "mov.b64 %0, {a0, a1};\n\t"
+      "mov.b64 %1, {a2, a3};\n\t"
+      "mov.b64 %2, {a4, a5};\n\t"
+      "mov.b64 %3, {a6, a7};\n\t"
+      "mov.b64 %4, {a8, a9};\n\t"
+      "mov.b64 %5, {a10, a11};\n\t"
+      "mov.b64 %6, {a12, a13};\n\t"
+      "mov.b64 %7, {a14, a15};\n\t"
+      "mov.b64 %8, {a16, a17};\n\t"
+      "mov.b64 %9, {a18, a19};\n\t"
+      "mov.b64 %10, {a20, a21};\n\t"
+      "mov.b64 %11, {a22, a23};\n\t"
+      "mov.b64 %12, {a24, a25};\n\t"
+      "mov.b64 %13, {a26, a27};\n\t"
+      "mov.b64 %14, {a28, a29};\n\t"
+      "mov.b64 %15, {a30, a31};\n\t"
+      "}"
+      : "=l"(r[0]), "=l"(r[1]), "=l"(r[2]), "=l"(r[3]), "=l"(r[4]), "=l"(r[5]), "=l"(r[6]), "=l"(r[7]),
+        "=l"(r[8]), "=l"(r[9]), "=l"(r[10]), "=l"(r[11]), "=l"(r[12]), "=l"(r[13]), "=l"(r[14]), "=l"(r[15])
+      : "r"(taddr));
+}
+
 // 32 lanes (this warp's quadrant) x 16 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(

@@ -383,10 +383,11 @@ def test_gemm_tc_group_dots_exact(kc, oracle, m, n, k):
     assert (host(dots) == oracle.group_dots(xq, wq, 64)).all()
 
 
-# Partial token tiles skip the promotion of column chunks past the last token: M = 64 fills exactly one of the two
-# 64-column halves, M = 65 puts one token in the second.
+# Partial token tiles skip the promotion of 16-column chunks past the last token (each epilogue warp holds 32 of a
+# tile's 128 token columns): M = 64 fills exactly two quarters, M = 65, 33 and 97 put one token in the next quarter,
+# M = 17 one token in a quarter's second chunk, M = 7 fills part of one chunk.
 TC_SHAPES = [(128, 128, 256), (33, 48, 1024), (257, 300, 2048), (7, 4096, 4096), (130, 129, 14336), (64, 200, 512),
-             (65, 96, 768)]
+             (65, 96, 768), (17, 64, 256), (97, 130, 512)]
 
 
 @pytest.mark.parametrize("m,n,k", TC_SHAPES)
@@ -454,6 +455,21 @@ def test_gemm_tc_config1_full_size(kc, oracle):
         mag = oracle.group_dots(np.abs(host(xq)[t]).astype(np.int8), np.abs(hw).astype(np.int8), gs)[:, 0, :]
         budget = 2e-5 * (mag * host(ws)[rows].T * host(xs)[t][:, None]).sum(0) + 1e-6
         assert np.all(np.abs(y[rows] - host(c)[t, rows]) <= 2 * budget)
+
+
+@pytest.mark.parametrize("N,K", [(14336, 4096), (4096, 14336)], ids=["up", "down"])
+def test_gemm_tc_config1_t2048(kc, oracle, N, K):
+    # Config 1 at its largest batch, T = 2048, on both FFN projections: bitwise the oracle on 48 sampled weight rows
+    # (every one of the 2048 token rows, so every token tile and every column quarter of the epilogue is covered).
+    T, gs = 2048, 64
+    g = torch.Generator(device="cuda").manual_seed(N + K)
+    wq, ws = kc.quantize(torch.randn((N, K), generator=g, device="cuda") * 0.02, gs)
+    xq, xs = kc.quantize(torch.randn((T, K), generator=g, device="cuda"), gs)
+    c = kc.gemm(xq, xs, wq, ws, gs, backend=kc.Q8_GEMM_GPU_TCGEN05)
+    kc.status()
+    rows = np.sort(np.random.default_rng(N).choice(N, 48, replace=False))
+    ref = oracle.gemm(host(xq), host(xs), host(wq)[rows], host(ws)[rows], gs)
+    assert (bits(host(c)[:, rows]) == bits(ref)).all()
 
 
 def test_k_gemm_q8_picks_tensor_cores_for_batches(kc, oracle):
