@@ -34,13 +34,10 @@
 
 namespace {
 
-constexpr int kThreads = 256;
 constexpr int kTile = 32;        // positions per tile of the batched variant (its TILED_POS)
 constexpr int kSplitMax = 256;   // positions of a split chunk at most (attention_chunks' shortest bound)
-constexpr int kQV = 64;          // query vectors of a batched CTA
 constexpr int kMaxHd = 256;      // the reference's AVX-512 attention takes head_dim <= 256
 constexpr int kMaxNq = 16;       // query heads per KV head (TILED_MAX_Q)
-constexpr int kMergeChunks = 16; // chunk partials a merge CTA stages at a time
 
 // ---- the reference's arithmetic, one lane ---------------------------------------------------------------------------
 
@@ -132,8 +129,6 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
   pdl_launch_dependents();
   __shared__ float red[kMaxHd / 32];
   __shared__ float vals[kMaxHd];
-  __shared__ float stage[kMergeChunks * (kMaxHd + 2)];
-  __shared__ float wts[kMergeChunks];
   const int h = blockIdx.x, rr = blockIdx.y, r = row0 + rr, d = threadIdx.x;
   const int base = pos_dev ? *pos_dev : pos0;
   const int vis = base + r + 1;  // positions the row sees
@@ -151,39 +146,31 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
     chunks = plan_chunks(vis, n_kv, limit, workers);
     live = chunks;
   }
-  const int slot = hd + 2, nt = blockDim.x;
+  const int slot = hd + 2;
   const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
-  // The maximum over the chunks (order-free), every chunk's maximum loaded at once.
+  // Every thread walks the chunks itself (the maximum, then in chunk order the weight, the sum and its element),
+  // eight chunks' values loaded at a time, all in flight together; the shared loads coalesce within each warp.
   float mx = -FLT_MAX;
-  for (int c = d; c < live; c += nt)
+  for (int c = 0; c < live; c++)
     mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + hd));
-#pragma unroll
-  for (int off = 16; off; off >>= 1)
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if ((d & 31) == 0)
-    red[d >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
-  for (int w = 1; w < nt / 32; w++)
-    mx = fmaxf(mx, red[w]);
-  // Then the chunks in order, kMergeChunks at a time staged in shared memory by one round of parallel loads; each
-  // chunk's weight is taken once, and every thread adds the sums in chunk order.
   float sum = 0.0f, o = 0.0f;
-  for (int c0 = 0; c0 < live; c0 += kMergeChunks) {
-    const int nc = min(kMergeChunks, live - c0);
-    __syncthreads();  // the previous block's reads are done (and red's, above)
-    for (int i = d; i < nc * slot; i += nt)
-      stage[i] = __ldcg(pb + (long long)c0 * slot + i);
-    __syncthreads();
-    if (d < nc)
-      wts[d] = expf_libc(__fsub_rn(stage[d * slot + hd], mx));
-    __syncthreads();
-    for (int c = 0; c < nc; c++) {
-      const float w = wts[c];
-      sum = __fadd_rn(sum, __fmul_rn(w, stage[c * slot + hd + 1]));
-      if (d < hd)
-        o = __fadd_rn(o, __fmul_rn(w, stage[c * slot + d]));
+  for (int c0 = 0; c0 < live; c0 += 8) {
+    float mv[8], lv[8], av[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float *pc = pb + (long long)(c0 + i) * slot;
+      const bool in = c0 + i < live;
+      mv[i] = in ? __ldcg(pc + hd) : 0.0f;
+      lv[i] = in ? __ldcg(pc + hd + 1) : 0.0f;
+      av[i] = in && d < hd ? __ldcg(pc + d) : 0.0f;
     }
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (c0 + i < live) {
+        const float w = expf_libc(__fsub_rn(mv[i], mx));
+        sum = __fadd_rn(sum, __fmul_rn(w, lv[i]));
+        o = __fadd_rn(o, __fmul_rn(w, av[i]));
+      }
   }
   (void)chunks;
   const float v = __fdiv_rn(o, sum);
@@ -332,37 +319,45 @@ __global__ void tiled_generic_kernel(const float *q, long long q_ld, const float
 
 // ---- the split variant for one row (decode) -----------------------------------------------------------------------
 // A cluster of kSplitCtas CTAs per (KV head g, chunk c) of the row at position pos: CTA k of the cluster loads K rows
-// [k n / 4, (k + 1) n / 4) of the chunk's n <= 256 positions (one bulk copy) and computes their scores for the group's
-// nq heads, which it stores into every CTA of the cluster (distributed shared memory); after a cluster barrier each
-// CTA holds all the chunk's scores, takes the maximum, exp512 and the 16-lane exp-sum per head (the same in every
-// CTA), and runs the P.V chains of its quarter of the head's elements over V[chunk rows][its quarter] (cp.async
-// copies). So each K and V element is read once. A cluster walks chunks y, y + gridDim.y, ... (about one wave of
-// clusters). With `tickets`, the CTA that finishes a KV head's last chunk also merges the group's partials (the
-// arithmetic of merge_kernel) and writes its outputs, so no second launch waits on the partials.
+// [k n / 4, (k + 1) n / 4) of the chunk's n <= 256 positions (one bulk copy) and V[chunk rows][its quarter of the
+// head's elements] (cp.async), computes the scores of its K rows for the group's nq heads into its own shared memory,
+// and after a cluster barrier gathers the other three quarters' scores through distributed shared memory, so that
+// each CTA holds all of the chunk's scores. Each CTA then takes the maximum, exp512 and the 16-lane exp-sum per head
+// (the same in every CTA) and runs the P.V chains of its quarter of the head's elements. So each K and V element is
+// read once. A cluster walks chunks y, y + gridDim.y, ... (about one wave of clusters). With `tickets`, the CTA that
+// finishes a KV head's last chunk also merges the group's partials (the arithmetic of merge_kernel) and writes its
+// outputs, so no second launch waits on the partials.
+// With `early` (the position read from device memory), the K and V rows below the newest position are requested
+// before the wait on the preceding kernel: the caller guarantees that the launch before this one writes neither the
+// position word nor any cache row below it (a decode step's K/V store writes only the newest row), so those copies
+// overlap the preceding kernel's tail. The newest row, Q and everything else is read after the wait.
 constexpr int kSplitCtas = 4;
 constexpr int kSplitThreads = 256;
 constexpr int kSplitTickets = 256;  // KV heads the fused merge serves (a ticket word each, past the partials)
+constexpr int kSplitRows = kSplitMax / kSplitCtas;  // K rows of a CTA at most
 
-// Floats before the mbarrier: K quarter [kSplitMax / 4][hd], V quarter [kSplitMax][hd / 4], Q [nq][hd],
-// scores [nq][kSplitMax], the per-head maximum and exp-sum.
+// Floats before the mbarrier: K quarter [kSplitRows][hd], V quarter [kSplitMax][hd / 4], Q [nq][hd], this CTA's
+// scores [nq][kSplitRows], the chunk's scores (then probabilities) [nq][kSplitMax], the per-head maximum and exp-sum.
 __host__ __device__ constexpr size_t split_smem_floats(int hd, int nq) {
-  return (size_t)(kSplitMax / kSplitCtas) * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)nq * hd +
+  return (size_t)kSplitRows * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)nq * hd + (size_t)nq * kSplitRows +
          (size_t)nq * kSplitMax + 2 * kMaxNq;
 }
 __host__ __device__ constexpr size_t split_smem_bytes(int hd, int nq) {
   return split_smem_floats(hd, nq) * sizeof(float) + sizeof(uint64_t);
 }
 
-__device__ __forceinline__ void st_cluster_f32(float *local, unsigned rank, float v) {
-  unsigned remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-
 __device__ __forceinline__ void st_cluster_u32(unsigned *local, unsigned rank, unsigned v) {
   unsigned remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ float ld_cluster_f32(const float *local, unsigned rank) {
+  unsigned remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -387,66 +382,71 @@ __device__ __forceinline__ void tree_step(const float *in, float *outv, int L, i
 }
 
 // Group g's merge by the CTA that finished its last chunk: merge_kernel's arithmetic (the maximum over the chunks, then
-// in chunk order sum += w l and o += w acc with w = expf(m_c - max), then o / sum, then the optional quantization),
-// for the nq heads at once, chunk partials staged in shared memory a block at a time.
+// in chunk order sum += w l and o += w acc with w = expf(m_c - max), then o / sum, then the optional quantization)
+// for the nq heads at once. A warp per head loads every chunk's maximum and sum at once and computes the weights and
+// the sum; then every thread loads the chunk accumulators of its outputs kBatch at a time (all in flight together)
+// and adds them in chunk order.
+// Chunks per head whose weights and sums the fused merge keeps in shared memory, beside the head sums, the outputs and
+// the group scales (608 at head_dim 128 with 16 query heads per KV head: a 155648-position context). Longer contexts
+// merge in merge_kernel.
+__host__ __device__ constexpr int split_merge_chunks(int hd, int nq) {
+  return (int)((split_smem_floats(hd, nq) - (kMaxNq + 2 * (size_t)nq * hd)) / (2 * (size_t)nq));
+}
+
 template <int HD>
-__device__ void merge_group(float *sm, int sm_floats, const float *part, int g, int nq, int chunks, int cstride,
+__device__ void merge_group(float *sm, const float *part, int g, int nq, int chunks, int cstride,
                             float *out, int8_t *oq, float *os, int gs) {
-  constexpr int slot = HD + 2, nt = kSplitThreads, kOut = (kMaxNq * HD + nt - 1) / nt;
+  constexpr int slot = HD + 2, nt = kSplitThreads, kOut = (kMaxNq * HD + nt - 1) / nt, kBatch = 16;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, outs = nq * HD;
-  float *mxs = sm, *vals = mxs + kMaxNq, *scl = vals + nq * HD, *wts = scl + nq * HD;
-  // At least 8 chunks a block for every shape fast_shape admits (the K and V quarters alone hold 128 hd floats).
-  const int cb = (sm_floats - (kMaxNq + 2 * nq * HD)) / (nq * (slot + 1));
-  float *stage = wts + nq * cb;
+  float *hs = sm, *vals = hs + kMaxNq, *scl = vals + nq * HD, *wts = scl + nq * HD;
+  const int wcap = split_merge_chunks(HD, nq);  // the host merges here only when chunks <= wcap
   const float *pg = part + (long long)g * nq * cstride * slot;
   for (int hh = warp; hh < nq; hh += nt / 32) {
+    const float *ph = pg + (long long)hh * cstride * slot;
     float mx = -FLT_MAX;
     for (int c = lane; c < chunks; c += 32)
-      mx = fmaxf(mx, __ldcg(pg + ((long long)hh * cstride + c) * slot + HD));
+      mx = fmaxf(mx, __ldcg(ph + (long long)c * slot + HD));
 #pragma unroll
     for (int off = 16; off; off >>= 1)
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (lane == 0)
-      mxs[hh] = mx;
-  }
-  float sum[kOut], acc[kOut];
-#pragma unroll
-  for (int u = 0; u < kOut; u++)
-    sum[u] = 0.0f, acc[u] = 0.0f;
-  for (int c0 = 0; c0 < chunks; c0 += cb) {
-    const int nc = chunks - c0 < cb ? chunks - c0 : cb;
-    __syncthreads();  // the maxima are in; the previous block's reads are done
-    for (int i = tid; i < nq * nc * slot; i += nt) {
-      const int hh = i / (nc * slot), rem = i - hh * nc * slot;
-      stage[i] = __ldcg(pg + ((long long)hh * cstride + c0) * slot + rem);
+    // The weights and sums into shared memory, then the sum in chunk order by lane 0.
+    float *wh = wts + hh * wcap, *lh = wh + nq * wcap;
+    for (int c = lane; c < chunks; c += 32) {
+      wh[c] = expf_libc(__fsub_rn(__ldcg(ph + (long long)c * slot + HD), mx));
+      lh[c] = __ldcg(ph + (long long)c * slot + HD + 1);
     }
-    __syncthreads();
-    for (int i = tid; i < nq * nc; i += nt) {
-      const int hh = i / nc;
-      wts[i] = expf_libc(__fsub_rn(stage[i * slot + HD], mxs[hh]));
-    }
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < kOut; u++) {
-      const int o = tid + u * nt;
-      if (o < outs) {
-        const int hh = o / HD, d = o - hh * HD;
-        const float *sp = stage + hh * nc * slot, *wp = wts + hh * nc;
-        for (int c = 0; c < nc; c++) {
-          const float w = wp[c];
-          sum[u] = __fadd_rn(sum[u], __fmul_rn(w, sp[c * slot + HD + 1]));
-          acc[u] = __fadd_rn(acc[u], __fmul_rn(w, sp[c * slot + d]));
-        }
-      }
+    __syncwarp();
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int c = 0; c < chunks; c++)
+        sum = __fadd_rn(sum, __fmul_rn(wh[c], lh[c]));
+      hs[hh] = sum;
     }
   }
+  __syncthreads();
   float *dst = out + (long long)g * outs;
   int bad = 0;
 #pragma unroll
   for (int u = 0; u < kOut; u++) {
     const int o = tid + u * nt;
     if (o < outs) {
-      const float v = __fdiv_rn(acc[u], sum[u]);
+      const int hh = o / HD, d = o - hh * HD;
+      const float *pc = pg + (long long)hh * cstride * slot + d;
+      const float *wh = wts + hh * wcap;
+      float acc = 0.0f;
+      for (int c0 = 0; c0 < chunks; c0 += kBatch) {
+        float a[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; i++)
+          a[i] = c0 + i < chunks ? __ldcg(pc + (long long)(c0 + i) * slot) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < kBatch; i++) {
+          const int c = c0 + i;
+          if (c < chunks)
+            acc = __fadd_rn(acc, __fmul_rn(wh[c], a[i]));
+        }
+      }
+      const float v = __fdiv_rn(acc, hs[hh]);
       dst[o] = v;
       vals[o] = v;
       bad |= !isfinite(v);
@@ -480,24 +480,44 @@ __device__ void merge_group(float *sm, int sm_floats, const float *part, int g, 
   }
 }
 
+// K rows [r0, r1) of the chunk starting at position t0 into this CTA's K quarter (its first row k0), one bulk copy.
+template <int HD>
+__device__ __forceinline__ void split_copy_k(float *Kq, const float *Kh, uint64_t *bar, int t0, int k0, int r0,
+                                             int r1) {
+  if (threadIdx.x == 0 && r1 > r0)
+    bulk_g2s(Kq + (long long)(r0 - k0) * HD, Kh + (long long)(t0 + r0) * HD, (unsigned)(r1 - r0) * HD * 4, bar);
+}
+
+// V rows [r0, r1) of the chunk, the columns of CTA k's quarter, as 16-byte cp.async pieces.
+template <int HD>
+__device__ __forceinline__ void split_copy_v(float *Vq, const float *Vh, int t0, int k, int r0, int r1) {
+  constexpr int QD = HD / kSplitCtas, PR = QD / 4;
+  for (int i = threadIdx.x; i < (r1 - r0) * PR; i += kSplitThreads) {
+    const int t = r0 + i / PR, p4 = i % PR;
+    cp_async16(Vq + t * QD + 4 * p4, Vh + (long long)(t0 + t) * HD + k * QD + 4 * p4);
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q, const float *kc, const float *vc,
                                                               const int *pos_dev, int pos0, int n_kv, int nq, int seq,
                                                               int limit, int workers, int cstride, float *part,
                                                               unsigned *tickets, float *out, int8_t *oq, float *os,
-                                                              int gs) {
-  pdl_wait();
-  pdl_launch_dependents();
+                                                              int gs, int early) {
   constexpr int QD = HD / kSplitCtas;  // elements of the head this CTA's P.V covers
   extern __shared__ __align__(16) float sm[];
-  const int sm_floats = (int)split_smem_floats(HD, nq);
-  float *Kq = sm, *Vq = Kq + (kSplitMax / kSplitCtas) * HD, *Q = Vq + kSplitMax * QD, *S = Q + nq * HD;
+  float *Kq = sm, *Vq = Kq + kSplitRows * HD, *Q = Vq + kSplitMax * QD, *Sl = Q + nq * HD, *S = Sl + nq * kSplitRows;
   float *hmax = S + nq * kSplitMax, *hsum = hmax + kMaxNq;
-  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + sm_floats);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + split_smem_floats(HD, nq));
   __shared__ unsigned fails[kSplitCtas];
   __shared__ int last;
   static_assert(kSplitCtas == 4, "the failure vote reads four slots");
   const int g = blockIdx.x, k = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  bool waited = !early;
+  if (waited) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   const int P = (pos_dev ? *pos_dev : pos0) + 1;
   if (P < 1 || P > seq) {  // every CTA of the cluster leaves here together
     if (tickets && g == 0 && blockIdx.y == 0 && k == 0 && tid == 0)
@@ -511,25 +531,32 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  for (int i = tid; i < nq * HD; i += kSplitThreads)
-    Q[i] = q[(long long)g * nq * HD + i];
   __syncthreads();
+  const int newest = P - 1;  // the only cache row the preceding launch may write (early mode)
+  const float *Kh = kc + (long long)g * seq * HD, *Vh = vc + (long long)g * seq * HD;
   // The cluster walks chunks blockIdx.y, blockIdx.y + gridDim.y, ...; every CTA of it takes the same steps.
   unsigned phase = 0;
   for (int c = blockIdx.y; c < chunks; c += gridDim.y) {
     const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;  // <= 256
     const int k0 = n * k / kSplitCtas, kn = n * (k + 1) / kSplitCtas - k0;  // this CTA's K rows
-    const float *Kg = kc + ((long long)g * seq + t0) * HD, *Vg = vc + ((long long)g * seq + t0) * HD;
-    if (tid == 0 && kn > 0) {
+    // Rows [t0 + r0, t0 + r1) of K (this CTA's) and V (the whole chunk, this CTA's columns); before the wait only
+    // those below the newest row.
+    if (tid == 0 && kn > 0)
       mbar_arrive_expect_tx(bar, (unsigned)kn * HD * sizeof(float));
-      bulk_g2s(Kq, Kg + (long long)k0 * HD, (unsigned)kn * HD * sizeof(float), bar);
-    }
-    // V[chunk rows][k QD .. (k + 1) QD): QD / 4 16-byte pieces a row.
-    for (int i = tid; i < n * (QD / 4); i += kSplitThreads) {
-      const int t = i / (QD / 4), p4 = i - t * (QD / 4);
-      cp_async16(Vq + t * QD + 4 * p4, Vg + (long long)t * HD + k * QD + 4 * p4);
+    const int split_at = waited ? n : min(n, max(0, newest - t0));  // chunk rows safe to read before the wait
+    split_copy_k<HD>(Kq, Kh, bar, t0, k0, k0, min(k0 + kn, max(k0, split_at)));
+    split_copy_v<HD>(Vq, Vh, t0, k, 0, split_at);
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+      waited = true;
+      split_copy_k<HD>(Kq, Kh, bar, t0, k0, max(k0, split_at), k0 + kn);
+      split_copy_v<HD>(Vq, Vh, t0, k, split_at, n);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = tid; i < nq * HD; i += kSplitThreads)
+      Q[i] = q[(long long)g * nq * HD + i];
+    __syncthreads();
     bool ok = true;
     if (kn > 0) {
       ok = __syncthreads_and(mbar_wait_bounded(bar, phase));
@@ -566,12 +593,8 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
         tree_step<4>(t4, t2, L, 2);
         tree_step<2>(t2, t1, L, 1);
         const int t = grp * 16 + L;
-        if (h < nq && t < kn) {
-          const float sc = __fdiv_rn(t1[0], divisor);
-#pragma unroll
-          for (int r = 0; r < kSplitCtas; r++)
-            st_cluster_f32(S + h * kSplitMax + k0 + t, (unsigned)r, sc);
-        }
+        if (h < nq && t < kn)
+          Sl[h * kSplitRows + t] = __fdiv_rn(t1[0], divisor);
       }
     } else if (tid == 0) {
       mbar_wait_bounded(bar, phase ^ 1u);  // let the copy in flight land (bounded) before leaving
@@ -582,47 +605,79 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
     cluster_sync_all();  // every CTA of the cluster arrives, whatever happened above
     if (fails[0] | fails[1] | fails[2] | fails[3]) {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
-      break;  // the whole cluster stops in the same iteration (the error is raised)
+      cluster_sync_all();  // no CTA leaves while another may still read its scores
+      break;             // the whole cluster stops in the same iteration (the error is raised)
     }
-    // Per head (a warp each): the maximum, exp512 in place, the exp-sum in 16 lanes then the tree.
+    // The chunk's scores from the four CTAs (position t is CTA kk's row t - k0(kk)), all loads in flight together.
+    for (int i = tid; i < nq * n; i += kSplitThreads) {
+      const int h = i / n, t = i - h * n;
+      int kk = kSplitCtas - 1;
+      while (kk > 0 && n * kk / kSplitCtas > t)
+        kk--;
+      S[h * kSplitMax + t] = ld_cluster_f32(Sl + h * kSplitRows + t - n * kk / kSplitCtas, (unsigned)kk);
+    }
+    __syncthreads();
+    // Per head (a warp each): the maximum, exp512, the exp-sum in 16 lanes (lane l adds positions l, l + 16, l + 32,
+    // ... in order: l + 32 i is its own value i, l + 16 + 32 i lane l + 16's) then the tree.
     for (int h = warp; h < nq; h += kSplitThreads / 32) {
       float *sh = S + h * kSplitMax;
+      float sv[kSplitMax / 32];
       float mx = -FLT_MAX;
-      for (int t = lane; t < n; t += 32)
-        mx = fmaxf(mx, sh[t]);
+#pragma unroll
+      for (int i = 0; i < kSplitMax / 32; i++) {
+        const int t = lane + 32 * i;
+        sv[i] = t < n ? sh[t] : -FLT_MAX;
+        mx = fmaxf(mx, sv[i]);
+      }
 #pragma unroll
       for (int off = 16; off; off >>= 1)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      for (int t = lane; t < n; t += 32)
-        sh[t] = exp512_dev(__fsub_rn(sh[t], mx));
-      __syncwarp();
       float vs = 0.0f;
-      if (lane < 16)
-        for (int t = lane; t < n; t += 16)
-          vs = __fadd_rn(vs, sh[t]);
+#pragma unroll
+      for (int i = 0; i < kSplitMax / 32; i++) {
+        const int t = lane + 32 * i;
+        const float e = t < n ? exp512_dev(__fsub_rn(sv[i], mx)) : 0.0f;
+        if (t < n)
+          sh[t] = e;
+        const float hi = __shfl_down_sync(0xffffffffu, e, 16);
+        if (t < n)
+          vs = __fadd_rn(vs, e);
+        if (t + 16 < n)
+          vs = __fadd_rn(vs, hi);
+      }
       vs = tree16_lanes(vs);
       if (lane == 0)
         hmax[h] = mx, hsum[h] = vs;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    // P.V: a chain per (head, element of this CTA's quarter) over the chunk's positions in order.
+    // P.V: a chain per (head, element of this CTA's quarter) over the chunk's positions in order; the next eight
+    // positions' operands are loaded while the current eight are added.
     for (int i = tid; i < nq * QD; i += kSplitThreads) {
       const int h = i / QD, d = i - h * QD;
-      const float *e = S + h * kSplitMax;
+      const float *e = S + h * kSplitMax, *vd = Vq + d;
       float acc = 0.0f;
+      float ea[8], va[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        ea[u] = e[u], va[u] = vd[u * QD];
       int t = 0;
       for (; t + 8 <= n; t += 8) {
-        float ev[8], vv[8];
+        float eb[8], vb[8];
 #pragma unroll
         for (int u = 0; u < 8; u++)
-          ev[u] = e[t + u], vv[u] = Vq[(t + u) * QD + d];
+          eb[u] = e[t + 8 + u], vb[u] = vd[(t + 8 + u) * QD];  // (reads past n stay inside shared memory)
 #pragma unroll
         for (int u = 0; u < 8; u++)
-          acc = __fmaf_rn(ev[u], vv[u], acc);
+          acc = __fmaf_rn(ea[u], va[u], acc);
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          ea[u] = eb[u], va[u] = vb[u];
       }
-      for (; t < n; t++)
-        acc = __fmaf_rn(e[t], Vq[t * QD + d], acc);
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (t + u < n)
+          acc = __fmaf_rn(ea[u], va[u], acc);
       part[((long long)(g * nq + h) * cstride + c) * (HD + 2) + k * QD + d] = acc;
     }
     if (k == 0 && tid < nq) {
@@ -630,7 +685,8 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
       o[HD] = hmax[tid];
       o[HD + 1] = hsum[tid];
     }
-    // The scores, K and V buffers are refilled by the cluster's next chunk: every CTA is done with them first.
+    // The scores, K and V buffers are refilled by the cluster's next chunk, and a CTA's scores are read by the others
+    // until they pass this barrier: every CTA is done with them first.
     cluster_sync_all();
   }
   if (!tickets)
@@ -650,52 +706,63 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
   }
   __syncthreads();
   if (last)
-    merge_group<HD>(sm, sm_floats, part, g, nq, chunks, cstride, out, oq, os, gs);
+    merge_group<HD>(sm, part, g, nq, chunks, cstride, out, oq, os, gs);
 }
 
 // ---- the tiled variant for a batch of rows (prefill) ---------------------------------------------------------------
-// CTA (KV head g, group of R rows = whole or part blocks): its query vectors v = (row - first row) * nq + head, at
-// most 64, over the 32-position tiles of the group's causal range. Per tile: K and V rows by bulk copy (two buffers,
-// the next tile's copy in flight), K transposed for the score tiles; then each thread takes 2 queries x 4 positions:
-// their scores (chains over the head's elements in order) and, with the 8 threads that share the queries (8
-// consecutive lanes, 32 positions), the online softmax of the tile: the tile maximum by shuffles, the rescale of the
-// running sum, exp512, and the tile sum in the reference's order (positions j and 16 + j, then the 16-lane tree) by
-// shuffles across the 8 lanes. Every lane of a group keeps the queries' running maximum, sum and chunk. Then P.V
-// (4 queries x hd/16 elements a thread, chains over the tile's positions in order). A query whose chunk (its block's
-// plan) changes at a tile writes the finished chunk's partial first and starts again from zero.
+// CTA (KV head g, group of R rows = whole blocks): its query vectors v = (row - first row) * nq + head, at most 128,
+// over the 32-position K/V tiles of the group's causal range (bulk copies, two buffers, the next tile's copy in
+// flight; K rows padded in shared memory so that rows read together sit in different banks). Warp w owns query
+// vectors 16 w .. 16 w + 15 from the scores to the P.V product, so within a tile its warps never wait for one
+// another:
+//  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 16 w + lv + 4 i and positions lp + 8 j (i, j < 4),
+//    each score one FMA chain over the head's elements in order, operands read four elements at a time;
+//  - the online softmax of the tile for each query, among the 8 lanes that share it: the tile maximum, the rescale of
+//    the running sum, exp512, and the tile sum in the reference's order (positions p and 16 + p are the same lane's
+//    j and j + 2, then the 16-lane tree by shuffles across the 8 lanes); every lane keeps the queries' running
+//    maximum, sum and chunk;
+//  - P.V: every lane takes the warp's 16 queries x hd / 32 elements, one FMA chain per (query, element) over the
+//    tile's positions in order.
+// A query whose chunk (its block's plan) changes at a tile writes the finished chunk's partial first and starts again
+// from zero. The partials are merged by merge_kernel.
+constexpr int kTQ = 128;            // query vectors of a batched CTA
+constexpr int kTWarps = kTQ / 16;   // 8 warps of 16 query vectors
+constexpr int kPStride = kTQ + 4;   // probabilities [tile position][query vector], padded
+
+__host__ __device__ constexpr int tiled_kstride(int hd) { return hd + 4; }  // padded K and Q rows
 __host__ __device__ constexpr size_t tiled_smem_bytes(int hd) {
-  return ((size_t)4 * kTile * hd + (size_t)hd * kTile + (size_t)hd * kQV + (size_t)kTile * kQV + 2 * kQV) *
-             sizeof(float) + 2 * sizeof(uint64_t);
+  return ((size_t)kTQ * tiled_kstride(hd) + 2 * (size_t)kTile * tiled_kstride(hd) + 2 * (size_t)kTile * hd +
+          (size_t)kTile * kPStride + 2 * kTQ) * sizeof(float) + 2 * sizeof(uint64_t);
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long long q_ld, const float *kc,
-                                                         const float *vc, const int *pos_dev, int pos0, int row0,
-                                                         int rows, int m, int R, int n_kv, int nq, int seq, int limit,
-                                                         int workers, int cstride, float *part) {
+__global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, long long q_ld, const float *kc,
+                                                             const float *vc, const int *pos_dev, int pos0, int row0,
+                                                             int rows, int m, int R, int n_kv, int nq, int seq,
+                                                             int limit, int workers, int cstride, float *part) {
   pdl_wait();
   pdl_launch_dependents();
+  constexpr int KS = tiled_kstride(HD), DL = HD / 32;  // padded row; P.V elements of a lane
   extern __shared__ __align__(16) float sm[];
-  float *Kb = sm, *Vb = Kb + 2 * kTile * HD, *kt = Vb + 2 * kTile * HD, *qs = kt + HD * kTile;
-  float *P = qs + HD * kQV, *al = P + kTile * kQV;
-  int *fl = reinterpret_cast<int *>(al + kQV);
-  uint64_t *bar = reinterpret_cast<uint64_t *>(fl + kQV);
-  constexpr int DB = HD / 16;
-  const int g = blockIdx.x, tid = threadIdx.x;
+  float *qs = sm, *Kb = qs + kTQ * KS, *Vb = Kb + 2 * kTile * KS, *P = Vb + 2 * kTile * HD, *al = P + kTile * kPStride;
+  int *fl = reinterpret_cast<int *>(al + kTQ);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(fl + kTQ);
+  const int g = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int base = pos_dev ? *pos_dev : pos0;
-  const int rl0 = blockIdx.y * R, nr = min(R, rows - rl0);  // rows of this CTA, from wave row rl0
+  // Row groups in reverse order: the longest causal ranges start first.
+  const int rl0 = (gridDim.y - 1 - blockIdx.y) * R, nr = min(R, rows - rl0);  // rows of this CTA, from wave row rl0
   if (nr <= 0 || base < 0 || base + row0 + rl0 + nr > seq)
     return;  // the merge kernel reports bad positions
   const int qv = nr * nq, rblock = tile_rblock(nq), n_heads = n_kv * nq;
   const int vis_max = base + row0 + rl0 + nr, ntiles = (vis_max + kTile - 1) / kTile;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  // Queries, scaled, transposed: qs[d][v].
-  for (int i = tid; i < kQV * HD; i += kThreads) {
+  // Queries, scaled: qs[v][d].
+  for (int i = tid; i < kTQ * HD; i += kTWarps * 32) {
     const int v = i / HD, d = i - v * HD;
     float x = 0.0f;
     if (v < qv)
       x = __fmul_rn(q[(long long)(row0 + rl0 + v / nq) * q_ld + (long long)(g * nq + v % nq) * HD + d], scale);
-    qs[d * kQV + v] = x;
+    qs[v * KS + d] = x;
   }
   if (tid == 0) {
     mbar_init(&bar[0], 1);
@@ -704,36 +771,39 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
   }
   __syncthreads();
   const float *Kg = kc + (long long)g * seq * HD, *Vg = vc + (long long)g * seq * HD;
+  // Tile k into buffer k & 1: K row by row into the padded rows (a lane per row), V in one copy.
   auto issue = [&](int k) {
-    const int t = k * kTile, cnt = min(kTile, vis_max - t);
-    const unsigned bytes = (unsigned)cnt * HD * sizeof(float);
-    mbar_arrive_expect_tx(&bar[k & 1], 2 * bytes);
-    bulk_g2s(Kb + (k & 1) * kTile * HD, Kg + (long long)t * HD, bytes, &bar[k & 1]);
-    bulk_g2s(Vb + (k & 1) * kTile * HD, Vg + (long long)t * HD, bytes, &bar[k & 1]);
+    const int t = k * kTile, cnt = min(kTile, vis_max - t), b = k & 1;
+    if (lane == 0)
+      mbar_arrive_expect_tx(&bar[b], 2u * cnt * HD * sizeof(float));
+    __syncwarp();
+    if (lane < cnt)
+      bulk_g2s(Kb + (b * kTile + lane) * KS, Kg + (long long)(t + lane) * HD, HD * sizeof(float), &bar[b]);
+    if (lane == 0)
+      bulk_g2s(Vb + b * kTile * HD, Vg + (long long)t * HD, (unsigned)cnt * HD * sizeof(float), &bar[b]);
   };
-  if (tid == 0)
+  if (warp == 0)
     issue(0);
   auto out_of = [&](int v, int chunk) {  // partial of query v, chunk `chunk`
     return part + (((long long)(rl0 + v / nq) * n_heads + g * nq + v % nq) * cstride + chunk) * (HD + 2);
   };
-  // Score / softmax role: queries 2 qp + i (i = 0, 1), positions 4 pq + j (j = 0..3) of each tile.
-  const int qp = tid >> 3, pq = tid & 7;
-  int vis[2], len[2], cur[2] = {-1, -1};
-  float mrun[2] = {-FLT_MAX, -FLT_MAX}, lrun[2] = {0.0f, 0.0f};
+  // Score / softmax role: queries 16 warp + lv + 4 i, positions lp + 8 j.
+  const int lv = lane >> 3, lp = lane & 7, v0 = 16 * warp;
+  int vis[4], len[4], cur[4] = {-1, -1, -1, -1};
+  float mrun[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX}, lrun[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int i = 0; i < 2; i++) {
-    const int v = 2 * qp + i, r = row0 + rl0 + v / nq;
+  for (int i = 0; i < 4; i++) {
+    const int v = v0 + lv + 4 * i, r = row0 + rl0 + v / nq;
     vis[i] = v < qv ? base + r + 1 : 0;
     len[i] = tile_plan(r, rblock, m, base, n_kv, limit, workers).len;
   }
-  // P.V role: queries 4 qq.., elements DB dg...
-  const int qq = tid >> 4, dg = tid & 15;
-  float acc[4][DB];
+  // P.V role: the warp's 16 queries x elements DL lane ...
+  float acc[16][DL];
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int x = 0; x < 16; x++)
 #pragma unroll
-    for (int d = 0; d < DB; d++)
-      acc[i][d] = 0.0f;
+    for (int e = 0; e < DL; e++)
+      acc[x][e] = 0.0f;
   int failed = -1;  // the tile whose copy did not complete in time
   for (int k = 0; k < ntiles; k++) {
     const int t = k * kTile, cnt = min(kTile, vis_max - t), b = k & 1;
@@ -741,39 +811,46 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
       failed = k;
       break;
     }
-    if (tid == 0 && k + 1 < ntiles)
-      issue(k + 1);  // its buffer's last readers finished before the barrier above
-    for (int i = tid; i < kTile * HD; i += kThreads) {
-      const int p = i / HD, d = i - p * HD;
-      kt[d * kTile + p] = p < cnt ? Kb[b * kTile * HD + i] : 0.0f;
-    }
-    __syncthreads();
-    float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-#pragma unroll 8
-    for (int d = 0; d < HD; d++) {
-      const float2 qv2 = *reinterpret_cast<const float2 *>(qs + d * kQV + 2 * qp);
-      const float4 kv4 = *reinterpret_cast<const float4 *>(kt + d * kTile + 4 * pq);
-      s[0][0] = __fmaf_rn(qv2.x, kv4.x, s[0][0]);
-      s[0][1] = __fmaf_rn(qv2.x, kv4.y, s[0][1]);
-      s[0][2] = __fmaf_rn(qv2.x, kv4.z, s[0][2]);
-      s[0][3] = __fmaf_rn(qv2.x, kv4.w, s[0][3]);
-      s[1][0] = __fmaf_rn(qv2.y, kv4.x, s[1][0]);
-      s[1][1] = __fmaf_rn(qv2.y, kv4.y, s[1][1]);
-      s[1][2] = __fmaf_rn(qv2.y, kv4.z, s[1][2]);
-      s[1][3] = __fmaf_rn(qv2.y, kv4.w, s[1][3]);
-    }
-    // Online softmax. The 4 groups of a warp may differ in whether they see the tile, so every shuffle runs in every
-    // lane; the state only moves where the group sees positions.
+    if (warp == 0 && k + 1 < ntiles)
+      issue(k + 1);  // its buffer's last readers finished before the barrier that ended the previous tile
+    const float *Kt = Kb + b * kTile * KS;
+    float s[4][4];
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int v = 2 * qp + i, nv = max(0, min(kTile, vis[i] - t));
-      const bool live = nv > 0;  // the same in all 8 lanes of the group
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        s[i][j] = 0.0f;
+#pragma unroll 2
+    for (int d = 0; d < HD; d += 4) {
+      float4 qq[4], kk[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        qq[i] = *reinterpret_cast<const float4 *>(qs + (v0 + lv + 4 * i) * KS + d);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        kk[j] = *reinterpret_cast<const float4 *>(Kt + (lp + 8 * j) * KS + d);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          s[i][j] = __fmaf_rn(qq[i].x, kk[j].x, s[i][j]);
+          s[i][j] = __fmaf_rn(qq[i].y, kk[j].y, s[i][j]);
+          s[i][j] = __fmaf_rn(qq[i].z, kk[j].z, s[i][j]);
+          s[i][j] = __fmaf_rn(qq[i].w, kk[j].w, s[i][j]);
+        }
+    }
+    // Online softmax, query by query. The 8 lanes of a query agree on whether it sees the tile, and every shuffle runs
+    // in every lane; the state only moves where the query sees positions.
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int v = v0 + lv + 4 * i, nv = max(0, min(kTile, vis[i] - t));
+      const bool live = nv > 0;
       float alpha = 1.0f;
-      int marker = -2;  // for the P.V threads: -2 nothing, -1 first chunk, else the chunk to write out first
+      int marker = -2;  // for P.V: -2 nothing, -1 first chunk, else the chunk to write out first
       if (live) {
         const int ck = t / len[i];
         if (ck != cur[i]) {
-          if (cur[i] >= 0 && pq == 0) {
+          if (cur[i] >= 0 && lp == 0) {
             float *o = out_of(v, cur[i]);
             o[HD] = mrun[i];
             o[HD + 1] = lrun[i];
@@ -786,7 +863,7 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
       float tmax = -FLT_MAX;
 #pragma unroll
       for (int j = 0; j < 4; j++)
-        if (4 * pq + j < nv)
+        if (lp + 8 * j < nv)
           tmax = fmaxf(tmax, s[i][j]);
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
@@ -799,65 +876,69 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
       float e[4];
 #pragma unroll
       for (int j = 0; j < 4; j++)
-        e[j] = 4 * pq + j < nv ? exp512_dev(__fsub_rn(s[i][j], mrun[i])) : 0.0f;
-      // Tile sum: pair[p] = e[p] + e[16 + p] (p < 16: lanes pq < 4 hold p, pq + 4 hold 16 + p), t8[p] =
-      // pair[8 + p] + pair[p] (p < 8: lanes pq and pq + 2), t4[p] = t8[4 + p] + t8[p] (lanes 0 and 1), then
-      // (t4[0] + t4[2]) + (t4[1] + t4[3]) in lane 0 of the group.
-      float a[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        a[j] = __fadd_rn(e[j], __shfl_xor_sync(0xffffffffu, e[j], 4));
-        a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], 2));
-        a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], 1));
-      }
-      const float tsum = __shfl_sync(0xffffffffu, __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3])), 0, 8);
+        e[j] = lp + 8 * j < nv ? exp512_dev(__fsub_rn(s[i][j], mrun[i])) : 0.0f;
+      // Tile sum: lanes[p] = e[p] + e[16 + p] (p = lp: this lane's j = 0 and 2; p = 8 + lp: j = 1 and 3), t8[p] =
+      // lanes[8 + p] + lanes[p] (this lane), t4[p] = t8[4 + p] + t8[p] (lanes lp and lp ^ 4), then
+      // (t4[0] + t4[2]) + (t4[1] + t4[3]) (lanes lp ^ 2, then lp ^ 1): every lane of the query ends with the sum.
+      float ts = __fadd_rn(__fadd_rn(e[1], e[3]), __fadd_rn(e[0], e[2]));
+      ts = __fadd_rn(ts, __shfl_xor_sync(0xffffffffu, ts, 4));
+      ts = __fadd_rn(ts, __shfl_xor_sync(0xffffffffu, ts, 2));
+      ts = __fadd_rn(ts, __shfl_xor_sync(0xffffffffu, ts, 1));
       if (live)
-        lrun[i] = __fadd_rn(lrun[i], tsum);
+        lrun[i] = __fadd_rn(lrun[i], ts);
 #pragma unroll
       for (int j = 0; j < 4; j++)
-        P[(4 * pq + j) * kQV + v] = e[j];
-      if (pq == 0)
+        P[(lp + 8 * j) * kPStride + v] = e[j];
+      if (lp == 0)
         al[v] = alpha, fl[v] = marker;
     }
-    __syncthreads();
+    __syncwarp();
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int v = 4 * qq + i, f = fl[v];
+    for (int x = 0; x < 16; x++) {
+      const int v = v0 + x, f = fl[v];
       if (f >= 0) {  // the query's previous chunk is finished: write it out, start from zero
-        float *o = out_of(v, f);
+        float *o = out_of(v, f) + DL * lane;
 #pragma unroll
-        for (int d = 0; d < DB; d++) {
-          o[dg * DB + d] = acc[i][d];
-          acc[i][d] = 0.0f;
+        for (int e = 0; e < DL; e++) {
+          o[e] = acc[x][e];
+          acc[x][e] = 0.0f;
         }
       } else if (f == -1) {  // the query's first chunk starts here
 #pragma unroll
-        for (int d = 0; d < DB; d++)
-          acc[i][d] = 0.0f;
+        for (int e = 0; e < DL; e++)
+          acc[x][e] = 0.0f;
       }
       const float a = al[v];
 #pragma unroll
-      for (int d = 0; d < DB; d++)
-        acc[i][d] = __fmul_rn(acc[i][d], a);
+      for (int e = 0; e < DL; e++)
+        acc[x][e] = __fmul_rn(acc[x][e], a);
     }
-    const float *Vt = Vb + b * kTile * HD;
-#pragma unroll 4
+    const float *Vt = Vb + b * kTile * HD + DL * lane;
+    const float *Pw = P + v0;
+#pragma unroll 2
     for (int p = 0; p < cnt; p++) {
-      const float4 pv = *reinterpret_cast<const float4 *>(P + p * kQV + 4 * qq);
-      float vv[DB];
-#pragma unroll
-      for (int d = 0; d < DB; d += 4) {
-        const float4 x = *reinterpret_cast<const float4 *>(Vt + p * HD + dg * DB + d);
-        vv[d] = x.x, vv[d + 1] = x.y, vv[d + 2] = x.z, vv[d + 3] = x.w;
+      float vv[DL];
+      if (DL == 4) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(Vt + p * HD);
+        vv[0] = x4.x, vv[1 % DL] = x4.y, vv[2 % DL] = x4.z, vv[3 % DL] = x4.w;
+      } else if (DL == 2) {
+        const float2 x2 = *reinterpret_cast<const float2 *>(Vt + p * HD);
+        vv[0] = x2.x, vv[1 % DL] = x2.y;
+      } else {
+        vv[0] = Vt[p * HD];
       }
-      const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int y = 0; y < 4; y++) {
+        const float4 e4 = *reinterpret_cast<const float4 *>(Pw + p * kPStride + 4 * y);
+        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
-        for (int d = 0; d < DB; d++)
-          acc[i][d] = __fmaf_rn(pr[i], vv[d], acc[i][d]);
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int e = 0; e < DL; e++)
+            acc[4 * y + u][e] = __fmaf_rn(ev[u], vv[e], acc[4 * y + u][e]);
+      }
     }
-    __syncthreads();  // the buffers of this tile are refilled two tiles on
+    __syncthreads();  // the buffers of this tile are refilled two tiles on (and P, al, fl by the next tile)
   }
   if (failed >= 0) {  // that tile's copy is the only one in flight: let it land (bounded) before leaving
     if (tid == 0)
@@ -866,26 +947,26 @@ __global__ void __launch_bounds__(kThreads) tiled_kernel(const float *q, long lo
   }
   // The last chunk of every query.
 #pragma unroll
-  for (int i = 0; i < 2; i++)
-    if (pq == 0 && cur[i] >= 0) {
-      float *o = out_of(2 * qp + i, cur[i]);
-      o[HD] = mrun[i];
-      o[HD + 1] = lrun[i];
-    }
-  __syncthreads();  // fl: the P.V threads read the final chunk of their queries from the score threads' state below
-  if (pq == 0) {
-    fl[2 * qp] = cur[0];
-    fl[2 * qp + 1] = cur[1];
-  }
-  __syncthreads();
-#pragma unroll
   for (int i = 0; i < 4; i++) {
-    const int v = 4 * qq + i;
-    if (v < qv && fl[v] >= 0) {
-      float *o = out_of(v, fl[v]);
+    const int v = v0 + lv + 4 * i;
+    if (lp == 0) {
+      if (cur[i] >= 0) {
+        float *o = out_of(v, cur[i]);
+        o[HD] = mrun[i];
+        o[HD + 1] = lrun[i];
+      }
+      fl[v] = cur[i];
+    }
+  }
+  __syncwarp();
 #pragma unroll
-      for (int d = 0; d < DB; d++)
-        o[dg * DB + d] = acc[i][d];
+  for (int x = 0; x < 16; x++) {
+    const int v = v0 + x;
+    if (v < qv && fl[v] >= 0) {
+      float *o = out_of(v, fl[v]) + DL * lane;
+#pragma unroll
+      for (int e = 0; e < DL; e++)
+        o[e] = acc[x][e];
     }
   }
 }
@@ -922,7 +1003,7 @@ bool smem_ready(int hd) {
 
 // Rows of the tiled variant's CTA: whole blocks of 16 / nq rows, 64 query vectors at most.
 int tiled_rows_per_cta(int nq) {
-  const int rb = tile_rblock(nq), blocks = kQV / (rb * nq);
+  const int rb = tile_rblock(nq), blocks = kTQ / (rb * nq);
   return (blocks < 1 ? 1 : blocks) * rb;
 }
 
@@ -974,7 +1055,7 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
                     hd, seq, limit, workers, limit, w->partial);
     } else {
       void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *,
-                unsigned *, float *, int8_t *, float *, int) =
+                unsigned *, float *, int8_t *, float *, int, int) =
           hd == 128 ? split_kernel<128> : hd == 64 ? split_kernel<64> : split_kernel<32>;
       cudaLaunchConfig_t cfg = {};
       // About one wave of clusters (as many as fit at once): each walks the chunks y, y + gridDim.y, ... of the row.
@@ -994,14 +1075,17 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
       }
       const int per_kv = clusters / n_kv;
       cfg.gridDim.y = per_kv < 1 ? 1 : per_kv < limit ? per_kv : limit;
-      unsigned *tickets = n_kv <= kSplitTickets ? work_tickets(w) : nullptr;
+      unsigned *tickets =
+          n_kv <= kSplitTickets && limit <= split_merge_chunks(hd, nq) ? work_tickets(w) : nullptr;
       if (tickets)
         merged = true;
       attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
       attr[1].val.programmaticStreamSerializationAllowed = kc_pdl_enabled() ? 1 : 0;
       cfg.numAttrs = 2;
+      // A position read from device memory is the decode step's: the cache rows below it may be read early.
       cudaLaunchKernelEx(&cfg, k, q, kc, vc, pos_dev, pos0, n_kv, nq, seq, limit, workers, limit, w->partial, tickets,
-                         out, fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, gs);
+                         out, fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, gs,
+                         pos_dev ? 1 : 0);
     }
     if (!launched(name))
       return false;
@@ -1042,7 +1126,7 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
         void (*k)(const float *, long long, const float *, const float *, const int *, int, int, int, int, int, int,
                   int, int, int, int, int, float *) =
             hd == 128 ? tiled_kernel<128> : hd == 64 ? tiled_kernel<64> : tiled_kernel<32>;
-        kc_launch_pdl(k, dim3(n_kv, (wave + R - 1) / R), dim3(kThreads), tiled_smem_bytes(hd), st, q, q_ld, kc, vc,
+        kc_launch_pdl(k, dim3(n_kv, (wave + R - 1) / R), dim3(kTWarps * 32), tiled_smem_bytes(hd), st, q, q_ld, kc, vc,
                       pos_dev, pos0, row0, wave, rows, R, n_kv, nq, seq, limit, workers, cstride, w->partial);
       }
       if (!launched(name))
