@@ -491,6 +491,7 @@ def run_engine(args):
             if line.startswith("traffic_bytes_per_launch:"):
                 traffic = int(line.split(":")[1].split()[0])
     weights = sum(v for v in weight_bytes(a, world).values())
+    kernels = kernel_figures(kc, torch, args) if world == 1 and args.workload == "8b" else None
     line = {
         "metric": METRIC, "value": round(decode, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round((prefill_ms + decode_ms) / args.steps, 3),
@@ -514,6 +515,8 @@ def run_engine(args):
         "gpu_launches": int(st["kernel_launches"]),
         "clocks": clocks.summary(),
     }
+    if kernels:
+        line["kernels"] = kernels
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = reference_engine_sample(args.workload, steps=2, warmup=1)
     if rank == 0:
@@ -521,6 +524,28 @@ def run_engine(args):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def kernel_figures(kc, torch, args):
+    """The two kernel metrics BASELINE names beside the engine, measured in the same run on one GPU: the config 0 GEMV
+    (8192 x 2048, activations already quantized) as HBM GB/s and its fraction of the measured copy peak, and the
+    config 1 GEMM (k_gemm_q8 STORE, up and down projections at T = 2048) as int8 TOPS and the fraction of the int8
+    roof. Same timing method as --workload gemv / gemm."""
+    hbm, peak_kind = peaks()
+    int8_tops, int8_source = int8_peak()
+    alg, us = gemv_roofline(kc, torch, *GEMV_SHAPES["gemv"], launches=40, swiglu=False)
+    gbs = alg / (us / 1e6) / 1e9
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    gemm = []
+    for name, (N, K) in GEMM_SHAPES.items():
+        gemm += gemm_points(kc, torch, g, name, N, K, (GEMM_T[-1],), 3, 8, int8_tops, hbm)
+    for p in gemm:
+        del p["key"]
+    torch.cuda.empty_cache()
+    return {"config0_gemv": {"shape": "8192x2048", "kernel_us": round(us, 3), "achieved_gbs": round(gbs, 1),
+                             "frac": round(gbs / hbm, 4), "peak": hbm, "peak_source": f"{peak_kind} hbm_gbs"},
+            "config1_gemm": {"shapes": gemm, "int8_peak_tops": int8_tops, "peak_source": int8_source}}
 
 
 def engine_config(arch, P, D, world):
@@ -653,6 +678,48 @@ GEMM_SHAPES = {"up": (14336, 4096), "down": (4096, 14336)}  # (N weight rows, K)
 GEMM_T = (128, 512, 2048)
 
 
+def gemm_points(kc, torch, g, name, N, K, ts, warmup, launches, int8_tops, hbm, gs=64):
+    """k_gemm_q8 (STORE) of an N x K weight at each T in ts, timed with timed_graph over enough weight copies to exceed
+    L2 three times. Per T: microseconds, int8 TOPS and the fraction of the binding roof (the int8 tensor peak or HBM
+    for the call's bytes, whichever takes longer)."""
+    w = torch.randn((N, K), generator=g, device="cuda") * 0.02
+    wq, ws = kc.quantize(w, gs)
+    del w
+    wbytes = wq.numel() + ws.numel() * 4
+    copies = max(2, -(-3 * L2_BYTES // wbytes))
+    W = [(wq.clone(), ws.clone()) for _ in range(copies)]
+    out = []
+    for T in ts:
+        x = torch.randn((T, K), generator=g, device="cuda")
+        xq, xs = kc.quantize(x, gs)
+        c = torch.empty((T, N), device="cuda")
+
+        def launch(i):
+            kc.k_gemm_q8(xq, xs, T, K, gs, [kc.segment(c, W[i % copies])])
+
+        us = timed_graph(torch, launch, warmup, launches)
+        kc.status()
+        ops = 2.0 * T * N * K
+        nbytes = wbytes + T * K * (1 + 4 / gs) + 4 * T * N
+        t_tensor, t_hbm = ops / (int8_tops * 1e12), nbytes / (hbm * 1e9)
+        out.append({"shape": f"{name} T={T} N={N} K={K}", "key": (N, K, T), "us": round(us, 2),
+                    "int8_tops": round(ops / (us * 1e-6) / 1e12, 1), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                    "bound": "tensor" if t_tensor >= t_hbm else "hbm",
+                    "frac": round(max(t_tensor, t_hbm) / (us * 1e-6), 4)})
+        del x, xq, xs, c
+    del W, wq, ws
+    return out
+
+
+def int8_peak():
+    """The int8 tensor roof in TOPS: twice the measured dense bf16 GEMM peak (the dense int8/bf16 ratio), and its
+    source."""
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        return 2 * float(json.loads(pk.read_text())["bf16_tflops"]), "2 x measured bf16_tflops"
+    return 2 * 1590.0, "2 x fallback bf16_tflops"
+
+
 def run_gemm(args):
     """Config 1: k_gemm_q8 (STORE) on the 8B up (14336 x 4096) and down (4096 x 14336) projections at T = 128, 512 and
     2048 activation rows, each launch timed with CUDA events inside a captured graph, the weights rotating over enough
@@ -662,45 +729,17 @@ def run_gemm(args):
     kc = load_package()
     kc.init()
     hbm, peak_kind = peaks()
-    pk = ROOT / "MEASURED_PEAKS.json"
-    bf16 = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
-    int8_tops = 2 * bf16
-    gs, shapes = 64, []
+    int8_tops, int8_source = int8_peak()
+    shapes = []
     g = torch.Generator(device="cuda")
     g.manual_seed(2)
     for name, (N, K) in GEMM_SHAPES.items():
-        w = torch.randn((N, K), generator=g, device="cuda") * 0.02
-        wq, ws = kc.quantize(w, gs)
-        del w
-        wbytes = wq.numel() + ws.numel() * 4
-        copies = max(2, -(-3 * L2_BYTES // wbytes))
-        W = [(wq.clone(), ws.clone()) for _ in range(copies)]
-        for T in GEMM_T:
-            x = torch.randn((T, K), generator=g, device="cuda")
-            xq, xs = kc.quantize(x, gs)
-            c = torch.empty((T, N), device="cuda")
-
-            def launch(i):
-                kc.k_gemm_q8(xq, xs, T, K, gs, [kc.segment(c, W[i % copies])])
-
-            us = timed_graph(torch, launch, args.warmup, max(4, args.steps))
-            kc.status()
-            ops = 2.0 * T * N * K
-            nbytes = wbytes + T * K * (1 + 4 / gs) + 4 * T * N
-            t_tensor, t_hbm = ops / (int8_tops * 1e12), nbytes / (hbm * 1e9)
-            bound = "tensor" if t_tensor >= t_hbm else "hbm"
-            tops = ops / (us * 1e-6) / 1e12
-            shapes.append({"shape": f"{name} T={T} N={N} K={K}", "key": (N, K, T), "us": round(us, 2),
-                           "int8_tops": round(tops, 1),
-                           "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "bound": bound,
-                           "frac": round(max(t_tensor, t_hbm) / (us * 1e-6), 4)})
-            del x, xq, xs, c
-        del W, wq, ws
+        shapes += gemm_points(kc, torch, g, name, N, K, GEMM_T, args.warmup, max(4, args.steps), int8_tops, hbm)
     head = next(s for s in shapes if s["key"] == (*GEMM_SHAPES["up"], GEMM_T[-1]))
     line = {"metric": GEMM_METRIC, "value": head["int8_tops"],
             "unit": "TOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "int8",
             "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
-                      "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} hbm_gbs"},
+                      "source": f"{int8_source}; {peak_kind} hbm_gbs"},
             "shapes": shapes}
     if not args.no_cpu_baseline:
         ref = reference_gemm_points(list(GEMM_SHAPES.values()), GEMM_T)
@@ -742,9 +781,7 @@ def run_sweep(args):
     kc = load_package()
     kc.init()
     hbm, peak_kind = peaks()
-    pk = ROOT / "MEASURED_PEAKS.json"
-    bf16 = float(json.loads(pk.read_text())["bf16_tflops"]) if pk.exists() else 1590.0
-    int8_tops = 2 * bf16
+    int8_tops, int8_source = int8_peak()
     ts = [int(t) for t in args.sweep_t.split(",")] if args.sweep_t else list(SWEEP_T)
     splits = [int(s) for s in args.sweep_s.split(",")]
     gs, points, crossover = 64, [], {}
@@ -810,8 +847,7 @@ def run_sweep(args):
                                  "T": ts, "S": splits, "rows_rung_max_T": args.sweep_rows_max,
                                  "l2": "weights rotate over > 3x L2"},
                       "peaks": {"int8_tops": int8_tops, "hbm_gbs": hbm,
-                                "source": f"2 x {peak_kind if pk.exists() else 'fallback'} bf16_tflops; {peak_kind} "
-                                          "hbm_gbs"},
+                                "source": f"{int8_source}; {peak_kind} hbm_gbs"},
                       "crossover": crossover, "points": points}), flush=True)
 
 
