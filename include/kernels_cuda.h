@@ -256,7 +256,10 @@ void k_rope_kv_store_rows(float *q, size_t q_ld, const float *k, const float *v,
                           float *value_cache, const float *table, const int *position, int pos0, int rows, int n_heads,
                           int n_kv_heads, int head_dim, int seq_len);
 /* k_attention_batch_kv whose output is also quantized for the Wo product (k_quantize_rows fused, src/tp.c:562),
- * oq/os may be NULL; with a device `position` the rows are at *position + r. */
+ * oq/os may be NULL; with a device `position` the rows are at *position + r.
+ * With a device `position` and one row (the decode step), the kernel reads *position and requests the cache rows
+ * below it before it waits on the kernel launched just before it on the stream: that launch must write neither the
+ * position word nor any cache row below *position (a decode step's K/V store of row *position itself is fine). */
 void k_attention_q8_rows(float *out, int8_t *oq, float *os, const float *q, const float *key_cache,
                          const float *value_cache, AttentionWork *work, int n_heads, int n_kv_heads, int head_dim,
                          int seq_len, const int *position, int pos0, int rows, int gs);
