@@ -38,6 +38,7 @@ constexpr int kTile = 32;        // positions per tile of the batched variant (i
 constexpr int kSplitMax = 256;   // positions of a split chunk at most (attention_chunks' shortest bound)
 constexpr int kMaxHd = 256;      // the reference's AVX-512 attention takes head_dim <= 256
 constexpr int kMaxNq = 16;       // query heads per KV head (TILED_MAX_Q)
+constexpr int kMergeChunks = 16; // chunk partials a merge CTA stages at a time
 
 // ---- the reference's arithmetic, one lane ---------------------------------------------------------------------------
 
@@ -129,6 +130,8 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
   pdl_launch_dependents();
   __shared__ float red[kMaxHd / 32];
   __shared__ float vals[kMaxHd];
+  __shared__ float stage[kMergeChunks * (kMaxHd + 2)];
+  __shared__ float wts[kMergeChunks];
   const int h = blockIdx.x, rr = blockIdx.y, r = row0 + rr, d = threadIdx.x;
   const int base = pos_dev ? *pos_dev : pos0;
   const int vis = base + r + 1;  // positions the row sees
@@ -146,31 +149,39 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
     chunks = plan_chunks(vis, n_kv, limit, workers);
     live = chunks;
   }
-  const int slot = hd + 2;
+  const int slot = hd + 2, nt = blockDim.x;
   const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
-  // Every thread walks the chunks itself (the maximum, then in chunk order the weight, the sum and its element),
-  // eight chunks' values loaded at a time, all in flight together; the shared loads coalesce within each warp.
+  // The maximum over the chunks (order-free), every chunk's maximum loaded at once.
   float mx = -FLT_MAX;
-  for (int c = 0; c < live; c++)
+  for (int c = d; c < live; c += nt)
     mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + hd));
+#pragma unroll
+  for (int off = 16; off; off >>= 1)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((d & 31) == 0)
+    red[d >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < nt / 32; w++)
+    mx = fmaxf(mx, red[w]);
+  // Then the chunks in order, kMergeChunks at a time staged in shared memory by one round of parallel loads; each
+  // chunk's weight is taken once, and every thread adds the sums in chunk order.
   float sum = 0.0f, o = 0.0f;
-  for (int c0 = 0; c0 < live; c0 += 8) {
-    float mv[8], lv[8], av[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float *pc = pb + (long long)(c0 + i) * slot;
-      const bool in = c0 + i < live;
-      mv[i] = in ? __ldcg(pc + hd) : 0.0f;
-      lv[i] = in ? __ldcg(pc + hd + 1) : 0.0f;
-      av[i] = in && d < hd ? __ldcg(pc + d) : 0.0f;
+  for (int c0 = 0; c0 < live; c0 += kMergeChunks) {
+    const int nc = min(kMergeChunks, live - c0);
+    __syncthreads();  // the previous block's reads are done (and red's, above)
+    for (int i = d; i < nc * slot; i += nt)
+      stage[i] = __ldcg(pb + (long long)c0 * slot + i);
+    __syncthreads();
+    if (d < nc)
+      wts[d] = expf_libc(__fsub_rn(stage[d * slot + hd], mx));
+    __syncthreads();
+    for (int c = 0; c < nc; c++) {
+      const float w = wts[c];
+      sum = __fadd_rn(sum, __fmul_rn(w, stage[c * slot + hd + 1]));
+      if (d < hd)
+        o = __fadd_rn(o, __fmul_rn(w, stage[c * slot + d]));
     }
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-      if (c0 + i < live) {
-        const float w = expf_libc(__fsub_rn(mv[i], mx));
-        sum = __fadd_rn(sum, __fmul_rn(w, lv[i]));
-        o = __fadd_rn(o, __fmul_rn(w, av[i]));
-      }
   }
   (void)chunks;
   const float v = __fdiv_rn(o, sum);
@@ -211,6 +222,101 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
     if (d == g0)
       os[e / gs] = scl;
   }
+}
+
+// The same merge for a batch of rows on the fast shapes, a warp per (row, query head): lane c takes chunk c's maximum,
+// weight and weighted sum (the sum then runs over the chunks in order through shuffles), and each lane adds up
+// hd / 32 elements over the chunks in order, eight chunks' values in flight at a time. The optional quantization of
+// the head's outputs is done in the warp as well (group maxima by shuffles), so no CTA-wide step remains.
+// Requires gs % (hd / 32) == 0 with gs / (hd / 32) a power of two <= 32 when quantizing (merge_warp_quantizes).
+template <int HD>
+__global__ void __launch_bounds__(256) merge_warp_kernel(float *out, long long out_ld, int8_t *oq, float *os,
+                                                         const float *part, const int *pos_dev, int pos0, int row0,
+                                                         int m, int wave, int n_heads, int n_kv, int seq, int limit,
+                                                         int workers, int cstride, int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  constexpr int DL = HD / 32, slot = HD + 2;
+  const int lane = threadIdx.x & 31, pair = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pair >= wave * n_heads)
+    return;
+  const int rr = pair / n_heads, h = pair - rr * n_heads, r = row0 + rr;
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int vis = base + r + 1;  // positions the row sees
+  if (base < 0 || vis > seq) {
+    if (pair == 0 && lane == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+    return;
+  }
+  const TilePlan p = tile_plan(r, tile_rblock(n_heads / n_kv), m, base, n_kv, limit, workers);
+  const int live = min((vis + p.len - 1) / p.len, p.chunks);  // chunks past the visible positions hold nothing
+  const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
+  float mx = -FLT_MAX;
+  for (int c = lane; c < live; c += 32)
+    mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + HD));
+#pragma unroll
+  for (int off = 16; off; off >>= 1)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  float sum = 0.0f, o[DL];
+#pragma unroll
+  for (int e = 0; e < DL; e++)
+    o[e] = 0.0f;
+  for (int c0 = 0; c0 < live; c0 += 32) {
+    float w = 0.0f, wl = 0.0f;
+    if (c0 + lane < live) {
+      const float *pc = pb + (long long)(c0 + lane) * slot;
+      w = expf_libc(__fsub_rn(__ldcg(pc + HD), mx));
+      wl = __fmul_rn(w, __ldcg(pc + HD + 1));
+    }
+    const int nb = min(32, live - c0);
+    for (int i = 0; i < nb; i += 8) {
+      float a[8][DL];
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int e = 0; e < DL; e++)
+          a[u][e] = i + u < nb ? __ldcg(pb + (long long)(c0 + i + u) * slot + DL * lane + e) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const float wc = __shfl_sync(0xffffffffu, w, (i + u) & 31), wlc = __shfl_sync(0xffffffffu, wl, (i + u) & 31);
+        if (i + u < nb) {
+          sum = __fadd_rn(sum, wlc);
+#pragma unroll
+          for (int e = 0; e < DL; e++)
+            o[e] = __fadd_rn(o[e], __fmul_rn(wc, a[u][e]));
+        }
+      }
+    }
+  }
+  const long long e0 = (long long)r * out_ld + (long long)h * HD + DL * lane;
+  float v[DL];
+  bool bad = false;
+#pragma unroll
+  for (int e = 0; e < DL; e++) {
+    v[e] = __fdiv_rn(o[e], sum);
+    out[e0 + e] = v[e];
+    bad |= !isfinite(v[e]);
+  }
+  if (!oq)
+    return;
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0)
+      kc_raise(KC_ERR_NONFINITE);
+    return;
+  }
+  // Group maximum of |v| over the gs / DL lanes that hold the group (order-free), scale = max / 127.
+  float amax = 0.0f;
+#pragma unroll
+  for (int e = 0; e < DL; e++)
+    amax = fmaxf(amax, fabsf(v[e]));
+  for (int off = gs / DL / 2; off; off >>= 1)
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float scl = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+  for (int e = 0; e < DL; e++)
+    oq[e0 + e] = (int8_t)quantize_value(v[e], scl);
+  if ((DL * lane) % gs == 0)
+    os[e0 / gs] = scl;
 }
 
 // ---- slow restatements for the shapes the fast kernels do not take --------------------------------------------------
@@ -989,6 +1095,13 @@ bool fast_shape(int n_heads, int n_kv, int hd) {
   return (hd == 32 || hd == 64 || hd == 128) && nq <= kMaxNq && kMaxNq % nq == 0;
 }
 
+// Whether merge_warp_kernel can quantize a head's outputs in gs-groups: whole groups of hd / 32 elements per lane, a
+// power-of-two number of lanes per group.
+bool merge_warp_quantizes(int hd, int gs) {
+  const int dl = hd / 32, lanes = gs / dl;
+  return gs > 0 && hd % gs == 0 && gs % dl == 0 && lanes <= 32 && (lanes & (lanes - 1)) == 0;
+}
+
 // Shared-memory limits of the fast kernels, raised once per device.
 bool smem_ready(int hd) {
   const void *split = hd == 128  ? reinterpret_cast<const void *>(split_kernel<128>)
@@ -1131,9 +1244,18 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
       }
       if (!launched(name))
         return false;
-      kc_launch_pdl(merge_kernel, dim3(n_heads, wave), dim3(merge_threads), 0, st, out, out_ld,
-                    fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
-                    pos_dev, pos0, row0, rows, 1, n_heads, n_kv, hd, seq, limit, workers, cstride, gs);
+      if (fast && (!fused_q || merge_warp_quantizes(hd, gs))) {
+        void (*mk)(float *, long long, int8_t *, float *, const float *, const int *, int, int, int, int, int, int,
+                   int, int, int, int, int) =
+            hd == 128 ? merge_warp_kernel<128> : hd == 64 ? merge_warp_kernel<64> : merge_warp_kernel<32>;
+        kc_launch_pdl(mk, dim3((unsigned)(((long long)wave * n_heads + 7) / 8)), dim3(256), 0, st, out, out_ld,
+                      fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
+                      pos_dev, pos0, row0, rows, wave, n_heads, n_kv, seq, limit, workers, cstride, gs);
+      } else {
+        kc_launch_pdl(merge_kernel, dim3(n_heads, wave), dim3(merge_threads), 0, st, out, out_ld,
+                      fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, (const float *)w->partial,
+                      pos_dev, pos0, row0, rows, 1, n_heads, n_kv, hd, seq, limit, workers, cstride, gs);
+      }
       if (!launched(name))
         return false;
       row0 += wave;
