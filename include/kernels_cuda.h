@@ -255,6 +255,16 @@ void k_attention_batch_kv(float *out, const float *q, const float *key_cache, co
 void k_rope_kv_store_rows(float *q, size_t q_ld, const float *k, const float *v, size_t kv_ld, float *key_cache,
                           float *value_cache, const float *table, const int *position, int pos0, int rows, int n_heads,
                           int n_kv_heads, int head_dim, int seq_len);
+/* The decode step's k_rope_kv_store_rows + k_attention_q8_rows (one row, device position) in one launch: q, k, v are
+ * the unrotated QKV product of position *position; the queries and the new key are rotated with `table` (row
+ * *position) as k_rope_kv_store_rows does, the new K/V row is used directly and written into the caches for later
+ * positions, and q is left unrotated. Bitwise the two calls it replaces. The launch before it must write neither
+ * *position nor any cache row at or below *position. k_rope_attention_q8_step_ok(n_heads, n_kv_heads, head_dim, gs)
+ * tells whether a shape is supported (gs <= 0: without the output quantization); other shapes use the two calls. */
+int k_rope_attention_q8_step_ok(int n_heads, int n_kv_heads, int head_dim, int gs);
+void k_rope_attention_q8_step(float *out, int8_t *oq, float *os, const float *q, const float *k, const float *v,
+                              float *key_cache, float *value_cache, const float *table, AttentionWork *work,
+                              int n_heads, int n_kv_heads, int head_dim, int seq_len, const int *position, int gs);
 /* k_attention_batch_kv whose output is also quantized for the Wo product (k_quantize_rows fused, src/tp.c:562),
  * oq/os may be NULL; with a device `position` the rows are at *position + r.
  * With a device `position` and one row (the decode step), the kernel reads *position and requests the cache rows

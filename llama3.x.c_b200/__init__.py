@@ -125,6 +125,10 @@ _SIGNATURES = {
                                     _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
     "k_attention_q8_rows": (None, [_f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _c.POINTER(AttentionWork), _c.c_int,
                                    _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int, _c.c_int]),
+    "k_rope_attention_q8_step_ok": (_c.c_int, [_c.c_int, _c.c_int, _c.c_int, _c.c_int]),
+    "k_rope_attention_q8_step": (None, [_f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                        _c.POINTER(AttentionWork), _c.c_int, _c.c_int, _c.c_int, _c.c_int,
+                                        _c.c_void_p, _c.c_int]),
     "k_embed_q8_rows": (None, [_f32p, _c.c_void_p, K8Weight, _c.c_int, _c.c_int, _c.c_int, _c.c_int]),
     "k_add": (None, [_f32p, _f32p, _c.c_size_t]),
     "k_argmax_key": (None, [_c.c_void_p, _f32p, _c.c_int, _c.c_int]),
@@ -427,6 +431,16 @@ def k_attention_q8_rows(out, oq, os_, q, kc, vc, work, n_heads, n_kv_heads, head
                         gs):
     _call("k_attention_q8_rows", _ptr(out), _ptr(oq), _ptr(os_), _ptr(q), _ptr(kc), _ptr(vc), ctypes.byref(work),
           n_heads, n_kv_heads, head_dim, seq_len, _ptr(position) if position is not None else None, pos0, rows, gs)
+
+
+def k_rope_attention_q8_step_ok(n_heads, n_kv_heads, head_dim, gs):
+    return int(load().k_rope_attention_q8_step_ok(n_heads, n_kv_heads, head_dim, gs))
+
+
+def k_rope_attention_q8_step(out, oq, os_, q, k, v, kc, vc, table, work, n_heads, n_kv_heads, head_dim, seq_len,
+                             position, gs):
+    _call("k_rope_attention_q8_step", _ptr(out), _ptr(oq), _ptr(os_), _ptr(q), _ptr(k), _ptr(v), _ptr(kc), _ptr(vc),
+          _ptr(table), ctypes.byref(work), n_heads, n_kv_heads, head_dim, seq_len, _ptr(position), gs)
 
 
 def k_kv_store(cache, src, src_ld, pos0, count, n_kv_heads, head_dim, seq_len):

@@ -224,33 +224,16 @@ __global__ void __launch_bounds__(kMaxHd) merge_kernel(float *out, long long out
   }
 }
 
-// The same merge for a batch of rows on the fast shapes, a warp per (row, query head): lane c takes chunk c's maximum,
-// weight and weighted sum (the sum then runs over the chunks in order through shuffles), and each lane adds up
-// hd / 32 elements over the chunks in order, eight chunks' values in flight at a time. The optional quantization of
-// the head's outputs is done in the warp as well (group maxima by shuffles), so no CTA-wide step remains.
-// Requires gs % (hd / 32) == 0 with gs / (hd / 32) a power of two <= 32 when quantizing (merge_warp_quantizes).
+// merge_chunks for one (row, query head) by one warp: lane c takes chunk c's maximum, weight and weighted sum (the sum
+// then runs over the chunks in order through shuffles), and each lane adds up hd / 32 elements over the chunks in
+// order, eight chunks' values in flight at a time. pb: the head's chunk partials (slot hd + 2 floats apart), `live`
+// of them; dst: its hd outputs; with oq, the outputs are also quantized in gs-groups (group maxima by shuffles over
+// the gs / (hd / 32) lanes that hold a group; merge_warp_quantizes) into oq[e0 ..] and os[e0 / gs ..], e0 being the
+// outputs' element index. Returns false (the error raised) when an output is not finite, before quantizing.
 template <int HD>
-__global__ void __launch_bounds__(256) merge_warp_kernel(float *out, long long out_ld, int8_t *oq, float *os,
-                                                         const float *part, const int *pos_dev, int pos0, int row0,
-                                                         int m, int wave, int n_heads, int n_kv, int seq, int limit,
-                                                         int workers, int cstride, int gs) {
-  pdl_wait();
-  pdl_launch_dependents();
+__device__ bool merge_head_warp(const float *pb, int live, float *dst, int8_t *oq, float *os, long long e0, int gs) {
   constexpr int DL = HD / 32, slot = HD + 2;
-  const int lane = threadIdx.x & 31, pair = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (pair >= wave * n_heads)
-    return;
-  const int rr = pair / n_heads, h = pair - rr * n_heads, r = row0 + rr;
-  const int base = pos_dev ? *pos_dev : pos0;
-  const int vis = base + r + 1;  // positions the row sees
-  if (base < 0 || vis > seq) {
-    if (pair == 0 && lane == 0)
-      kc_raise(KC_ERR_BAD_ARGS);
-    return;
-  }
-  const TilePlan p = tile_plan(r, tile_rblock(n_heads / n_kv), m, base, n_kv, limit, workers);
-  const int live = min((vis + p.len - 1) / p.len, p.chunks);  // chunks past the visible positions hold nothing
-  const float *pb = part + ((long long)rr * n_heads + h) * cstride * slot;
+  const int lane = threadIdx.x & 31;
   float mx = -FLT_MAX;
   for (int c = lane; c < live; c += 32)
     mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + HD));
@@ -288,21 +271,20 @@ __global__ void __launch_bounds__(256) merge_warp_kernel(float *out, long long o
       }
     }
   }
-  const long long e0 = (long long)r * out_ld + (long long)h * HD + DL * lane;
   float v[DL];
   bool bad = false;
 #pragma unroll
   for (int e = 0; e < DL; e++) {
     v[e] = __fdiv_rn(o[e], sum);
-    out[e0 + e] = v[e];
+    dst[DL * lane + e] = v[e];
     bad |= !isfinite(v[e]);
   }
   if (!oq)
-    return;
+    return true;
   if (__any_sync(0xffffffffu, bad)) {
     if (lane == 0)
       kc_raise(KC_ERR_NONFINITE);
-    return;
+    return false;
   }
   // Group maximum of |v| over the gs / DL lanes that hold the group (order-free), scale = max / 127.
   float amax = 0.0f;
@@ -312,11 +294,39 @@ __global__ void __launch_bounds__(256) merge_warp_kernel(float *out, long long o
   for (int off = gs / DL / 2; off; off >>= 1)
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
   const float scl = __fdiv_rn(amax, 127.0f);
+  const long long el = e0 + DL * lane;
 #pragma unroll
   for (int e = 0; e < DL; e++)
-    oq[e0 + e] = (int8_t)quantize_value(v[e], scl);
+    oq[el + e] = (int8_t)quantize_value(v[e], scl);
   if ((DL * lane) % gs == 0)
-    os[e0 / gs] = scl;
+    os[el / gs] = scl;
+  return true;
+}
+
+// The merge of a batch of rows on the fast shapes, a warp per (row, query head) (merge_head_warp), so no CTA-wide
+// step remains. Quantizes only when merge_warp_quantizes(hd, gs).
+template <int HD>
+__global__ void __launch_bounds__(256) merge_warp_kernel(float *out, long long out_ld, int8_t *oq, float *os,
+                                                         const float *part, const int *pos_dev, int pos0, int row0,
+                                                         int m, int wave, int n_heads, int n_kv, int seq, int limit,
+                                                         int workers, int cstride, int gs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31, pair = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (pair >= wave * n_heads)
+    return;
+  const int rr = pair / n_heads, h = pair - rr * n_heads, r = row0 + rr;
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int vis = base + r + 1;  // positions the row sees
+  if (base < 0 || vis > seq) {
+    if (pair == 0 && lane == 0)
+      kc_raise(KC_ERR_BAD_ARGS);
+    return;
+  }
+  const TilePlan p = tile_plan(r, tile_rblock(n_heads / n_kv), m, base, n_kv, limit, workers);
+  const int live = min((vis + p.len - 1) / p.len, p.chunks);  // chunks past the visible positions hold nothing
+  const long long e0 = (long long)r * out_ld + (long long)h * HD;
+  merge_head_warp<HD>(part + ((long long)rr * n_heads + h) * cstride * (HD + 2), live, out + e0, oq, os, e0, gs);
 }
 
 // ---- slow restatements for the shapes the fast kernels do not take --------------------------------------------------
@@ -488,103 +498,25 @@ __device__ __forceinline__ void tree_step(const float *in, float *outv, int L, i
 }
 
 // Group g's merge by the CTA that finished its last chunk: merge_kernel's arithmetic (the maximum over the chunks, then
-// in chunk order sum += w l and o += w acc with w = expf(m_c - max), then o / sum, then the optional quantization)
-// for the nq heads at once. A warp per head loads every chunk's maximum and sum at once and computes the weights and
-// the sum; then every thread loads the chunk accumulators of its outputs kBatch at a time (all in flight together)
-// and adds them in chunk order.
-// Chunks per head whose weights and sums the fused merge keeps in shared memory, beside the head sums, the outputs and
-// the group scales (608 at head_dim 128 with 16 query heads per KV head: a 155648-position context). Longer contexts
-// merge in merge_kernel.
-__host__ __device__ constexpr int split_merge_chunks(int hd, int nq) {
-  return (int)((split_smem_floats(hd, nq) - (kMaxNq + 2 * (size_t)nq * hd)) / (2 * (size_t)nq));
+// in chunk order sum += w l and o += w acc with w = expf(m_c - max), then o / sum, then the optional quantization),
+// a warp per query head of the group (merge_head_warp).
+template <int HD>
+__device__ void merge_group(const float *part, int g, int nq, int chunks, int cstride, float *out, int8_t *oq,
+                            float *os, int gs) {
+  for (int hh = threadIdx.x >> 5; hh < nq; hh += kSplitThreads / 32) {
+    const long long e0 = (long long)(g * nq + hh) * HD;
+    merge_head_warp<HD>(part + (long long)(g * nq + hh) * cstride * (HD + 2), chunks, out + e0, oq, os, e0, gs);
+  }
 }
 
-template <int HD>
-__device__ void merge_group(float *sm, const float *part, int g, int nq, int chunks, int cstride,
-                            float *out, int8_t *oq, float *os, int gs) {
-  constexpr int slot = HD + 2, nt = kSplitThreads, kOut = (kMaxNq * HD + nt - 1) / nt, kBatch = 16;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, outs = nq * HD;
-  float *hs = sm, *vals = hs + kMaxNq, *scl = vals + nq * HD, *wts = scl + nq * HD;
-  const int wcap = split_merge_chunks(HD, nq);  // the host merges here only when chunks <= wcap
-  const float *pg = part + (long long)g * nq * cstride * slot;
-  for (int hh = warp; hh < nq; hh += nt / 32) {
-    const float *ph = pg + (long long)hh * cstride * slot;
-    float mx = -FLT_MAX;
-    for (int c = lane; c < chunks; c += 32)
-      mx = fmaxf(mx, __ldcg(ph + (long long)c * slot + HD));
-#pragma unroll
-    for (int off = 16; off; off >>= 1)
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    // The weights and sums into shared memory, then the sum in chunk order by lane 0.
-    float *wh = wts + hh * wcap, *lh = wh + nq * wcap;
-    for (int c = lane; c < chunks; c += 32) {
-      wh[c] = expf_libc(__fsub_rn(__ldcg(ph + (long long)c * slot + HD), mx));
-      lh[c] = __ldcg(ph + (long long)c * slot + HD + 1);
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float sum = 0.0f;
-      for (int c = 0; c < chunks; c++)
-        sum = __fadd_rn(sum, __fmul_rn(wh[c], lh[c]));
-      hs[hh] = sum;
-    }
-  }
-  __syncthreads();
-  float *dst = out + (long long)g * outs;
-  int bad = 0;
-#pragma unroll
-  for (int u = 0; u < kOut; u++) {
-    const int o = tid + u * nt;
-    if (o < outs) {
-      const int hh = o / HD, d = o - hh * HD;
-      const float *pc = pg + (long long)hh * cstride * slot + d;
-      const float *wh = wts + hh * wcap;
-      float acc = 0.0f;
-      for (int c0 = 0; c0 < chunks; c0 += kBatch) {
-        float a[kBatch];
-#pragma unroll
-        for (int i = 0; i < kBatch; i++)
-          a[i] = c0 + i < chunks ? __ldcg(pc + (long long)(c0 + i) * slot) : 0.0f;
-#pragma unroll
-        for (int i = 0; i < kBatch; i++) {
-          const int c = c0 + i;
-          if (c < chunks)
-            acc = __fadd_rn(acc, __fmul_rn(wh[c], a[i]));
-        }
-      }
-      const float v = __fdiv_rn(acc, hs[hh]);
-      dst[o] = v;
-      vals[o] = v;
-      bad |= !isfinite(v);
-    }
-  }
-  if (!oq || gs <= 0 || HD % gs)
-    return;
-  if (__syncthreads_or(bad)) {
-    if (tid == 0)
-      kc_raise(KC_ERR_NONFINITE);
-    return;
-  }
-  // Group maxima of |v| (order-free), a warp per group; scale = max / 127.
-  for (int grp = warp; grp < outs / gs; grp += nt / 32) {
-    float a = 0.0f;
-    for (int i = lane; i < gs; i += 32)
-      a = fmaxf(a, fabsf(vals[grp * gs + i]));
-#pragma unroll
-    for (int off = 16; off; off >>= 1)
-      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-    if (lane == 0)
-      scl[grp] = __fdiv_rn(a, 127.0f);
-  }
-  __syncthreads();
-  const long long e0 = (long long)g * outs;
-  for (int o = tid; o < outs; o += nt) {
-    const float sc = scl[o / gs];
-    oq[e0 + o] = (int8_t)quantize_value(vals[o], sc);
-    if (o % gs == 0)
-      os[(e0 + o) / gs] = sc;
-  }
-}
+// The decode step's RoPE and K/V store folded into the split kernel (k_rope_attention_q8_step): q, k, v are the QKV
+// product of the newest position, unrotated; the kernel rotates q and k with the table row of that position as
+// rope_store_kernel does, uses the newest row from registers instead of the cache, and writes it into the caches
+// (kc, vc) for the positions after it. table == nullptr: off (q is then the rotated queries, the caches complete).
+struct RopeStep {
+  const float *k, *v, *table;
+  float *kc, *vc;
+};
 
 // K rows [r0, r1) of the chunk starting at position t0 into this CTA's K quarter (its first row k0), one bulk copy.
 template <int HD>
@@ -609,7 +541,7 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
                                                               const int *pos_dev, int pos0, int n_kv, int nq, int seq,
                                                               int limit, int workers, int cstride, float *part,
                                                               unsigned *tickets, float *out, int8_t *oq, float *os,
-                                                              int gs, int early) {
+                                                              int gs, int early, const RopeStep rope) {
   constexpr int QD = HD / kSplitCtas;  // elements of the head this CTA's P.V covers
   extern __shared__ __align__(16) float sm[];
   float *Kq = sm, *Vq = Kq + kSplitRows * HD, *Q = Vq + kSplitMax * QD, *Sl = Q + nq * HD, *S = Sl + nq * kSplitRows;
@@ -646,28 +578,61 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
     const int t0 = (int)((long long)P * c / chunks), n = (int)((long long)P * (c + 1) / chunks) - t0;  // <= 256
     const int k0 = n * k / kSplitCtas, kn = n * (k + 1) / kSplitCtas - k0;  // this CTA's K rows
     // Rows [t0 + r0, t0 + r1) of K (this CTA's) and V (the whole chunk, this CTA's columns); before the wait only
-    // those below the newest row.
-    if (tid == 0 && kn > 0)
-      mbar_arrive_expect_tx(bar, (unsigned)kn * HD * sizeof(float));
-    const int split_at = waited ? n : min(n, max(0, newest - t0));  // chunk rows safe to read before the wait
+    // those below the newest row. With the RoPE step the newest row comes from the QKV product instead (new_k: it
+    // is one of this CTA's K rows), and Q is rotated here rather than copied.
+    const bool rope_on = rope.table != nullptr, has_new = rope_on && newest - t0 < n;
+    const bool new_k = has_new && newest - t0 >= k0 && newest - t0 < k0 + kn;
+    if (tid == 0)
+      mbar_arrive_expect_tx(bar, (unsigned)(kn - (new_k ? 1 : 0) + (rope_on ? 0 : nq)) * HD * sizeof(float));
+    const int below_new = min(n, max(0, newest - t0));
+    const int split_at = rope_on || !waited ? below_new : n;  // chunk rows to copy now (the RoPE step: ever)
     split_copy_k<HD>(Kq, Kh, bar, t0, k0, k0, min(k0 + kn, max(k0, split_at)));
     split_copy_v<HD>(Vq, Vh, t0, k, 0, split_at);
     if (!waited) {
       pdl_wait();
       pdl_launch_dependents();
       waited = true;
-      split_copy_k<HD>(Kq, Kh, bar, t0, k0, max(k0, split_at), k0 + kn);
-      split_copy_v<HD>(Vq, Vh, t0, k, split_at, n);
+      if (!rope_on) {
+        split_copy_k<HD>(Kq, Kh, bar, t0, k0, max(k0, split_at), k0 + kn);
+        split_copy_v<HD>(Vq, Vh, t0, k, split_at, n);
+      }
+    }
+    if (!rope_on) {
+      if (tid == 0)  // the group's queries (written by the previous kernel: after the wait)
+        bulk_g2s(Q, q + (long long)g * nq * HD, (unsigned)nq * HD * sizeof(float), bar);
+    } else {
+      // rope_store_kernel's rotation of the pairs (j, j + 1) with the newest position's table row.
+      const float *tr = rope.table + (long long)newest * 2 * HD;
+      for (int i = tid; i < nq * HD / 2; i += kSplitThreads) {
+        const int h = i / (HD / 2), j = 2 * (i - h * (HD / 2));
+        const float *src = q + (long long)(g * nq + h) * HD + j;
+        const float cs = tr[j], sn = tr[HD + j + 1], a0 = src[0], b0 = src[1];
+        Q[h * HD + j] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(b0, sn));
+        Q[h * HD + j + 1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, cs));
+      }
+      if (has_new) {
+        const float *kr = rope.k + (long long)g * HD, *vr = rope.v + (long long)g * HD;
+        float *kcw = rope.kc + ((long long)g * seq + newest) * HD, *vcw = rope.vc + ((long long)g * seq + newest) * HD;
+        for (int i = tid; i < HD / 2; i += kSplitThreads) {
+          const int j = 2 * i;
+          const float cs = tr[j], sn = tr[HD + j + 1], a0 = kr[j], b0 = kr[j + 1];
+          const float o0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(b0, sn));
+          const float o1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(b0, cs));
+          if (new_k)
+            Kq[(newest - t0 - k0) * HD + j] = o0, Kq[(newest - t0 - k0) * HD + j + 1] = o1;
+          if (k == 0)  // the cache row, for the positions after this one
+            kcw[j] = o0, kcw[j + 1] = o1;
+        }
+        for (int i = tid; i < QD; i += kSplitThreads)
+          Vq[(newest - t0) * QD + i] = vr[k * QD + i];
+        if (k == 0)
+          for (int i = tid; i < HD; i += kSplitThreads)
+            vcw[i] = vr[i];
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int i = tid; i < nq * HD; i += kSplitThreads)
-      Q[i] = q[(long long)g * nq * HD + i];
-    __syncthreads();
-    bool ok = true;
-    if (kn > 0) {
-      ok = __syncthreads_and(mbar_wait_bounded(bar, phase));
-      phase ^= 1u;
-    }
+    const bool ok = __syncthreads_and(mbar_wait_bounded(bar, phase));
+    phase ^= 1u;
     if (ok) {
       // Scores: a warp per (16 positions, 2 heads), a half-warp per head, lane L the reference's lane L (its FMA
       // chain over elements 16 v + L); the 16-lane tree of all 16 positions runs as one butterfly, after which lane
@@ -812,27 +777,29 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
   }
   __syncthreads();
   if (last)
-    merge_group<HD>(sm, part, g, nq, chunks, cstride, out, oq, os, gs);
+    merge_group<HD>(part, g, nq, chunks, cstride, out, oq, os, gs);
 }
 
 // ---- the tiled variant for a batch of rows (prefill) ---------------------------------------------------------------
 // CTA (KV head g, group of R rows = whole blocks): its query vectors v = (row - first row) * nq + head, at most 128,
 // over the 32-position K/V tiles of the group's causal range (bulk copies, two buffers, the next tile's copy in
 // flight; K rows padded in shared memory so that rows read together sit in different banks). Warp w owns query
-// vectors 16 w .. 16 w + 15 from the scores to the P.V product, so within a tile its warps never wait for one
-// another:
-//  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 16 w + lv + 4 i and positions lp + 8 j (i, j < 4),
-//    each score one FMA chain over the head's elements in order, operands read four elements at a time;
+// vectors 8 w .. 8 w + 7 from the scores to the P.V product, so within a tile its warps never wait for one another
+// (16 warps, four per SM sub-partition, cover one another's shared-memory and FMA latencies):
+//  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 8 w + lv + 4 i (i < 2) and positions lp + 8 j
+//    (j < 4), each score one FMA chain over the head's elements in order, operands read four elements at a time;
 //  - the online softmax of the tile for each query, among the 8 lanes that share it: the tile maximum, the rescale of
 //    the running sum, exp512, and the tile sum in the reference's order (positions p and 16 + p are the same lane's
 //    j and j + 2, then the 16-lane tree by shuffles across the 8 lanes); every lane keeps the queries' running
 //    maximum, sum and chunk;
-//  - P.V: every lane takes the warp's 16 queries x hd / 32 elements, one FMA chain per (query, element) over the
+//  - P.V: every lane takes the warp's 8 queries x hd / 32 elements, one FMA chain per (query, element) over the
 //    tile's positions in order.
 // A query whose chunk (its block's plan) changes at a tile writes the finished chunk's partial first and starts again
 // from zero. The partials are merged by merge_kernel.
 constexpr int kTQ = 128;            // query vectors of a batched CTA
-constexpr int kTWarps = kTQ / 16;   // 8 warps of 16 query vectors
+constexpr int kQW = 8;              // query vectors of a warp
+constexpr int kQL = kQW / 4;        // query vectors of a lane in the score role
+constexpr int kTWarps = kTQ / kQW;  // 16 warps
 constexpr int kPStride = kTQ + 4;   // probabilities [tile position][query vector], padded
 
 __host__ __device__ constexpr int tiled_kstride(int hd) { return hd + 4; }  // padded K and Q rows
@@ -894,19 +861,20 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
     return part + (((long long)(rl0 + v / nq) * n_heads + g * nq + v % nq) * cstride + chunk) * (HD + 2);
   };
   // Score / softmax role: queries 16 warp + lv + 4 i, positions lp + 8 j.
-  const int lv = lane >> 3, lp = lane & 7, v0 = 16 * warp;
-  int vis[4], len[4], cur[4] = {-1, -1, -1, -1};
-  float mrun[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX}, lrun[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int lv = lane >> 3, lp = lane & 7, v0 = kQW * warp;
+  int vis[kQL], len[kQL], cur[kQL];
+  float mrun[kQL], lrun[kQL];
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < kQL; i++) {
+    cur[i] = -1, mrun[i] = -FLT_MAX, lrun[i] = 0.0f;
     const int v = v0 + lv + 4 * i, r = row0 + rl0 + v / nq;
     vis[i] = v < qv ? base + r + 1 : 0;
     len[i] = tile_plan(r, rblock, m, base, n_kv, limit, workers).len;
   }
-  // P.V role: the warp's 16 queries x elements DL lane ...
-  float acc[16][DL];
+  // P.V role: the warp's kQW queries x elements DL lane ...
+  float acc[kQW][DL];
 #pragma unroll
-  for (int x = 0; x < 16; x++)
+  for (int x = 0; x < kQW; x++)
 #pragma unroll
     for (int e = 0; e < DL; e++)
       acc[x][e] = 0.0f;
@@ -920,23 +888,23 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
     if (warp == 0 && k + 1 < ntiles)
       issue(k + 1);  // its buffer's last readers finished before the barrier that ended the previous tile
     const float *Kt = Kb + b * kTile * KS;
-    float s[4][4];
+    float s[kQL][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < kQL; i++)
 #pragma unroll
       for (int j = 0; j < 4; j++)
         s[i][j] = 0.0f;
 #pragma unroll 2
     for (int d = 0; d < HD; d += 4) {
-      float4 qq[4], kk[4];
+      float4 qq[kQL], kk[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int i = 0; i < kQL; i++)
         qq[i] = *reinterpret_cast<const float4 *>(qs + (v0 + lv + 4 * i) * KS + d);
 #pragma unroll
       for (int j = 0; j < 4; j++)
         kk[j] = *reinterpret_cast<const float4 *>(Kt + (lp + 8 * j) * KS + d);
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int i = 0; i < kQL; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) {
           s[i][j] = __fmaf_rn(qq[i].x, kk[j].x, s[i][j]);
@@ -948,7 +916,7 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
     // Online softmax, query by query. The 8 lanes of a query agree on whether it sees the tile, and every shuffle runs
     // in every lane; the state only moves where the query sees positions.
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < kQL; i++) {
       const int v = v0 + lv + 4 * i, nv = max(0, min(kTile, vis[i] - t));
       const bool live = nv > 0;
       float alpha = 1.0f;
@@ -1000,7 +968,7 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
     }
     __syncwarp();
 #pragma unroll
-    for (int x = 0; x < 16; x++) {
+    for (int x = 0; x < kQW; x++) {
       const int v = v0 + x, f = fl[v];
       if (f >= 0) {  // the query's previous chunk is finished: write it out, start from zero
         float *o = out_of(v, f) + DL * lane;
@@ -1034,7 +1002,7 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
         vv[0] = Vt[p * HD];
       }
 #pragma unroll
-      for (int y = 0; y < 4; y++) {
+      for (int y = 0; y < kQW / 4; y++) {
         const float4 e4 = *reinterpret_cast<const float4 *>(Pw + p * kPStride + 4 * y);
         const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
@@ -1053,7 +1021,7 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
   }
   // The last chunk of every query.
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
+  for (int i = 0; i < kQL; i++) {
     const int v = v0 + lv + 4 * i;
     if (lp == 0) {
       if (cur[i] >= 0) {
@@ -1066,7 +1034,7 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
   }
   __syncwarp();
 #pragma unroll
-  for (int x = 0; x < 16; x++) {
+  for (int x = 0; x < kQW; x++) {
     const int v = v0 + x;
     if (v < qv && fl[v] >= 0) {
       float *o = out_of(v, fl[v]) + DL * lane;
@@ -1138,7 +1106,7 @@ unsigned *work_tickets(AttentionWork *w) { return reinterpret_cast<unsigned *>(w
 // One row (decode) or a batch of rows of attention into out (row stride out_ld), optionally quantized into oq/os.
 bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, float *os, const float *q,
                     long long q_ld, const float *kc, const float *vc, AttentionWork *w, int n_heads, int n_kv, int hd,
-                    int seq, const int *pos_dev, int pos0, int rows, int gs) {
+                    int seq, const int *pos_dev, int pos0, int rows, int gs, const RopeStep *rope = nullptr) {
   if (!w || !w->partial)
     return kc_fail("%s: attention work is not initialized", name);
   if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || hd <= 0 || hd > kMaxHd || seq <= 0 || rows < 0 ||
@@ -1168,7 +1136,7 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
                     hd, seq, limit, workers, limit, w->partial);
     } else {
       void (*k)(const float *, const float *, const float *, const int *, int, int, int, int, int, int, int, float *,
-                unsigned *, float *, int8_t *, float *, int, int) =
+                unsigned *, float *, int8_t *, float *, int, int, RopeStep) =
           hd == 128 ? split_kernel<128> : hd == 64 ? split_kernel<64> : split_kernel<32>;
       cudaLaunchConfig_t cfg = {};
       // About one wave of clusters (as many as fit at once): each walks the chunks y, y + gridDim.y, ... of the row.
@@ -1188,8 +1156,9 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
       }
       const int per_kv = clusters / n_kv;
       cfg.gridDim.y = per_kv < 1 ? 1 : per_kv < limit ? per_kv : limit;
+      // The fused merge quantizes in the warp (merge_warp_quantizes); other group sizes merge in merge_kernel.
       unsigned *tickets =
-          n_kv <= kSplitTickets && limit <= split_merge_chunks(hd, nq) ? work_tickets(w) : nullptr;
+          n_kv <= kSplitTickets && (!fused_q || merge_warp_quantizes(hd, gs)) ? work_tickets(w) : nullptr;
       if (tickets)
         merged = true;
       attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1198,7 +1167,7 @@ bool attention_rows(const char *name, float *out, long long out_ld, int8_t *oq, 
       // A position read from device memory is the decode step's: the cache rows below it may be read early.
       cudaLaunchKernelEx(&cfg, k, q, kc, vc, pos_dev, pos0, n_kv, nq, seq, limit, workers, limit, w->partial, tickets,
                          out, fused_q ? oq : (int8_t *)nullptr, fused_q ? os : (float *)nullptr, gs,
-                         pos_dev ? 1 : 0);
+                         pos_dev ? 1 : 0, rope ? *rope : RopeStep{});
     }
     if (!launched(name))
       return false;
@@ -1335,6 +1304,26 @@ void k_attention_batch_kv(float *out, const float *q, const float *key_cache, co
   const long long ld = (long long)n_heads * head_dim;
   attention_rows("k_attention_batch_kv", out, ld, nullptr, nullptr, q, ld, key_cache, value_cache, work, n_heads,
                  n_kv_heads, head_dim, seq_len, nullptr, pos0, m, 0);
+}
+
+int k_rope_attention_q8_step_ok(int n_heads, int n_kv_heads, int head_dim, int gs) {
+  return n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0 && n_kv_heads <= kSplitTickets &&
+         fast_shape(n_heads, n_kv_heads, head_dim) && (gs <= 0 || merge_warp_quantizes(head_dim, gs));
+}
+
+void k_rope_attention_q8_step(float *out, int8_t *oq, float *os, const float *q, const float *k, const float *v,
+                              float *key_cache, float *value_cache, const float *table, AttentionWork *work,
+                              int n_heads, int n_kv_heads, int head_dim, int seq_len, const int *position, int gs) {
+  if (!position || !q || !k || !v || !table || !key_cache || !value_cache ||
+      !k_rope_attention_q8_step_ok(n_heads, n_kv_heads, head_dim, oq ? gs : 0)) {
+    kc_fail("k_rope_attention_q8_step: needs a device position, head_dim 32, 64 or 128, query heads per KV head "
+            "dividing 16, and a group size whose groups a warp's lanes hold");
+    return;
+  }
+  const long long ld = (long long)n_heads * head_dim;
+  const RopeStep rope = {k, v, table, key_cache, value_cache};
+  attention_rows("k_rope_attention_q8_step", out, ld, oq, os, q, ld, key_cache, value_cache, work, n_heads,
+                 n_kv_heads, head_dim, seq_len, position, 0, 1, gs, &rope);
 }
 
 void k_attention_q8_rows(float *out, int8_t *oq, float *os, const float *q, const float *key_cache,

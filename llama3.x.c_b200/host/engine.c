@@ -66,6 +66,7 @@ typedef struct {
   int w8a32;  /* LLAMA_Q8_ACTIVATIONS=fp32: fp32 activations against the int8 weights, one row per forward */
   long batch_env; /* rows per engine_forward_batch the environment asks for, before the context cap */
   int fused;  /* the decode step's fused GEMV modes fit these shapes (fused_shapes) */
+  int rope_step; /* the decode step's RoPE + K/V store run inside its attention launch (k_rope_attention_q8_step) */
   int reduce_fused; /* with peer: Wo and W2 reduce inside their GEMV (kd_peer_matmul_q8_add, reduce_shapes) */
   float *xb;  /* W8A32: the normalized row the projections read */
   void *graph_logits, *graph_greedy;
@@ -291,6 +292,7 @@ static int reduce_shapes(const Engine *e) {
  * which decode kernels the shard shapes allow. */
 static int max_batch_for(Engine *e) {
   e->fused = fused_shapes(e); /* plan() has set the shard shapes */
+  e->rope_step = k_rope_attention_q8_step_ok(e->hl, e->kl, e->hd, e->gs);
   e->reduce_fused = reduce_shapes(e);
   return e->w8a32 ? 1 : e->batch_env < e->context ? (int)e->batch_env : e->context;
 }
@@ -912,10 +914,15 @@ static void decode_layers(Engine *e) {
                             segment(e->k, e->kvl, y->wk, none, e->kvl, GEMM_STORE),
                             segment(e->v, e->kvl, y->wv, none, e->kvl, GEMM_STORE)};
     k_matmul_q8_fused(e->x, y->rms_att, p->norm_eps, dim, dim, gs, qkv, 3, NULL);
-    k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
-                         e->context);
-    k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev, 0,
-                        1, gs);
+    if (e->rope_step) {
+      k_rope_attention_q8_step(e->att, e->aq, e->as, e->q, e->k, e->v, kc, vc, e->rope, &e->attn, e->hl, e->kl, e->hd,
+                               e->context, e->pos_dev, gs);
+    } else {
+      k_rope_kv_store_rows(e->q, e->ql, e->k, e->v, e->kvl, kc, vc, e->rope, e->pos_dev, 0, 1, e->hl, e->kl, e->hd,
+                           e->context);
+      k_attention_q8_rows(e->att, e->aq, e->as, e->q, kc, vc, &e->attn, e->hl, e->kl, e->hd, e->context, e->pos_dev,
+                          0, 1, gs);
+    }
     /* Tensor parallel with the peer path: the shard's product and the sum over ranks in one kernel. */
     const int reduce_in_gemv = e->S > 1 && e->peer && e->reduce_fused;
     if (e->S == 1) {

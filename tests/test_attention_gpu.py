@@ -130,6 +130,74 @@ def test_device_position_matches_host_position(kc, n_heads, n_kv, seq):
         kc.k_attention_free(work)
 
 
+@pytest.mark.parametrize("n_heads,n_kv,hd,gs", [(32, 8, 128, 64), (8, 2, 64, 32), (16, 2, 128, 128)])
+def test_decode_step_quantized_output(kc, oracle, n_heads, n_kv, hd, gs):
+    """One row at a device position with the output quantized for Wo (the decode step's call): the fp32 output
+    bitwise the host-position call and the oracle, the int8 values and group scales bitwise k_quantize of it, across
+    chunk counts 1 to 9 (the merge that the last CTA of each KV head runs, its quantization in the warp)."""
+    seq = 4096
+    rng = np.random.default_rng(hd + gs)
+    qh = rng.standard_normal(n_heads * hd, dtype=np.float32)
+    kh = rng.standard_normal((n_kv, seq, hd), dtype=np.float32)
+    vh = rng.standard_normal((n_kv, seq, hd), dtype=np.float32)
+    q, kcache, vcache = dev(qh), dev(kh), dev(vh)
+    work = kc.attention_work(n_heads, n_kv, hd, seq)
+    try:
+        for pos in (5, 255, 256, 2303):
+            a, b = torch.zeros(n_heads * hd, device="cuda"), torch.zeros(n_heads * hd, device="cuda")
+            oq = torch.zeros(n_heads * hd, dtype=torch.int8, device="cuda")
+            os_ = torch.zeros(n_heads * hd // gs, device="cuda")
+            kc.k_attention_kv(a, q, kcache, vcache, work, n_heads, n_kv, hd, seq, pos)
+            p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+            kc.k_attention_q8_rows(b, oq, os_, q, kcache, vcache, work, n_heads, n_kv, hd, seq, p, 0, 1, gs)
+            kc.status()
+            got = host(b)
+            assert (bits(got) == bits(host(a))).all(), pos
+            assert (bits(got) == bits(oracle.attention_decode(qh, kh, vh, n_heads, n_kv, hd, seq, pos))).all(), pos
+            wq, ws = oracle.quantize(got, gs)
+            assert (host(oq) == wq).all() and (bits(host(os_)) == bits(ws)).all(), pos
+    finally:
+        kc.k_attention_free(work)
+
+
+@pytest.mark.parametrize("n_heads,n_kv,hd", [(32, 8, 128), (4, 1, 128), (8, 2, 64)])
+def test_rope_attention_step_equals_the_two_calls(kc, oracle, n_heads, n_kv, hd):
+    """k_rope_attention_q8_step (the decode step's RoPE, K/V store and attention in one launch) bitwise
+    k_rope_kv_store_rows followed by k_attention_q8_rows: outputs, quantized outputs and scales, and the cache row it
+    writes; positions in the first and later chunks, and the context's last. The 8B shapes at 1 and 8 ranks."""
+    seq, gs = 4096, 64
+    assert kc.k_rope_attention_q8_step_ok(n_heads, n_kv, hd, gs) == 1
+    rng = np.random.default_rng(n_heads + hd)
+    kh = rng.standard_normal((n_kv, seq, hd), dtype=np.float32)
+    vh = rng.standard_normal((n_kv, seq, hd), dtype=np.float32)
+    table = dev(np.stack([oracle.rope_table(p, hd) for p in range(seq)]))
+    work = kc.attention_work(n_heads, n_kv, hd, seq)
+    try:
+        for pos in (0, 255, 256, 2303, seq - 1):
+            qh = rng.standard_normal(n_heads * hd, dtype=np.float32)
+            k_, v_ = rng.standard_normal(n_kv * hd, dtype=np.float32), rng.standard_normal(n_kv * hd, dtype=np.float32)
+            p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+            outs = []
+            for fused in (False, True):
+                q, kd, vd, kcache, vcache = dev(qh), dev(k_), dev(v_), dev(kh), dev(vh)
+                out = torch.zeros(n_heads * hd, device="cuda")
+                oq = torch.zeros(n_heads * hd, dtype=torch.int8, device="cuda")
+                os_ = torch.zeros(n_heads * hd // gs, device="cuda")
+                if fused:
+                    kc.k_rope_attention_q8_step(out, oq, os_, q, kd, vd, kcache, vcache, table, work, n_heads, n_kv,
+                                                hd, seq, p, gs)
+                else:
+                    kc.k_rope_kv_store_rows(q, n_heads * hd, kd, vd, n_kv * hd, kcache, vcache, table, p, 0, 1,
+                                            n_heads, n_kv, hd, seq)
+                    kc.k_attention_q8_rows(out, oq, os_, q, kcache, vcache, work, n_heads, n_kv, hd, seq, p, 0, 1, gs)
+                kc.status()
+                outs.append([host(t) for t in (out, oq, os_, kcache[:, pos], vcache[:, pos])])
+            for a, b in zip(*outs):
+                assert (a.view(np.uint8) == b.view(np.uint8)).all(), pos
+    finally:
+        kc.k_attention_free(work)
+
+
 def test_rope_kv_store_bitwise(kc, oracle):
     n_heads, n_kv, hd, seq, rows, pos0 = 8, 2, 64, 64, 5, 30
     rng = np.random.default_rng(7)
