@@ -383,6 +383,25 @@ def test_gemm_tc_group_dots_exact(kc, oracle, m, n, k):
     assert (host(dots) == oracle.group_dots(xq, wq, 64)).all()
 
 
+def test_gemm_tc_group_dots_exact_at_the_extremes(kc, oracle):
+    """The group dots at the largest magnitudes int8 allows (64 x 127 x 127 = 1032256 per group, positive and
+    negative, and sign patterns between), exact like the integer oracle."""
+    m, n, k = 130, 136, 512
+    rng = np.random.default_rng(5)
+    xq = np.full((m, k), 127, np.int8)
+    xq[1::2] = -127
+    xq[2::5] = rng.choice(np.array([-127, 127], np.int8), (len(xq[2::5]), k))
+    wq = np.full((n, k), 127, np.int8)
+    wq[3::3] = -127
+    wq[5::7] = rng.integers(-127, 128, (len(wq[5::7]), k), dtype=np.int8)
+    dots = torch.zeros((k // 64, m, n), dtype=torch.int32, device="cuda")
+    assert kc.k_gemm_q8_dots_test(dots, dev(xq), m, k, 64, dev(wq), n) == 1
+    kc.status()
+    ref = oracle.group_dots(xq, wq, 64)
+    assert np.abs(ref).max() == 64 * 127 * 127
+    assert (host(dots) == ref).all()
+
+
 # Partial token tiles skip the promotion of 16-column chunks past the last token (each epilogue warp holds 32 of a
 # tile's 128 token columns): M = 64 fills exactly two quarters, M = 65, 33 and 97 put one token in the next quarter,
 # M = 17 one token in a quarter's second chunk, M = 7 fills part of one chunk.
