@@ -234,8 +234,20 @@ template <int HD>
 __device__ bool merge_head_warp(const float *pb, int live, float *dst, int8_t *oq, float *os, long long e0, int gs) {
   constexpr int DL = HD / 32, slot = HD + 2;
   const int lane = threadIdx.x & 31;
-  float mx = -FLT_MAX;
-  for (int c = lane; c < live; c += 32)
+  // One round of loads covers the common case: lane c's chunk maximum and sum (chunks < 32) and the first eight
+  // chunks' elements, all in flight together; only the maxima of chunks 32.. and the elements of chunks 8.. follow.
+  float m0 = -FLT_MAX, l0 = 0.0f, a[8][DL];
+  if (lane < live) {
+    m0 = __ldcg(pb + (long long)lane * slot + HD);
+    l0 = __ldcg(pb + (long long)lane * slot + HD + 1);
+  }
+#pragma unroll
+  for (int u = 0; u < 8; u++)
+#pragma unroll
+    for (int e = 0; e < DL; e++)
+      a[u][e] = u < live ? __ldcg(pb + (long long)u * slot + DL * lane + e) : 0.0f;
+  float mx = fmaxf(-FLT_MAX, m0);
+  for (int c = lane + 32; c < live; c += 32)
     mx = fmaxf(mx, __ldcg(pb + (long long)c * slot + HD));
 #pragma unroll
   for (int off = 16; off; off >>= 1)
@@ -248,17 +260,19 @@ __device__ bool merge_head_warp(const float *pb, int live, float *dst, int8_t *o
     float w = 0.0f, wl = 0.0f;
     if (c0 + lane < live) {
       const float *pc = pb + (long long)(c0 + lane) * slot;
-      w = expf_libc(__fsub_rn(__ldcg(pc + HD), mx));
-      wl = __fmul_rn(w, __ldcg(pc + HD + 1));
+      const float mc = c0 == 0 ? m0 : __ldcg(pc + HD), lc = c0 == 0 ? l0 : __ldcg(pc + HD + 1);
+      w = expf_libc(__fsub_rn(mc, mx));
+      wl = __fmul_rn(w, lc);
     }
     const int nb = min(32, live - c0);
     for (int i = 0; i < nb; i += 8) {
-      float a[8][DL];
+      if (c0 > 0 || i > 0) {
 #pragma unroll
-      for (int u = 0; u < 8; u++)
+        for (int u = 0; u < 8; u++)
 #pragma unroll
-        for (int e = 0; e < DL; e++)
-          a[u][e] = i + u < nb ? __ldcg(pb + (long long)(c0 + i + u) * slot + DL * lane + e) : 0.0f;
+          for (int e = 0; e < DL; e++)
+            a[u][e] = i + u < nb ? __ldcg(pb + (long long)(c0 + i + u) * slot + DL * lane + e) : 0.0f;
+      }
 #pragma unroll
       for (int u = 0; u < 8; u++) {
         const float wc = __shfl_sync(0xffffffffu, w, (i + u) & 31), wlc = __shfl_sync(0xffffffffu, wl, (i + u) & 31);
@@ -436,9 +450,9 @@ __global__ void tiled_generic_kernel(const float *q, long long q_ld, const float
 // ---- the split variant for one row (decode) -----------------------------------------------------------------------
 // A cluster of kSplitCtas CTAs per (KV head g, chunk c) of the row at position pos: CTA k of the cluster loads K rows
 // [k n / 4, (k + 1) n / 4) of the chunk's n <= 256 positions (one bulk copy) and V[chunk rows][its quarter of the
-// head's elements] (cp.async), computes the scores of its K rows for the group's nq heads into its own shared memory,
-// and after a cluster barrier gathers the other three quarters' scores through distributed shared memory, so that
-// each CTA holds all of the chunk's scores. Each CTA then takes the maximum, exp512 and the 16-lane exp-sum per head
+// head's elements] (cp.async), computes the scores of its K rows for the group's nq heads and stores each into the
+// score buffer of every CTA of the cluster through distributed shared memory, so that after one cluster barrier each
+// CTA holds all of the chunk's scores. Each CTA then takes the maximum, exp512 and the 16-lane exp-sum per head
 // (the same in every CTA) and runs the P.V chains of its quarter of the head's elements. So each K and V element is
 // read once. A cluster walks chunks y, y + gridDim.y, ... (about one wave of clusters). With `tickets`, the CTA that
 // finishes a KV head's last chunk also merges the group's partials (the arithmetic of merge_kernel) and writes its
@@ -452,11 +466,12 @@ constexpr int kSplitThreads = 256;
 constexpr int kSplitTickets = 256;  // KV heads the fused merge serves (a ticket word each, past the partials)
 constexpr int kSplitRows = kSplitMax / kSplitCtas;  // K rows of a CTA at most
 
-// Floats before the mbarrier: K quarter [kSplitRows][hd], V quarter [kSplitMax][hd / 4], Q [nq][hd], this CTA's
-// scores [nq][kSplitRows], the chunk's scores (then probabilities) [nq][kSplitMax], the per-head maximum and exp-sum.
+// Floats before the mbarrier: K quarter [kSplitRows][hd], V quarter [kSplitMax][hd / 4], Q [nq][hd], the chunk's
+// scores (then probabilities) [nq][kSplitMax], which every CTA of the cluster writes its rows into, the per-head
+// maximum and exp-sum.
 __host__ __device__ constexpr size_t split_smem_floats(int hd, int nq) {
-  return (size_t)kSplitRows * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)nq * hd + (size_t)nq * kSplitRows +
-         (size_t)nq * kSplitMax + 2 * kMaxNq;
+  return (size_t)kSplitRows * hd + (size_t)kSplitMax * (hd / kSplitCtas) + (size_t)nq * hd + (size_t)nq * kSplitMax +
+         2 * kMaxNq;
 }
 __host__ __device__ constexpr size_t split_smem_bytes(int hd, int nq) {
   return split_smem_floats(hd, nq) * sizeof(float) + sizeof(uint64_t);
@@ -468,13 +483,12 @@ __device__ __forceinline__ void st_cluster_u32(unsigned *local, unsigned rank, u
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ float ld_cluster_f32(const float *local, unsigned rank) {
+__device__ __forceinline__ void st_cluster_f32(float *local, unsigned rank, float v) {
   unsigned remote;
-  float v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
+
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -544,7 +558,7 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
                                                               int gs, int early, const RopeStep rope) {
   constexpr int QD = HD / kSplitCtas;  // elements of the head this CTA's P.V covers
   extern __shared__ __align__(16) float sm[];
-  float *Kq = sm, *Vq = Kq + kSplitRows * HD, *Q = Vq + kSplitMax * QD, *Sl = Q + nq * HD, *S = Sl + nq * kSplitRows;
+  float *Kq = sm, *Vq = Kq + kSplitRows * HD, *Q = Vq + kSplitMax * QD, *S = Q + nq * HD;
   float *hmax = S + nq * kSplitMax, *hsum = hmax + kMaxNq;
   uint64_t *bar = reinterpret_cast<uint64_t *>(sm + split_smem_floats(HD, nq));
   __shared__ unsigned fails[kSplitCtas];
@@ -664,8 +678,14 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
         tree_step<4>(t4, t2, L, 2);
         tree_step<2>(t2, t1, L, 1);
         const int t = grp * 16 + L;
-        if (h < nq && t < kn)
-          Sl[h * kSplitRows + t] = __fdiv_rn(t1[0], divisor);
+        if (h < nq && t < kn) {
+          // Position k0 + t of the chunk: into the scores of every CTA of the cluster (its own included), so the
+          // barrier below leaves each with all of the chunk's scores and nothing has to be fetched afterwards.
+          const float sc = __fdiv_rn(t1[0], divisor);
+#pragma unroll
+          for (int r = 0; r < kSplitCtas; r++)
+            st_cluster_f32(S + h * kSplitMax + k0 + t, (unsigned)r, sc);
+        }
       }
     } else if (tid == 0) {
       mbar_wait_bounded(bar, phase ^ 1u);  // let the copy in flight land (bounded) before leaving
@@ -679,15 +699,6 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
       cluster_sync_all();  // no CTA leaves while another may still read its scores
       break;             // the whole cluster stops in the same iteration (the error is raised)
     }
-    // The chunk's scores from the four CTAs (position t is CTA kk's row t - k0(kk)), all loads in flight together.
-    for (int i = tid; i < nq * n; i += kSplitThreads) {
-      const int h = i / n, t = i - h * n;
-      int kk = kSplitCtas - 1;
-      while (kk > 0 && n * kk / kSplitCtas > t)
-        kk--;
-      S[h * kSplitMax + t] = ld_cluster_f32(Sl + h * kSplitRows + t - n * kk / kSplitCtas, (unsigned)kk);
-    }
-    __syncthreads();
     // Per head (a warp each): the maximum, exp512, the exp-sum in 16 lanes (lane l adds positions l, l + 16, l + 32,
     // ... in order: l + 32 i is its own value i, l + 16 + 32 i lane l + 16's) then the tree.
     for (int h = warp; h < nq; h += kSplitThreads / 32) {

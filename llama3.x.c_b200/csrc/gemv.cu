@@ -306,14 +306,18 @@ __device__ __forceinline__ void quantize_staged(const float *XF, const float *NW
 // weights) staged into shared memory, RMSNorm (the k_rmsnorm_q8_rows arithmetic: rms_lane_sum, rms_inverse,
 // rms_apply) when asked, then each gs-group quantized by k_quantize's rule into XQ / XS. Bitwise the separate kernels'
 // result. scratch: 65 floats (the chain buffers, unused until the main loop).
+// The norm weights depend on no kernel: the caller stages them (stage_norm_weights) before waiting on the previous one.
+__device__ __forceinline__ void stage_norm_weights(const GemvArgs &a, float *XF) {
+  if (a.act == kActNormQuantize)
+    stage_floats(XF + a.n, a.normw, a.n, false);
+}
+
 __device__ __forceinline__ void prepare_activation(const GemvArgs &a, int8_t *XQ, float *XS, float *XF, float *scratch,
                                                    int gs) {
   const int tid = threadIdx.x, n = a.n;
   const bool norm = a.act == kActNormQuantize;
   float *NW = XF + n;
   stage_floats(XF, a.xf, n, false);
-  if (norm)
-    stage_floats(NW, a.normw, n, false);
   __syncthreads();
   if (norm) {
     if (tid < 64)
@@ -554,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q8_kernel(const __grid_const
   // prefetch on the way into this SM.
   if (warp == kComputeWarps && S > 0)
     issue_stage(m, gpc, a.kblock, subtile(plan, 0), 0, swiglu, lane, stages, &full[0]);
+  stage_norm_weights(a, reinterpret_cast<float *>(XQ + ((n + 15) & ~15)));
   pdl_wait();
   // The counter was written by the previous reducing call, complete once pdl_wait returns.
   const unsigned seq = RED ? a.peer.epoch[c] + 1u : 0u;
