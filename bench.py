@@ -426,7 +426,26 @@ def parity_block(eng, m, arch, world, rank, prompt, tokens):
         "first_logits_bitwise": bool((np.asarray(logits, np.float32).view(np.int32) == first.view(np.int32)).all()),
         "first_logits_max_rel_diff": float(np.abs(logits - first).max() / np.abs(first).max()),
     })
+    if world > 2:
+        drift = reference_split_drift(g, arch)
+        if drift is not None:
+            block["reference_two_socket_vs_one"] = drift
     return block
+
+
+def reference_split_drift(g, arch):
+    """How far the reference's own two-socket split moves it from its one-socket run on the benchmark request (both in
+    tests/golden/bench_golden.npz): the scale against which a split this engine runs, and the reference cannot, is to
+    be read. None when the golden file lacks either run."""
+    s1, s2 = f"{arch}_s1", f"{arch}_s2"
+    if s1 + "_tokens" not in g.files or s2 + "_tokens" not in g.files:
+        return None
+    first, margins, maxes = g[s1 + "_first"], g[s1 + "_margins"], g[s1 + "_maxes"]
+    r1, r2 = g[s1 + "_tokens"].tolist(), g[s2 + "_tokens"].tolist()
+    rdiv = next((i for i, (x, y) in enumerate(zip(r1, r2)) if x != y), None)
+    return {"first_logits_max_rel_diff": float(np.abs(g[s2 + "_first"] - first).max() / np.abs(first).max()),
+            "first_divergence_step": rdiv,
+            "ref_margin_at_divergence": None if rdiv is None else round(float(margins[rdiv] / maxes[rdiv]), 6)}
 
 
 def run_engine(args):

@@ -168,3 +168,16 @@ def test_reference_gemm_bench_output_parses(bench):
     pts = bench.reference_gemm_points([(256, 512)], (8, 32))
     assert set(pts["points"]) == {(256, 512, 8), (256, 512, 32)}
     assert all(us > 0 and tops > 0 for us, tops, _ in pts["points"].values())
+
+
+def test_reference_split_drift_from_the_golden_runs(bench):
+    """The reference's own two-socket run against its one-socket run on the benchmark request (the committed golden
+    file): its first logits move by 6.3% of the largest and its tokens part at step 5, at a 1.8e-3 margin. The bench
+    reports this beside its 4- and 8-GPU parity, which can only be compared with the one-socket run."""
+    import numpy as np
+    g = np.load(Path(__file__).parent / "golden" / "bench_golden.npz")
+    d = bench.reference_split_drift(g, "8b")
+    assert d["first_divergence_step"] == 5
+    assert 0.06 < d["first_logits_max_rel_diff"] < 0.07
+    assert d["ref_margin_at_divergence"] < 2e-3
+    assert bench.reference_split_drift(g, "1b") is None  # no two-socket run of the 1B request
