@@ -767,9 +767,11 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
       o[HD] = hmax[tid];
       o[HD + 1] = hsum[tid];
     }
-    // The scores, K and V buffers are refilled by the cluster's next chunk, and a CTA's scores are read by the others
-    // until they pass this barrier: every CTA is done with them first.
-    cluster_sync_all();
+    // The scores, K and V buffers are refilled by the cluster's next chunk, whose scores the other CTAs write into
+    // this CTA's buffer: every CTA is done with them first. After the cluster's last chunk no CTA touches another's
+    // shared memory any more (the scores were exchanged before the barrier above), so none waits.
+    if (c + (int)gridDim.y < chunks)
+      cluster_sync_all();
   }
   if (!tickets)
     return;
