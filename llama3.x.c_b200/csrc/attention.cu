@@ -780,13 +780,14 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
   const unsigned mine = (unsigned)((chunks - 1 - (int)blockIdx.y) / (int)gridDim.y + 1);
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const unsigned before = atomicAdd(tickets + g, mine);
+    // One acquire-release add: it publishes this CTA's partials (written before the barrier above) and, for the CTA
+    // that completes the count, makes every other CTA's partials visible to the merge after the barrier below. The
+    // reset is read by the next call, a later kernel.
+    unsigned before;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(before) : "l"(tickets + g), "r"(mine) : "memory");
     last = before + mine == (unsigned)(kSplitCtas * chunks);
-    if (last) {
+    if (last)
       tickets[g] = 0u;
-      __threadfence();
-    }
   }
   __syncthreads();
   if (last)
