@@ -401,18 +401,25 @@ __device__ unsigned kc_gemv_group_counter[kMaxOutputGroups];
 __device__ void quantize_output_groups(const KcGemvTail &t, const float *out, int r0, int r1, int gs, int *flags) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g0 = r0 / gs, ng = (r1 - 1) / gs - g0 + 1;
-  __threadfence();  // this CTA's outputs, visible before the counts say so
-  __syncthreads();
+  __syncthreads();  // this CTA's outputs are written
+  // Acquire-release adds: each publishes the CTA's outputs (ordered before it by the barrier above) and, when it
+  // completes a group, makes the other CTAs' rows of that group visible to the warp that quantizes it (ordered after
+  // it by the barrier below).
   for (int i = tid; i < ng; i += kThreads) {
-    const int g = g0 + i, lo = max(r0, g * gs), hi = min(r1, (g + 1) * gs);
-    flags[i] = atomicAdd(&kc_gemv_group_counter[g], (unsigned)(hi - lo)) + (unsigned)(hi - lo) == (unsigned)gs;
+    const int g = g0 + i;
+    const unsigned cnt = (unsigned)(min(r1, (g + 1) * gs) - max(r0, g * gs));
+    unsigned before;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                 : "=r"(before)
+                 : "l"(kc_gemv_group_counter + g), "r"(cnt)
+                 : "memory");
+    flags[i] = before + cnt == (unsigned)gs;
   }
   __syncthreads();
   for (int i = warp; i < ng; i += kThreads / 32) {
     if (!flags[i])
       continue;
     const int g = g0 + i;
-    __threadfence();  // the other CTAs' rows of the group, counted in before the count completed
     float mx = 0.0f;
     int bad = 0;
     for (int j = lane; j < gs; j += 32) {
