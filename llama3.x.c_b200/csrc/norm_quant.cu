@@ -95,9 +95,60 @@ __global__ void quantize_rows64_kernel(int8_t *q, float *s, const float *x, long
   }
 }
 
+// gs = 64 with 16-byte rows: a half-warp per group, each lane a float4 of it, a warp taking kQuant4Groups groups with
+// every load in flight before the first reduction (the group maximum is four shuffles within the half-warp); per
+// element the arithmetic is quantize_rows_kernel's.
+constexpr int kQuant4Groups = 8;
+
+__global__ void quantize_rows64x4_kernel(int8_t *q, float *s, const float *x, long long ldx, int m, int n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
+  const int groups = n / 64;
+  const long long total = (long long)m * groups;
+  const long long g0 = ((long long)blockIdx.x * (blockDim.x >> 5) + warp) * kQuant4Groups;
+  float4 v[kQuant4Groups / 2];
+#pragma unroll
+  for (int k = 0; k < kQuant4Groups / 2; k++) {
+    const long long gid = g0 + 2 * k + half;
+    if (gid < total) {
+      const long long row = gid / groups, g = gid - row * groups;
+      v[k] = *reinterpret_cast<const float4 *>(x + row * ldx + g * 64 + 4 * l16);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kQuant4Groups / 2; k++) {
+    const long long gid = g0 + 2 * k + half;
+    const bool live = gid < total;
+    const int bad = live && (!isfinite(v[k].x) || !isfinite(v[k].y) || !isfinite(v[k].z) || !isfinite(v[k].w));
+    const unsigned ballot = __ballot_sync(0xffffffffu, bad);
+    float mx = live ? fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))) : 0.0f;
+#pragma unroll
+    for (int o = 8; o; o >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (!live)
+      continue;
+    if ((ballot >> (16 * half)) & 0xFFFFu) {
+      if (l16 == 0)
+        kc_raise(KC_ERR_NONFINITE);
+      continue;
+    }
+    const long long row = gid / groups, g = gid - row * groups;
+    const float scale = __fdiv_rn(mx, 127.0f);
+    if (l16 == 0)
+      s[row * groups + g] = scale;
+    char4 c;
+    c.x = (signed char)quantize_value(v[k].x, scale);
+    c.y = (signed char)quantize_value(v[k].y, scale);
+    c.z = (signed char)quantize_value(v[k].z, scale);
+    c.w = (signed char)quantize_value(v[k].w, scale);
+    *reinterpret_cast<char4 *>(q + row * n + g * 64 + 4 * l16) = c;
+  }
+}
+
 constexpr int kNormThreads = 256;
 constexpr int kMaxValuesPerLane = 8;    // fused quantize: gs <= 256
-constexpr int kNormStagedMax = 16384;   // sizes whose row and weights are staged in shared memory (128 KB)
+constexpr int kNormStagedMax = 16384;   // sizes whose row is staged in shared memory (64 KB)
 
 // Copies n floats (global, any alignment) to shared memory with all threads, each keeping 8 loads in flight before
 // its first store (a load-then-store loop would wait one memory round trip per element).
@@ -135,7 +186,7 @@ __device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
 // One CTA per row. With STAGED the row and the weights are first copied to shared memory (2 * size floats of dynamic
 // shared memory); without, they are read from global memory (sizes beyond kNormStagedMax).
 template <bool STAGED>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_t *q, float *s, const float *x,
+__global__ void __launch_bounds__(kNormThreads, 5) rmsnorm_kernel(float *out, int8_t *q, float *s, const float *x,
                                                                 const float *w, int size, long long ldx, float eps,
                                                                 int gs) {
   pdl_wait();
@@ -145,12 +196,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *out, int8_
   __shared__ float inv;
   const int tid = threadIdx.x, row = blockIdx.x;
   const float *xr = x + row * ldx;
-  if (STAGED) {
+  if (STAGED) {  // the row only: the weights are the same for every row, so every CTA of the SM reads them cached
     stage_row(norm_dyn, xr, size);
-    stage_row(norm_dyn + size, w, size);
     __syncthreads();
     xr = norm_dyn;
-    w = norm_dyn + size;
   }
   if (tid < 64)
     lanes[tid] = rms_lane_sum(xr, size, tid);
@@ -240,7 +289,11 @@ int kc_launch_quantize_rows(int8_t *q, float *s, const float *x, long long ldx, 
   if (groups == 0)
     return 0;
   const int warps = 8;
-  if (gs == 64 && ((uintptr_t)x & 7) == 0 && (ldx & 1) == 0 && ((uintptr_t)q & 1) == 0) {
+  if (gs == 64 && ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0 && ((uintptr_t)q & 3) == 0 && (n & 3) == 0) {
+    const long long per_block = (long long)warps * kQuant4Groups;
+    kc_launch_pdl(quantize_rows64x4_kernel, (unsigned)((groups + per_block - 1) / per_block), warps * 32, 0, stream,
+                  q, s, x, ldx, m, n);
+  } else if (gs == 64 && ((uintptr_t)x & 7) == 0 && (ldx & 1) == 0 && ((uintptr_t)q & 1) == 0) {
     const long long per_block = (long long)warps * kQuantGroupsPerWarp;
     kc_launch_pdl(quantize_rows64_kernel, (unsigned)((groups + per_block - 1) / per_block), warps * 32, 0, stream, q,
                   s, x, ldx, m, n);
@@ -261,12 +314,12 @@ int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const flo
     static int attr_bytes[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    const int bytes = 2 * size * (int)sizeof(float);
+    const int bytes = size * (int)sizeof(float);
     if (dev >= 0 && dev < 64 && bytes > attr_bytes[dev]) {
       if (cudaFuncSetAttribute(rmsnorm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kNormStagedMax * (int)sizeof(float)) != cudaSuccess)
+                               kNormStagedMax * (int)sizeof(float)) != cudaSuccess)
         return -2;
-      attr_bytes[dev] = 2 * kNormStagedMax * (int)sizeof(float);
+      attr_bytes[dev] = kNormStagedMax * (int)sizeof(float);
     }
     kc_launch_pdl(rmsnorm_kernel<true>, rows, kNormThreads, bytes, stream, out, q, s, x, w, size, ldx, eps, gs);
   } else {
