@@ -311,16 +311,11 @@ int kc_launch_rmsnorm(float *out, int8_t *q, float *s, const float *x, const flo
   if (q && (gs <= 0 || gs > 32 * kMaxValuesPerLane || size % gs))
     return -1;
   if (size <= kNormStagedMax) {
-    static int attr_bytes[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
     const int bytes = size * (int)sizeof(float);
-    if (dev >= 0 && dev < 64 && bytes > attr_bytes[dev]) {
-      if (cudaFuncSetAttribute(rmsnorm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kNormStagedMax * (int)sizeof(float)) != cudaSuccess)
-        return -2;
-      attr_bytes[dev] = kNormStagedMax * (int)sizeof(float);
-    }
+    // Raised once per device to the largest staged row (kc_allow_smem keeps its own locked record).
+    if (bytes > 48 * 1024 && kc_allow_smem(reinterpret_cast<const void *>(rmsnorm_kernel<true>),
+                                           kNormStagedMax * (int)sizeof(float)) != cudaSuccess)
+      return -2;
     kc_launch_pdl(rmsnorm_kernel<true>, rows, kNormThreads, bytes, stream, out, q, s, x, w, size, ldx, eps, gs);
   } else {
     kc_launch_pdl(rmsnorm_kernel<false>, rows, kNormThreads, 0, stream, out, q, s, x, w, size, ldx, eps, gs);
