@@ -485,7 +485,8 @@ def run_engine(args):
     parity = parity_block(eng, m, args.workload, world, rank, prompt, tokens)
 
     # End to end through the reference-facing API with host buffers: engine_forward per token (the token and position
-    # go host -> device, the vocabulary's logits come back to the host), host argmax, as probe-int8 generate does.
+    # go host -> device, the vocabulary's logits come back to the host), host argmax over the returned buffer, as
+    # probe-int8 generate does with the pointer engine_forward returns.
     E = 32
     logits = m.forward_batch(prompt, 0, eng.LOGITS_LAST)
     tok = int(np.argmax(logits))
@@ -494,7 +495,7 @@ def run_engine(args):
     barrier(world)
     t0 = time.perf_counter()
     for j in range(E):
-        tok = int(np.argmax(m.forward(tok, P + j)))
+        tok = int(np.argmax(m.forward_view(tok, P + j)))
     e2e_s = max_over_ranks(world, time.perf_counter() - t0)
     m.close()
 

@@ -233,6 +233,15 @@ class Engine:
             raise _kc().KernelError("engine_forward failed")
         return np.ctypeslib.as_array(p, (self.config.vocab_size,)).copy()
 
+    def forward_view(self, token, position):
+        """engine_forward with the reference's contract kept: a view of the engine's own host logits, valid until the
+        next call on this model (forward() returns a copy instead)."""
+        p = self.lib.engine_forward(self._m, int(token), int(position))
+        _check()
+        if not p:
+            raise _kc().KernelError("engine_forward failed")
+        return np.ctypeslib.as_array(p, (self.config.vocab_size,))
+
     def forward_batch(self, tokens, pos0, want=LOGITS_LAST):
         arr = _ints(tokens)
         p = self.lib.engine_forward_batch(self._m, arr, len(tokens), int(pos0), want)

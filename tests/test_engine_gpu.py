@@ -159,6 +159,21 @@ def test_device_greedy_equals_host_greedy_loop(eng, files):
     assert device == host
 
 
+def test_forward_view_is_the_engines_buffer(eng):
+    """forward_view returns the engine's own host logits (the reference's engine_forward contract: valid until the next
+    call), bitwise what forward copies out; the next call overwrites it in place."""
+    cfg = dict(dim=256, hidden_dim=512, n_layers=2, n_heads=8, n_kv_heads=2, vocab_size=1000, seq_len=64)
+    with eng.Engine.random(**cfg, seed=4) as m:
+        copies = [m.forward(t, i) for i, t in enumerate((3, 9, 27))]
+    with eng.Engine.random(**cfg, seed=4) as m:
+        views = []
+        for i, t in enumerate((3, 9, 27)):
+            v = m.forward_view(t, i)
+            assert (v.view(np.int32) == copies[i].view(np.int32)).all()
+            views.append(v)
+        assert (views[0].view(np.int32) == copies[2].view(np.int32)).all()  # one buffer, last call's logits
+
+
 def test_small_batches_and_chunked_prefill(eng, files, monkeypatch):
     """Prefill through the row-kernel GEMM (batches below 8 rows) and in several chunks gives the reference's tokens."""
     monkeypatch.setenv("LLAMA_PREFILL_BATCH", "7")
