@@ -271,6 +271,8 @@ __device__ __forceinline__ void quantize_staged(const float *XF, const float *NW
   // Four lanes per group, each taking every fourth value (gs / 4 of them), the walk rotated by the group's place in
   // the warp so the 32 lanes read 32 different banks; the group max comes from two shuffles. The max is
   // order-independent and each value is quantized on its own, so the mapping does not change a bit of the result.
+  // The loops stay rolled: this runs once per CTA at the start of every launch, from a cold instruction cache, and
+  // unrolled copies measured slower (decode step 2.38 ms rolled, 2.39 / 2.46 / 2.66 ms unrolled by 2 / 4 / 8).
   const int per = gs / 4, sub = lane & 3, g8 = (lane >> 2) & 7;
   const int groups = n / gs, slots = (groups + 7) / 8 * 32;  // 8 groups per warp-sized slot
   for (int t = tid; t < slots; t += kThreads) {
@@ -280,6 +282,7 @@ __device__ __forceinline__ void quantize_staged(const float *XF, const float *NW
     float mx = 0.0f;
     int bad = 0;
     if (live)
+#pragma unroll 1
       for (int i = 0; i < per; i++) {
         const int j = (4 * (i + g8) + sub) & (gs - 1);
         const float v = norm ? rms_apply(xg[j], wg[j], inv) : xg[j];
@@ -295,6 +298,7 @@ __device__ __forceinline__ void quantize_staged(const float *XF, const float *NW
     const float scale = __fdiv_rn(mx, 127.0f);
     if (sub == 0)
       s[grp] = scale;
+#pragma unroll 1
     for (int i = 0; i < per; i++) {
       const int j = (4 * (i + g8) + sub) & (gs - 1);
       q[grp * gs + j] = (int8_t)quantize_value(norm ? rms_apply(xg[j], wg[j], inv) : xg[j], scale);
