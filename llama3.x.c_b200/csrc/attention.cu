@@ -798,22 +798,22 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
 // CTA (KV head g, group of R rows = whole blocks): its query vectors v = (row - first row) * nq + head, at most 128,
 // over the 32-position K/V tiles of the group's causal range (bulk copies, two buffers, the next tile's copy in
 // flight; K rows padded in shared memory so that rows read together sit in different banks). Warp w owns query
-// vectors 8 w .. 8 w + 7 from the scores to the P.V product, so within a tile its warps never wait for one another
-// (16 warps, four per SM sub-partition, cover one another's shared-memory and FMA latencies):
-//  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 8 w + lv + 4 i (i < 2) and positions lp + 8 j
+// vectors 16 w .. 16 w + 15 from the scores to the P.V product, so within a tile its warps never wait for one another
+// (8 warps, two per SM sub-partition: 16 queries a warp give each shared-memory operand twice the FMAs that 8 did):
+//  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 16 w + lv + 4 i (i < 4) and positions lp + 8 j
 //    (j < 4), each score one FMA chain over the head's elements in order, operands read four elements at a time;
 //  - the online softmax of the tile for each query, among the 8 lanes that share it: the tile maximum, the rescale of
 //    the running sum, exp512, and the tile sum in the reference's order (positions p and 16 + p are the same lane's
 //    j and j + 2, then the 16-lane tree by shuffles across the 8 lanes); every lane keeps the queries' running
 //    maximum, sum and chunk;
-//  - P.V: every lane takes the warp's 8 queries x hd / 32 elements, one FMA chain per (query, element) over the
-//    tile's positions in order.
+//  - P.V: every lane takes the warp's 16 queries x hd / 32 elements, one FMA chain per (query, element) over the
+//    tile's positions in order; the probabilities are read as warp-wide broadcasts.
 // A query whose chunk (its block's plan) changes at a tile writes the finished chunk's partial first and starts again
 // from zero. The partials are merged by merge_kernel.
 constexpr int kTQ = 128;            // query vectors of a batched CTA
-constexpr int kQW = 8;              // query vectors of a warp
+constexpr int kQW = 16;             // query vectors of a warp
 constexpr int kQL = kQW / 4;        // query vectors of a lane in the score role
-constexpr int kTWarps = kTQ / kQW;  // 16 warps
+constexpr int kTWarps = kTQ / kQW;  // 8 warps
 constexpr int kPStride = kTQ + 4;   // probabilities [tile position][query vector], padded
 
 __host__ __device__ constexpr int tiled_kstride(int hd) { return hd + 4; }  // padded K and Q rows
