@@ -908,15 +908,24 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
 #pragma unroll
       for (int j = 0; j < 4; j++)
         s[i][j] = 0.0f;
+    float4 qq[kQL], kk[4];
+#pragma unroll
+    for (int i = 0; i < kQL; i++)
+      qq[i] = *reinterpret_cast<const float4 *>(qs + (v0 + lv + 4 * i) * KS);
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      kk[j] = *reinterpret_cast<const float4 *>(Kt + (lp + 8 * j) * KS);
 #pragma unroll 2
     for (int d = 0; d < HD; d += 4) {
-      float4 qq[kQL], kk[4];
+      // The next four elements' operands are read before this step's FMAs (the last step re-reads its own).
+      const int dn = d + 4 < HD ? d + 4 : d;
+      float4 qn[kQL], kn[4];
 #pragma unroll
       for (int i = 0; i < kQL; i++)
-        qq[i] = *reinterpret_cast<const float4 *>(qs + (v0 + lv + 4 * i) * KS + d);
+        qn[i] = *reinterpret_cast<const float4 *>(qs + (v0 + lv + 4 * i) * KS + dn);
 #pragma unroll
       for (int j = 0; j < 4; j++)
-        kk[j] = *reinterpret_cast<const float4 *>(Kt + (lp + 8 * j) * KS + d);
+        kn[j] = *reinterpret_cast<const float4 *>(Kt + (lp + 8 * j) * KS + dn);
 #pragma unroll
       for (int i = 0; i < kQL; i++)
 #pragma unroll
@@ -926,6 +935,12 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
           s[i][j] = __fmaf_rn(qq[i].z, kk[j].z, s[i][j]);
           s[i][j] = __fmaf_rn(qq[i].w, kk[j].w, s[i][j]);
         }
+#pragma unroll
+      for (int i = 0; i < kQL; i++)
+        qq[i] = qn[i];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        kk[j] = kn[j];
     }
     // Online softmax, query by query. The 8 lanes of a query agree on whether it sees the tile, and every shuffle runs
     // in every lane; the state only moves where the query sees positions.
@@ -1003,9 +1018,8 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
     }
     const float *Vt = Vb + b * kTile * HD + DL * lane;
     const float *Pw = P + v0;
-#pragma unroll 2
-    for (int p = 0; p < cnt; p++) {
-      float vv[DL];
+    // Row p's operands: the lane's DL elements of V and the warp's kQW probabilities (broadcasts).
+    auto load_pv = [&](int p, float (&vv)[DL], float4 (&pe)[kQW / 4]) {
       if (DL == 4) {
         const float4 x4 = *reinterpret_cast<const float4 *>(Vt + p * HD);
         vv[0] = x4.x, vv[1 % DL] = x4.y, vv[2 % DL] = x4.z, vv[3 % DL] = x4.w;
@@ -1016,15 +1030,33 @@ __global__ void __launch_bounds__(kTWarps * 32, 1) tiled_kernel(const float *q, 
         vv[0] = Vt[p * HD];
       }
 #pragma unroll
+      for (int y = 0; y < kQW / 4; y++)
+        pe[y] = *reinterpret_cast<const float4 *>(Pw + p * kPStride + 4 * y);
+    };
+    float vv[DL];
+    float4 pe[kQW / 4];
+    load_pv(0, vv, pe);
+#pragma unroll 2
+    for (int p = 0; p < cnt; p++) {
+      // The next row's operands are read before this row's FMAs (the last row re-reads its own).
+      float vn[DL];
+      float4 pn[kQW / 4];
+      load_pv(p + 1 < cnt ? p + 1 : p, vn, pn);
+#pragma unroll
       for (int y = 0; y < kQW / 4; y++) {
-        const float4 e4 = *reinterpret_cast<const float4 *>(Pw + p * kPStride + 4 * y);
-        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+        const float ev[4] = {pe[y].x, pe[y].y, pe[y].z, pe[y].w};
 #pragma unroll
         for (int u = 0; u < 4; u++)
 #pragma unroll
           for (int e = 0; e < DL; e++)
             acc[4 * y + u][e] = __fmaf_rn(ev[u], vv[e], acc[4 * y + u][e]);
       }
+#pragma unroll
+      for (int e = 0; e < DL; e++)
+        vv[e] = vn[e];
+#pragma unroll
+      for (int y = 0; y < kQW / 4; y++)
+        pe[y] = pn[y];
     }
     __syncthreads();  // the buffers of this tile are refilled two tiles on (and P, al, fl by the next tile)
   }
