@@ -799,7 +799,8 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_kernel(const float *q,
 // over the 32-position K/V tiles of the group's causal range (bulk copies, two buffers, the next tile's copy in
 // flight; K rows padded in shared memory so that rows read together sit in different banks). Warp w owns query
 // vectors 16 w .. 16 w + 15 from the scores to the P.V product, so within a tile its warps never wait for one another
-// (8 warps, two per SM sub-partition: 16 queries a warp give each shared-memory operand twice the FMAs that 8 did):
+// (8 warps, two per SM sub-partition: with 16 queries a warp, 4 x 4 scores a lane take 8 operand reads per 64 FMAs
+// where 2 x 4 took 6 per 32, and P.V's probabilities are warp-wide broadcasts):
 //  - scores: lane (lv, lp) = (lane / 8, lane % 8) takes queries 16 w + lv + 4 i (i < 4) and positions lp + 8 j
 //    (j < 4), each score one FMA chain over the head's elements in order, operands read four elements at a time;
 //  - the online softmax of the tile for each query, among the 8 lanes that share it: the tile maximum, the rescale of
